@@ -1,0 +1,252 @@
+"""numpy front end for the CPU oracle (liboracle.so, built from du_oracle.c).
+
+TEST INFRASTRUCTURE ONLY: the checker that tests/, ``__graft_entry__.smoke()``
+and bench.py's CPU-baseline leg compare the CUDA library against.  The product
+package (deepunity_b200) never imports this module.
+
+Each function names the reference code it restates; see du_oracle.c.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import subprocess
+
+import numpy as np
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+_LIB_PATH = os.path.join(_HERE, "liboracle.so")
+_lib = None
+
+FP16, INT8, INT4 = 0, 1, 2
+_QUANT_IDS = {"fp16": FP16, "int8": INT8, "int4": INT4}
+
+
+def build() -> str:
+    """Compile liboracle.so in place (make) if it is missing or stale."""
+    src = os.path.join(_HERE, "du_oracle.c")
+    if not os.path.exists(_LIB_PATH) or os.path.getmtime(_LIB_PATH) < os.path.getmtime(src):
+        subprocess.run(["make", "-C", _HERE, "-s"], check=True)
+    return _LIB_PATH
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        build()
+        _lib = C.CDLL(_LIB_PATH)
+        P = C.c_void_p
+        _lib.orc_f32_to_f16.restype = C.c_uint16
+        _lib.orc_f32_to_f16.argtypes = [C.c_float]
+        _lib.orc_f16_to_f32.restype = C.c_float
+        _lib.orc_f16_to_f32.argtypes = [C.c_uint16]
+        _lib.orc_quantize_int8.argtypes = [P, C.c_int64, C.c_int64, P, P]
+        _lib.orc_quantize_int4.argtypes = [P, C.c_int64, C.c_int64, C.c_int, P, P]
+        _lib.orc_dequant.argtypes = [P, P, C.c_int, C.c_int, C.c_int64, C.c_int64, P]
+        _lib.orc_gemv.argtypes = [P, C.c_int, C.c_int, P, P, C.c_int, C.c_int, C.c_int64, C.c_int, P]
+        _lib.orc_rmsnorm.argtypes = [P, C.c_int, C.c_int, P, C.c_float, P]
+        _lib.orc_rope_table.argtypes = [C.c_int, C.c_int, C.c_float, P, P]
+        _lib.orc_rope_apply.argtypes = [P, C.c_int, C.c_int, C.c_int, C.c_int, P, P]
+        _lib.orc_kv_write.argtypes = [P, C.c_int, C.c_int, C.c_int, C.c_int, P]
+        _lib.orc_flash_attention.argtypes = [P, P, P, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int,
+                                             C.c_float, P]
+        _lib.orc_argmax.restype = C.c_int
+        _lib.orc_argmax.argtypes = [P, C.c_int]
+        _lib.orc_forward.restype = C.c_int
+        _lib.orc_forward.argtypes = [P, P, C.c_int, C.c_int, P]
+        _lib.orc_dense_linear.argtypes = [P, C.c_int, C.c_int, C.c_int, C.c_int, P, P, P, C.c_int]
+        _lib.orc_module_layer_decode.argtypes = [P, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int,
+                                                 C.c_float, C.c_float, P, P, P, P, P, P, P, P, P,
+                                                 C.c_int, P, C.c_int]
+        _lib.orc_max_threads.restype = C.c_int
+    return _lib
+
+
+def _p(a: np.ndarray):
+    assert a.flags["C_CONTIGUOUS"], "oracle arrays must be C-contiguous"
+    return a.ctypes.data_as(C.c_void_p)
+
+
+def f32_to_f16_bits(x: float) -> int:
+    return int(lib().orc_f32_to_f16(float(x)))
+
+
+def quantize_int8(w: np.ndarray):
+    """import_params.quantize_int8 restated: (int8 [rows, cols], fp16 bits [rows])."""
+    w = np.ascontiguousarray(w, dtype=np.float32)
+    rows, cols = w.shape
+    q = np.empty((rows, cols), np.int8)
+    s = np.empty(rows, np.uint16)
+    lib().orc_quantize_int8(_p(w), rows, cols, _p(q), _p(s))
+    return q, s
+
+
+def quantize_int4(w: np.ndarray, group: int = 32):
+    """import_params.quantize_int4 restated with a group parameter:
+    (packed uint8 [rows, cols/2], fp16 bits [rows, cols/group])."""
+    w = np.ascontiguousarray(w, dtype=np.float32)
+    rows, cols = w.shape
+    assert cols % group == 0 and group % 2 == 0
+    p = np.empty((rows, cols // 2), np.uint8)
+    s = np.empty((rows, cols // group), np.uint16)
+    lib().orc_quantize_int4(_p(w), rows, cols, group, _p(p), _p(s))
+    return p, s
+
+
+def dequant(w: np.ndarray, s, quant: str, rows: int, cols: int, group: int = 32) -> np.ndarray:
+    out = np.empty((rows, cols), np.float32)
+    s_arr = np.ascontiguousarray(s, dtype=np.uint16) if s is not None else None
+    lib().orc_dequant(_p(np.ascontiguousarray(w)), _p(s_arr) if s_arr is not None else None,
+                      _QUANT_IDS[quant], group, rows, cols, _p(out))
+    return out
+
+
+def gemv(x: np.ndarray, w: np.ndarray, s, quant: str, n_rows: int, group: int = 32,
+         row_off: int = 0) -> np.ndarray:
+    """Coalesced GEMV/GEMM restatement: y[m, n] for rows [row_off, row_off + n_rows)."""
+    x = np.ascontiguousarray(np.atleast_2d(x), dtype=np.float32)
+    M, K = x.shape
+    y = np.empty((M, n_rows), np.float32)
+    s_arr = np.ascontiguousarray(s, dtype=np.uint16) if s is not None else None
+    lib().orc_gemv(_p(x), M, K, _p(np.ascontiguousarray(w)), _p(s_arr) if s_arr is not None else None,
+                   _QUANT_IDS[quant], group, row_off, n_rows, _p(y))
+    return y
+
+
+def rmsnorm(x: np.ndarray, gamma_m1_bits: np.ndarray, eps: float) -> np.ndarray:
+    x = np.ascontiguousarray(np.atleast_2d(x), dtype=np.float32)
+    y = np.empty_like(x)
+    lib().orc_rmsnorm(_p(x), x.shape[0], x.shape[1], _p(np.ascontiguousarray(gamma_m1_bits, np.uint16)),
+                      eps, _p(y))
+    return y
+
+
+def rope_table(max_seq: int, head_dim: int, theta: float):
+    c = np.empty((max_seq, head_dim // 2), np.uint16)
+    s = np.empty((max_seq, head_dim // 2), np.uint16)
+    lib().orc_rope_table(max_seq, head_dim, theta, _p(c), _p(s))
+    return c, s
+
+
+def rope_apply(buf: np.ndarray, num_heads: int, head_dim: int, pos_offset: int, cos_t, sin_t):
+    b = np.ascontiguousarray(buf, dtype=np.float32).copy()
+    seq = b.size // (num_heads * head_dim)
+    lib().orc_rope_apply(_p(b), seq, num_heads, head_dim, pos_offset, _p(cos_t), _p(sin_t))
+    return b
+
+
+def flash_attention(q: np.ndarray, k_cache: np.ndarray, v_cache: np.ndarray, kv_len: int,
+                    hq: int, hkv: int, hd: int, scale: float) -> np.ndarray:
+    """FA-1 restatement.  q fp32 [seq_q, hq, hd]; caches fp16 bits [pos, hkv, hd]."""
+    q = np.ascontiguousarray(q, dtype=np.float32)
+    seq_q = q.size // (hq * hd)
+    out = np.empty((seq_q, hq, hd), np.float32)
+    lib().orc_flash_attention(_p(q), _p(np.ascontiguousarray(k_cache, np.uint16)),
+                              _p(np.ascontiguousarray(v_cache, np.uint16)), seq_q, kv_len, hq, hkv, hd,
+                              scale, _p(out))
+    return out
+
+
+def argmax(logits: np.ndarray) -> int:
+    lg = np.ascontiguousarray(logits, dtype=np.float32)
+    return int(lib().orc_argmax(_p(lg), lg.size))
+
+
+def dense_linear(x: np.ndarray, W: np.ndarray, bias=None, threads: int = 0) -> np.ndarray:
+    """Dense.Linear restatement on fp32 weights [h_out, h_in]."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    W = np.ascontiguousarray(W, dtype=np.float32)
+    batched = 1 if x.ndim == 2 else 0
+    batch = x.shape[0] if batched else 1
+    h_out, h_in = W.shape
+    y = np.empty((batch, h_out) if batched else (h_out,), np.float32)
+    b = np.ascontiguousarray(bias, np.float32) if bias is not None else None
+    lib().orc_dense_linear(_p(x), batch, batched, h_in, h_out, _p(W), _p(b) if b is not None else None,
+                           _p(y), threads)
+    return y
+
+
+def max_threads() -> int:
+    return int(lib().orc_max_threads())
+
+
+class _OrcModel(C.Structure):
+    _fields_ = [("hidden", C.c_int32), ("inter", C.c_int32), ("layers", C.c_int32),
+                ("hq", C.c_int32), ("hkv", C.c_int32), ("hd", C.c_int32), ("vocab", C.c_int32),
+                ("quant", C.c_int32), ("group", C.c_int32), ("capacity", C.c_int32),
+                ("eps", C.c_float), ("theta", C.c_float), ("embed_scale", C.c_float),
+                ("w_qkv", C.POINTER(C.c_void_p)), ("s_qkv", C.POINTER(C.c_void_p)),
+                ("w_o", C.POINTER(C.c_void_p)), ("s_o", C.POINTER(C.c_void_p)),
+                ("w_mlp", C.POINTER(C.c_void_p)), ("s_mlp", C.POINTER(C.c_void_p)),
+                ("ln1", C.POINTER(C.c_void_p)), ("ln2", C.POINTER(C.c_void_p)),
+                ("final_norm", C.c_void_p), ("embed", C.c_void_p), ("lm_head", C.c_void_p),
+                ("rope_cos", C.c_void_p), ("rope_sin", C.c_void_p),
+                ("k_cache", C.POINTER(C.c_void_p)), ("v_cache", C.POINTER(C.c_void_p)),
+                ("cache_len", C.c_int32)]
+
+
+class OracleModel:
+    """One sequence of the reference llama executor (MiniCPM5Model.Forward with
+    use_cache = true) over host weights from :class:`tests.modelgen.ModelWeights`."""
+
+    def __init__(self, weights, capacity: int):
+        cfg = weights.cfg
+        self.cfg, self.w = cfg, weights
+        L = cfg.layers
+        self.k_cache = [np.zeros((capacity, cfg.hkv, cfg.hd), np.uint16) for _ in range(L)]
+        self.v_cache = [np.zeros((capacity, cfg.hkv, cfg.hd), np.uint16) for _ in range(L)]
+        self.rope_cos, self.rope_sin = rope_table(capacity, cfg.hd, cfg.theta)
+
+        def arr(lst):
+            a = (C.c_void_p * L)()
+            for i, x in enumerate(lst):
+                a[i] = _p(x).value if x is not None else None
+            return a
+
+        self._keep = []
+        m = _OrcModel()
+        m.hidden, m.inter, m.layers = cfg.hidden, cfg.inter, L
+        m.hq, m.hkv, m.hd, m.vocab = cfg.hq, cfg.hkv, cfg.hd, cfg.vocab
+        m.quant, m.group, m.capacity = _QUANT_IDS[cfg.quant], cfg.group, capacity
+        m.eps, m.theta, m.embed_scale = cfg.eps, cfg.theta, 1.0
+        for name in ("w_qkv", "s_qkv", "w_o", "s_o", "w_mlp", "s_mlp", "ln1", "ln2"):
+            a = arr(getattr(weights, name))
+            self._keep.append(a)
+            setattr(m, name, C.cast(a, C.POINTER(C.c_void_p)))
+        m.final_norm = _p(weights.final_norm).value
+        m.embed = _p(weights.embed).value
+        m.lm_head = _p(weights.lm_head).value
+        m.rope_cos = _p(self.rope_cos).value
+        m.rope_sin = _p(self.rope_sin).value
+        kc, vc = arr(self.k_cache), arr(self.v_cache)
+        self._keep += [kc, vc]
+        m.k_cache = C.cast(kc, C.POINTER(C.c_void_p))
+        m.v_cache = C.cast(vc, C.POINTER(C.c_void_p))
+        m.cache_len = 0
+        self.m = m
+
+    @property
+    def cache_len(self) -> int:
+        return int(self.m.cache_len)
+
+    def reset(self):
+        self.m.cache_len = 0
+
+    def forward(self, ids, last_pos_only: bool = True) -> np.ndarray:
+        ids = np.ascontiguousarray(ids, dtype=np.int32)
+        S = ids.size
+        V = self.cfg.vocab
+        out = np.empty((V,) if last_pos_only else (S, V), np.float32)
+        rc = lib().orc_forward(C.byref(self.m), _p(ids), S, 1 if last_pos_only else 0, _p(out))
+        if rc != 0:
+            raise RuntimeError("oracle forward: KV cache capacity exceeded")
+        return out
+
+    def generate_greedy(self, prompt, steps: int):
+        logits = self.forward(prompt)
+        toks = []
+        for _ in range(steps):
+            t = argmax(logits)
+            toks.append(t)
+            logits = self.forward([t])
+        return toks
