@@ -1,0 +1,62 @@
+// common.cuh -- shared helpers for libdeepunity_cuda (sm_100a).
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <string>
+
+namespace du {
+
+// Thread-local error message surfaced by du_last_error().
+void set_error(const std::string &msg);
+int fail(int code, const std::string &msg);
+int cuda_fail(cudaError_t e, const char *what);
+
+#define DU_CUDA_TRY(expr)                                              \
+    do {                                                               \
+        cudaError_t _e = (expr);                                       \
+        if (_e != cudaSuccess) return ::du::cuda_fail(_e, #expr);      \
+    } while (0)
+
+#define DU_CHECK_ARG(cond, msg)                                        \
+    do {                                                               \
+        if (!(cond)) return ::du::fail(DU_EINVAL, msg);                \
+    } while (0)
+
+enum QuantKind { Q_F16 = 0, Q_I8 = 1, Q_I4 = 2 };
+
+// 16-byte streaming load: weights are read exactly once per launch, so they
+// bypass L1 (no_allocate) and come through the read-only path.
+__device__ __forceinline__ uint4 ldg_stream(const void *p)
+{
+    uint4 v;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "l"(p));
+    return v;
+}
+
+__device__ __forceinline__ float warp_sum(float v)
+{
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+__device__ __forceinline__ float warp_max(float v)
+{
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+// Programmatic dependent launch: wait for the producer grid's memory, and
+// allow the next grid in the stream to start its prologue.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;"); }
+
+__device__ __forceinline__ float silu(float x) { return x / (1.0f + __expf(-x)); }
+
+}  // namespace du

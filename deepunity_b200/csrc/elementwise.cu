@@ -1,0 +1,336 @@
+// elementwise.cu -- the small kernels around the GEMVs: embedding gather,
+// RMSNorm, argmax finalisation, IMP-exact quantizers and seeded synthetic
+// weights.
+#include "internal.h"
+
+namespace du {
+
+// EmbeddingLookup (Gemma3CS.compute:189-201): h[t, :] = fp16 embed[tok, :] * scale.
+__global__ void embed_kernel(const int *ids, const __half *embed, float scale, int H, float *out)
+{
+    const int m = blockIdx.y;
+    const size_t tok = (size_t)ids[m];
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < H; i += gridDim.x * blockDim.x)
+        out[(size_t)m * H + i] = __half2float(embed[tok * H + i]) * scale;
+}
+
+int launch_embed(const int *ids, const __half *embed, float scale, int M, int H, float *out, cudaStream_t st)
+{
+    if (M <= 0) return DU_OK;
+    dim3 grid((H + 255) / 256, M);
+    embed_kernel<<<grid, 256, 0, st>>>(ids, embed, scale, H, out);
+    DU_CUDA_TRY(cudaGetLastError());
+    return DU_OK;
+}
+
+// RmsNormHidden (Gemma3CS.compute:204-223): one CTA per row.
+__global__ void rmsnorm_kernel(const float *x, const __half *g, int H, float eps, float *y)
+{
+    __shared__ float part[32];
+    const float *xr = x + (size_t)blockIdx.x * H;
+    float ss = 0.0f;
+    for (int i = threadIdx.x; i < H; i += blockDim.x) ss += xr[i] * xr[i];
+    ss = warp_sum(ss);
+    if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    float tot = 0.0f;
+    for (int i = 0; i < (int)(blockDim.x >> 5); i++) tot += part[i];
+    const float inv = 1.0f / sqrtf(tot / (float)H + eps);
+    for (int i = threadIdx.x; i < H; i += blockDim.x)
+        y[(size_t)blockIdx.x * H + i] = xr[i] * inv * (1.0f + __half2float(g[i]));
+}
+
+int launch_rmsnorm(const float *x, const __half *g, int rows, int H, float eps, float *y, cudaStream_t st)
+{
+    if (rows <= 0) return DU_OK;
+    rmsnorm_kernel<<<rows, 256, 0, st>>>(x, g, H, eps, y);
+    DU_CUDA_TRY(cudaGetLastError());
+    return DU_OK;
+}
+
+// Final greedy pick from the per-CTA (max, argmax) partials of the lm_head
+// GEMV: the largest value wins, the lowest vocab index breaks a tie.
+// Writes the id (and optionally the next step's input id, for the
+// device-resident loop) or, with `pairs`, the (value, index-bits) pair that
+// tensor-parallel ranks exchange.
+__device__ __forceinline__ bool am_better(float v, int i, float bv, int bi)
+{
+    return v > bv || (v == bv && i < bi);
+}
+
+__global__ void argmax_final_kernel(const float *am_val, const int *am_idx, int nparts, int *out_ids,
+                                    int *feed_ids, float *pairs)
+{
+    const int m = blockIdx.x;
+    __shared__ float sv[32];
+    __shared__ int si[32];
+    float bv = -INFINITY;
+    int bi = 0x7fffffff;
+    for (int i = threadIdx.x; i < nparts; i += blockDim.x) {
+        const float v = am_val[(size_t)m * nparts + i];
+        const int ix = am_idx[(size_t)m * nparts + i];
+        if (am_better(v, ix, bv, bi)) { bv = v; bi = ix; }
+    }
+    for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+        if (am_better(ov, oi, bv, bi)) { bv = ov; bi = oi; }
+    }
+    if ((threadIdx.x & 31) == 0) { sv[threadIdx.x >> 5] = bv; si[threadIdx.x >> 5] = bi; }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        bv = sv[0]; bi = si[0];
+        for (int w = 1; w < (int)(blockDim.x >> 5); w++)
+            if (am_better(sv[w], si[w], bv, bi)) { bv = sv[w]; bi = si[w]; }
+        if (pairs) {
+            pairs[2 * m] = bv;
+            pairs[2 * m + 1] = __int_as_float(bi);
+        } else {
+            out_ids[m] = bi;
+            if (feed_ids) feed_ids[m] = bi;
+        }
+    }
+}
+
+int launch_argmax_final(const float *am_val, const int *am_idx, int M, int nparts, int *out_ids, int *feed_ids,
+                        cudaStream_t st)
+{
+    if (M <= 0) return DU_OK;
+    argmax_final_kernel<<<M, 256, 0, st>>>(am_val, am_idx, nparts, out_ids, feed_ids, nullptr);
+    DU_CUDA_TRY(cudaGetLastError());
+    return DU_OK;
+}
+
+int launch_argmax_final_pairs(const float *am_val, const int *am_idx, int M, int nparts, float *pairs,
+                              cudaStream_t st)
+{
+    if (M <= 0) return DU_OK;
+    argmax_final_kernel<<<M, 256, 0, st>>>(am_val, am_idx, nparts, nullptr, nullptr, pairs);
+    DU_CUDA_TRY(cudaGetLastError());
+    return DU_OK;
+}
+
+// gpairs [tp][maxb][2]: best (value, index) of each rank's vocab shard
+__global__ void argmax_pick_tp_kernel(const float *gpairs, int tp, int maxb, int M, int *out_ids, int *feed_ids)
+{
+    const int m = blockIdx.x * blockDim.x + threadIdx.x;
+    if (m >= M) return;
+    float bv = -INFINITY;
+    int bi = 0x7fffffff;
+    for (int r = 0; r < tp; r++) {
+        const float v = gpairs[((size_t)r * maxb + m) * 2];
+        const int i = __float_as_int(gpairs[((size_t)r * maxb + m) * 2 + 1]);
+        if (am_better(v, i, bv, bi)) { bv = v; bi = i; }
+    }
+    out_ids[m] = bi;
+    if (feed_ids) feed_ids[m] = bi;
+}
+
+int launch_argmax_pick_tp(const float *gpairs, int tp, int maxb, int M, int *out_ids, int *feed_ids,
+                          cudaStream_t st)
+{
+    if (M <= 0) return DU_OK;
+    argmax_pick_tp_kernel<<<(M + 127) / 128, 128, 0, st>>>(gpairs, tp, maxb, M, out_ids, feed_ids);
+    DU_CUDA_TRY(cudaGetLastError());
+    return DU_OK;
+}
+
+__global__ void add_inplace_kernel(float *y, const float *x, size_t n)
+{
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
+        y[i] += x[i];
+}
+
+int launch_add_inplace(float *y, const float *x, size_t n, cudaStream_t st)
+{
+    if (n == 0) return DU_OK;
+    const int grid = (int)((n + 255) / 256 < 4096 ? (n + 255) / 256 : 4096);
+    add_inplace_kernel<<<grid, 256, 0, st>>>(y, x, n);
+    DU_CUDA_TRY(cudaGetLastError());
+    return DU_OK;
+}
+
+__global__ void step_advance_kernel(int *cache_len, int M)
+{
+    const int m = blockIdx.x * blockDim.x + threadIdx.x;
+    if (m < M) cache_len[m] += 1;
+}
+
+int launch_step_advance(int *cache_len, int M, cudaStream_t st)
+{
+    step_advance_kernel<<<(M + 127) / 128, 128, 0, st>>>(cache_len, M);
+    DU_CUDA_TRY(cudaGetLastError());
+    return DU_OK;
+}
+
+// ---------------------------------------------------------------- quantizers
+
+// quantize_int8 (import_params.py:229-233), one CTA per row: fp32 absmax,
+// s = max(absmax / 127, 1e-8), q = clip(rint(w / s), -127, 127) with IEEE
+// division and round-half-even, s stored as fp16 (RNE).  Bit-exact with numpy.
+__global__ void quantize_int8_kernel(const float *w, int64_t cols, int8_t *q, __half *s)
+{
+    __shared__ float part[32];
+    const float *wr = w + (size_t)blockIdx.x * cols;
+    float mx = 0.0f;
+    for (int64_t c = threadIdx.x; c < cols; c += blockDim.x) mx = fmaxf(mx, fabsf(wr[c]));
+    mx = warp_max(mx);
+    if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = mx;
+    __syncthreads();
+    float m = 0.0f;
+    for (int i = 0; i < (int)(blockDim.x >> 5); i++) m = fmaxf(m, part[i]);
+    float sc = __fdiv_rn(m, 127.0f);
+    if (!(sc >= 1e-8f)) sc = 1e-8f;
+    for (int64_t c = threadIdx.x; c < cols; c += blockDim.x) {
+        float v = rintf(__fdiv_rn(wr[c], sc));
+        v = fminf(fmaxf(v, -127.0f), 127.0f);
+        q[(size_t)blockIdx.x * cols + c] = (int8_t)v;
+    }
+    if (threadIdx.x == 0) s[blockIdx.x] = __float2half_rn(sc);
+}
+
+int launch_quantize_int8(const float *w, int64_t rows, int64_t cols, int8_t *q, __half *s, cudaStream_t st)
+{
+    if (rows <= 0) return DU_OK;
+    if (rows > 0x7fffffff) return fail(DU_EINVAL, "quantize_int8: too many rows");
+    quantize_int8_kernel<<<(unsigned)rows, 256, 0, st>>>(w, cols, q, s);
+    DU_CUDA_TRY(cudaGetLastError());
+    return DU_OK;
+}
+
+// quantize_int4 (import_params.py:236-248) with group size G: one warp per
+// group; the element of largest |w| (lowest index on ties, numpy argmax)
+// gives d = w / -8, |d| < 1e-10 -> 1e-10, q = clip(rint(w / d) + 8, 0, 15),
+// low nibble = even column, d stored fp16 [rows, cols / G].
+__global__ void quantize_int4_kernel(const float *w, int64_t rows, int64_t cols, int group, uint8_t *p,
+                                     __half *s)
+{
+    const int64_t ng = cols / group;
+    const int64_t gid = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    if (gid >= rows * ng) return;
+    const int64_t r = gid / ng, g = gid - r * ng;
+    const float *gr = w + r * cols + g * group;
+    float ba = -1.0f;
+    int bi = 0;
+    for (int k = lane; k < group; k += 32) {
+        const float a = fabsf(gr[k]);
+        if (a > ba) { ba = a; bi = k; }
+    }
+    for (int o = 16; o > 0; o >>= 1) {
+        const float oa = __shfl_xor_sync(0xffffffffu, ba, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+        if (oa > ba || (oa == ba && oi < bi)) { ba = oa; bi = oi; }
+    }
+    float d = __fdiv_rn(gr[bi], -8.0f);
+    if (fabsf(d) < 1e-10f) d = 1e-10f;
+    uint8_t *pr = p + (r * cols + g * group) / 2;
+    for (int k = 2 * lane; k < group; k += 64) {
+        float v0 = rintf(__fdiv_rn(gr[k], d)) + 8.0f;
+        float v1 = rintf(__fdiv_rn(gr[k + 1], d)) + 8.0f;
+        v0 = fminf(fmaxf(v0, 0.0f), 15.0f);
+        v1 = fminf(fmaxf(v1, 0.0f), 15.0f);
+        pr[k >> 1] = (uint8_t)((unsigned)v0 | ((unsigned)v1 << 4));
+    }
+    if (lane == 0) s[r * ng + g] = __float2half_rn(d);
+}
+
+int launch_quantize_int4(const float *w, int64_t rows, int64_t cols, int group, uint8_t *p, __half *s,
+                         cudaStream_t st)
+{
+    if (rows <= 0) return DU_OK;
+    if (group <= 0 || group % 2 || cols % group) return fail(DU_EINVAL, "quantize_int4: cols % group != 0");
+    const int64_t groups = rows * (cols / group);
+    const int64_t blocks = (groups + 7) / 8;
+    if (blocks > 0x7fffffff) return fail(DU_EINVAL, "quantize_int4: matrix too large");
+    quantize_int4_kernel<<<(unsigned)blocks, 256, 0, st>>>(w, rows, cols, group, p, s);
+    DU_CUDA_TRY(cudaGetLastError());
+    return DU_OK;
+}
+
+// ------------------------------------------------------- synthetic weights
+// Counter-based generator: a 64-bit mix (splitmix64 finaliser) of
+// (seed, index) gives two uniforms, Box-Muller turns them into a normal.
+// Only used to stand in for checkpoints; parity tests load host weights.
+__device__ __forceinline__ uint64_t mix64(uint64_t z)
+{
+    z += 0x9E3779B97F4A7C15ull;
+    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+    z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+    return z ^ (z >> 31);
+}
+
+__device__ __forceinline__ float normal_at(uint64_t seed, uint64_t i)
+{
+    const uint64_t h = mix64(seed ^ mix64(i));
+    const float u1 = ((float)(uint32_t)(h >> 40) + 0.5f) * (1.0f / 16777216.0f);
+    const float u2 = (float)(uint32_t)(h & 0xFFFFFFu) * (1.0f / 16777216.0f);
+    return sqrtf(-2.0f * logf(u1)) * cospif(2.0f * u2);
+}
+
+__global__ void random_normal_kernel(float *out, size_t n, uint64_t seed, uint64_t off, float std)
+{
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
+        out[i] = std * normal_at(seed, off + i);
+}
+
+__global__ void random_normal_half_kernel(__half *out, size_t n, uint64_t seed, uint64_t off, float std)
+{
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
+        out[i] = __float2half_rn(std * normal_at(seed, off + i));
+}
+
+int launch_random_normal(float *out, size_t n, uint64_t seed, uint64_t off, float std, cudaStream_t st)
+{
+    if (n == 0) return DU_OK;
+    random_normal_kernel<<<num_sms() * 8, 256, 0, st>>>(out, n, seed, off, std);
+    DU_CUDA_TRY(cudaGetLastError());
+    return DU_OK;
+}
+
+int launch_random_normal_half(__half *out, size_t n, uint64_t seed, uint64_t off, float std, cudaStream_t st)
+{
+    if (n == 0) return DU_OK;
+    random_normal_half_kernel<<<num_sms() * 8, 256, 0, st>>>(out, n, seed, off, std);
+    DU_CUDA_TRY(cudaGetLastError());
+    return DU_OK;
+}
+
+__global__ void fill_half_kernel(__half *out, size_t n, float v)
+{
+    const __half h = __float2half_rn(v);
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
+        out[i] = h;
+}
+
+int launch_fill_half(__half *out, size_t n, float v, cudaStream_t st)
+{
+    if (n == 0) return DU_OK;
+    fill_half_kernel<<<num_sms() * 4, 256, 0, st>>>(out, n, v);
+    DU_CUDA_TRY(cudaGetLastError());
+    return DU_OK;
+}
+
+__global__ void convert_kernel(const void *x, int dtype, size_t n, float *out)
+{
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+        float v;
+        if (dtype == DU_DTYPE_F16) v = __half2float(reinterpret_cast<const __half *>(x)[i]);
+        else if (dtype == DU_DTYPE_BF16) {
+            const uint16_t b = reinterpret_cast<const uint16_t *>(x)[i];
+            v = __uint_as_float((uint32_t)b << 16);
+        } else v = reinterpret_cast<const float *>(x)[i];
+        out[i] = v;
+    }
+}
+
+int launch_convert_to_f32(const void *x, int dtype, size_t n, float *out, cudaStream_t st)
+{
+    if (n == 0) return DU_OK;
+    const int grid = (int)((n + 255) / 256 < 4096 ? (n + 255) / 256 : 4096);
+    convert_kernel<<<grid, 256, 0, st>>>(x, dtype, n, out);
+    DU_CUDA_TRY(cudaGetLastError());
+    return DU_OK;
+}
+
+}  // namespace du

@@ -1,0 +1,49 @@
+// internal.h -- declarations shared by the library's translation units.
+#pragma once
+
+#include "../../include/deepunity_cuda.h"
+#include "common.cuh"
+
+namespace du {
+
+struct GemvParams;
+
+int num_sms();
+
+// gemv.cu
+int launch_gemv(int qt, GemvParams p, cudaStream_t st);
+size_t gemv_smem_bytes(int qt, int mt, int64_t row_bytes);
+
+// attention.cu
+int fd_choose_splits(int nq, int hkv, int max_kv);
+size_t fd_scratch_floats(int nq, int hkv, int G, int hd, int nsplit);
+int launch_flash_decode(const float *q, const __half *kc, const __half *vc, const int *seq_of,
+                        const int *kv_len, int kv_len_add, int nq, int hq, int hkv, int hd, int cap,
+                        float scale, float *out, float *scratch, unsigned *counters, int nsplit,
+                        cudaStream_t st);
+
+// elementwise.cu
+int launch_embed(const int *ids, const __half *embed, float scale, int M, int H, float *out, cudaStream_t st);
+int launch_rmsnorm(const float *x, const __half *gamma_m1, int rows, int H, float eps, float *y,
+                   cudaStream_t st);
+int launch_argmax_final(const float *am_val, const int *am_idx, int M, int nparts, int *out_ids,
+                        int *feed_ids, cudaStream_t st);
+int launch_argmax_final_pairs(const float *am_val, const int *am_idx, int M, int nparts, float *pairs,
+                              cudaStream_t st);
+int launch_argmax_pick_tp(const float *gpairs, int tp, int maxb, int M, int *out_ids, int *feed_ids,
+                          cudaStream_t st);
+int launch_add_inplace(float *y, const float *x, size_t n, cudaStream_t st);
+int launch_quantize_int8(const float *w, int64_t rows, int64_t cols, int8_t *q, __half *s, cudaStream_t st);
+int launch_quantize_int4(const float *w, int64_t rows, int64_t cols, int group, uint8_t *p, __half *s,
+                         cudaStream_t st);
+int launch_random_normal(float *out, size_t n, uint64_t seed, uint64_t offset, float std, cudaStream_t st);
+int launch_random_normal_half(__half *out, size_t n, uint64_t seed, uint64_t offset, float std,
+                              cudaStream_t st);
+int launch_fill_half(__half *out, size_t n, float v, cudaStream_t st);
+int launch_convert_to_f32(const void *x, int dtype, size_t n, float *out, cudaStream_t st);
+int launch_step_advance(int *cache_len, int M, cudaStream_t st);
+
+// scratch owned by the library for kernel-level entry points (grow-only, per device)
+void *device_scratch(size_t bytes, int slot);
+
+}  // namespace du

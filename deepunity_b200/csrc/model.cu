@@ -1,0 +1,1113 @@
+// model.cu -- the decode executor: weights, KV cache, per-step launch
+// sequence, CUDA-graph capture and tensor parallelism.
+//
+// Replaces MiniCPM5Model (InferenceEngine/LLM/MiniCPM5/MiniCPM5Model.cs): the
+// 16 dispatches per layer of DispatchLayer (:294-518) become 5 fused kernels
+//   1. QKV GEMV  <- RMSNorm(ln1) prologue, split + RoPE + fp16 KV-write epilogue
+//   2. flash-decode (split-K, GQA) with the LSE combine
+//   3. O GEMV    -> residual add (TP1) / partial sum + NCCL allreduce (TP>1)
+//   4. gate|up GEMV <- RMSNorm(ln2) prologue, SiLU(g) * u epilogue
+//   5. down GEMV -> residual add / allreduce
+// plus embedding gather, the final RMSNorm + lm_head GEMV with per-CTA argmax
+// partials, and the greedy pick.  A decode step is captured once per batch
+// size as a CUDA graph; positions and KV lengths live in device memory, so
+// the same graph replays for every step.
+#include <atomic>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <map>
+#include <string>
+#include <thread>
+#include <chrono>
+#include <vector>
+
+#include "gemv.cuh"
+#include "internal.h"
+#include "nccl_shim.h"
+
+namespace du {
+
+struct Layer {
+    uint8_t *w_qkv = nullptr; __half *s_qkv = nullptr;    // [(hq+2hkv)*hd local rows, H]
+    uint8_t *w_o = nullptr;   __half *s_o = nullptr;      // [H, hq_l*hd]
+    uint8_t *w_gu = nullptr;  __half *s_gu = nullptr;     // gate|up [2*I_l, H]
+    uint8_t *w_d = nullptr;   __half *s_d = nullptr;      // [H, I_l]
+    __half *ln1 = nullptr, *ln2 = nullptr;                // gamma - 1, [H]
+};
+
+struct Graph {
+    cudaGraph_t g = nullptr;
+    cudaGraphExec_t exec = nullptr;
+};
+
+}  // namespace du
+
+struct du_model {
+    du_model_config cfg;
+    int device = 0;
+    cudaStream_t stream = nullptr;
+    int H, I, L, hq, hkv, hd, V, tp, rank;
+    int hq_l, hkv_l, I_l, V_l, qkv_rows;
+    int quant, group, cap, maxb;
+    int max_tokens;                         // tokens per forward chunk (prefill)
+    std::vector<du::Layer> layers;
+    std::vector<void *> allocs;
+    __half *final_norm = nullptr, *embed = nullptr, *lm_head = nullptr;
+    __half *rope_cos = nullptr, *rope_sin = nullptr;
+    __half *k_cache = nullptr, *v_cache = nullptr;      // [L][maxb][cap][hkv_l][hd]
+    size_t kv_layer_elems = 0;
+    // device state
+    int *d_cache_len = nullptr;             // [maxb]
+    int *d_ids = nullptr;                   // [max_tokens] input ids
+    int *d_next = nullptr;                  // [maxb] greedy ids
+    int *d_pos = nullptr, *d_seq = nullptr, *d_kvlen = nullptr;   // per-token (prefill)
+    float *x_res = nullptr;                 // [max_tokens][H]
+    float *part = nullptr;                  // [max_tokens][H] TP partial sums
+    float *q = nullptr;                     // [max_tokens][hq_l*hd]
+    float *att = nullptr;                   // [max_tokens][hq_l*hd]
+    float *inter = nullptr;                 // [max_tokens][I_l]
+    float *logits = nullptr;                // [maxb][V_l] local shard
+    float *logits_all = nullptr;            // [tp][maxb][V_l] (TP gather)
+    float *am_val = nullptr; int *am_idx = nullptr;   // [maxb][am_parts]
+    float *best_val = nullptr; int *best_idx = nullptr;  // TP: [maxb] local, [tp][maxb] gathered
+    float *gbest_val = nullptr; int *gbest_idx = nullptr;
+    int am_parts = 0;
+    float *fd_scratch = nullptr; unsigned *fd_counters = nullptr;
+    int fd_nsplit_decode = 1;
+    size_t fd_scratch_fl = 0;
+    int *h_pin_ids = nullptr, *h_pin_next = nullptr;
+    std::vector<int> h_cache_len;
+    std::map<int, du::Graph> graphs;
+    int last_batch = 0, last_rows = 0;      // rows of logits written by the last call
+    std::atomic<int> busy{0};
+    // TP
+    ncclComm_t comm = nullptr;
+    bool tp_ready = false;
+    int nccl_timeout_ms = 60000;
+    uint64_t weight_bytes = 0;
+};
+
+namespace du {
+
+static void *dalloc(du_model *m, size_t bytes, int *rc)
+{
+    void *p = nullptr;
+    if (*rc) return nullptr;
+    if (bytes == 0) bytes = 16;
+    cudaError_t e = cudaMalloc(&p, bytes);
+    if (e != cudaSuccess) {
+        *rc = cuda_fail(e, "cudaMalloc");
+        return nullptr;
+    }
+    cudaMemset(p, 0, bytes);
+    m->allocs.push_back(p);
+    return p;
+}
+
+static int64_t qbytes(int quant, int64_t rows, int64_t cols)
+{
+    return quant == DU_QUANT_INT4 ? rows * cols / 2 : quant == DU_QUANT_INT8 ? rows * cols : rows * cols * 2;
+}
+
+static int64_t sbytes(int quant, int group, int64_t rows, int64_t cols)
+{
+    return quant == DU_QUANT_INT4 ? rows * (cols / group) * 2 : quant == DU_QUANT_INT8 ? rows * 2 : 0;
+}
+
+// float32 -> float16 round-to-nearest-even (same rounding as the managed
+// converter of MiniCPM5Model.cs:205-234 for all finite inputs)
+static uint16_t f32_to_f16(float v)
+{
+    uint32_t x;
+    memcpy(&x, &v, 4);
+    const uint32_t sign = (x >> 16) & 0x8000u;
+    int32_t e = (int32_t)((x >> 23) & 0xff) - 127 + 15;
+    uint32_t m = x & 0x7fffffu;
+    if (((x >> 23) & 0xff) == 0xff) return (uint16_t)(sign | 0x7c00u | (m ? 0x200u : 0u));
+    if (e >= 31) return (uint16_t)(sign | 0x7c00u);
+    if (e <= 0) {
+        if (e < -10) return (uint16_t)sign;
+        m |= 0x800000u;
+        const int t = 14 - e;
+        const uint32_t half = 1u << (t - 1);
+        uint32_t r = m >> t;
+        const uint32_t rem = m & ((1u << t) - 1);
+        if (rem > half || (rem == half && (r & 1))) r++;
+        return (uint16_t)(sign | r);
+    }
+    uint32_t r = ((uint32_t)e << 10) | (m >> 13);
+    const uint32_t rem = m & 0x1fffu;
+    if (rem > 0x1000u || (rem == 0x1000u && (r & 1))) r++;
+    return (uint16_t)(sign | r);
+}
+
+static int check_cfg(const du_model_config &c)
+{
+    DU_CHECK_ARG(c.hidden_size > 0 && c.intermediate_size > 0 && c.num_layers > 0, "config: non-positive dims");
+    DU_CHECK_ARG(c.num_heads_q > 0 && c.num_heads_kv > 0 && c.num_heads_q % c.num_heads_kv == 0,
+                 "config: num_heads_q must be a multiple of num_heads_kv");
+    DU_CHECK_ARG(c.head_dim == 64 || c.head_dim == 128, "config: head_dim must be 64 or 128");
+    const int G = c.num_heads_q / c.num_heads_kv;
+    DU_CHECK_ARG(G == 1 || G == 2 || G == 4 || G == 8, "config: GQA group must be 1, 2, 4 or 8");
+    DU_CHECK_ARG(c.vocab_size > 0 && c.kv_capacity > 0 && c.max_batch > 0, "config: vocab/capacity/batch");
+    DU_CHECK_ARG(c.quant >= DU_QUANT_FP16 && c.quant <= DU_QUANT_INT4, "config: unknown quant");
+    const int tp = c.tp_size <= 0 ? 1 : c.tp_size;
+    DU_CHECK_ARG(c.tp_rank >= 0 && c.tp_rank < tp, "config: tp_rank out of range");
+    DU_CHECK_ARG(c.num_heads_q % tp == 0 && c.num_heads_kv % tp == 0, "config: heads must divide by tp_size");
+    DU_CHECK_ARG(c.intermediate_size % tp == 0 && c.vocab_size % tp == 0, "config: intermediate/vocab % tp");
+    const int H = c.hidden_size, I_l = c.intermediate_size / tp, K_o = c.num_heads_q / tp * c.head_dim;
+    if (c.quant == DU_QUANT_INT4) {
+        DU_CHECK_ARG(c.group_size > 0 && c.group_size % 32 == 0, "config: int4 group must be a multiple of 32");
+        DU_CHECK_ARG(H % c.group_size == 0 && I_l % c.group_size == 0 && K_o % c.group_size == 0,
+                     "config: every (sharded) K must be a multiple of the int4 group");
+    }
+    DU_CHECK_ARG(H % 32 == 0 && I_l % 32 == 0 && K_o % 32 == 0, "config: K dims must be multiples of 32");
+    DU_CHECK_ARG(c.tie_embedding == 0 || tp == 1, "config: tied embedding with tp > 1 is not supported");
+    return DU_OK;
+}
+
+// -------------------------------------------------------------- creation
+
+static int model_alloc(du_model *m)
+{
+    int rc = DU_OK;
+    const int H = m->H, hd = m->hd;
+    m->layers.resize(m->L);
+    const int64_t Ko = (int64_t)m->hq_l * hd;
+    for (int l = 0; l < m->L; l++) {
+        Layer &ly = m->layers[l];
+        ly.w_qkv = (uint8_t *)dalloc(m, qbytes(m->quant, m->qkv_rows, H), &rc);
+        ly.s_qkv = (__half *)dalloc(m, sbytes(m->quant, m->group, m->qkv_rows, H), &rc);
+        ly.w_o = (uint8_t *)dalloc(m, qbytes(m->quant, H, Ko), &rc);
+        ly.s_o = (__half *)dalloc(m, sbytes(m->quant, m->group, H, Ko), &rc);
+        ly.w_gu = (uint8_t *)dalloc(m, qbytes(m->quant, 2LL * m->I_l, H), &rc);
+        ly.s_gu = (__half *)dalloc(m, sbytes(m->quant, m->group, 2LL * m->I_l, H), &rc);
+        ly.w_d = (uint8_t *)dalloc(m, qbytes(m->quant, H, m->I_l), &rc);
+        ly.s_d = (__half *)dalloc(m, sbytes(m->quant, m->group, H, m->I_l), &rc);
+        ly.ln1 = (__half *)dalloc(m, (size_t)H * 2, &rc);
+        ly.ln2 = (__half *)dalloc(m, (size_t)H * 2, &rc);
+        m->weight_bytes += qbytes(m->quant, m->qkv_rows, H) + sbytes(m->quant, m->group, m->qkv_rows, H) +
+                           qbytes(m->quant, H, Ko) + sbytes(m->quant, m->group, H, Ko) +
+                           qbytes(m->quant, 2LL * m->I_l, H) + sbytes(m->quant, m->group, 2LL * m->I_l, H) +
+                           qbytes(m->quant, H, m->I_l) + sbytes(m->quant, m->group, H, m->I_l) + 4LL * H;
+    }
+    m->final_norm = (__half *)dalloc(m, (size_t)H * 2, &rc);
+    m->embed = (__half *)dalloc(m, (size_t)m->V * H * 2, &rc);
+    m->lm_head = m->cfg.tie_embedding ? m->embed : (__half *)dalloc(m, (size_t)m->V_l * H * 2, &rc);
+    m->weight_bytes += 2ull * H + 2ull * m->V_l * H;
+    m->rope_cos = (__half *)dalloc(m, (size_t)m->cap * (hd / 2) * 2, &rc);
+    m->rope_sin = (__half *)dalloc(m, (size_t)m->cap * (hd / 2) * 2, &rc);
+    m->kv_layer_elems = (size_t)m->maxb * m->cap * m->hkv_l * hd;
+    m->k_cache = (__half *)dalloc(m, m->kv_layer_elems * m->L * 2, &rc);
+    m->v_cache = (__half *)dalloc(m, m->kv_layer_elems * m->L * 2, &rc);
+    const int T = m->max_tokens;
+    m->d_cache_len = (int *)dalloc(m, sizeof(int) * m->maxb, &rc);
+    m->d_ids = (int *)dalloc(m, sizeof(int) * T, &rc);
+    m->d_next = (int *)dalloc(m, sizeof(int) * T, &rc);
+    m->d_pos = (int *)dalloc(m, sizeof(int) * T, &rc);
+    m->d_seq = (int *)dalloc(m, sizeof(int) * T, &rc);
+    m->d_kvlen = (int *)dalloc(m, sizeof(int) * T, &rc);
+    m->x_res = (float *)dalloc(m, sizeof(float) * T * H, &rc);
+    m->part = (float *)dalloc(m, sizeof(float) * T * H, &rc);
+    m->q = (float *)dalloc(m, sizeof(float) * T * m->hq_l * hd, &rc);
+    m->att = (float *)dalloc(m, sizeof(float) * T * m->hq_l * hd, &rc);
+    m->inter = (float *)dalloc(m, sizeof(float) * T * m->I_l, &rc);
+    m->logits = (float *)dalloc(m, sizeof(float) * m->maxb * m->V_l, &rc);
+    if (m->tp > 1) m->logits_all = (float *)dalloc(m, sizeof(float) * m->tp * m->maxb * m->V_l, &rc);
+    m->am_parts = 2 * num_sms();
+    // per-row greedy state is sized for the largest forward chunk (all-position logits)
+    m->am_val = (float *)dalloc(m, sizeof(float) * T * m->am_parts, &rc);
+    m->am_idx = (int *)dalloc(m, sizeof(int) * T * m->am_parts, &rc);
+    m->best_val = (float *)dalloc(m, sizeof(float) * T * 2, &rc);
+    m->gbest_val = (float *)dalloc(m, sizeof(float) * T * 2 * m->tp, &rc);
+    const int G = m->hq_l / m->hkv_l;
+    // flash-decode scratch: decode rows (maxb) use fd_nsplit_decode splits; prefill rows use 1..n
+    m->fd_nsplit_decode = fd_choose_splits(m->maxb, m->hkv_l, m->cap);
+    m->fd_scratch_fl = 0;
+    for (int rows = 1; rows <= T; rows++) {   // every row count a decode graph or prefill chunk can use
+        const size_t f = fd_scratch_floats(rows, m->hkv_l, G, hd, fd_choose_splits(rows, m->hkv_l, m->cap));
+        if (f > m->fd_scratch_fl) m->fd_scratch_fl = f;
+    }
+    m->fd_scratch = (float *)dalloc(m, sizeof(float) * m->fd_scratch_fl, &rc);
+    m->fd_counters = (unsigned *)dalloc(m, sizeof(unsigned) * (size_t)T * m->hkv_l, &rc);
+    if (rc) return rc;
+    DU_CUDA_TRY(cudaMallocHost(&m->h_pin_ids, sizeof(int) * T));
+    DU_CUDA_TRY(cudaMallocHost(&m->h_pin_next, sizeof(int) * m->maxb));
+    m->h_cache_len.assign(m->maxb, 0);
+
+    // RoPE tables on the host with the reference formula (MiniCPM5Model.cs:163-191)
+    const int hd2 = hd / 2;
+    std::vector<uint16_t> c((size_t)m->cap * hd2), s((size_t)m->cap * hd2);
+    for (int pos = 0; pos < m->cap; pos++)
+        for (int i = 0; i < hd2; i++) {
+            const float f = 1.0f / powf(m->cfg.rope_theta, 2.0f * (float)i / (float)hd);
+            const float ang = (float)pos * f;
+            c[(size_t)pos * hd2 + i] = f32_to_f16(cosf(ang));
+            s[(size_t)pos * hd2 + i] = f32_to_f16(sinf(ang));
+        }
+    DU_CUDA_TRY(cudaMemcpy(m->rope_cos, c.data(), c.size() * 2, cudaMemcpyHostToDevice));
+    DU_CUDA_TRY(cudaMemcpy(m->rope_sin, s.data(), s.size() * 2, cudaMemcpyHostToDevice));
+    DU_CUDA_TRY(cudaDeviceSynchronize());
+    return DU_OK;
+}
+
+static void model_free(du_model *m)
+{
+    cudaSetDevice(m->device);
+    if (m->stream) cudaStreamSynchronize(m->stream);
+    for (auto &kv : m->graphs) {
+        if (kv.second.exec) cudaGraphExecDestroy(kv.second.exec);
+        if (kv.second.g) cudaGraphDestroy(kv.second.g);
+    }
+    m->graphs.clear();
+    if (m->comm) {
+        const NcclApi *n = nccl_api();
+        if (n) n->CommDestroy(m->comm);
+        m->comm = nullptr;
+    }
+    for (void *p : m->allocs) cudaFree(p);
+    m->allocs.clear();
+    if (m->h_pin_ids) cudaFreeHost(m->h_pin_ids);
+    if (m->h_pin_next) cudaFreeHost(m->h_pin_next);
+    m->h_pin_ids = m->h_pin_next = nullptr;
+    if (m->stream) cudaStreamDestroy(m->stream);
+    m->stream = nullptr;
+}
+
+// ------------------------------------------------------------- loading
+
+// Copies rows [r0, r1) x byte-columns [c0, c1) of a row-major source with
+// `src_pitch` bytes per row into dst (pitch dst_pitch).
+static int copy2d(void *dst, size_t dst_pitch, const void *src, size_t src_pitch, int64_t r0, int64_t r1, int64_t c0,
+                  int64_t c1, cudaMemcpyKind kind, cudaStream_t st)
+{
+    if (r1 <= r0 || c1 <= c0) return DU_OK;
+    DU_CUDA_TRY(cudaMemcpy2DAsync(dst, dst_pitch, (const uint8_t *)src + r0 * src_pitch + c0, src_pitch,
+                                  (size_t)(c1 - c0), (size_t)(r1 - r0), kind, st));
+    return DU_OK;
+}
+
+enum TensorKind { T_NONE, T_Q, T_K, T_V, T_O, T_GATE, T_UP, T_DOWN };
+
+// Places one IMP tensor (weights, or its scales) into the sharded device layout.
+static int place_tensor(du_model *m, const char *name, const void *src, size_t bytes, cudaMemcpyKind kind)
+{
+    cudaStream_t st = m->stream;
+    const int H = m->H, hd = m->hd, r = m->rank;
+    std::string n(name);
+    if (n == "norm.bin") {
+        DU_CHECK_ARG(bytes == (size_t)H * 2, "norm.bin: size mismatch");
+        DU_CUDA_TRY(cudaMemcpyAsync(m->final_norm, src, bytes, kind, st));
+        return DU_OK;
+    }
+    int part = -1;
+    const bool is_embed = sscanf(name, "embed_tokens/part_%d.bin", &part) == 1;
+    const bool is_head = !is_embed && sscanf(name, "lm_head/part_%d.bin", &part) == 1;
+    if (is_embed || is_head) {
+        DU_CHECK_ARG(m->V % 16 == 0, "embedding parts need vocab % 16 == 0 (IMP EMBED_CHUNKS)");
+        const int64_t rows = m->V / 16;
+        DU_CHECK_ARG(part >= 0 && part < 16 && bytes == (size_t)rows * H * 2, "embedding part: bad index or size");
+        const int64_t g0 = (int64_t)part * rows, g1 = g0 + rows;
+        if (is_embed) {
+            int rc = copy2d((uint8_t *)m->embed + g0 * H * 2, (size_t)H * 2, src, (size_t)H * 2, 0, rows, 0,
+                            (int64_t)H * 2, kind, st);
+            if (rc) return rc;
+            return DU_OK;
+        }
+        DU_CHECK_ARG(!m->cfg.tie_embedding, "lm_head parts given for a tied-embedding model");
+        const int64_t s0 = (int64_t)r * m->V_l, s1 = s0 + m->V_l;      // this rank's vocab shard
+        const int64_t a = g0 > s0 ? g0 : s0, b = g1 < s1 ? g1 : s1;
+        if (a >= b) return DU_OK;
+        return copy2d((uint8_t *)m->lm_head + (a - s0) * H * 2, (size_t)H * 2, src, (size_t)H * 2, a - g0, b - g0, 0,
+                      (int64_t)H * 2, kind, st);
+    }
+    int li = -1;
+    char rest[128] = {0};
+    if (sscanf(name, "layer_%d/%127s", &li, rest) != 2 || li < 0 || li >= m->L)
+        return fail(DU_ENOTFOUND, std::string("unknown tensor: ") + name);
+    Layer &ly = m->layers[li];
+    std::string t(rest);
+    if (t == "input_layernorm.bin" || t == "post_attention_layernorm.bin") {
+        DU_CHECK_ARG(bytes == (size_t)H * 2, "layernorm: size mismatch");
+        DU_CUDA_TRY(cudaMemcpyAsync(t[0] == 'i' ? ly.ln1 : ly.ln2, src, bytes, kind, st));
+        return DU_OK;
+    }
+    static const struct { const char *stem; TensorKind k; } stems[] = {
+        {"self_attn_q_proj", T_Q}, {"self_attn_k_proj", T_K}, {"self_attn_v_proj", T_V},
+        {"self_attn_o_proj", T_O}, {"mlp_gate_proj", T_GATE}, {"mlp_up_proj", T_UP}, {"mlp_down_proj", T_DOWN}};
+    TensorKind tk = T_NONE;
+    std::string suffix;
+    for (auto &sdef : stems) {
+        const size_t len = strlen(sdef.stem);
+        if (t.compare(0, len, sdef.stem) == 0) { tk = sdef.k; suffix = t.substr(len); break; }
+    }
+    if (tk == T_NONE) return fail(DU_ENOTFOUND, std::string("unknown tensor: ") + name);
+    const char *wext = m->quant == DU_QUANT_INT4 ? ".int4.bin" : m->quant == DU_QUANT_INT8 ? ".int8.bin" : ".bin";
+    const bool is_scale = suffix == ".scales.bin";
+    if (!is_scale && suffix != wext) return fail(DU_EINVAL, std::string("tensor format does not match the model quant: ") + name);
+    if (is_scale && m->quant == DU_QUANT_FP16) return fail(DU_EINVAL, "fp16 model has no scales");
+
+    // global shape [rows, cols], this rank's row/col window, destination
+    int64_t rows = 0, cols = 0, r0 = 0, r1 = 0, c0 = 0, c1 = 0, drow = 0;
+    uint8_t *dw = nullptr;
+    __half *ds = nullptr;
+    int64_t dcols = 0;   // destination row length (elements)
+    switch (tk) {
+    case T_Q: rows = (int64_t)m->hq * hd; cols = H; r0 = (int64_t)r * m->hq_l * hd; r1 = r0 + (int64_t)m->hq_l * hd;
+        c0 = 0; c1 = H; dw = ly.w_qkv; ds = ly.s_qkv; drow = 0; dcols = H; break;
+    case T_K: rows = (int64_t)m->hkv * hd; cols = H; r0 = (int64_t)r * m->hkv_l * hd; r1 = r0 + (int64_t)m->hkv_l * hd;
+        c0 = 0; c1 = H; dw = ly.w_qkv; ds = ly.s_qkv; drow = (int64_t)m->hq_l * hd; dcols = H; break;
+    case T_V: rows = (int64_t)m->hkv * hd; cols = H; r0 = (int64_t)r * m->hkv_l * hd; r1 = r0 + (int64_t)m->hkv_l * hd;
+        c0 = 0; c1 = H; dw = ly.w_qkv; ds = ly.s_qkv; drow = (int64_t)(m->hq_l + m->hkv_l) * hd; dcols = H; break;
+    case T_O: rows = H; cols = (int64_t)m->hq * hd; r0 = 0; r1 = H; c0 = (int64_t)r * m->hq_l * hd;
+        c1 = c0 + (int64_t)m->hq_l * hd; dw = ly.w_o; ds = ly.s_o; drow = 0; dcols = (int64_t)m->hq_l * hd; break;
+    case T_GATE: rows = m->I; cols = H; r0 = (int64_t)r * m->I_l; r1 = r0 + m->I_l; c0 = 0; c1 = H;
+        dw = ly.w_gu; ds = ly.s_gu; drow = 0; dcols = H; break;
+    case T_UP: rows = m->I; cols = H; r0 = (int64_t)r * m->I_l; r1 = r0 + m->I_l; c0 = 0; c1 = H;
+        dw = ly.w_gu; ds = ly.s_gu; drow = m->I_l; dcols = H; break;
+    case T_DOWN: rows = H; cols = m->I; r0 = 0; r1 = H; c0 = (int64_t)r * m->I_l; c1 = c0 + m->I_l;
+        dw = ly.w_d; ds = ly.s_d; drow = 0; dcols = m->I_l; break;
+    default: break;
+    }
+    if (!is_scale) {
+        const int64_t need = qbytes(m->quant, rows, cols);
+        DU_CHECK_ARG((int64_t)bytes == need, (std::string("size mismatch for ") + name).c_str());
+        const int64_t rb = qbytes(m->quant, 1, cols);          // bytes per source row
+        const int64_t db = qbytes(m->quant, 1, dcols);         // bytes per destination row
+        const int64_t cb0 = qbytes(m->quant, 1, c0), cb1 = qbytes(m->quant, 1, c1);
+        return copy2d(dw + drow * db, (size_t)db, src, (size_t)rb, r0, r1, cb0, cb1, kind, st);
+    }
+    if (m->quant == DU_QUANT_INT8) {
+        DU_CHECK_ARG((int64_t)bytes == rows * 2, (std::string("size mismatch for ") + name).c_str());
+        // per-row scales: row-split tensors take their rows; K-split tensors keep every row
+        return copy2d((uint8_t *)ds + drow * 2, 2, src, 2, r0, r1, 0, 2, kind, st);
+    }
+    const int64_t g = m->group;
+    DU_CHECK_ARG(cols % g == 0, "int4 scales: cols % group != 0");
+    DU_CHECK_ARG((int64_t)bytes == rows * (cols / g) * 2, (std::string("size mismatch for ") + name).c_str());
+    return copy2d((uint8_t *)ds + drow * (dcols / g) * 2, (size_t)(dcols / g) * 2, src, (size_t)(cols / g) * 2, r0, r1,
+                  (c0 / g) * 2, (c1 / g) * 2, kind, st);
+}
+
+// ------------------------------------------------------------ execution
+
+static GemvParams gp_base(du_model *m, const uint8_t *w, const __half *s, int64_t K)
+{
+    GemvParams p = {};
+    p.w = w;
+    p.scales = s;
+    p.row_bytes = qbytes(m->quant, 1, K);
+    p.K = (int)K;
+    p.group = m->group;
+    return p;
+}
+
+static int qt_of(int quant) { return quant == DU_QUANT_INT4 ? Q_I4 : quant == DU_QUANT_INT8 ? Q_I8 : Q_F16; }
+
+static int gemv_max_tokens(int qt, int64_t row_bytes)
+{
+    int mt = 8;
+    while (mt > 1 && gemv_smem_bytes(qt, mt, row_bytes) > 220 * 1024) mt >>= 1;
+    return mt;
+}
+
+// Launches one GEMV over M tokens in chunks the kernel's smem stage holds.
+// Token-indexed pointers of `p` are advanced per chunk.
+static int run_gemv(du_model *m, int qt, GemvParams p, int M)
+{
+    const int mt = gemv_max_tokens(qt, p.row_bytes);
+    for (int t0 = 0; t0 < M; t0 += mt) {
+        GemvParams c = p;
+        c.M = M - t0 < mt ? M - t0 : mt;
+        c.x = p.x + (size_t)t0 * p.ldx;
+        if (p.y) c.y = p.y + (size_t)t0 * p.ldy;
+        if (p.q_out) c.q_out = p.q_out + (size_t)t0 * p.hq * p.hd;
+        if (p.pos) c.pos = p.pos + t0;
+        if (p.seq_of) c.seq_of = p.seq_of + t0;
+        if (p.logits) c.logits = p.logits + (size_t)t0 * p.ldl;
+        int rc = launch_gemv(qt, c, m->stream);
+        if (rc) return rc;
+    }
+    return DU_OK;
+}
+
+static int nccl_check(du_model *m, ncclResult_t r, const char *what)
+{
+    const NcclApi *n = nccl_api();
+    if (r == ncclSuccess) return DU_OK;
+    if (r == ncclInProgress) {
+        auto t0 = std::chrono::steady_clock::now();
+        for (;;) {
+            ncclResult_t a = ncclSuccess;
+            n->CommGetAsyncError(m->comm, &a);
+            if (a == ncclSuccess) return DU_OK;
+            if (a != ncclInProgress) return fail(DU_ENCCL, std::string(what) + ": " + n->GetErrorString(a));
+            if (std::chrono::duration_cast<std::chrono::milliseconds>(std::chrono::steady_clock::now() - t0).count() >
+                m->nccl_timeout_ms) {
+                n->CommAbort(m->comm);
+                m->comm = nullptr;
+                m->tp_ready = false;
+                return fail(DU_ENCCL, std::string(what) + ": timed out, communicator aborted");
+            }
+            std::this_thread::sleep_for(std::chrono::microseconds(50));
+        }
+    }
+    return fail(DU_ENCCL, std::string(what) + ": " + n->GetErrorString(r));
+}
+
+static int allreduce_sum(du_model *m, float *buf, size_t n)
+{
+    const NcclApi *api = nccl_api();
+    return nccl_check(m, api->AllReduce(buf, buf, n, ncclFloat32, ncclSum, m->comm, m->stream), "ncclAllReduce");
+}
+
+struct StepIO {
+    int M;                 // token rows
+    const int *ids;        // [M] device
+    const int *pos;        // [M] cache slot / rope position
+    const int *seq_of;     // [M] or nullptr
+    const int *kv_len;     // [M] kv length before kv_len_add
+    int kv_len_add;
+    int fd_nsplit;
+    int logits_rows;       // rows whose logits are produced (last token per sequence, or all)
+    const int *logit_tok;  // tokens -> which rows of x_res feed the lm_head: nullptr = all M
+    int logit_stride;      // if logit_tok == nullptr: take every logit_stride-th token starting at logit_first
+    int logit_first;
+    int *next_out;         // [logits_rows] greedy ids
+    int *feed;             // optional: also write ids here (device loop)
+    bool advance;          // cache_len[m] += 1 at the end (decode)
+};
+
+enum Stage { ST_QKV = 0, ST_ATTN = 1, ST_O = 2, ST_GATEUP = 3, ST_DOWN = 4 };
+
+// One stage of layer l for the token rows of `io`.  With tensor parallelism
+// the O and down stages end in an allreduce of the partial sums plus the
+// residual add (collective = false leaves both out, for kernel timing).
+static int enqueue_stage(du_model *m, const StepIO &io, int l, int stage, bool collective)
+{
+    const int H = m->H, hd = m->hd, M = io.M, qt = qt_of(m->quant);
+    cudaStream_t st = m->stream;
+    const int64_t Ko = (int64_t)m->hq_l * hd;
+    const Layer &ly = m->layers[l];
+    __half *kc = m->k_cache + (size_t)l * m->kv_layer_elems;
+    __half *vc = m->v_cache + (size_t)l * m->kv_layer_elems;
+    int rc = DU_OK;
+    GemvParams p;
+    switch (stage) {
+    case ST_QKV:   // RMSNorm(ln1) -> QKV GEMV -> RoPE -> q, fp16 K/V into the cache
+        p = gp_base(m, ly.w_qkv, ly.s_qkv, H);
+        p.x = m->x_res; p.ldx = H; p.gamma = ly.ln1; p.eps = m->cfg.rms_eps;
+        p.N = m->qkv_rows; p.map = MAP_ROPE_PAIR; p.map_hd = hd;
+        p.epi = EPI_QKV; p.q_out = m->q; p.k_cache = kc; p.v_cache = vc;
+        p.pos = io.pos; p.seq_of = io.seq_of; p.hq = m->hq_l; p.hkv = m->hkv_l; p.hd = hd; p.cap = m->cap;
+        p.rope_cos = m->rope_cos; p.rope_sin = m->rope_sin;
+        return run_gemv(m, qt, p, M);
+    case ST_ATTN:
+        return launch_flash_decode(m->q, kc, vc, io.seq_of, io.kv_len, io.kv_len_add, M, m->hq_l, m->hkv_l, hd,
+                                   m->cap, powf((float)hd, -0.5f), m->att, m->fd_scratch, m->fd_counters,
+                                   io.fd_nsplit, st);
+    case ST_O:
+    case ST_DOWN:  // O / down GEMV -> residual add (TP1) or partial sum -> allreduce -> add
+        if (stage == ST_O) {
+            p = gp_base(m, ly.w_o, ly.s_o, Ko);
+            p.x = m->att; p.ldx = (int)Ko;
+        } else {
+            p = gp_base(m, ly.w_d, ly.s_d, m->I_l);
+            p.x = m->inter; p.ldx = m->I_l;
+        }
+        p.N = H; p.map = MAP_IDENT;
+        if (m->tp == 1) { p.epi = EPI_RESID; p.y = m->x_res; p.ldy = H; }
+        else { p.epi = EPI_STORE; p.y = m->part; p.ldy = H; }
+        if ((rc = run_gemv(m, qt, p, M))) return rc;
+        if (m->tp > 1 && collective) {
+            if ((rc = allreduce_sum(m, m->part, (size_t)M * H))) return rc;
+            if ((rc = launch_add_inplace(m->x_res, m->part, (size_t)M * H, st))) return rc;
+        }
+        return DU_OK;
+    case ST_GATEUP:  // RMSNorm(ln2) -> gate|up GEMV -> SiLU(g) * u
+        p = gp_base(m, ly.w_gu, ly.s_gu, H);
+        p.x = m->x_res; p.ldx = H; p.gamma = ly.ln2; p.eps = m->cfg.rms_eps;
+        p.N = 2 * m->I_l; p.map = MAP_GATEUP; p.map_I = m->I_l;
+        p.epi = EPI_GATEUP; p.y = m->inter; p.ldy = m->I_l;
+        return run_gemv(m, qt, p, M);
+    default:
+        return fail(DU_EINVAL, "unknown stage");
+    }
+}
+
+static int enqueue_head(du_model *m, const StepIO &io);
+
+// The launch sequence for M token rows (decode: one per sequence; prefill: a chunk).
+static int enqueue_forward(du_model *m, const StepIO &io)
+{
+    int rc = launch_embed(io.ids, m->embed, m->cfg.embed_scale, io.M, m->H, m->x_res, m->stream);
+    if (rc) return rc;
+    for (int l = 0; l < m->L; l++)
+        for (int s = ST_QKV; s <= ST_DOWN; s++)
+            if ((rc = enqueue_stage(m, io, l, s, true))) return rc;
+    return enqueue_head(m, io);
+}
+
+// final RMSNorm + lm_head (+ argmax partials) on the selected rows, greedy pick
+static int enqueue_head(du_model *m, const StepIO &io)
+{
+    const int H = m->H, M = io.M;
+    cudaStream_t st = m->stream;
+    int rc = DU_OK;
+    const int R = io.logits_rows;
+    const float *xsel = m->x_res;
+    if (io.logit_stride != 1 || io.logit_first != 0) {
+        // gather the selected rows (last token of each sequence) into part[0..R)
+        for (int i = 0; i < R; i++)
+            DU_CUDA_TRY(cudaMemcpyAsync(m->part + (size_t)i * H,
+                                        m->x_res + (size_t)(io.logit_first + i * io.logit_stride) * H,
+                                        sizeof(float) * H, cudaMemcpyDeviceToDevice, st));
+        xsel = m->part;
+    }
+    GemvParams p = gp_base(m, (const uint8_t *)m->lm_head, nullptr, H);
+    p.row_bytes = 2LL * H;
+    p.x = xsel; p.ldx = H; p.gamma = m->final_norm; p.eps = m->cfg.rms_eps;
+    p.N = m->V_l; p.map = MAP_IDENT; p.epi = EPI_LOGITS;
+    p.logits = m->logits; p.ldl = m->V_l; p.vocab_off = m->rank * m->V_l;
+    const int rpc_target = m->am_parts;
+    int rpc = (p.N + rpc_target - 1) / rpc_target;
+    rpc = (rpc + 1) & ~1;
+    p.rows_per_cta = rpc;
+    const int nparts = (p.N + rpc - 1) / rpc;
+    const int mt = gemv_max_tokens(Q_F16, p.row_bytes);
+    for (int t0 = 0; t0 < R; t0 += mt) {
+        GemvParams c = p;
+        c.M = R - t0 < mt ? R - t0 : mt;
+        c.x = p.x + (size_t)t0 * H;
+        c.logits = p.logits + (size_t)t0 * p.ldl;
+        c.am_val = m->am_val + (size_t)t0 * nparts;
+        c.am_idx = m->am_idx + (size_t)t0 * nparts;
+        if ((rc = launch_gemv(Q_F16, c, st))) return rc;
+    }
+    if (m->tp == 1) {
+        if ((rc = launch_argmax_final(m->am_val, m->am_idx, R, nparts, io.next_out, io.feed, st))) return rc;
+    } else {
+        // local best (val, idx) per row, exchange the pairs between ranks, pick the global best
+        if ((rc = launch_argmax_final_pairs(m->am_val, m->am_idx, R, nparts, m->best_val, st))) return rc;
+        const NcclApi *api = nccl_api();
+        if ((rc = nccl_check(m, api->AllGather(m->best_val, m->gbest_val, (size_t)m->max_tokens * 2, ncclFloat32,
+                                               m->comm, st), "ncclAllGather")))
+            return rc;
+        if ((rc = launch_argmax_pick_tp(m->gbest_val, m->tp, m->max_tokens, R, io.next_out, io.feed, st))) return rc;
+    }
+    if (io.advance) {
+        if ((rc = launch_step_advance(m->d_cache_len, M, st))) return rc;
+    }
+    return DU_OK;
+}
+
+// One forward per call at a time per handle (LLM Busy guard, LLM.cs:393-406).
+struct CallGuard {
+    du_model *m;
+    bool ok;
+    explicit CallGuard(du_model *mm) : m(mm), ok(false)
+    {
+        if (m && m->busy.exchange(1) == 0) {
+            ok = true;
+            cudaSetDevice(m->device);
+        }
+    }
+    ~CallGuard()
+    {
+        if (ok) m->busy.store(0);
+    }
+};
+
+#define DU_GUARD(m)                                                                   \
+    if (!(m)) return fail(DU_EINVAL, "null model handle");                            \
+    CallGuard _guard(m);                                                              \
+    if (!_guard.ok) return fail(DU_EBUSY, "model is busy with another call")
+
+static int sync_cache_len(du_model *m)
+{
+    DU_CUDA_TRY(cudaMemcpyAsync(m->d_cache_len, m->h_cache_len.data(), sizeof(int) * m->maxb, cudaMemcpyHostToDevice,
+                                m->stream));
+    return DU_OK;
+}
+
+static StepIO decode_io(du_model *m, int batch)
+{
+    StepIO io = {};
+    io.M = batch;
+    io.ids = m->d_ids;
+    io.pos = m->d_cache_len;
+    io.seq_of = nullptr;
+    io.kv_len = m->d_cache_len;
+    io.kv_len_add = 1;
+    io.fd_nsplit = fd_choose_splits(batch, m->hkv_l, m->cap);
+    io.logits_rows = batch;
+    io.logit_stride = 1;
+    io.logit_first = 0;
+    io.next_out = m->d_next;
+    io.feed = m->d_ids;
+    io.advance = true;
+    return io;
+}
+
+static int get_graph(du_model *m, int batch, cudaGraphExec_t *out, Graph **gout = nullptr)
+{
+    auto it = m->graphs.find(batch);
+    if (it != m->graphs.end()) {
+        *out = it->second.exec;
+        if (gout) *gout = &it->second;
+        return DU_OK;
+    }
+    const StepIO io = decode_io(m, batch);
+    Graph g;
+    DU_CUDA_TRY(cudaStreamBeginCapture(m->stream, cudaStreamCaptureModeThreadLocal));
+    int rc = enqueue_forward(m, io);
+    cudaError_t e = cudaStreamEndCapture(m->stream, &g.g);
+    if (rc) {
+        if (g.g) cudaGraphDestroy(g.g);
+        return rc;
+    }
+    if (e != cudaSuccess) return cuda_fail(e, "cudaStreamEndCapture");
+    e = cudaGraphInstantiate(&g.exec, g.g, 0);
+    if (e != cudaSuccess) {
+        cudaGraphDestroy(g.g);
+        return cuda_fail(e, "cudaGraphInstantiate");
+    }
+    m->graphs[batch] = g;
+    *out = g.exec;
+    if (gout) *gout = &m->graphs[batch];
+    return DU_OK;
+}
+
+static int check_ids(du_model *m, const int32_t *ids, size_t n)
+{
+    for (size_t i = 0; i < n; i++)
+        if (ids[i] < 0 || ids[i] >= m->V) return fail(DU_EINVAL, "token id outside [0, vocab_size)");
+    return DU_OK;
+}
+
+}  // namespace du
+
+using namespace du;
+
+extern "C" {
+
+DU_API int du_model_create(const du_model_config *cfg, du_model **out)
+{
+    DU_CHECK_ARG(cfg && out, "du_model_create: null argument");
+    *out = nullptr;
+    int rc = check_cfg(*cfg);
+    if (rc) return rc;
+    du_model *m = new du_model();
+    m->cfg = *cfg;
+    cudaGetDevice(&m->device);
+    m->tp = cfg->tp_size <= 0 ? 1 : cfg->tp_size;
+    m->cfg.tp_size = m->tp;
+    m->rank = cfg->tp_rank;
+    m->H = cfg->hidden_size; m->I = cfg->intermediate_size; m->L = cfg->num_layers;
+    m->hq = cfg->num_heads_q; m->hkv = cfg->num_heads_kv; m->hd = cfg->head_dim; m->V = cfg->vocab_size;
+    m->hq_l = m->hq / m->tp; m->hkv_l = m->hkv / m->tp; m->I_l = m->I / m->tp; m->V_l = m->V / m->tp;
+    m->qkv_rows = (m->hq_l + 2 * m->hkv_l) * m->hd;
+    m->quant = cfg->quant;
+    m->group = cfg->quant == DU_QUANT_INT4 ? cfg->group_size : 32;
+    m->cap = cfg->kv_capacity;
+    m->maxb = cfg->max_batch;
+    m->max_tokens = m->maxb > 256 ? m->maxb : 256;
+    if (m->cfg.embed_scale == 0.0f) m->cfg.embed_scale = 1.0f;
+    cudaError_t e = cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking);
+    if (e != cudaSuccess) {
+        delete m;
+        return cuda_fail(e, "cudaStreamCreate");
+    }
+    rc = model_alloc(m);
+    if (rc) {
+        model_free(m);
+        delete m;
+        return rc;
+    }
+    *out = m;
+    return DU_OK;
+}
+
+DU_API int du_model_destroy(du_model *m)
+{
+    if (!m) return DU_OK;
+    if (m->busy.exchange(1) != 0) return fail(DU_EBUSY, "du_model_destroy: model is busy");
+    model_free(m);
+    delete m;
+    return DU_OK;
+}
+
+DU_API int du_model_load_tensor(du_model *m, const char *name, const void *host, size_t bytes)
+{
+    DU_GUARD(m);
+    DU_CHECK_ARG(name && host, "du_model_load_tensor: null argument");
+    int rc = place_tensor(m, name, host, bytes, cudaMemcpyHostToDevice);
+    if (rc) return rc;
+    DU_CUDA_TRY(cudaStreamSynchronize(m->stream));
+    return DU_OK;
+}
+
+DU_API int du_model_init_random(du_model *m, uint64_t seed, float std)
+{
+    DU_GUARD(m);
+    cudaStream_t st = m->stream;
+    const int H = m->H, hd = m->hd;
+    const int64_t big = (int64_t)m->I * H > (int64_t)(m->hq + 2 * m->hkv) * hd * H ? (int64_t)m->I * H
+                                                                                   : (int64_t)m->hq * hd * H;
+    float *tmp = nullptr;
+    uint8_t *qtmp = nullptr;
+    __half *stmp = nullptr;
+    DU_CUDA_TRY(cudaMalloc(&tmp, sizeof(float) * big));
+    int rc = DU_OK;
+    if (cudaMalloc(&qtmp, (size_t)big * 2) != cudaSuccess || cudaMalloc(&stmp, (size_t)big / 16 + 1024) != cudaSuccess)
+        rc = fail(DU_ENOMEM, "du_model_init_random: temp allocation failed");
+    const char *ext = m->quant == DU_QUANT_INT4 ? ".int4.bin" : m->quant == DU_QUANT_INT8 ? ".int8.bin" : ".bin";
+    static const char *stems[] = {"self_attn_q_proj", "self_attn_k_proj", "self_attn_v_proj", "self_attn_o_proj",
+                                  "mlp_gate_proj", "mlp_up_proj", "mlp_down_proj"};
+    uint64_t tid = 0;
+    for (int l = 0; l < m->L && !rc; l++) {
+        for (int t = 0; t < 7 && !rc; t++) {
+            int64_t rows, cols;
+            switch (t) {
+            case 0: rows = (int64_t)m->hq * hd; cols = H; break;
+            case 1: case 2: rows = (int64_t)m->hkv * hd; cols = H; break;
+            case 3: rows = H; cols = (int64_t)m->hq * hd; break;
+            case 4: case 5: rows = m->I; cols = H; break;
+            default: rows = H; cols = m->I; break;
+            }
+            const uint64_t s = seed * 0x9E3779B97F4A7C15ull + (++tid);
+            if ((rc = launch_random_normal(tmp, (size_t)(rows * cols), s, 0, std, st))) break;
+            char name[96];
+            snprintf(name, sizeof name, "layer_%d/%s%s", l, stems[t], ext);
+            if (m->quant == DU_QUANT_FP16) {
+                // fp16 linears: convert in place through the half generator for the same values
+                if ((rc = launch_random_normal_half((__half *)qtmp, (size_t)(rows * cols), s, 0, std, st))) break;
+                rc = place_tensor(m, name, qtmp, (size_t)(rows * cols * 2), cudaMemcpyDeviceToDevice);
+                continue;
+            }
+            if (m->quant == DU_QUANT_INT8) rc = launch_quantize_int8(tmp, rows, cols, (int8_t *)qtmp, stmp, st);
+            else rc = launch_quantize_int4(tmp, rows, cols, m->group, qtmp, stmp, st);
+            if (rc) break;
+            if ((rc = place_tensor(m, name, qtmp, (size_t)qbytes(m->quant, rows, cols), cudaMemcpyDeviceToDevice)))
+                break;
+            snprintf(name, sizeof name, "layer_%d/%s.scales.bin", l, stems[t]);
+            rc = place_tensor(m, name, stmp, (size_t)sbytes(m->quant, m->group, rows, cols), cudaMemcpyDeviceToDevice);
+        }
+        if (!rc) rc = launch_fill_half(m->layers[l].ln1, H, 0.0f, st);
+        if (!rc) rc = launch_fill_half(m->layers[l].ln2, H, 0.0f, st);
+    }
+    if (!rc) rc = launch_fill_half(m->final_norm, H, 0.0f, st);
+    if (!rc) rc = launch_random_normal_half(m->embed, (size_t)m->V * H, seed * 0x9E3779B97F4A7C15ull + 0xE1ull, 0, std, st);
+    if (!rc && !m->cfg.tie_embedding)
+        rc = launch_random_normal_half(m->lm_head, (size_t)m->V_l * H, seed * 0x9E3779B97F4A7C15ull + 0xE2ull,
+                                       (uint64_t)m->rank * m->V_l * H, std, st);
+    cudaStreamSynchronize(st);
+    cudaFree(tmp);
+    if (qtmp) cudaFree(qtmp);
+    if (stmp) cudaFree(stmp);
+    if (rc) return rc;
+    DU_CUDA_TRY(cudaGetLastError());
+    return DU_OK;
+}
+
+DU_API int du_tp_init(du_model *m, const void *nccl_unique_id, int timeout_ms)
+{
+    DU_GUARD(m);
+    DU_CHECK_ARG(nccl_unique_id != nullptr, "du_tp_init: null unique id");
+    if (m->tp == 1) return DU_OK;
+    const NcclApi *n = nccl_api();
+    if (!n) return DU_ENCCL;
+    ncclUniqueId id;
+    memcpy(&id, nccl_unique_id, sizeof id);
+    ncclConfig_t config = NCCL_CONFIG_INITIALIZER;
+    config.blocking = 0;
+    m->nccl_timeout_ms = timeout_ms > 0 ? timeout_ms : 60000;
+    ncclResult_t r = n->CommInitRankConfig(&m->comm, m->tp, id, m->rank, &config);
+    if (r != ncclSuccess && r != ncclInProgress)
+        return fail(DU_ENCCL, std::string("ncclCommInitRankConfig: ") + n->GetErrorString(r));
+    int rc = nccl_check(m, ncclInProgress, "ncclCommInitRankConfig");
+    if (rc) return rc;
+    m->tp_ready = true;
+    return DU_OK;
+}
+
+DU_API int du_forward(du_model *m, const int32_t *ids, int batch, int seq_len, int use_cache, int last_pos_only,
+                      float *logits_out, int32_t *next_ids_out)
+{
+    DU_GUARD(m);
+    DU_CHECK_ARG(ids && batch > 0 && seq_len > 0, "du_forward: bad arguments");
+    DU_CHECK_ARG(batch <= m->maxb, "du_forward: batch exceeds max_batch");
+    if (m->tp > 1 && !m->tp_ready) return fail(DU_ESTATE, "du_forward: call du_tp_init first");
+    int rc = check_ids(m, ids, (size_t)batch * seq_len);
+    if (rc) return rc;
+    if (!use_cache)
+        for (int b = 0; b < batch; b++) m->h_cache_len[b] = 0;   // stateless forward from position 0
+    for (int b = 0; b < batch; b++)
+        if (m->h_cache_len[b] + seq_len > m->cap) return fail(DU_EINVAL, "du_forward: KV cache capacity exceeded");
+    cudaStream_t st = m->stream;
+    const int H = m->H;
+    // chunk the positions so that batch * chunk <= max_tokens
+    int chunk = m->max_tokens / batch;
+    if (chunk < 1) chunk = 1;
+    std::vector<int> hbuf;
+    float *big_logits = nullptr;
+    if (!last_pos_only && logits_out) {
+        DU_CUDA_TRY(cudaMalloc(&big_logits, sizeof(float) * (size_t)m->max_tokens * m->V_l * (m->tp > 1 ? m->tp + 1 : 1)));
+    }
+    for (int s0 = 0; s0 < seq_len && !rc; s0 += chunk) {
+        const int s1 = s0 + chunk < seq_len ? s0 + chunk : seq_len;
+        const int Lc = s1 - s0, M = batch * Lc;
+        hbuf.assign((size_t)4 * M, 0);
+        for (int b = 0; b < batch; b++)
+            for (int l = 0; l < Lc; l++) {
+                const int t = b * Lc + l;
+                hbuf[t] = ids[(size_t)b * seq_len + s0 + l];
+                hbuf[M + t] = m->h_cache_len[b] + s0 + l;           // position / cache slot
+                hbuf[2 * M + t] = b;                                // sequence
+                hbuf[3 * M + t] = m->h_cache_len[b] + s0 + l + 1;   // causal kv length
+            }
+        DU_CUDA_TRY(cudaMemcpyAsync(m->d_ids, hbuf.data(), sizeof(int) * M, cudaMemcpyHostToDevice, st));
+        DU_CUDA_TRY(cudaMemcpyAsync(m->d_pos, hbuf.data() + M, sizeof(int) * M, cudaMemcpyHostToDevice, st));
+        DU_CUDA_TRY(cudaMemcpyAsync(m->d_seq, hbuf.data() + 2 * M, sizeof(int) * M, cudaMemcpyHostToDevice, st));
+        DU_CUDA_TRY(cudaMemcpyAsync(m->d_kvlen, hbuf.data() + 3 * M, sizeof(int) * M, cudaMemcpyHostToDevice, st));
+        StepIO io = {};
+        io.M = M; io.ids = m->d_ids; io.pos = m->d_pos; io.seq_of = m->d_seq; io.kv_len = m->d_kvlen;
+        io.kv_len_add = 0;
+        int maxkv = 0;
+        for (int b = 0; b < batch; b++) maxkv = maxkv > m->h_cache_len[b] + s1 ? maxkv : m->h_cache_len[b] + s1;
+        io.fd_nsplit = fd_choose_splits(M, m->hkv_l, maxkv);
+        const bool last_chunk = s1 == seq_len;
+        if (last_pos_only) {
+            io.logits_rows = batch; io.logit_first = Lc - 1; io.logit_stride = Lc;
+        } else {
+            io.logits_rows = M; io.logit_first = 0; io.logit_stride = 1;
+        }
+        io.next_out = m->d_next;
+        io.feed = nullptr;
+        io.advance = false;
+        if (!last_pos_only && logits_out) {
+            // all-position logits: run the head per chunk into the big buffer
+            float *saved = m->logits;
+            m->logits = big_logits;
+            rc = enqueue_forward(m, io);
+            m->logits = saved;
+            if (rc) break;
+            float *src = big_logits;
+            if (m->tp > 1) {
+                const NcclApi *api = nccl_api();
+                float *dst = big_logits + (size_t)m->max_tokens * m->V_l;
+                if ((rc = nccl_check(m, api->AllGather(big_logits, dst, (size_t)m->max_tokens * m->V_l, ncclFloat32,
+                                                       m->comm, st), "ncclAllGather")))
+                    break;
+                src = dst;
+            }
+            std::vector<float> tmp((size_t)M * m->V_l * m->tp);
+            for (int r = 0; r < m->tp; r++)
+                DU_CUDA_TRY(cudaMemcpyAsync(tmp.data() + (size_t)r * M * m->V_l, src + (size_t)r * m->max_tokens * m->V_l,
+                                            sizeof(float) * M * m->V_l, cudaMemcpyDeviceToHost, st));
+            DU_CUDA_TRY(cudaStreamSynchronize(st));
+            for (int b = 0; b < batch; b++)
+                for (int l = 0; l < Lc; l++)
+                    for (int r = 0; r < m->tp; r++)
+                        memcpy(logits_out + ((size_t)b * seq_len + s0 + l) * m->V + (size_t)r * m->V_l,
+                               tmp.data() + ((size_t)r * M + b * Lc + l) * m->V_l, sizeof(float) * m->V_l);
+        } else if (last_chunk || !last_pos_only) {
+            rc = enqueue_forward(m, io);
+        } else {
+            // earlier chunks of a last-position-only prefill: no head needed, but the
+            // launch sequence is the same; the logits of the last chunk overwrite these
+            rc = enqueue_forward(m, io);
+        }
+    }
+    if (big_logits) {
+        cudaStreamSynchronize(st);
+        cudaFree(big_logits);
+    }
+    if (rc) return rc;
+    // use_cache == 0 (LLM.Predict): the cache rows served as scratch, nothing stays visible
+    for (int b = 0; b < batch; b++) m->h_cache_len[b] = use_cache ? m->h_cache_len[b] + seq_len : 0;
+    if ((rc = sync_cache_len(m))) return rc;
+    m->last_batch = batch;
+    if (next_ids_out) {
+        DU_CUDA_TRY(cudaMemcpyAsync(m->h_pin_next, m->d_next, sizeof(int) * batch, cudaMemcpyDeviceToHost, st));
+    }
+    DU_CUDA_TRY(cudaStreamSynchronize(st));
+    if (next_ids_out) memcpy(next_ids_out, m->h_pin_next, sizeof(int) * batch);
+    if (last_pos_only && logits_out) {
+        m->busy.store(0);
+        _guard.ok = false;
+        return du_read_logits(m, logits_out, batch);
+    }
+    (void)H;
+    return DU_OK;
+}
+
+DU_API int du_read_logits(du_model *m, float *host_out, int batch)
+{
+    DU_GUARD(m);
+    DU_CHECK_ARG(host_out && batch > 0 && batch <= m->maxb, "du_read_logits: bad arguments");
+    cudaStream_t st = m->stream;
+    if (m->tp == 1) {
+        DU_CUDA_TRY(cudaMemcpyAsync(host_out, m->logits, sizeof(float) * batch * m->V_l, cudaMemcpyDeviceToHost, st));
+        DU_CUDA_TRY(cudaStreamSynchronize(st));
+        return DU_OK;
+    }
+    const NcclApi *api = nccl_api();
+    int rc = nccl_check(m, api->AllGather(m->logits, m->logits_all, (size_t)m->maxb * m->V_l, ncclFloat32, m->comm, st),
+                        "ncclAllGather");
+    if (rc) return rc;
+    std::vector<float> tmp((size_t)m->tp * m->maxb * m->V_l);
+    DU_CUDA_TRY(cudaMemcpyAsync(tmp.data(), m->logits_all, sizeof(float) * tmp.size(), cudaMemcpyDeviceToHost, st));
+    DU_CUDA_TRY(cudaStreamSynchronize(st));
+    for (int b = 0; b < batch; b++)
+        for (int r = 0; r < m->tp; r++)
+            memcpy(host_out + (size_t)b * m->V + (size_t)r * m->V_l, tmp.data() + ((size_t)r * m->maxb + b) * m->V_l,
+                   sizeof(float) * m->V_l);
+    return DU_OK;
+}
+
+DU_API int du_decode_step(du_model *m, const int32_t *ids, int batch, int32_t *next_ids)
+{
+    DU_GUARD(m);
+    DU_CHECK_ARG(ids && next_ids && batch > 0 && batch <= m->maxb, "du_decode_step: bad arguments");
+    if (m->tp > 1 && !m->tp_ready) return fail(DU_ESTATE, "du_decode_step: call du_tp_init first");
+    int rc = check_ids(m, ids, batch);
+    if (rc) return rc;
+    for (int b = 0; b < batch; b++)
+        if (m->h_cache_len[b] + 1 > m->cap) return fail(DU_EINVAL, "du_decode_step: KV cache capacity exceeded");
+    cudaGraphExec_t exec;
+    if ((rc = get_graph(m, batch, &exec))) return rc;
+    cudaStream_t st = m->stream;
+    memcpy(m->h_pin_ids, ids, sizeof(int) * batch);
+    DU_CUDA_TRY(cudaMemcpyAsync(m->d_ids, m->h_pin_ids, sizeof(int) * batch, cudaMemcpyHostToDevice, st));
+    DU_CUDA_TRY(cudaGraphLaunch(exec, st));
+    DU_CUDA_TRY(cudaMemcpyAsync(m->h_pin_next, m->d_next, sizeof(int) * batch, cudaMemcpyDeviceToHost, st));
+    DU_CUDA_TRY(cudaStreamSynchronize(st));
+    memcpy(next_ids, m->h_pin_next, sizeof(int) * batch);
+    for (int b = 0; b < batch; b++) m->h_cache_len[b] += 1;
+    m->last_batch = batch;
+    return DU_OK;
+}
+
+DU_API int du_decode_loop(du_model *m, const int32_t *ids, int batch, int n_steps, int32_t *tokens_out)
+{
+    DU_GUARD(m);
+    DU_CHECK_ARG(ids && tokens_out && batch > 0 && batch <= m->maxb && n_steps >= 0, "du_decode_loop: bad arguments");
+    if (m->tp > 1 && !m->tp_ready) return fail(DU_ESTATE, "du_decode_loop: call du_tp_init first");
+    int rc = check_ids(m, ids, batch);
+    if (rc) return rc;
+    for (int b = 0; b < batch; b++)
+        if (m->h_cache_len[b] + n_steps > m->cap) return fail(DU_EINVAL, "du_decode_loop: KV cache capacity exceeded");
+    if (n_steps == 0) return DU_OK;
+    cudaGraphExec_t exec;
+    if ((rc = get_graph(m, batch, &exec))) return rc;
+    cudaStream_t st = m->stream;
+    int *hist = nullptr;
+    DU_CUDA_TRY(cudaMallocAsync((void **)&hist, sizeof(int) * (size_t)n_steps * batch, st));
+    memcpy(m->h_pin_ids, ids, sizeof(int) * batch);
+    DU_CUDA_TRY(cudaMemcpyAsync(m->d_ids, m->h_pin_ids, sizeof(int) * batch, cudaMemcpyHostToDevice, st));
+    for (int s = 0; s < n_steps; s++) {
+        DU_CUDA_TRY(cudaGraphLaunch(exec, st));
+        DU_CUDA_TRY(cudaMemcpyAsync(hist + (size_t)s * batch, m->d_next, sizeof(int) * batch, cudaMemcpyDeviceToDevice, st));
+    }
+    DU_CUDA_TRY(cudaMemcpyAsync(tokens_out, hist, sizeof(int) * (size_t)n_steps * batch, cudaMemcpyDeviceToHost, st));
+    DU_CUDA_TRY(cudaFreeAsync(hist, st));
+    DU_CUDA_TRY(cudaStreamSynchronize(st));
+    for (int b = 0; b < batch; b++) m->h_cache_len[b] += n_steps;
+    m->last_batch = batch;
+    return DU_OK;
+}
+
+DU_API int du_reset_cache(du_model *m)
+{
+    DU_GUARD(m);
+    for (int b = 0; b < m->maxb; b++) m->h_cache_len[b] = 0;
+    int rc = sync_cache_len(m);
+    if (rc) return rc;
+    DU_CUDA_TRY(cudaStreamSynchronize(m->stream));
+    return DU_OK;
+}
+
+DU_API int du_cache_len(du_model *m, int seq, int *out)
+{
+    DU_GUARD(m);
+    DU_CHECK_ARG(out && seq >= 0 && seq < m->maxb, "du_cache_len: bad arguments");
+    *out = m->h_cache_len[seq];
+    return DU_OK;
+}
+
+DU_API int du_model_stream(du_model *m, void **stream_out)
+{
+    DU_CHECK_ARG(m && stream_out, "du_model_stream: null argument");
+    *stream_out = m->stream;
+    return DU_OK;
+}
+
+DU_API int du_model_weight_bytes(du_model *m, uint64_t *out)
+{
+    DU_CHECK_ARG(m && out, "du_model_weight_bytes: null argument");
+    *out = m->weight_bytes;
+    return DU_OK;
+}
+
+DU_API int du_model_graph_info(du_model *m, int batch, int *kernel_nodes, int *total_nodes)
+{
+    DU_GUARD(m);
+    DU_CHECK_ARG(kernel_nodes && total_nodes && batch > 0 && batch <= m->maxb, "du_model_graph_info: bad arguments");
+    if (m->tp > 1 && !m->tp_ready) return fail(DU_ESTATE, "du_model_graph_info: call du_tp_init first");
+    cudaGraphExec_t exec;
+    Graph *g = nullptr;
+    int rc = get_graph(m, batch, &exec, &g);
+    if (rc) return rc;
+    size_t n = 0;
+    DU_CUDA_TRY(cudaGraphGetNodes(g->g, nullptr, &n));
+    std::vector<cudaGraphNode_t> nodes(n);
+    DU_CUDA_TRY(cudaGraphGetNodes(g->g, nodes.data(), &n));
+    int k = 0;
+    for (auto nd : nodes) {
+        cudaGraphNodeType t;
+        DU_CUDA_TRY(cudaGraphNodeGetType(nd, &t));
+        if (t == cudaGraphNodeTypeKernel) k++;
+    }
+    *kernel_nodes = k;
+    *total_nodes = (int)n;
+    return DU_OK;
+}
+
+DU_API int du_model_kernel_times(du_model *m, int batch, int reps, float *ms_out)
+{
+    DU_GUARD(m);
+    DU_CHECK_ARG(ms_out && batch > 0 && batch <= m->maxb && reps > 0, "du_model_kernel_times: bad arguments");
+    for (int b = 0; b < batch; b++)
+        if (m->h_cache_len[b] + 1 > m->cap) return fail(DU_EINVAL, "du_model_kernel_times: KV cache is full");
+    StepIO io = decode_io(m, batch);
+    io.feed = nullptr;
+    io.advance = false;
+    cudaStream_t st = m->stream;
+    cudaEvent_t e0, e1;
+    DU_CUDA_TRY(cudaEventCreate(&e0));
+    DU_CUDA_TRY(cudaEventCreate(&e1));
+    int rc = DU_OK;
+    for (int s = 0; s <= 5 && !rc; s++) {
+        for (int pass = 0; pass < 2 && !rc; pass++) {          // pass 0 warms up
+            cudaEventRecord(e0, st);
+            for (int r = 0; r < reps && !rc; r++)
+                for (int l = 0; l < m->L && !rc; l++)
+                    rc = s < 5 ? enqueue_stage(m, io, l, s, false) : (l == 0 ? enqueue_head(m, io) : DU_OK);
+            cudaEventRecord(e1, st);
+        }
+        if (rc) break;
+        cudaEventSynchronize(e1);
+        float ms = 0.0f;
+        cudaEventElapsedTime(&ms, e0, e1);
+        ms_out[s] = ms / (float)(reps * (s < 5 ? m->L : 1));
+    }
+    cudaEventDestroy(e0);
+    cudaEventDestroy(e1);
+    if (rc) return rc;
+    DU_CUDA_TRY(cudaStreamSynchronize(st));
+    return DU_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,232 @@
+"""Host-side mirror of DeepUnity's LLM API for the llama decode path.
+
+Mirrors (paths relative to the DeepUnity project root):
+  * ``LLMQuant`` / ``KVQuant`` enums        -- LLM/Base/LLM.cs:15-87
+  * ``LLM`` (Predict / Generate / Release)  -- LLM/Base/LLM.cs:365-655
+  * ``LLMRegistry.Create(id, quant, ...)``  -- LLM/Base/LLMRegistry.cs:61-73
+  * ``LlamaForCausalLM`` = MiniCPM5ForCausalLM's role (LLM/MiniCPM5/MiniCPM5.cs) on
+    MiniCPM5Model's executor (MiniCPM5Model.cs), backed by libdeepunity_cuda.
+Weights come from an ``import_params.py`` export folder (same file names and
+formats) or from the library's seeded synthetic initialiser.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import enum
+import os
+from dataclasses import dataclass, field
+from typing import Callable, Iterator, Optional, Sequence
+
+import numpy as np
+
+from . import _lib
+
+
+class LLMQuant(enum.IntEnum):
+    FP16 = _lib.QUANT_FP16
+    INT8 = _lib.QUANT_INT8
+    INT4 = _lib.QUANT_INT4
+
+
+class KVQuant(enum.IntEnum):
+    FP32 = 0
+    FP16 = 1
+    INT8 = 2
+
+
+@dataclass
+class LlamaConfig:
+    """Architecture constants (the role of MiniCPM5Config.cs:11-37, as data)."""
+    hidden_size: int
+    intermediate_size: int
+    num_layers: int
+    num_heads_q: int
+    num_heads_kv: int
+    head_dim: int
+    vocab_size: int
+    rms_eps: float = 1e-5
+    rope_theta: float = 10000.0
+    tie_embedding: bool = False
+    group_size: int = 128
+    name: str = "llama"
+
+
+# Configurations named by the benchmark (BASELINE configs 4 and 5) and the
+# reference's own llama-style model (MiniCPM5Config.cs:11-37).
+CONFIGS = {
+    "llama-1.1b": LlamaConfig(2048, 5632, 22, 32, 4, 64, 32000, 1e-5, 10000.0, name="llama-1.1b"),
+    "llama-8b": LlamaConfig(4096, 14336, 32, 32, 8, 128, 128256, 1e-5, 10000.0, name="llama-8b"),
+    "MiniCPM5-1B": LlamaConfig(1536, 4608, 24, 16, 2, 128, 130560, 1e-6, 5_000_000.0, group_size=32,
+                               name="MiniCPM5-1B"),
+}
+
+
+class LLM:
+    """Abstract LLM surface (LLM/Base/LLM.cs)."""
+
+    def Predict(self, input_ids, attn_mask=None) -> np.ndarray:
+        raise NotImplementedError
+
+    def Generate(self, input_ids, on_token: Optional[Callable[[int], None]] = None,
+                 max_new_tokens: int = 64, stop_tokens: Sequence[int] = ()) -> Iterator[int]:
+        raise NotImplementedError
+
+    def Release(self):
+        raise NotImplementedError
+
+
+class LlamaForCausalLM(LLM):
+    """Llama-style decoder on libdeepunity_cuda (one GPU, or one tensor-parallel rank)."""
+
+    def __init__(self, config: LlamaConfig, quant: LLMQuant = LLMQuant.INT8, kv_quant: KVQuant = KVQuant.FP16,
+                 max_context_length: int = 8192, max_batch: int = 1, params_path: Optional[str] = None,
+                 seed: Optional[int] = 0, init_std: float = 0.02, device: int = 0,
+                 tp_rank: int = 0, tp_size: int = 1):
+        if kv_quant != KVQuant.FP16:
+            raise NotImplementedError("only the fp16 KV cache is implemented (KVQuant.FP16)")
+        self.config = config
+        self.quant = LLMQuant(quant)
+        self.max_batch = max_batch
+        self.capacity = max_context_length
+        self.tp_rank, self.tp_size = tp_rank, tp_size
+        _lib.call("du_init", device)
+        cfg = _lib.ModelConfig()
+        cfg.hidden_size, cfg.intermediate_size = config.hidden_size, config.intermediate_size
+        cfg.num_layers, cfg.num_heads_q, cfg.num_heads_kv = config.num_layers, config.num_heads_q, config.num_heads_kv
+        cfg.head_dim, cfg.vocab_size = config.head_dim, config.vocab_size
+        cfg.rms_eps, cfg.rope_theta, cfg.embed_scale = config.rms_eps, config.rope_theta, 1.0
+        cfg.quant, cfg.group_size = int(self.quant), config.group_size
+        cfg.kv_capacity, cfg.max_batch = max_context_length, max_batch
+        cfg.tp_rank, cfg.tp_size, cfg.tie_embedding = tp_rank, tp_size, int(config.tie_embedding)
+        h = C.c_void_p()
+        _lib.call("du_model_create", C.byref(cfg), C.byref(h))
+        self._h = h
+        self._busy = False
+        if params_path is not None:
+            self.load_params(params_path)
+        elif seed is not None:
+            _lib.call("du_model_init_random", self._h, seed, init_std)
+
+    # ------------------------------------------------------------------ loading
+    def load_tensor(self, name: str, data: np.ndarray):
+        a = np.ascontiguousarray(data)
+        _lib.call("du_model_load_tensor", self._h, name.encode(), a.ctypes.data_as(C.c_void_p), a.nbytes)
+
+    def load_params(self, folder: str):
+        """Streams an import_params.py export folder (MiniCPM5Weights' role)."""
+        for root, _, files in os.walk(folder):
+            for f in sorted(files):
+                if not f.endswith(".bin"):
+                    continue
+                rel = os.path.relpath(os.path.join(root, f), folder).replace(os.sep, "/")
+                self.load_tensor(rel, np.fromfile(os.path.join(root, f), dtype=np.uint8))
+
+    # ---------------------------------------------------------------- inference
+    @property
+    def handle(self):
+        return self._h
+
+    def init_tp(self, unique_id: bytes, timeout_ms: int = 60000):
+        buf = C.create_string_buffer(bytes(unique_id), 128)
+        _lib.call("du_tp_init", self._h, buf, timeout_ms)
+
+    def forward(self, ids, use_cache: bool = True, last_pos_only: bool = True, want_logits: bool = True):
+        """MiniCPM5Model.Forward: ids [batch, seq] -> (logits, greedy next ids)."""
+        ids = np.ascontiguousarray(np.atleast_2d(np.asarray(ids, dtype=np.int32)))
+        B, S = ids.shape
+        V = self.config.vocab_size
+        logits = None
+        if want_logits:
+            logits = np.empty((B, V) if last_pos_only else (B, S, V), np.float32)
+        nxt = np.empty(B, np.int32)
+        _lib.call("du_forward", self._h, ids.ctypes.data_as(C.c_void_p), B, S, int(use_cache), int(last_pos_only),
+                  logits.ctypes.data_as(C.c_void_p) if logits is not None else None, nxt.ctypes.data_as(C.c_void_p))
+        return logits, nxt
+
+    def Predict(self, input_ids, attn_mask=None) -> np.ndarray:
+        """LLM.Predict (MiniCPM5.cs:121-128): logits for every position, stateless."""
+        if attn_mask is not None:
+            raise NotImplementedError("attention masks are not supported by the decode path")
+        ids = np.asarray(input_ids, dtype=np.int32).reshape(1, -1)
+        logits, _ = self.forward(ids, use_cache=False, last_pos_only=False)
+        return logits[0]
+
+    def decode_step(self, ids) -> np.ndarray:
+        ids = np.ascontiguousarray(np.asarray(ids, dtype=np.int32).reshape(-1))
+        out = np.empty_like(ids)
+        _lib.call("du_decode_step", self._h, ids.ctypes.data_as(C.c_void_p), ids.size, out.ctypes.data_as(C.c_void_p))
+        return out
+
+    def decode_loop(self, ids, steps: int) -> np.ndarray:
+        ids = np.ascontiguousarray(np.asarray(ids, dtype=np.int32).reshape(-1))
+        out = np.empty((steps, ids.size), np.int32)
+        _lib.call("du_decode_loop", self._h, ids.ctypes.data_as(C.c_void_p), ids.size, steps,
+                  out.ctypes.data_as(C.c_void_p))
+        return out
+
+    def read_logits(self, batch: int = 1) -> np.ndarray:
+        out = np.empty((batch, self.config.vocab_size), np.float32)
+        _lib.call("du_read_logits", self._h, out.ctypes.data_as(C.c_void_p), batch)
+        return out
+
+    def Generate(self, input_ids, on_token: Optional[Callable[[int], None]] = None,
+                 max_new_tokens: int = 64, stop_tokens: Sequence[int] = ()) -> Iterator[int]:
+        """LLM.Generate (MiniCPM5.cs:133-172), greedy: prefill the prompt, then one
+        graph-replayed decode step per token.  Yields token ids (the reference yields
+        frames and reports text through a callback)."""
+        if self._busy:
+            raise RuntimeError("LLM is busy")   # LLM.cs:393-406
+        self._busy = True
+        try:
+            _, nxt = self.forward(np.asarray(input_ids, np.int32).reshape(1, -1), use_cache=True, want_logits=False)
+            tok = int(nxt[0])
+            for _ in range(max_new_tokens):
+                if on_token:
+                    on_token(tok)
+                yield tok
+                if tok in stop_tokens:
+                    break
+                tok = int(self.decode_step([tok])[0])
+        finally:
+            self._busy = False
+
+    def ResetCache(self):
+        _lib.call("du_reset_cache", self._h)
+
+    def cache_len(self, seq: int = 0) -> int:
+        v = C.c_int()
+        _lib.call("du_cache_len", self._h, seq, C.byref(v))
+        return v.value
+
+    def weight_bytes(self) -> int:
+        v = C.c_uint64()
+        _lib.call("du_model_weight_bytes", self._h, C.byref(v))
+        return v.value
+
+    def stream(self) -> int:
+        v = C.c_void_p()
+        _lib.call("du_model_stream", self._h, C.byref(v))
+        return v.value or 0
+
+    def Release(self):
+        """Idempotent (LLM.cs:654-655)."""
+        if getattr(self, "_h", None) is not None and self._h.value:
+            _lib.call("du_model_destroy", self._h)
+            self._h = C.c_void_p()
+
+    def __del__(self):
+        try:
+            self.Release()
+        except Exception:
+            pass
+
+
+class LLMRegistry:
+    """LLMRegistry.Create (LLMRegistry.cs:61-73) over the configurations above."""
+
+    @staticmethod
+    def Create(model_id: str, quant: LLMQuant = LLMQuant.INT8, kv_quant: KVQuant = KVQuant.FP16,
+               max_context_length: int = 8192, **kw) -> LlamaForCausalLM:
+        if model_id not in CONFIGS:
+            raise KeyError(f"unknown model id {model_id!r}; known: {sorted(CONFIGS)}")
+        return LlamaForCausalLM(CONFIGS[model_id], quant, kv_quant, max_context_length, **kw)

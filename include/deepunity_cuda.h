@@ -1,0 +1,202 @@
+/*
+ * deepunity_cuda.h -- C ABI of libdeepunity_cuda.so, the B200 (sm_100a)
+ * library behind DeepUnity's quantized llama decode path.
+ *
+ * Every call returns an int status: 0 = OK, otherwise a DU_E* code, with a
+ * message from du_last_error() (thread-local).  Opaque handles; the library
+ * owns all device memory it allocates, the caller owns host buffers.  One CUDA
+ * stream per model.  A handle is not re-entrant (the reference's Busy guard,
+ * LLM.cs:393-406, becomes DU_EBUSY); different handles are independent.
+ * Kernel-level entry points take device pointers and a cudaStream_t passed as
+ * void* (NULL = the legacy default stream).
+ *
+ * Reference paths are relative to the DeepUnity project root:
+ *   G3CS = Assets/Resources/ComputeShaders/Gemma3CS.compute
+ *   M5M  = Assets/DeepUnity/InferenceEngine/LLM/MiniCPM5/MiniCPM5Model.cs
+ *   M5W  = Assets/DeepUnity/InferenceEngine/LLM/MiniCPM5/MiniCPM5Weights.cs
+ *   M5C  = Assets/DeepUnity/InferenceEngine/LLM/MiniCPM5/MiniCPM5Cache.cs
+ *   LLMB = Assets/DeepUnity/InferenceEngine/LLM/Base/
+ *   IMP  = Assets/DeepUnity/InferenceEngine/import_params.py
+ */
+#ifndef DEEPUNITY_CUDA_H
+#define DEEPUNITY_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define DU_API __attribute__((visibility("default")))
+
+enum {
+    DU_OK = 0,
+    DU_EINVAL = 1,     /* bad argument (shape, id >= vocab, position >= capacity, ...) */
+    DU_ECUDA = 2,      /* CUDA runtime error */
+    DU_ENOMEM = 3,     /* device allocation failed */
+    DU_EBUSY = 4,      /* handle already inside a call (reference Busy guard) */
+    DU_ENCCL = 5,      /* NCCL error or collective timeout */
+    DU_ENOTFOUND = 6,  /* unknown tensor name */
+    DU_ESTATE = 7      /* call not valid in the current state */
+};
+
+/* Weight formats of IMP (LLMQuant, LLMB/LLM.cs:15-59). */
+enum { DU_QUANT_FP16 = 0, DU_QUANT_INT8 = 1, DU_QUANT_INT4 = 2 };
+/* Element types for kernel-level activations. */
+enum { DU_DTYPE_F32 = 0, DU_DTYPE_F16 = 1, DU_DTYPE_BF16 = 2 };
+
+/* Architecture + runtime configuration; replaces the static MiniCPM5Config
+ * constants (M5/MiniCPM5Config.cs:11-37) and the LLMQuant/KVQuant keywords. */
+typedef struct du_model_config {
+    int32_t hidden_size;
+    int32_t intermediate_size;
+    int32_t num_layers;
+    int32_t num_heads_q;
+    int32_t num_heads_kv;
+    int32_t head_dim;
+    int32_t vocab_size;
+    float rms_eps;
+    float rope_theta;
+    float embed_scale;       /* 1.0 for llama (M5M:588) */
+    int32_t quant;           /* DU_QUANT_* for the block linears */
+    int32_t group_size;      /* INT4 group: 32 = reference Q4_0 (IMP:78), 128 = baseline */
+    int32_t kv_capacity;     /* tokens per sequence (M5C ctor) */
+    int32_t max_batch;       /* sequences decoded together */
+    int32_t tp_rank;         /* tensor-parallel rank / size (1 = single GPU) */
+    int32_t tp_size;
+    int32_t tie_embedding;   /* 1: lm_head = embedding */
+    int32_t reserved[5];
+} du_model_config;
+
+typedef struct du_model du_model;
+
+/* ---------------------------------------------------------------- runtime */
+
+/* Message for the last failing call on this thread. */
+DU_API const char *du_last_error(void);
+/* Library version string. */
+DU_API const char *du_version(void);
+/* Selects and initialises a device; replaces the shader-asset lookup
+ * DeepUnityMeta.Gemma3CS (Assets/DeepUnity/Main/DeepUnityMeta.cs:25). */
+DU_API int du_init(int device_ordinal);
+
+/* ------------------------------------------------------------------ model */
+
+/* Allocates weights, KV cache and scratch for one model (MiniCPM5Model ctor,
+ * M5M:79-118, + MiniCPM5Cache ctor, M5C:34-72).  RoPE tables are built on the
+ * host with the reference formula (M5M:163-191) and uploaded. */
+DU_API int du_model_create(const du_model_config *cfg, du_model **out);
+
+/* Copies one tensor of an IMP export from host memory into the model, in the
+ * concatenated device layout of AddConcatW (M5W:139-191); with tp_size > 1
+ * only this rank's shard is kept.  Names follow IMP's file layout (IMP:40-60,
+ * 305-337): "norm.bin", "embed_tokens/part_<k>.bin", "lm_head/part_<k>.bin",
+ * "layer_<i>/input_layernorm.bin", "layer_<i>/post_attention_layernorm.bin",
+ * "layer_<i>/<self_attn_q_proj|..|mlp_down_proj>.<int8|int4>.bin",
+ * "layer_<i>/<...>.scales.bin", fp16 linears as "layer_<i>/<...>.bin".
+ * `bytes` must equal the file size.  Replaces MiniCPM5Weights' UploadPump
+ * (M5W:315-380). */
+DU_API int du_model_load_tensor(du_model *m, const char *name, const void *host, size_t bytes);
+
+/* Fills every weight with seeded synthetic values on the device: linears
+ * ~N(0, std) quantized with the IMP formulas, embedding / lm_head fp16
+ * ~N(0, std), norm gammas 1 (stored as gamma - 1 = 0, IMP:314-315).  No
+ * reference counterpart: stands in for a checkpoint when none exists. */
+DU_API int du_model_init_random(du_model *m, uint64_t seed, float std);
+
+/* Writes a 128-byte NCCL unique id (call on rank 0, share with the others). */
+DU_API int du_nccl_unique_id(void *out128);
+/* Joins a tensor-parallel group of cfg.tp_size ranks (no reference
+ * counterpart: the reference is single-GPU).  Non-blocking communicator
+ * polled against timeout_ms. */
+DU_API int du_tp_init(du_model *m, const void *nccl_unique_id, int timeout_ms);
+
+/* MiniCPM5Model.Forward(ids, useCache, lastPosOnly) (M5M:531-549): runs
+ * `seq_len` tokens of each of `batch` sequences (ids [batch, seq_len], host),
+ * appending to the KV cache when use_cache != 0.  logits_out (host, may be
+ * NULL): [batch, V] if last_pos_only else [batch, seq_len, V]; with TP each
+ * rank receives the full vocab.  next_ids_out (host, may be NULL): greedy
+ * argmax of the last position per sequence (ArgMax, G3CS:911-928). */
+DU_API int du_forward(du_model *m, const int32_t *ids, int batch, int seq_len, int use_cache,
+                      int last_pos_only, float *logits_out, int32_t *next_ids_out);
+
+/* One greedy decode step for `batch` sequences (LLM.Generate inner loop:
+ * M5/MiniCPM5.cs:152-166 -> ForwardYielding + SampleYielding, M5M:551-585,
+ * 690-705): ids [batch] host in, next_ids [batch] host out.  The step is a
+ * CUDA graph replay; the first call per batch size captures it. */
+DU_API int du_decode_step(du_model *m, const int32_t *ids, int batch, int32_t *next_ids);
+
+/* Device-resident greedy loop: n_steps decode steps, each feeding its argmax
+ * into the next, without host round trips; tokens_out (host) [n_steps, batch].
+ * ids (host) [batch] seeds the first step. */
+DU_API int du_decode_loop(du_model *m, const int32_t *ids, int batch, int n_steps,
+                          int32_t *tokens_out);
+
+/* Logits of the last forward / decode step: [batch, V] fp32 (host). */
+DU_API int du_read_logits(du_model *m, float *host_out, int batch);
+
+/* MiniCPM5Model.ResetCache (M5M:714) / CachedTokenCount (M5C:16-22). */
+DU_API int du_reset_cache(du_model *m);
+DU_API int du_cache_len(du_model *m, int seq, int *out);
+/* Model stream (cudaStream_t) for callers that chain their own work. */
+DU_API int du_model_stream(du_model *m, void **stream_out);
+/* Bytes of weights resident on this rank (for roofline accounting). */
+DU_API int du_model_weight_bytes(du_model *m, uint64_t *out);
+/* Idempotent release (LLM.Release, LLMB/LLM.cs:654-655). */
+DU_API int du_model_destroy(du_model *m);
+
+/* Measurement hooks (the role of the reference's StageProfile,
+ * LLM/Gemma3/Gemma3Model.cs:593-622, without its per-stage readbacks).
+ * du_model_graph_info: kernel nodes / all nodes of the decode-step graph for
+ * `batch` (captured on first use).  du_model_kernel_times: replays each of the
+ * per-layer stages (0 QKV, 1 attention, 2 O proj, 3 gate|up, 4 down, 5 lm_head)
+ * over every layer `reps` times on the model stream, timed with CUDA events;
+ * ms_out[6] = average milliseconds per launch.  Valid after a prefill; it
+ * rewrites the KV slot of the next position, which the next decode step
+ * overwrites anyway. */
+DU_API int du_model_graph_info(du_model *m, int batch, int *kernel_nodes, int *total_nodes);
+DU_API int du_model_kernel_times(du_model *m, int batch, int reps, float *ms_out);
+
+/* ------------------------------------------------ kernel-level entry points
+ * Used by tests/benchmarks and by the secondary dispatch sites
+ * (Dense.Predict's Device.GPU branch, Modules/Learnable/Dense.cs:88-132).
+ * All pointers are device pointers. */
+
+/* y[M, N] fp32 = x[M, K] (x_dtype) . W^T with W int8 [N, K] (row-major bytes,
+ * IMP:229-233) and per-row scales (scale_dtype F16 as exported, or F32), the
+ * scale applied once after the dot (QKVProj1VecCoal etc., G3CS:1217-1282). */
+DU_API int du_gemv_q8(float *y, const void *x, int x_dtype, const int8_t *w, const void *scales,
+                      int scale_dtype, int M, int N, int K, void *stream);
+/* Same for INT4: packed nibbles [N, K/2] (low nibble = even column) and fp16
+ * group scales [N, K/group] (IMP:236-248; readQ4, G3CS:84-101). */
+DU_API int du_gemv_q4(float *y, const void *x, int x_dtype, const uint8_t *w,
+                      const uint16_t *scales_f16, int group, int M, int N, int K, void *stream);
+/* fp16 weights [N, K] (LmHeadPredict1VecCoal, G3CS:1284-1302). */
+DU_API int du_gemv_f16(float *y, const void *x, int x_dtype, const uint16_t *w, int M, int N, int K,
+                       void *stream);
+
+/* Split-K flash-decode (FlashAttention, G3CS:643-753) for one new query per
+ * sequence: q fp32 [batch, hq, hd] (already roped, unscaled); caches fp16
+ * [batch, capacity, hkv, hd] (position-major as KVCache.hlsl); kv_len int32
+ * [batch] device; out fp32 [batch, hq, hd].  scale = 1/sqrt(hd) in the ref. */
+DU_API int du_flash_decode(float *out, const float *q, const uint16_t *k_cache,
+                           const uint16_t *v_cache, const int32_t *kv_len, int batch, int hq,
+                           int hkv, int hd, int capacity, float scale, void *stream);
+
+/* IMP quantizers on the device, bit-exact with quantize_int8 / quantize_int4
+ * (IMP:229-248); group is a parameter (reference G4 = 32). */
+DU_API int du_quantize_int8(const float *w, int64_t rows, int64_t cols, int8_t *q,
+                            uint16_t *scales_f16, void *stream);
+DU_API int du_quantize_int4(const float *w, int64_t rows, int64_t cols, int group,
+                            uint8_t *packed, uint16_t *scales_f16, void *stream);
+
+/* RmsNormHidden (G3CS:204-223): y = x * rsqrt(mean(x^2) + eps) * (1 + gamma_m1). */
+DU_API int du_rmsnorm(float *y, const float *x, const uint16_t *gamma_m1, int rows, int H, float eps,
+                      void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* DEEPUNITY_CUDA_H */

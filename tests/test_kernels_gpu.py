@@ -1,0 +1,219 @@
+"""Kernel parity on the GPU, through the C ABI, against the CPU oracle.
+
+Tolerances (stated per test): integer work is bit-exact; fp32 outputs are
+compared as max|gpu - oracle| / max|oracle| (the norm-wise relative error; the
+north-star gate for layer outputs is 1e-3)."""
+import ctypes as C
+
+import numpy as np
+import pytest
+import torch
+
+from deepunity_b200 import _lib
+from oracle import oracle as orc
+
+pytestmark = pytest.mark.gpu
+
+GEMV_TOL = 1e-4     # max-abs error relative to max |y| for one GEMV
+ATTN_TOL = 1e-4
+
+
+@pytest.fixture(scope="module", autouse=True)
+def device():
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    _lib.call("du_init", 0)
+    torch.cuda.set_device(0)
+    yield
+
+
+def ptr(t: torch.Tensor):
+    return C.c_void_p(t.data_ptr())
+
+
+def dev(a: np.ndarray) -> torch.Tensor:
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+def relerr(a, b):
+    return float(np.max(np.abs(a - b)) / max(np.max(np.abs(b)), 1e-30))
+
+
+# ------------------------------------------------------------ quantizers
+@pytest.mark.parametrize("rows,cols", [(64, 256), (333, 1024), (4096, 4096)])
+def test_device_quantize_int8_bit_exact(rows, cols):
+    w = (np.random.default_rng(rows).standard_normal((rows, cols), dtype=np.float32) * 0.02)
+    w[0] = 0.0                                   # exercise the 1e-8 floor
+    q_ref, s_ref = orc.quantize_int8(w)
+    wd = dev(w)
+    q = torch.empty((rows, cols), dtype=torch.int8, device="cuda")
+    s = torch.empty(rows, dtype=torch.int16, device="cuda")
+    _lib.call("du_quantize_int8", ptr(wd), rows, cols, ptr(q), ptr(s), None)
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(q.cpu().numpy(), q_ref)
+    np.testing.assert_array_equal(s.cpu().numpy().view(np.uint16), s_ref)
+
+
+@pytest.mark.parametrize("group", [32, 128])
+@pytest.mark.parametrize("rows,cols", [(64, 256), (37, 1024), (4096, 4096)])
+def test_device_quantize_int4_bit_exact(rows, cols, group):
+    w = (np.random.default_rng(cols).standard_normal((rows, cols), dtype=np.float32) * 0.02)
+    w[1, :group] = 0.0                           # 1e-10 floor
+    w[2, 5] = 0.5; w[2, 9] = -0.5                # tie on |w|: first index wins
+    p_ref, d_ref = orc.quantize_int4(w, group)
+    wd = dev(w)
+    p = torch.empty((rows, cols // 2), dtype=torch.uint8, device="cuda")
+    d = torch.empty((rows, cols // group), dtype=torch.int16, device="cuda")
+    _lib.call("du_quantize_int4", ptr(wd), rows, cols, group, ptr(p), ptr(d), None)
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(p.cpu().numpy(), p_ref)
+    np.testing.assert_array_equal(d.cpu().numpy().view(np.uint16), d_ref)
+
+
+# ------------------------------------------------------------------ GEMV
+def _gemv(quant, x, wq, s, N, K, group=128, scale_f32=False):
+    M = x.shape[0]
+    y = torch.empty((M, N), dtype=torch.float32, device="cuda")
+    xd, wd = dev(x), dev(wq)
+    if quant == "int8":
+        sd = dev(s.view(np.float16).astype(np.float32) if scale_f32 else s)
+        _lib.call("du_gemv_q8", ptr(y), ptr(xd), _lib.DTYPE_F32, ptr(wd), ptr(sd),
+                  _lib.DTYPE_F32 if scale_f32 else _lib.DTYPE_F16, M, N, K, None)
+    elif quant == "int4":
+        _lib.call("du_gemv_q4", ptr(y), ptr(xd), _lib.DTYPE_F32, ptr(wd), ptr(dev(s)), group, M, N, K, None)
+    else:
+        _lib.call("du_gemv_f16", ptr(y), ptr(xd), _lib.DTYPE_F32, ptr(wd), M, N, K, None)
+    torch.cuda.synchronize()
+    return y.cpu().numpy()
+
+
+def test_config1_int8_linear():
+    """x [1,1024] ~N(0,1), W [1024,1024] ~N(0,0.02) -> int8 per-row, seed 0,
+    with fp16 scales (reference) and fp32 scales (baseline wording)."""
+    rng = np.random.default_rng(0)
+    x = rng.standard_normal((1, 1024)).astype(np.float32)
+    w = (rng.standard_normal((1024, 1024)) * 0.02).astype(np.float32)
+    q, s = orc.quantize_int8(w)
+    ref = orc.gemv(x, q, s, "int8", 1024)
+    for f32 in (False, True):
+        y = _gemv("int8", x, q, s, 1024, 1024, scale_f32=f32)
+        assert relerr(y, ref) < GEMV_TOL
+    # and against the fp32 dequantised matmul of the CPU Dense path
+    deq = orc.dequant(q, s, "int8", 1024, 1024)
+    dense = orc.dense_linear(x[0], deq)
+    assert relerr(y[0], dense) < GEMV_TOL
+
+
+SHAPES = [(4096, 4096), (14336, 4096), (4096, 14336), (2560, 2048), (2048, 5632)]
+
+
+@pytest.mark.parametrize("N,K", SHAPES)
+@pytest.mark.parametrize("quant,group", [("int8", 0), ("int4", 128), ("int4", 32)])
+@pytest.mark.parametrize("M", [1, 4])
+def test_gemv_matches_oracle(N, K, quant, group, M):
+    rng = np.random.default_rng(N + K + M)
+    w = (rng.standard_normal((N, K), dtype=np.float32) * 0.02)
+    x = rng.standard_normal((M, K), dtype=np.float32)
+    if quant == "int8":
+        wq, s = orc.quantize_int8(w)
+    else:
+        wq, s = orc.quantize_int4(w, group)
+    ref = orc.gemv(x, wq, s, quant, N, group or 32)
+    y = _gemv(quant, x, wq, s, N, K, group or 128)
+    assert relerr(y, ref) < GEMV_TOL
+
+
+@pytest.mark.parametrize("M", [1, 3, 8, 16])
+def test_gemv_batch_sizes_and_fp16(M):
+    rng = np.random.default_rng(M)
+    N, K = 1000, 4096                              # N not a multiple of the CTA row tile
+    w = (rng.standard_normal((N, K), dtype=np.float32) * 0.02)
+    x = rng.standard_normal((M, K), dtype=np.float32)
+    wh = w.astype(np.float16).view(np.uint16)
+    ref = orc.gemv(x, wh, None, "fp16", N)
+    assert relerr(_gemv("fp16", x, wh, None, N, K), ref) < GEMV_TOL
+    wq, s = orc.quantize_int4(w, 128)
+    ref = orc.gemv(x, wq, s, "int4", N, 128)
+    assert relerr(_gemv("int4", x, wq, s, N, K), ref) < GEMV_TOL
+
+
+def test_gemv_real_int8_export_rows():
+    """Rows of the reference's shipped int8 export (known-answer data)."""
+    import os
+    ex = np.load(os.path.join(os.path.dirname(__file__), "golden", "int8_export.npz"))
+    q, s = ex["q"], ex["s"]
+    N, K = q.shape
+    x = np.random.default_rng(5).standard_normal((1, K)).astype(np.float32)
+    ref = orc.gemv(x, q, s, "int8", N)
+    assert relerr(_gemv("int8", x, q, s, N, K), ref) < GEMV_TOL
+
+
+def test_gemv_bf16_activations():
+    rng = np.random.default_rng(11)
+    N, K = 4096, 4096
+    w = (rng.standard_normal((N, K), dtype=np.float32) * 0.02)
+    wq, s = orc.quantize_int4(w, 128)
+    xb = torch.randn((4, K), generator=torch.Generator().manual_seed(0)).to(torch.bfloat16)
+    ref = orc.gemv(xb.float().numpy(), wq, s, "int4", N, 128)
+    y = torch.empty((4, N), dtype=torch.float32, device="cuda")
+    xd = xb.cuda()
+    _lib.call("du_gemv_q4", ptr(y), ptr(xd), _lib.DTYPE_BF16, ptr(dev(wq)), ptr(dev(s)), 128, 4, N, K, None)
+    torch.cuda.synchronize()
+    assert relerr(y.cpu().numpy(), ref) < GEMV_TOL
+
+
+# ------------------------------------------------------------- attention
+@pytest.mark.parametrize("hq,hkv,hd", [(32, 8, 128), (32, 4, 64), (8, 8, 128), (16, 8, 64)])
+def test_flash_decode_matches_oracle(hq, hkv, hd):
+    rng = np.random.default_rng(hq * hd)
+    B, cap = 3, 700
+    lens = np.array([1, 129, 700], np.int32)
+    q = rng.standard_normal((B, hq, hd)).astype(np.float32)
+    kc = rng.standard_normal((B, cap, hkv, hd)).astype(np.float16)
+    vc = rng.standard_normal((B, cap, hkv, hd)).astype(np.float16)
+    scale = 1.0 / np.sqrt(hd)
+    out = torch.empty((B, hq, hd), dtype=torch.float32, device="cuda")
+    qd, kd, vd, ld = dev(q), dev(kc), dev(vc), dev(lens)
+    _lib.call("du_flash_decode", ptr(out), ptr(qd), ptr(kd), ptr(vd), ptr(ld), B, hq, hkv, hd, cap,
+              C.c_float(scale), None)
+    torch.cuda.synchronize()
+    got = out.cpu().numpy()
+    for b in range(B):
+        ref = orc.flash_attention(q[b:b + 1], kc[b].view(np.uint16), vc[b].view(np.uint16), int(lens[b]),
+                                  hq, hkv, hd, scale)[0]
+        assert relerr(got[b], ref) < ATTN_TOL, b
+    # second launch reuses the self-resetting split counters
+    _lib.call("du_flash_decode", ptr(out), ptr(qd), ptr(kd), ptr(vd), ptr(ld), B, hq, hkv, hd, cap,
+              C.c_float(scale), None)
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(out.cpu().numpy(), got)
+
+
+@pytest.mark.parametrize("ctx,B", [(512, 1), (2048, 8), (8192, 1), (32768, 1), (8192, 32)])
+def test_flash_decode_baseline_config3(ctx, B):
+    """BASELINE config 3 shapes (32 q / 8 kv heads, hd 128); the oracle checks two sequences."""
+    hq, hkv, hd = 32, 8, 128
+    g = torch.Generator(device="cuda").manual_seed(ctx + B)
+    q = torch.randn((B, hq, hd), device="cuda", generator=g)
+    kc = torch.randn((B, ctx, hkv, hd), device="cuda", generator=g).half()
+    vc = torch.randn((B, ctx, hkv, hd), device="cuda", generator=g).half()
+    lens = torch.full((B,), ctx, dtype=torch.int32, device="cuda")
+    out = torch.empty((B, hq, hd), dtype=torch.float32, device="cuda")
+    _lib.call("du_flash_decode", ptr(out), ptr(q), ptr(kc), ptr(vc), ptr(lens), B, hq, hkv, hd, ctx,
+              C.c_float(1.0 / np.sqrt(hd)), None)
+    torch.cuda.synchronize()
+    for b in sorted({0, B - 1}):
+        ref = orc.flash_attention(q[b:b + 1].cpu().numpy(), kc[b].cpu().numpy().view(np.uint16),
+                                  vc[b].cpu().numpy().view(np.uint16), ctx, hq, hkv, hd, 1.0 / np.sqrt(hd))[0]
+        assert relerr(out[b].cpu().numpy(), ref) < ATTN_TOL
+
+
+def test_rmsnorm_matches_oracle():
+    rng = np.random.default_rng(3)
+    x = rng.standard_normal((5, 4096)).astype(np.float32)
+    g = (rng.standard_normal(4096) * 0.1).astype(np.float16).view(np.uint16)
+    ref = orc.rmsnorm(x, g, 1e-5)
+    y = torch.empty((5, 4096), dtype=torch.float32, device="cuda")
+    _lib.call("du_rmsnorm", ptr(y), ptr(dev(x)), ptr(dev(g)), 5, 4096, C.c_float(1e-5), None)
+    torch.cuda.synchronize()
+    assert relerr(y.cpu().numpy(), ref) < 1e-6

@@ -1,0 +1,138 @@
+"""Whole-model parity on the GPU: the executor behind du_forward /
+du_decode_step / du_decode_loop against the oracle's restatement of
+MiniCPM5Model.Forward, on identical weights loaded from an IMP-format export.
+
+Gates (north star): layer/logit outputs within max relative error 1e-3
+(max|gpu - oracle| / max|oracle| over the logits), greedy token ids identical
+for 64 steps."""
+import numpy as np
+import pytest
+import torch
+
+from deepunity_b200 import DUError, LlamaForCausalLM, LLMQuant
+from oracle import oracle as orc
+from tests.modelgen import C4, MID, SMALL, ModelWeights, TestConfig
+
+pytestmark = pytest.mark.gpu
+LOGIT_TOL = 1e-3
+
+
+@pytest.fixture(scope="module", autouse=True)
+def device():
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    yield
+
+
+def relerr(a, b):
+    return float(np.max(np.abs(a - b)) / max(np.max(np.abs(b)), 1e-30))
+
+
+def build(cfg: TestConfig, seed=0, cap=128, max_batch=1):
+    w = ModelWeights(cfg, seed=seed)
+    q = {"int8": LLMQuant.INT8, "int4": LLMQuant.INT4, "fp16": LLMQuant.FP16}[cfg.quant]
+    m = LlamaForCausalLM(cfg.du_kwargs(), q, max_context_length=cap, max_batch=max_batch, seed=None)
+    w.load_into(m)
+    return w, m
+
+
+VARIANTS = [SMALL, MID,
+            TestConfig(256, 512, 2, 4, 2, 64, 1024, quant="int4", group=128),
+            TestConfig(512, 1024, 2, 4, 1, 128, 2048, quant="int4", group=32),
+            TestConfig(256, 512, 2, 4, 4, 64, 1024, quant="fp16")]
+
+
+@pytest.mark.parametrize("cfg", VARIANTS, ids=lambda c: f"{c.quant}-h{c.hidden}-hd{c.hd}-g{c.group}")
+def test_prefill_then_greedy_64_matches_oracle(cfg):
+    w, m = build(cfg, cap=128)
+    om = orc.OracleModel(w, capacity=128)
+    prompt = np.random.default_rng(7).integers(0, cfg.vocab, 16).astype(np.int32)
+    logits, nxt = m.forward(prompt[None, :])
+    ref = om.forward(prompt)
+    assert relerr(logits[0], ref) < LOGIT_TOL
+    assert int(nxt[0]) == orc.argmax(ref)
+    toks, rtoks = [int(nxt[0])], [orc.argmax(ref)]
+    for _ in range(63):
+        toks.append(int(m.decode_step([toks[-1]])[0]))
+        r = om.forward([rtoks[-1]])
+        rtoks.append(orc.argmax(r))
+    assert toks == rtoks
+    assert relerr(m.read_logits(1)[0], r) < LOGIT_TOL
+    assert m.cache_len() == 16 + 63
+    m.Release()
+    m.Release()   # idempotent
+
+
+def test_predict_all_positions_and_device_loop():
+    cfg = MID
+    w, m = build(cfg, cap=96)
+    om = orc.OracleModel(w, capacity=96)
+    prompt = np.random.default_rng(8).integers(0, cfg.vocab, 12).astype(np.int32)
+    lg = m.Predict(prompt)
+    ref = om.forward(prompt, last_pos_only=False)
+    assert lg.shape == ref.shape
+    assert relerr(lg, ref) < LOGIT_TOL
+    # device-resident greedy loop == step-by-step oracle
+    m.ResetCache()
+    om.reset()
+    _, nxt = m.forward(prompt[None, :])
+    toks = m.decode_loop([int(nxt[0])], 40)[:, 0].tolist()
+    r = om.forward(prompt)
+    rt = [orc.argmax(r)]
+    for _ in range(40):
+        rt.append(orc.argmax(om.forward([rt[-1]])))
+    assert [int(nxt[0])] + toks == rt
+    m.Release()
+
+
+def test_batched_sequences_match_independent_oracles():
+    cfg = SMALL
+    w, m = build(cfg, cap=96, max_batch=3)
+    prompts = np.random.default_rng(9).integers(0, cfg.vocab, (3, 10)).astype(np.int32)
+    logits, nxt = m.forward(prompts)
+    oms = [orc.OracleModel(w, capacity=96) for _ in range(3)]
+    refs = [om.forward(prompts[b]) for b, om in enumerate(oms)]
+    for b in range(3):
+        assert relerr(logits[b], refs[b]) < LOGIT_TOL
+    cur = nxt.copy()
+    rcur = [orc.argmax(r) for r in refs]
+    assert cur.tolist() == rcur
+    for _ in range(20):
+        cur = m.decode_step(cur)
+        rcur = [orc.argmax(om.forward([t])) for om, t in zip(oms, rcur)]
+        assert cur.tolist() == rcur
+    m.Release()
+
+
+def test_errors_are_reported_not_crashed():
+    cfg = SMALL
+    w, m = build(cfg, cap=20)
+    with pytest.raises(DUError):
+        m.forward(np.array([[cfg.vocab]], np.int32))          # id out of range
+    with pytest.raises(DUError):
+        m.forward(np.zeros((1, 21), np.int32))                # beyond capacity
+    with pytest.raises(DUError):
+        m.load_tensor("layer_0/self_attn_q_proj.int8.bin", np.zeros(7, np.uint8))   # wrong size
+    with pytest.raises(DUError):
+        m.load_tensor("layer_9/self_attn_q_proj.int8.bin", np.zeros(7, np.uint8))   # unknown layer
+    m.forward(np.zeros((1, 19), np.int32))
+    m.decode_step([1])
+    with pytest.raises(DUError):
+        m.decode_step([1])                                    # cache full
+    m.Release()
+
+
+def test_config4_llama_1p1b_int8_greedy_64():
+    """1.1B llama, INT8 per-row, 128-token random prompt, 64 greedy steps."""
+    w, m = build(C4, seed=0, cap=256)
+    om = orc.OracleModel(w, capacity=256)
+    prompt = np.random.default_rng(0).integers(0, C4.vocab, 128).astype(np.int32)
+    logits, nxt = m.forward(prompt[None, :])
+    ref = om.forward(prompt)
+    assert relerr(logits[0], ref) < LOGIT_TOL
+    toks = [int(nxt[0])] + m.decode_loop([int(nxt[0])], 63)[:, 0].tolist()
+    rt = [orc.argmax(ref)]
+    for _ in range(63):
+        rt.append(orc.argmax(om.forward([rt[-1]])))
+    assert toks == rt
+    m.Release()
