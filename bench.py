@@ -46,6 +46,8 @@ def parse():
     ap.add_argument("--prompt", type=int, default=PROMPT)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--layers", type=int, default=0,
+                    help="profiling only: keep the first N decoder layers (smaller device footprint)")
     return ap.parse_args()
 
 
@@ -183,6 +185,9 @@ def run_ours(args):
     if world > 1:
         dist.init_process_group("gloo", timeout=timedelta(seconds=600))
     cfg = CONFIGS[CONFIG]
+    if args.layers:
+        import dataclasses
+        cfg = dataclasses.replace(cfg, num_layers=args.layers)
     B = args.batch
     need = args.prompt + args.warmup + 2 * args.steps + 4
     m = LlamaForCausalLM(cfg, LLMQuant.INT4, max_context_length=max(CAPACITY, need), max_batch=B, seed=0,
@@ -281,7 +286,8 @@ def run_ours(args):
             "data": "synthetic (seeded random-init weights, random prompt ids)",
             "config": {"workload": f"llama-8b INT4-g128 decode, batch {B}, prompt {args.prompt}, "
                                    f"kv {args.prompt}..{args.prompt + args.warmup + args.steps}",
-                       "model": CONFIG, "global_batch": B, "seq_len": args.prompt,
+                       "model": CONFIG if not args.layers else f"{CONFIG} (first {args.layers} layers, profiling)",
+                       "global_batch": B, "seq_len": args.prompt,
                        "parallelism": f"tp{world}", "l2": "no flush: ~4.8 GB streamed per step >> 126 MB L2"},
             "roofline": {"bound": "hbm", "kernel": "gate|up INT4 GEMV (RMSNorm prologue, SiLU epilogue)",
                          "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",

@@ -24,6 +24,7 @@ namespace du {
 constexpr int FD_THREADS = 128;
 constexpr int FD_TILE = 64;
 constexpr float FD_NEG = -3.0e38f;
+constexpr int FD_MAXSPLIT = 128;          // gridDim.x upper bound (combine weights live in smem)
 
 struct FdParams {
     const float *q;              // [nq][hq][HD] fp32 (roped, unscaled)
@@ -61,17 +62,22 @@ __global__ void __launch_bounds__(FD_THREADS) flash_decode_kernel(const FdParams
     __shared__ __align__(16) float qs[G][HD];
     __shared__ float ps[FD_TILE][G];                  // scores, then probabilities
     __shared__ float s_m[G], s_l[G], s_alpha[G];
+    __shared__ float s_w[G][FD_MAXSPLIT], s_inv[G];
     __shared__ unsigned s_last;
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int split = blockIdx.x, kvh = blockIdx.y, row = blockIdx.z;
+    pdl_wait();      // q (and this step's K/V row) come from the previous kernel
+    pdl_trigger();
     const int nsplit = gridDim.x;
     const int seq = p.seq_of ? p.seq_of[row] : row;
     const int kv_len = p.kv_len[row] + p.kv_len_add;
-    int chunk = (kv_len + nsplit - 1) / nsplit;
+    // splits actually used for this length: at least one tile each
+    const int ns_act = max(1, min(nsplit, (kv_len + FD_TILE - 1) / FD_TILE));
+    int chunk = (kv_len + ns_act - 1) / ns_act;
     chunk = (chunk + FD_TILE - 1) & ~(FD_TILE - 1);
     const int start = split * chunk;
-    const int end = min(start + chunk, kv_len);
+    const int end = split < ns_act ? min(start + chunk, kv_len) : start;
     const int ntiles = end > start ? (end - start + FD_TILE - 1) / FD_TILE : 0;
 
     const size_t pos_stride = (size_t)p.hkv * HD;    // halves between consecutive positions
@@ -226,21 +232,33 @@ __global__ void __launch_bounds__(FD_THREADS) flash_decode_kernel(const FdParams
     if (!s_last) return;
     __threadfence();
 
-    // ---- last CTA: log-sum-exp combine over the splits, fixed order
+    // ---- last CTA: log-sum-exp combine over the active splits, fixed order.
+    // One warp per head computes M = max m_s, the weights w_s = exp(m_s - M)
+    // and 1 / sum(l_s w_s) into smem; then every output element is an
+    // independent weighted sum over the splits.
     const float *pmb = p.part_ml + rk * nsplit * G * 2;
     const float *pob = p.part_o + rk * nsplit * G * HD;
+    for (int g = warp; g < G; g += FD_THREADS / 32) {
+        float M = FD_NEG;
+        for (int s = lane; s < ns_act; s += 32) M = fmaxf(M, __ldcg(&pmb[(s * G + g) * 2]));
+        M = warp_max(M);
+        float L = 0.0f;
+        for (int s = lane; s < ns_act; s += 32) {
+            const float w = expf(__ldcg(&pmb[(s * G + g) * 2]) - M);
+            s_w[g][s] = w;
+            L = fmaf(__ldcg(&pmb[(s * G + g) * 2 + 1]), w, L);
+        }
+        L = warp_sum(L);
+        if (lane == 0) s_inv[g] = 1.0f / fmaxf(L, 1e-12f);
+    }
+    __syncthreads();
     for (int i = tid; i < G * HD; i += FD_THREADS) {
         const int g = i / HD, d = i - g * HD;
-        float M = FD_NEG;
-        for (int s = 0; s < nsplit; s++) M = fmaxf(M, __ldcg(&pmb[(s * G + g) * 2]));
-        float L = 0.0f, O = 0.0f;
-        for (int s = 0; s < nsplit; s++) {
-            const float ms = __ldcg(&pmb[(s * G + g) * 2]);
-            const float w = expf(ms - M);
-            L = fmaf(__ldcg(&pmb[(s * G + g) * 2 + 1]), w, L);
-            O = fmaf(__ldcg(&pob[(size_t)s * G * HD + g * HD + d]), w, O);
-        }
-        p.out[((size_t)row * p.hq + kvh * G + g) * HD + d] = O / fmaxf(L, 1e-12f);
+        const float *po_gd = pob + g * HD + d;
+        float O = 0.0f;
+#pragma unroll 4
+        for (int s = 0; s < ns_act; s++) O = fmaf(__ldcg(po_gd + (size_t)s * G * HD), s_w[g][s], O);
+        p.out[((size_t)row * p.hq + kvh * G + g) * HD + d] = O * s_inv[g];
     }
     if (tid == 0) p.counters[rk] = 0u;   // ready for the next launch / graph replay
 }
@@ -258,8 +276,17 @@ static int fd_launch(const FdParams &p, int nsplit, int nq, cudaStream_t st)
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
         attr_set[dev & 63] = true;
     }
-    flash_decode_kernel<HD, G><<<grid, FD_THREADS, smem, st>>>(p);
-    DU_CUDA_TRY(cudaGetLastError());
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = dim3(FD_THREADS);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl_enabled() ? 1 : 0;
+    DU_CUDA_TRY(cudaLaunchKernelEx(&cfg, flash_decode_kernel<HD, G>, p));
     return DU_OK;
 }
 
@@ -269,7 +296,7 @@ int fd_choose_splits(int nq, int hkv, int max_kv)
     int ns = (target + nq * hkv - 1) / (nq * hkv);
     const int max_by_len = (max_kv + FD_TILE - 1) / FD_TILE;
     if (ns > max_by_len) ns = max_by_len;
-    if (ns > 128) ns = 128;
+    if (ns > FD_MAXSPLIT) ns = FD_MAXSPLIT;
     if (ns < 1) ns = 1;
     return ns;
 }

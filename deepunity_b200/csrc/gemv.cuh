@@ -8,20 +8,27 @@
 // partials, G3CS:911-928).
 //
 // Design (B200, HBM-bound at M = 1):
-//  * 256-thread CTA = 4 K-split warps x 2 row groups; each warp owns 4 rows
-//    per pass and streams 512 contiguous weight bytes per row per step with
-//    one 128-bit L1-bypassing load per lane; the next step's loads are in
-//    flight while the current step computes.
+//  * The grid is 2 CTAs per SM; each CTA owns a contiguous range of row
+//    groups (RW = 4 rows at M <= 2, else 2) so every SM streams the same
+//    number of bytes.  Warps take the CTA's groups round-robin and never
+//    synchronise with each other after the prologue.
+//  * A warp streams a row group 512 bytes per row per step (one 128-bit
+//    L1-bypassing load per lane and row) through a 4-deep register ring: the
+//    loads of the next 3 steps are in flight while one step computes.  The
+//    first 3 steps are issued before griddepcontrol.wait, so under
+//    programmatic dependent launch the weight fetch overlaps the previous
+//    kernel's tail and this kernel's own activation prologue.
 //  * The activation vector is staged once per CTA in shared memory, already
 //    multiplied by a per-column power of two (bank-conflict-free swizzle).
 //    Each weight nibble / byte is then turned into an fp32 operand with ONE
 //    bitwise AND: a masked nibble (or byte, xor 0x80 so it is unsigned) read
 //    as a float is the exact subnormal n * 2^(p - 149), p = its bit position,
-//    so x' * that = x * n * 2^-50 exactly-rounded in one FFMA.  The zero
-//    points (8 for INT4, 128 for INT8) come back out through per-chunk /
-//    per-token sums of x.  Cost: ~1.1 integer op + 1 FFMA per weight.
-//  * Partial sums are folded with a shuffle reduce-scatter (4 rows in 6
-//    shuffles instead of 20), then across the 4 K-warps through smem.
+//    so x' * that = x * n * 2^-50, rounded once, with two columns per packed
+//    fma.rn.f32x2.  The zero points (8 for INT4, 128 for INT8) come back out
+//    through per-chunk / per-token sums of x.  Cost per INT4 weight: ~1.1
+//    integer op + 0.5 FFMA2.
+//  * Each finished row group is folded with warp shuffles and its epilogue is
+//    run by the owning lanes.
 #pragma once
 
 #include "common.cuh"
@@ -29,10 +36,6 @@
 namespace du {
 
 constexpr int GV_THREADS = 256;
-constexpr int GV_KW = 4;                  // warps that split K
-constexpr int GV_RG = 2;                  // row groups
-constexpr int GV_RW = 4;                  // rows per warp per pass
-constexpr int GV_PASS = GV_RG * GV_RW;    // logical rows per pass
 constexpr float GV_TWO50 = 1125899906842624.0f;   // 2^50
 
 enum GemvMap { MAP_IDENT = 0, MAP_ROPE_PAIR = 1, MAP_GATEUP = 2 };
@@ -52,7 +55,7 @@ struct GemvParams {
     int K, N, M, group;
     int map, map_hd, map_I;
     int64_t row_off;        // added to the mapped physical row
-    int rows_per_cta;       // logical rows per CTA (even)
+    int grid;               // CTAs (0 = 2 per SM); also the number of argmax partials
     // epilogue
     int epi;
     float *y;
@@ -76,6 +79,9 @@ template <int QT> struct GvTraits;
 template <> struct GvTraits<Q_I4> { static constexpr int COLS = 32, F4 = 8; };   // cols per 16 B chunk
 template <> struct GvTraits<Q_I8> { static constexpr int COLS = 16, F4 = 4; };
 template <> struct GvTraits<Q_F16> { static constexpr int COLS = 8, F4 = 2; };
+
+// 2^e as an exact fp32 constant, e in [-126, 127]
+__device__ __forceinline__ float gv_pow2(int e) { return __int_as_float((127 + e) << 23); }
 
 // power-of-two exponent applied to x at column position k (see header note)
 template <int QT>
@@ -113,93 +119,43 @@ __device__ __forceinline__ int64_t gv_map_row(const GemvParams &p, int lr)
     return r + p.row_off;
 }
 
+// acc += a * b on two fp32 lanes with one packed FFMA2 (sm_100 fma.rn.f32x2)
+__device__ __forceinline__ void ffma2(float2 &acc, float a0, float a1, float b0, float b1)
+{
+    asm("{\n\t.reg .b64 ra, rb, rc;\n\t"
+        "mov.b64 ra, {%2, %3};\n\t"
+        "mov.b64 rb, {%4, %5};\n\t"
+        "mov.b64 rc, {%0, %1};\n\t"
+        "fma.rn.f32x2 rc, ra, rb, rc;\n\t"
+        "mov.b64 {%0, %1}, rc;\n\t}"
+        : "+f"(acc.x), "+f"(acc.y)
+        : "f"(a0), "f"(a1), "f"(b0), "f"(b1));
+}
+
 // 8 INT4 weights (one 32-bit word, nibble j = column k0 + j) against x'[0..7]
-__device__ __forceinline__ float gv_dot_i4(uint32_t w, float4 a, float4 b, float acc)
+__device__ __forceinline__ void gv_dot_i4(uint32_t w, float4 a, float4 b, float2 &acc)
 {
     const uint32_t w12 = w >> 12;
-    acc = fmaf(__uint_as_float(w & 0x0000000Fu), a.x, acc);
-    acc = fmaf(__uint_as_float(w & 0x000000F0u), a.y, acc);
-    acc = fmaf(__uint_as_float(w & 0x00000F00u), a.z, acc);
-    acc = fmaf(__uint_as_float(w & 0x0000F000u), a.w, acc);
-    acc = fmaf(__uint_as_float(w & 0x000F0000u), b.x, acc);
-    acc = fmaf(__uint_as_float(w12 & 0x00000F00u), b.y, acc);
-    acc = fmaf(__uint_as_float(w12 & 0x0000F000u), b.z, acc);
-    acc = fmaf(__uint_as_float(w12 & 0x000F0000u), b.w, acc);
-    return acc;
+    ffma2(acc, __uint_as_float(w & 0x0000000Fu), __uint_as_float(w & 0x000000F0u), a.x, a.y);
+    ffma2(acc, __uint_as_float(w & 0x00000F00u), __uint_as_float(w & 0x0000F000u), a.z, a.w);
+    ffma2(acc, __uint_as_float(w & 0x000F0000u), __uint_as_float(w12 & 0x00000F00u), b.x, b.y);
+    ffma2(acc, __uint_as_float(w12 & 0x0000F000u), __uint_as_float(w12 & 0x000F0000u), b.z, b.w);
 }
 
 // 4 INT8 weights (byte j = column k0 + j), offset to unsigned (q + 128)
-__device__ __forceinline__ float gv_dot_i8(uint32_t w, float4 a, float acc)
+__device__ __forceinline__ void gv_dot_i8(uint32_t w, float4 a, float2 &acc)
 {
     const uint32_t u = w ^ 0x80808080u;
     const uint32_t u16 = u >> 16;
-    acc = fmaf(__uint_as_float(u & 0x000000FFu), a.x, acc);
-    acc = fmaf(__uint_as_float(u & 0x0000FF00u), a.y, acc);
-    acc = fmaf(__uint_as_float(u16 & 0x000000FFu), a.z, acc);
-    acc = fmaf(__uint_as_float(u16 & 0x0000FF00u), a.w, acc);
-    return acc;
+    ffma2(acc, __uint_as_float(u & 0x000000FFu), __uint_as_float(u & 0x0000FF00u), a.x, a.y);
+    ffma2(acc, __uint_as_float(u16 & 0x000000FFu), __uint_as_float(u16 & 0x0000FF00u), a.z, a.w);
 }
 
-__device__ __forceinline__ float gv_dot_f16(uint32_t w, float a, float b, float acc)
+__device__ __forceinline__ void gv_dot_f16(uint32_t w, float a, float b, float2 &acc)
 {
     __half2 h = *reinterpret_cast<__half2 *>(&w);
-    float2 f = __half22float2(h);
-    acc = fmaf(f.x, a, acc);
-    acc = fmaf(f.y, b, acc);
-    return acc;
-}
-
-// Reduce-scatter of V values over the 32 lanes: afterwards lane l holds the
-// full sum of value index (l >> (5 - log2 V)) in v[0].
-template <int V>
-__device__ __forceinline__ float gv_reduce_scatter(float (&v)[V], int lane)
-{
-    if constexpr (V == 1) {
-        return warp_sum(v[0]);
-    } else {
-        constexpr int H = V / 2;
-        constexpr int OFF = 16 >> 0;
-        float nv[H];
-        const bool up = lane & OFF;
-#pragma unroll
-        for (int i = 0; i < H; i++) {
-            float send = up ? v[i] : v[i + H];
-            float keep = up ? v[i + H] : v[i];
-            nv[i] = keep + __shfl_xor_sync(0xffffffffu, send, OFF);
-        }
-        // continue with V/2 values and offsets 8, 4, ...
-        if constexpr (H == 1) {
-            float r = nv[0];
-#pragma unroll
-            for (int o = 8; o > 0; o >>= 1) r += __shfl_xor_sync(0xffffffffu, r, o);
-            return r;
-        } else {
-            // second level (offset 8)
-            constexpr int H2 = H / 2;
-            float n2[H2 > 0 ? H2 : 1];
-            const bool up2 = lane & 8;
-#pragma unroll
-            for (int i = 0; i < H2; i++) {
-                float send = up2 ? nv[i] : nv[i + H2];
-                float keep = up2 ? nv[i + H2] : nv[i];
-                n2[i] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
-            }
-            static_assert(H2 == 1, "reduce-scatter implemented for V <= 4");
-            float r = n2[0];
-#pragma unroll
-            for (int o = 4; o > 0; o >>= 1) r += __shfl_xor_sync(0xffffffffu, r, o);
-            return r;
-        }
-    }
-}
-
-// value index that lane l holds after gv_reduce_scatter<V>
-template <int V>
-__device__ __forceinline__ int gv_rs_index(int lane)
-{
-    if constexpr (V == 1) return 0;
-    else if constexpr (V == 2) return (lane >> 4) & 1;
-    else return ((lane >> 4) & 1) * 2 + ((lane >> 3) & 1);
+    const float2 f = __half22float2(h);
+    ffma2(acc, f.x, f.y, a, b);
 }
 
 }  // namespace du

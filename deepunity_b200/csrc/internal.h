@@ -13,6 +13,9 @@ int num_sms();
 // gemv.cu
 int launch_gemv(int qt, GemvParams p, cudaStream_t st);
 size_t gemv_smem_bytes(int qt, int mt, int64_t row_bytes);
+int gemv_grid_for(int N, int M, int want);
+void gemv_set_pdl(bool on);
+bool pdl_enabled();
 
 // attention.cu
 int fd_choose_splits(int nq, int hkv, int max_kv);

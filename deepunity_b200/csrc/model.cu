@@ -556,30 +556,22 @@ static int enqueue_head(du_model *m, const StepIO &io)
     cudaStream_t st = m->stream;
     int rc = DU_OK;
     const int R = io.logits_rows;
-    const float *xsel = m->x_res;
-    if (io.logit_stride != 1 || io.logit_first != 0) {
-        // gather the selected rows (last token of each sequence) into part[0..R)
-        for (int i = 0; i < R; i++)
-            DU_CUDA_TRY(cudaMemcpyAsync(m->part + (size_t)i * H,
-                                        m->x_res + (size_t)(io.logit_first + i * io.logit_stride) * H,
-                                        sizeof(float) * H, cudaMemcpyDeviceToDevice, st));
-        xsel = m->part;
-    }
+    // the selected rows (every token, or the last token of each sequence) are read
+    // in place: row i of the head input is x_res[logit_first + i * logit_stride]
     GemvParams p = gp_base(m, (const uint8_t *)m->lm_head, nullptr, H);
     p.row_bytes = 2LL * H;
-    p.x = xsel; p.ldx = H; p.gamma = m->final_norm; p.eps = m->cfg.rms_eps;
+    p.x = m->x_res + (size_t)io.logit_first * H;
+    p.ldx = H * io.logit_stride;
+    p.gamma = m->final_norm; p.eps = m->cfg.rms_eps;
     p.N = m->V_l; p.map = MAP_IDENT; p.epi = EPI_LOGITS;
     p.logits = m->logits; p.ldl = m->V_l; p.vocab_off = m->rank * m->V_l;
-    const int rpc_target = m->am_parts;
-    int rpc = (p.N + rpc_target - 1) / rpc_target;
-    rpc = (rpc + 1) & ~1;
-    p.rows_per_cta = rpc;
-    const int nparts = (p.N + rpc - 1) / rpc;
+    const int nparts = gemv_grid_for(p.N, 1, m->am_parts);   // same CTA count for every token tile
+    p.grid = nparts;
     const int mt = gemv_max_tokens(Q_F16, p.row_bytes);
     for (int t0 = 0; t0 < R; t0 += mt) {
         GemvParams c = p;
         c.M = R - t0 < mt ? R - t0 : mt;
-        c.x = p.x + (size_t)t0 * H;
+        c.x = p.x + (size_t)t0 * p.ldx;
         c.logits = p.logits + (size_t)t0 * p.ldl;
         c.am_val = m->am_val + (size_t)t0 * nparts;
         c.am_idx = m->am_idx + (size_t)t0 * nparts;

@@ -80,7 +80,8 @@ def _gemv(quant, x, wq, s, N, K, group=128, scale_f32=False):
         _lib.call("du_gemv_q8", ptr(y), ptr(xd), _lib.DTYPE_F32, ptr(wd), ptr(sd),
                   _lib.DTYPE_F32 if scale_f32 else _lib.DTYPE_F16, M, N, K, None)
     elif quant == "int4":
-        _lib.call("du_gemv_q4", ptr(y), ptr(xd), _lib.DTYPE_F32, ptr(wd), ptr(dev(s)), group, M, N, K, None)
+        sd = dev(s)
+        _lib.call("du_gemv_q4", ptr(y), ptr(xd), _lib.DTYPE_F32, ptr(wd), ptr(sd), group, M, N, K, None)
     else:
         _lib.call("du_gemv_f16", ptr(y), ptr(xd), _lib.DTYPE_F32, ptr(wd), M, N, K, None)
     torch.cuda.synchronize()
@@ -156,8 +157,8 @@ def test_gemv_bf16_activations():
     xb = torch.randn((4, K), generator=torch.Generator().manual_seed(0)).to(torch.bfloat16)
     ref = orc.gemv(xb.float().numpy(), wq, s, "int4", N, 128)
     y = torch.empty((4, N), dtype=torch.float32, device="cuda")
-    xd = xb.cuda()
-    _lib.call("du_gemv_q4", ptr(y), ptr(xd), _lib.DTYPE_BF16, ptr(dev(wq)), ptr(dev(s)), 128, 4, N, K, None)
+    xd, wd, sd = xb.cuda(), dev(wq), dev(s)
+    _lib.call("du_gemv_q4", ptr(y), ptr(xd), _lib.DTYPE_BF16, ptr(wd), ptr(sd), 128, 4, N, K, None)
     torch.cuda.synchronize()
     assert relerr(y.cpu().numpy(), ref) < GEMV_TOL
 
@@ -214,6 +215,7 @@ def test_rmsnorm_matches_oracle():
     g = (rng.standard_normal(4096) * 0.1).astype(np.float16).view(np.uint16)
     ref = orc.rmsnorm(x, g, 1e-5)
     y = torch.empty((5, 4096), dtype=torch.float32, device="cuda")
-    _lib.call("du_rmsnorm", ptr(y), ptr(dev(x)), ptr(dev(g)), 5, 4096, C.c_float(1e-5), None)
+    xd, gd = dev(x), dev(g)          # keep the device copies alive until the kernel has run
+    _lib.call("du_rmsnorm", ptr(y), ptr(xd), ptr(gd), 5, 4096, C.c_float(1e-5), None)
     torch.cuda.synchronize()
     assert relerr(y.cpu().numpy(), ref) < 1e-6
