@@ -19,6 +19,7 @@ full token.
 from __future__ import annotations
 
 import argparse
+import contextlib
 import json
 import os
 import statistics
@@ -46,6 +47,7 @@ def parse():
     ap.add_argument("--prompt", type=int, default=PROMPT)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--clock-sampler", choices=["nvml", "smi", "none"], default="nvml")
     ap.add_argument("--layers", type=int, default=0,
                     help="profiling only: keep the first N decoder layers (smaller device footprint)")
     return ap.parse_args()
@@ -61,6 +63,63 @@ def peaks():
 
 
 # ------------------------------------------------------------------ clocks
+class NvmlClockSampler:
+    """SM clock and clock-event (throttle) reasons read through NVML from a host
+    thread every `period` seconds during the timed region (in-process: no
+    nvidia-smi process competing for the driver)."""
+
+    REASONS = {"hw_slowdown": "nvmlClocksEventReasonHwSlowdown",
+               "hw_thermal_slowdown": "nvmlClocksEventReasonHwThermalSlowdown",
+               "sw_thermal_slowdown": "nvmlClocksEventReasonSwThermalSlowdown",
+               "sw_power_cap": "nvmlClocksEventReasonSwPowerCap"}
+
+    def __init__(self, gpu: int, period: float = 0.05):
+        self.gpu, self.period = gpu, period
+        self.samples = []
+        self.max_mhz = None
+
+    def __enter__(self):
+        import threading
+        try:
+            import pynvml as N
+            N.nvmlInit()
+            self.N = N
+            self.h = N.nvmlDeviceGetHandleByIndex(self.gpu)
+            self.max_mhz = N.nvmlDeviceGetMaxClockInfo(self.h, N.NVML_CLOCK_SM)
+        except Exception:
+            self.N = None
+            return self
+        self.stop = threading.Event()
+
+        def run():
+            while not self.stop.is_set():
+                try:
+                    mhz = self.N.nvmlDeviceGetClockInfo(self.h, self.N.NVML_CLOCK_SM)
+                    r = self.N.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+                    self.samples.append((mhz, r))
+                except Exception:
+                    pass
+                self.stop.wait(self.period)
+
+        self.t = threading.Thread(target=run, daemon=True)
+        self.t.start()
+        time.sleep(self.period)
+        return self
+
+    def __exit__(self, *a):
+        if self.N is not None:
+            self.stop.set()
+            self.t.join(timeout=5)
+
+    def summary(self):
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": ["unsampled"]}
+        reasons = sorted({name for _, r in self.samples for name, attr in self.REASONS.items()
+                          if r & getattr(self.N, attr, 0)})
+        return {"sm_mhz": statistics.median(m for m, _ in self.samples), "sm_max_mhz": self.max_mhz,
+                "reasons": reasons, "samples": len(self.samples), "sampler": "nvml"}
+
+
 class ClockSampler:
     """nvidia-smi clocks / throttle reasons sampled every 200 ms during the timed region."""
     Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
@@ -225,7 +284,8 @@ def run_ours(args):
         return float(t.item())
 
     # ---- device-timed: K graph replays with the argmax fed back on the device
-    with ClockSampler(local) as clk:
+    sampler = {"nvml": NvmlClockSampler, "smi": ClockSampler}.get(args.clock_sampler)
+    with (sampler(local) if sampler else contextlib.nullcontext()) as clk:
         barrier()
         torch.cuda.synchronize()
         ev0.record(stream)
@@ -301,7 +361,7 @@ def run_ours(args):
             "e2e": {"value": round(e2e, 2), "unit": "tok/s", "h2d_bytes_per_step": 4 * B,
                     "d2h_bytes_per_step": 4 * B},
             "gpu_launches": int(kn.value) * args.steps,
-            "clocks": clk.summary(),
+            "clocks": clk.summary() if clk is not None else {"sm_mhz": None, "reasons": ["unsampled"]},
             "cpu_baseline": cpu,
         }
         print(json.dumps(line), flush=True)
