@@ -48,6 +48,8 @@ def parse():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--clock-sampler", choices=["nvml", "smi", "none"], default="nvml")
+    ap.add_argument("--sweep", choices=["gemv", "attn"], default=None,
+                    help="kernel sweeps (one JSON line per case): config-2 GEMV, config-3 flash-decode")
     ap.add_argument("--layers", type=int, default=0,
                     help="profiling only: keep the first N decoder layers (smaller device footprint)")
     return ap.parse_args()
@@ -372,8 +374,98 @@ def run_ours(args):
     return 0
 
 
+def _events_ms(fn, reps: int, stream=None):
+    import torch
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    s.record(stream)
+    for i in range(reps):
+        fn(i)
+    e.record(stream)
+    torch.cuda.synchronize()
+    return s.elapsed_time(e) / reps
+
+
+def run_sweep_gemv(args):
+    """quant-GEMV HBM GB/s vs peak through du_gemv_q4 / du_gemv_q8.
+    Distinct weight copies (>= 1 GB in total) rotate between launches so no launch
+    finds its weights in the 126 MB L2."""
+    import ctypes as C
+    import torch
+    from deepunity_b200 import _lib
+    torch.cuda.set_device(0)
+    _lib.call("du_init", 0)
+    peak, kind = peaks()
+    g = torch.Generator(device="cuda").manual_seed(0)
+    for quant in ("int4", "int8"):
+        for (N, K) in [(4096, 4096), (14336, 4096), (4096, 14336)]:
+            wbytes = N * K // 2 if quant == "int4" else N * K
+            sbytes = N * (K // 128) * 2 if quant == "int4" else N * 2
+            copies = max(2, int(np.ceil(1.1e9 / (wbytes + sbytes))))
+            W = torch.randint(0, 256, (copies, wbytes), dtype=torch.uint8, device="cuda", generator=g)
+            Sc = (torch.rand((copies, sbytes // 2), device="cuda", generator=g) * 1e-3).half()
+            for M in (1, 4, 16, 64, 512):
+                x = torch.randn((M, K), device="cuda", generator=g).bfloat16()
+                y = torch.empty((M, N), device="cuda")
+                if quant == "int4":
+                    f = lambda i: _lib.call("du_gemv_q4", C.c_void_p(y.data_ptr()), C.c_void_p(x.data_ptr()),
+                                            _lib.DTYPE_BF16, C.c_void_p(W[i % copies].data_ptr()),
+                                            C.c_void_p(Sc[i % copies].data_ptr()), 128, M, N, K, None)
+                else:
+                    f = lambda i: _lib.call("du_gemv_q8", C.c_void_p(y.data_ptr()), C.c_void_p(x.data_ptr()),
+                                            _lib.DTYPE_BF16, C.c_void_p(W[i % copies].data_ptr()),
+                                            C.c_void_p(Sc[i % copies].data_ptr()), _lib.DTYPE_F16, M, N, K, None)
+                reps = max(4, min(200, int(2e9 / ((wbytes + sbytes) * max(1, M // 8)))))
+                _events_ms(f, 3)
+                ms = _events_ms(f, reps)
+                byts = wbytes + sbytes + M * K * 2 + M * N * 4
+                gbs = byts / (ms / 1e3) / 1e9
+                print(json.dumps({"sweep": "gemv", "quant": quant + ("-g128" if quant == "int4" else "-row"),
+                                  "N": N, "K": K, "M": M, "us": round(ms * 1e3, 2), "GB_s": round(gbs, 1),
+                                  "frac_hbm": round(gbs / peak, 4), "TFLOP_s": round(2 * M * N * K / (ms / 1e3) / 1e12, 2),
+                                  "peak_kind": kind, "copies": copies}), flush=True)
+            del W, Sc
+
+
+def run_sweep_attn(args):
+    """split-K flash-decode over fp16 KV, 32 q / 8 kv heads, hd 128."""
+    import ctypes as C
+    import torch
+    from deepunity_b200 import _lib
+    torch.cuda.set_device(0)
+    _lib.call("du_init", 0)
+    peak, kind = peaks()
+    g = torch.Generator(device="cuda").manual_seed(0)
+    hq, hkv, hd = 32, 8, 128
+    for ctx in (512, 2048, 8192, 32768):
+        for B in (1, 8, 32):
+            kv_bytes = B * ctx * hkv * hd * 2 * 2
+            copies = max(2, int(np.ceil(0.6e9 / kv_bytes)))
+            if copies * kv_bytes > 40e9:
+                copies = 1
+            kc = [torch.randn((B, ctx, hkv, hd), device="cuda", generator=g).half() for _ in range(copies)]
+            vc = [torch.randn((B, ctx, hkv, hd), device="cuda", generator=g).half() for _ in range(copies)]
+            q = torch.randn((B, hq, hd), device="cuda", generator=g)
+            out = torch.empty((B, hq, hd), device="cuda")
+            lens = torch.full((B,), ctx, dtype=torch.int32, device="cuda")
+            f = lambda i: _lib.call("du_flash_decode", C.c_void_p(out.data_ptr()), C.c_void_p(q.data_ptr()),
+                                    C.c_void_p(kc[i % copies].data_ptr()), C.c_void_p(vc[i % copies].data_ptr()),
+                                    C.c_void_p(lens.data_ptr()), B, hq, hkv, hd, ctx, C.c_float(hd ** -0.5), None)
+            _events_ms(f, 3)
+            ms = _events_ms(f, 20)
+            gbs = kv_bytes / (ms / 1e3) / 1e9
+            print(json.dumps({"sweep": "flash_decode", "ctx": ctx, "batch": B, "us": round(ms * 1e3, 2),
+                              "GB_s": round(gbs, 1), "frac_hbm": round(gbs / peak, 4), "peak_kind": kind,
+                              "copies": copies}), flush=True)
+            del kc, vc
+
+
 def main():
     args = parse()
+    if args.sweep == "gemv":
+        return run_sweep_gemv(args)
+    if args.sweep == "attn":
+        return run_sweep_attn(args)
     if args.impl == "reference":
         return run_reference(args)
     return run_ours(args)

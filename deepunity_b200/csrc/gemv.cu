@@ -4,102 +4,147 @@
 
 namespace du {
 
-constexpr int GV_WARPS = GV_THREADS / 32;
+// FP16 path: physical float4 slot of logical float4 f of a token row
+// (conflict-free for the lane-chunk reads of the main loop).
+__device__ __forceinline__ int gv_swz16(int f) { return f ^ ((f >> 3) & 1); }
 
-// x' = x * 2^e(k), staged in smem (swizzled), plus the zero-point sums.
-template <int QT, int MT>
-__device__ __forceinline__ void gv_stage_x(const GemvParams &p, float4 *xs, float *xsum, int k4, int nchunk,
-                                           float (*s_stat)[GV_WARPS])
+// Block-wide sum / max of one float per thread (all threads must call).
+__device__ __forceinline__ float block_sum(float v, float *red)
 {
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    for (int m = 0; m < MT; m++) {
-        float inv = 1.0f;
-        if (p.gamma != nullptr && m < p.M) {
-            float ss = 0.0f;
-            const float4 *xr = reinterpret_cast<const float4 *>(p.x + (size_t)m * p.ldx);
-            for (int f = tid; f < k4; f += GV_THREADS) {
-                const float4 v = xr[f];
-                ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
-            }
-            ss = warp_sum(ss);
-            if (lane == 0) s_stat[m][warp] = ss;
-            __syncthreads();
-            float tot = 0.0f;
-#pragma unroll
-            for (int i = 0; i < GV_WARPS; i++) tot += s_stat[m][i];
-            inv = 1.0f / sqrtf(tot / (float)p.K + p.eps);
-            __syncthreads();
-        }
-        const float4 *xr = reinterpret_cast<const float4 *>(p.x + (size_t)m * p.ldx);
-        for (int f = tid; f < k4; f += GV_THREADS) {
-            float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-            if (m < p.M) {
-                v = xr[f];
-                if (p.gamma != nullptr) {
-                    const __half2 *g2 = reinterpret_cast<const __half2 *>(p.gamma) + 2 * f;
-                    const float2 g01 = __half22float2(g2[0]), g23 = __half22float2(g2[1]);
-                    v.x = v.x * inv * (1.0f + g01.x);
-                    v.y = v.y * inv * (1.0f + g01.y);
-                    v.z = v.z * inv * (1.0f + g23.x);
-                    v.w = v.w * inv * (1.0f + g23.y);
-                }
-            }
-            if (QT != Q_F16) {
-                const int k0 = 4 * f;
-                v.x *= gv_pow2(gv_xexp<QT>(k0));
-                v.y *= gv_pow2(gv_xexp<QT>(k0 + 1));
-                v.z *= gv_pow2(gv_xexp<QT>(k0 + 2));
-                v.w *= gv_pow2(gv_xexp<QT>(k0 + 3));
-            }
-            xs[(size_t)m * k4 + gv_swz<QT>(f)] = v;
-        }
-    }
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    v = warp_sum(v);
     __syncthreads();
-    if (QT == Q_I4) {
-        // 8 * sum of x over each 32-column chunk (unscaled back exactly)
-        for (int i = tid; i < MT * nchunk; i += GV_THREADS) {
-            const int m = i / nchunk, c = i - m * nchunk;
-            float s = 0.0f;
-#pragma unroll
-            for (int j = 0; j < 8; j++) {
-                const float4 v = xs[(size_t)m * k4 + gv_swz<QT>(c * 8 + j)];
-                const int k0 = 4 * j;   // column position within the 8-column word only matters mod 8
-                s += v.x * gv_pow2(-gv_xexp<QT>(k0)) + v.y * gv_pow2(-gv_xexp<QT>(k0 + 1)) +
-                     v.z * gv_pow2(-gv_xexp<QT>(k0 + 2)) + v.w * gv_pow2(-gv_xexp<QT>(k0 + 3));
-            }
-            xsum[i] = 8.0f * s;
-        }
-    } else if (QT == Q_I8) {
-        for (int m = 0; m < MT; m++) {
-            float s = 0.0f;
-            for (int f = tid; f < k4; f += GV_THREADS) {
-                const float4 v = xs[(size_t)m * k4 + gv_swz<QT>(f)];
-                s += v.x * gv_pow2(-99) + v.y * gv_pow2(-91) + v.z * gv_pow2(-99) + v.w * gv_pow2(-91);
-            }
-            s = warp_sum(s);
-            if (lane == 0) s_stat[m][warp] = s;
-        }
-        __syncthreads();
-        if (tid < MT) {
-            float t = 0.0f;
-            for (int i = 0; i < GV_WARPS; i++) t += s_stat[tid][i];
-            xsum[tid] = 128.0f * t;
-        }
-    }
+    if (lane == 0) red[warp] = v;
     __syncthreads();
+    float t = 0.0f;
+#pragma unroll
+    for (int i = 0; i < GV_WARPS; i++) t += red[i];
+    return t;
+}
+__device__ __forceinline__ float block_max(float v, float *red)
+{
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    v = warp_max(v);
+    __syncthreads();
+    if (lane == 0) red[warp] = v;
+    __syncthreads();
+    float t = red[0];
+#pragma unroll
+    for (int i = 1; i < GV_WARPS; i++) t = fmaxf(t, red[i]);
+    return t;
 }
 
-// Epilogue for one finished value pair / value.  v: full sums (scaled for INT4).
-template <int QT>
-__device__ __forceinline__ float gv_finish(const GemvParams &p, const float *xsum, int lr, int m, float v)
+// x_k (optionally RMSNorm'd: x * rms * (1 + gamma'_k)), computed identically
+// wherever it is needed
+__device__ __forceinline__ float gv_xval(const GemvParams &p, const float *xr, float inv, int k)
 {
-    if (QT == Q_I8) {
-        const int64_t pr = gv_map_row(p, lr);
-        const float sc = p.scale_f32 ? reinterpret_cast<const float *>(p.scales)[pr]
-                                     : __half2float(reinterpret_cast<const __half *>(p.scales)[pr]);
-        v = sc * fmaf(v, GV_TWO50, -xsum[m]);
-    }
+    float v = xr[k];
+    if (p.gamma != nullptr) v = v * inv * (1.0f + __half2float(p.gamma[k]));
     return v;
+}
+
+// Stages the activations of the MT tokens in shared memory.
+//  INT4 / INT8: 22-bit fixed-point byte planes + zero-point sums, per-token shift
+//  FP16: fp32, swizzled
+template <int QT, int MT>
+__device__ void gv_stage_x(const GemvParams &p, uint4 *xq, float *xsumf, long long *xsum64, float *xscale,
+                           int nchunk, float *red)
+{
+    const int tid = threadIdx.x;
+    for (int m = 0; m < MT; m++) {
+        const float *xr = p.x + (size_t)m * p.ldx;
+        const bool live = m < p.M;
+        float inv = 1.0f;
+        if (p.gamma != nullptr) {
+            float ss = 0.0f;
+            if (live)
+                for (int k = tid; k < p.K; k += GV_THREADS) ss += xr[k] * xr[k];
+            ss = block_sum(ss, red);
+            inv = 1.0f / sqrtf(ss / (float)p.K + p.eps);
+        }
+        if (QT == Q_F16) {
+            float4 *xs = reinterpret_cast<float4 *>(xq) + (size_t)m * nchunk * 2;
+            for (int f = tid; f < nchunk * 2; f += GV_THREADS) {
+                float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+                if (live) {
+                    v.x = gv_xval(p, xr, inv, 4 * f);
+                    v.y = gv_xval(p, xr, inv, 4 * f + 1);
+                    v.z = gv_xval(p, xr, inv, 4 * f + 2);
+                    v.w = gv_xval(p, xr, inv, 4 * f + 3);
+                }
+                xs[gv_swz16(f)] = v;
+            }
+            continue;
+        }
+        // per-token power-of-two scale: max |x| * 2^s < 2^22
+        float mx = 0.0f;
+        if (live)
+            for (int k = tid; k < p.K; k += GV_THREADS) mx = fmaxf(mx, fabsf(gv_xval(p, xr, inv, k)));
+        mx = block_max(mx, red);
+        const int s = mx > 0.0f ? 21 - ilogbf(mx) : 0;
+        const float sc = ldexpf(1.0f, s);
+        if (tid == 0) xscale[m] = ldexpf(1.0f, -s);
+        uint32_t *xw = reinterpret_cast<uint32_t *>(xq) + (size_t)m * nchunk * GvTraits<QT>::XU4 * 4;
+        if (QT == Q_I4) {
+            // word-group g = 8 columns; chunk c = g / 4, slot wd = g % 4; words
+            // [P0 even, P0 odd, P1 even, P1 odd, P2 even, P2 odd] (even = columns 0,2,4,6)
+            const int ngroups = nchunk * 4;
+            for (int g0 = 0; g0 < ngroups; g0 += GV_THREADS) {
+                const int g = g0 + tid;
+                int part = 0;
+                if (g < ngroups) {
+                    uint32_t pe[3] = {0, 0, 0}, po[3] = {0, 0, 0};
+#pragma unroll
+                    for (int j = 0; j < 8; j++) {
+                        const int v = live ? __float2int_rn(gv_xval(p, xr, inv, 8 * g + j) * sc) : 0;
+                        part += v;
+                        const int sh = 8 * (j >> 1);
+                        uint32_t *dst = (j & 1) ? po : pe;
+                        dst[0] |= (uint32_t)(v & 0xFF) << sh;
+                        dst[1] |= (uint32_t)((v >> 8) & 0xFF) << sh;
+                        dst[2] |= (uint32_t)((v >> 16) & 0xFF) << sh;
+                    }
+                    const int c = g >> 2, wd = g & 3;
+                    uint32_t *o = xw + (size_t)c * GvTraits<QT>::XU4 * 4 + wd * 6;
+                    o[0] = pe[0]; o[1] = po[0]; o[2] = pe[1]; o[3] = po[1]; o[4] = pe[2]; o[5] = po[2];
+                }
+                // chunk sum over the 4 word-groups held by 4 consecutive lanes
+                part += __shfl_xor_sync(0xffffffffu, part, 1);
+                part += __shfl_xor_sync(0xffffffffu, part, 2);
+                if (g < ngroups && (g & 3) == 0) xsumf[(size_t)m * nchunk + (g >> 2)] = 8.0f * (float)part;
+            }
+        } else {
+            // word-group g = 4 columns; chunk c = g / 4, slot wd = g % 4; words [P0, P1, P2]
+            const int ngroups = nchunk * 4;
+            long long tot = 0;
+            for (int g = tid; g < ngroups; g += GV_THREADS) {
+                uint32_t pw[3] = {0, 0, 0};
+#pragma unroll
+                for (int j = 0; j < 4; j++) {
+                    const int v = live ? __float2int_rn(gv_xval(p, xr, inv, 4 * g + j) * sc) : 0;
+                    tot += v;
+                    pw[0] |= (uint32_t)(v & 0xFF) << (8 * j);
+                    pw[1] |= (uint32_t)((v >> 8) & 0xFF) << (8 * j);
+                    pw[2] |= (uint32_t)((v >> 16) & 0xFF) << (8 * j);
+                }
+                const int c = g >> 2, wd = g & 3;
+                uint32_t *o = xw + (size_t)c * GvTraits<QT>::XU4 * 4 + wd * 3;
+                o[0] = pw[0]; o[1] = pw[1]; o[2] = pw[2];
+            }
+            // exact block sum of the int64 totals (two 32-bit halves through fp-free shuffles)
+            for (int o = 16; o > 0; o >>= 1) tot += __shfl_xor_sync(0xffffffffu, tot, o);
+            __syncthreads();
+            long long *r64 = reinterpret_cast<long long *>(red);
+            if ((tid & 31) == 0) r64[tid >> 5] = tot;
+            __syncthreads();
+            if (tid == 0) {
+                long long t = 0;
+                for (int i = 0; i < GV_WARPS; i++) t += r64[i];
+                xsum64[m] = t;
+            }
+        }
+    }
+    __syncthreads();
 }
 
 __device__ __forceinline__ void gv_epi_pair(const GemvParams &p, int lr0, int m, float x1, float x2)
@@ -133,22 +178,32 @@ __device__ __forceinline__ void gv_epi_pair(const GemvParams &p, int lr0, int m,
     }
 }
 
-// Streaming GEMV.  Template: weight kind, token tile MT, rows per warp group RW
-// (even, so RoPE / gate-up pairs stay in one warp), ring depth D.
+template <int QT>
+__device__ __forceinline__ float gv_row_scale(const GemvParams &p, int lr)
+{
+    const int64_t pr = gv_map_row(p, lr);
+    return p.scale_f32 ? reinterpret_cast<const float *>(p.scales)[pr]
+                       : __half2float(reinterpret_cast<const __half *>(p.scales)[pr]);
+}
+
 template <int QT, int MT, int RW, int D>
-__global__ void __launch_bounds__(GV_THREADS, 2) qgemv_kernel(const GemvParams p)
+__global__ void __launch_bounds__(GV_THREADS) qgemv_kernel(const GemvParams p)
 {
     using T = GvTraits<QT>;
-    extern __shared__ __align__(16) float gv_smem[];
-    __shared__ float s_stat[MT][GV_WARPS];
+    extern __shared__ __align__(16) unsigned char gv_smem[];
+    __shared__ float s_red[2 * GV_WARPS];
+    __shared__ float s_xscale[MT];
+    __shared__ long long s_xsum64[MT];
     __shared__ float s_amv[GV_WARPS][MT];
     __shared__ int s_ami[GV_WARPS][MT];
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int nchunk = (int)(p.row_bytes >> 4);
     const int S = (nchunk + 31) >> 5;                    // 512-byte segments per row
-    const int k4 = nchunk * T::F4;
-    float4 *xs = reinterpret_cast<float4 *>(gv_smem);
-    float *xsum = gv_smem + (size_t)MT * k4 * 4;
+
+    // ring: [warp][stage][row][lane] 16-byte slots, then the staged activations
+    uint4 *ring = reinterpret_cast<uint4 *>(gv_smem) + (size_t)warp * D * RW * 32 + lane;
+    uint4 *xq = reinterpret_cast<uint4 *>(gv_smem) + (size_t)GV_WARPS * D * RW * 32;
+    float *xsumf = reinterpret_cast<float *>(xq + (size_t)MT * nchunk * T::XU4);
 
     // contiguous range of row groups for this CTA, round-robin over its warps
     const int NG = (p.N + RW - 1) / RW;
@@ -156,174 +211,215 @@ __global__ void __launch_bounds__(GV_THREADS, 2) qgemv_kernel(const GemvParams p
     const int g_end = (int)(((int64_t)(blockIdx.x + 1) * NG) / gridDim.x);
     const int my_groups = g_end - g_begin > warp ? (g_end - g_begin - warp + GV_WARPS - 1) / GV_WARPS : 0;
     const int nsteps = my_groups * S;
-    const int64_t spr = QT == Q_I4 ? (int64_t)p.K / p.group : 0;
-    const __half *sc4 = reinterpret_cast<const __half *>(p.scales);
 
-    // ---- issue side state: (group, segment) of the next step to load
+    // ---- issue side: (group, segment) of the next step to fetch
     int is_g = g_begin + warp, is_s = 0;
     const uint8_t *iw[RW];
-    const __half *isc[RW];
     bool iv[RW];
     auto set_issue_rows = [&]() {
 #pragma unroll
         for (int j = 0; j < RW; j++) {
             const int lr = is_g * RW + j;
             iv[j] = lr < p.N;
-            const int64_t pr = iv[j] ? gv_map_row(p, lr) : 0;
-            iw[j] = p.w + pr * p.row_bytes + lane * 16;
-            if (QT == Q_I4) isc[j] = sc4 + pr * spr;
+            iw[j] = p.w + (iv[j] ? gv_map_row(p, lr) : 0) * p.row_bytes + lane * 16;
         }
     };
-    uint4 buf[D][RW];
-    __half dsc[D][RW];          // INT4 group scales travel with their weights (fp16, packed in pairs)
-    auto issue = [&](uint4 (&b)[RW], __half (&d)[RW], int i) {
+    auto issue = [&](int i) {
         if (i < nsteps) {
-            const int c = is_s * 32 + lane;
-            const bool cv = c < nchunk;
+            const int stage = i % D;
+            const bool cv = is_s * 32 + lane < nchunk;
 #pragma unroll
-            for (int j = 0; j < RW; j++) {
-                const bool ok = cv && iv[j];
-                b[j] = ok ? ldg_stream(iw[j] + (int64_t)is_s * 512) : make_uint4(0, 0, 0, 0);
-                if (QT == Q_I4) d[j] = ok ? isc[j][(c * 32) / p.group] : __float2half_rn(0.0f);
-            }
+            for (int j = 0; j < RW; j++)
+                cp_async16_cg(ring + (stage * RW + j) * 32, iw[j] + (int64_t)is_s * 512, cv && iv[j]);
             if (++is_s == S) {
                 is_s = 0;
                 is_g += GV_WARPS;
                 set_issue_rows();
             }
         }
+        cp_async_commit_group();
     };
     set_issue_rows();
 #pragma unroll
-    for (int j = 0; j < D - 1; j++) issue(buf[j], dsc[j], j);
+    for (int j = 0; j < D - 1; j++) issue(j);
 
     // activations of the previous kernel are complete from here on
     pdl_wait();
-    gv_stage_x<QT, MT>(p, xs, xsum, k4, nchunk, s_stat);
+    gv_stage_x<QT, MT>(p, xq, xsumf, s_xsum64, s_xscale, nchunk, s_red);
     pdl_trigger();
 
+    const __half *sc4 = reinterpret_cast<const __half *>(p.scales);
+    const int64_t spr = QT == Q_I4 ? (int64_t)p.K / p.group : 0;
+
+    // accumulators: INT8 exact int32 plane sums; INT4 / FP16 fp32
+    int s8[RW][MT][3];
     float acc[RW][MT];
 #pragma unroll
     for (int j = 0; j < RW; j++)
 #pragma unroll
-        for (int m = 0; m < MT; m++) acc[j][m] = 0.0f;
+        for (int m = 0; m < MT; m++) {
+            acc[j][m] = 0.0f;
+            s8[j][m][0] = s8[j][m][1] = s8[j][m][2] = 0;
+        }
     float am_v[MT];
     int am_i[MT];
 #pragma unroll
     for (int m = 0; m < MT; m++) { am_v[m] = -INFINITY; am_i[m] = 0x7fffffff; }
 
     int cs_g = g_begin + warp, cs_s = 0;     // compute side (group, segment)
-    for (int base = 0; base < nsteps; base += D) {
+    int64_t srow[RW];                        // INT4: scale row bases of the group being computed
+    auto set_compute_rows = [&]() {
+        if (QT == Q_I4) {
 #pragma unroll
-        for (int jj = 0; jj < D; jj++) {
-            const int i = base + jj;
-            if (i >= nsteps) break;
-            issue(buf[(jj + D - 1) % D], dsc[(jj + D - 1) % D], i + D - 1);
-            const int c = cs_s * 32 + lane;
-            if (c < nchunk) {
+            for (int j = 0; j < RW; j++) {
+                const int lr = cs_g * RW + j;
+                srow[j] = (lr < p.N ? gv_map_row(p, lr) : 0) * spr;
+            }
+        }
+    };
+    set_compute_rows();
+
+    for (int i = 0; i < nsteps; i++) {
+        issue(i + D - 1);
+        cp_async_wait_group<D - 1>();
+        const int stage = i % D;
+        uint4 wv[RW];
+#pragma unroll
+        for (int j = 0; j < RW; j++) wv[j] = ring[(stage * RW + j) * 32];
+        const int c = cs_s * 32 + lane;
+        if (c < nchunk) {
+            if (QT == Q_I4) {
+                float d[RW];
+#pragma unroll
+                for (int j = 0; j < RW; j++) d[j] = __half2float(sc4[srow[j] + (c * 32) / p.group]);
 #pragma unroll
                 for (int m = 0; m < MT; m++) {
-                    const float4 *xm = xs + (size_t)m * k4;
-                    if (QT == Q_I4) {
-                        float2 part[RW];
+                    const uint4 *xp = xq + ((size_t)m * nchunk + c) * T::XU4;
+                    uint32_t xw[24];
 #pragma unroll
-                        for (int j = 0; j < RW; j++) part[j] = make_float2(0.f, 0.f);
+                    for (int q = 0; q < 6; q++) {
+                        const uint4 t = xp[q];
+                        xw[4 * q] = t.x; xw[4 * q + 1] = t.y; xw[4 * q + 2] = t.z; xw[4 * q + 3] = t.w;
+                    }
+                    const float xs8 = xsumf[(size_t)m * nchunk + c];
 #pragma unroll
-                        for (int wd = 0; wd < 4; wd++) {
-                            const float4 a = xm[gv_swz<QT>(c * 8 + 2 * wd)];
-                            const float4 b = xm[gv_swz<QT>(c * 8 + 2 * wd + 1)];
-#pragma unroll
-                            for (int j = 0; j < RW; j++) {
-                                const uint4 &w4 = buf[jj][j];
-                                const uint32_t wv = wd == 0 ? w4.x : wd == 1 ? w4.y : wd == 2 ? w4.z : w4.w;
-                                gv_dot_i4(wv, a, b, part[j]);
-                            }
-                        }
-                        const float xs8 = xsum[m * nchunk + c];
-#pragma unroll
-                        for (int j = 0; j < RW; j++)
-                            acc[j][m] = fmaf(__half2float(dsc[jj][j]), fmaf(part[j].x + part[j].y, GV_TWO50, -xs8),
-                                             acc[j][m]);
-                    } else if (QT == Q_I8) {
-                        float2 part[RW];
-#pragma unroll
-                        for (int j = 0; j < RW; j++) part[j] = make_float2(0.f, 0.f);
+                    for (int j = 0; j < RW; j++) {
+                        int a0 = 0, a1 = 0, a2 = 0;
 #pragma unroll
                         for (int wd = 0; wd < 4; wd++) {
-                            const float4 a = xm[gv_swz<QT>(c * 4 + wd)];
-#pragma unroll
-                            for (int j = 0; j < RW; j++) {
-                                const uint4 &w4 = buf[jj][j];
-                                const uint32_t wv = wd == 0 ? w4.x : wd == 1 ? w4.y : wd == 2 ? w4.z : w4.w;
-                                gv_dot_i8(wv, a, part[j]);
-                            }
+                            const uint32_t w = wd == 0 ? wv[j].x : wd == 1 ? wv[j].y : wd == 2 ? wv[j].z : wv[j].w;
+                            const uint32_t lo = w & 0x0F0F0F0Fu, hi = (w >> 4) & 0x0F0F0F0Fu;
+                            a0 = dp4a_uu(lo, xw[wd * 6 + 0], a0);
+                            a0 = dp4a_uu(hi, xw[wd * 6 + 1], a0);
+                            a1 = dp4a_uu(lo, xw[wd * 6 + 2], a1);
+                            a1 = dp4a_uu(hi, xw[wd * 6 + 3], a1);
+                            a2 = dp4a_us(lo, xw[wd * 6 + 4], a2);
+                            a2 = dp4a_us(hi, xw[wd * 6 + 5], a2);
                         }
+                        // sum n * x_int - 8 * sum x_int, exact planes, one rounding per term
+                        const float f = fmaf(gv_i2f_small(a2), 65536.0f,
+                                             fmaf(gv_i2f_small(a1), 256.0f, gv_i2f_small(a0))) - xs8;
+                        acc[j][m] = fmaf(d[j], f, acc[j][m]);
+                    }
+                }
+            } else if (QT == Q_I8) {
 #pragma unroll
-                        for (int j = 0; j < RW; j++) acc[j][m] += part[j].x + part[j].y;
-                    } else {
-                        float2 part[RW];
+                for (int m = 0; m < MT; m++) {
+                    const uint4 *xp = xq + ((size_t)m * nchunk + c) * T::XU4;
+                    const uint4 t0 = xp[0], t1 = xp[1], t2 = xp[2];
+                    const uint32_t xw[12] = {t0.x, t0.y, t0.z, t0.w, t1.x, t1.y, t1.z, t1.w, t2.x, t2.y, t2.z, t2.w};
 #pragma unroll
-                        for (int j = 0; j < RW; j++) part[j] = make_float2(0.f, 0.f);
+                    for (int j = 0; j < RW; j++)
 #pragma unroll
-                        for (int h = 0; h < 2; h++) {
-                            const float4 a = xm[gv_swz<QT>(c * 2 + h)];
-#pragma unroll
-                            for (int j = 0; j < RW; j++) {
-                                const uint4 &w4 = buf[jj][j];
-                                gv_dot_f16(h == 0 ? w4.x : w4.z, a.x, a.y, part[j]);
-                                gv_dot_f16(h == 0 ? w4.y : w4.w, a.z, a.w, part[j]);
-                            }
+                        for (int wd = 0; wd < 4; wd++) {
+                            const uint32_t w = wd == 0 ? wv[j].x : wd == 1 ? wv[j].y : wd == 2 ? wv[j].z : wv[j].w;
+                            s8[j][m][0] = dp4a_su(w, xw[wd * 3 + 0], s8[j][m][0]);
+                            s8[j][m][1] = dp4a_su(w, xw[wd * 3 + 1], s8[j][m][1]);
+                            s8[j][m][2] = dp4a_ss(w, xw[wd * 3 + 2], s8[j][m][2]);
                         }
+                }
+            } else {
 #pragma unroll
-                        for (int j = 0; j < RW; j++) acc[j][m] += part[j].x + part[j].y;
+                for (int m = 0; m < MT; m++) {
+                    const float4 *xm = reinterpret_cast<const float4 *>(xq) + (size_t)m * nchunk * 2;
+                    const float4 a = xm[gv_swz16(c * 2)];
+                    const float4 b = xm[gv_swz16(c * 2 + 1)];
+#pragma unroll
+                    for (int j = 0; j < RW; j++) {
+                        float2 part = make_float2(0.f, 0.f);
+                        gv_dot_f16(wv[j].x, a.x, a.y, part);
+                        gv_dot_f16(wv[j].y, a.z, a.w, part);
+                        gv_dot_f16(wv[j].z, b.x, b.y, part);
+                        gv_dot_f16(wv[j].w, b.z, b.w, part);
+                        acc[j][m] += part.x + part.y;
                     }
                 }
             }
-            if (++cs_s == S) {
-                // ---- row group done: fold the lanes, epilogue, reset
-                float v[RW][MT];
+        }
+        if (++cs_s == S) {
+            // ---- row group done: fold the lanes, epilogue, reset
+            float v[RW][MT];
+#pragma unroll
+            for (int j = 0; j < RW; j++)
+#pragma unroll
+                for (int m = 0; m < MT; m++) {
+                    if (QT == Q_I8) {
+                        long long t0 = s8[j][m][0], t1 = s8[j][m][1], t2 = s8[j][m][2];
+#pragma unroll
+                        for (int o = 16; o > 0; o >>= 1) {
+                            t0 += __shfl_xor_sync(0xffffffffu, t0, o);
+                            t1 += __shfl_xor_sync(0xffffffffu, t1, o);
+                            t2 += __shfl_xor_sync(0xffffffffu, t2, o);
+                        }
+                        const long long tot = t0 + (t1 << 8) + (t2 << 16);   // exact sum q * x_int
+                        v[j][m] = (float)tot * s_xscale[m];
+                        s8[j][m][0] = s8[j][m][1] = s8[j][m][2] = 0;
+                    } else {
+                        v[j][m] = warp_sum(acc[j][m]) * (QT == Q_I4 ? s_xscale[m] : 1.0f);
+                        acc[j][m] = 0.0f;
+                    }
+                }
+            const int lr0 = cs_g * RW;
+            if (p.epi == EPI_QKV || p.epi == EPI_GATEUP) {
+#pragma unroll
+                for (int jp = 0; jp < RW; jp += 2)
+#pragma unroll
+                    for (int m = 0; m < MT; m++)
+                        if (lane == (jp / 2) * MT + m && m < p.M && lr0 + jp + 1 < p.N) {
+                            float x1 = v[jp][m], x2 = v[jp + 1][m];
+                            if (QT == Q_I8) {
+                                x1 *= gv_row_scale<QT>(p, lr0 + jp);
+                                x2 *= gv_row_scale<QT>(p, lr0 + jp + 1);
+                            }
+                            gv_epi_pair(p, lr0 + jp, m, x1, x2);
+                        }
+            } else {
 #pragma unroll
                 for (int j = 0; j < RW; j++)
 #pragma unroll
                     for (int m = 0; m < MT; m++) {
-                        v[j][m] = warp_sum(acc[j][m]);
-                        acc[j][m] = 0.0f;
-                    }
-                const int lr0 = cs_g * RW;
-                if (p.epi == EPI_QKV || p.epi == EPI_GATEUP) {
-#pragma unroll
-                    for (int jp = 0; jp < RW; jp += 2)
-#pragma unroll
-                        for (int m = 0; m < MT; m++)
-                            if (lane == (jp / 2) * MT + m && m < p.M && lr0 + jp + 1 < p.N) {
-                                const float x1 = gv_finish<QT>(p, xsum, lr0 + jp, m, v[jp][m]);
-                                const float x2 = gv_finish<QT>(p, xsum, lr0 + jp + 1, m, v[jp + 1][m]);
-                                gv_epi_pair(p, lr0 + jp, m, x1, x2);
-                            }
-                } else {
-#pragma unroll
-                    for (int j = 0; j < RW; j++)
-#pragma unroll
-                        for (int m = 0; m < MT; m++) {
-                            const int lr = lr0 + j;
-                            if (m < p.M && lr < p.N) {
-                                if (p.epi == EPI_LOGITS) {
-                                    const float f = gv_finish<QT>(p, xsum, lr, m, v[j][m]);
-                                    if (f > am_v[m]) { am_v[m] = f; am_i[m] = p.vocab_off + lr; }
-                                    if (lane == j * MT + m && p.logits) p.logits[(size_t)m * p.ldl + p.vocab_off + lr] = f;
-                                } else if (lane == j * MT + m) {
-                                    const float f = gv_finish<QT>(p, xsum, lr, m, v[j][m]);
-                                    if (p.epi == EPI_STORE) p.y[(size_t)m * p.ldy + lr] = f;
-                                    else p.y[(size_t)m * p.ldy + lr] += f;      // EPI_RESID
-                                }
+                        const int lr = lr0 + j;
+                        if (m < p.M && lr < p.N) {
+                            if (p.epi == EPI_LOGITS) {
+                                const float f = v[j][m];
+                                if (f > am_v[m]) { am_v[m] = f; am_i[m] = p.vocab_off + lr; }
+                                if (lane == j * MT + m && p.logits)
+                                    p.logits[(size_t)m * p.ldl + p.vocab_off + lr] = f;
+                            } else if (lane == j * MT + m) {
+                                float f = v[j][m];
+                                if (QT == Q_I8) f *= gv_row_scale<QT>(p, lr);
+                                if (p.epi == EPI_STORE) p.y[(size_t)m * p.ldy + lr] = f;
+                                else p.y[(size_t)m * p.ldy + lr] += f;      // EPI_RESID
                             }
                         }
-                }
-                cs_s = 0;
-                cs_g += GV_WARPS;
+                    }
             }
+            cs_s = 0;
+            cs_g += GV_WARPS;
+            set_compute_rows();
         }
     }
+    cp_async_wait_group<0>();
 
     if (p.epi == EPI_LOGITS) {
         // per-CTA (max, argmax): rows ascend within a warp, so '>' keeps the lowest index on ties
@@ -335,9 +431,9 @@ __global__ void __launch_bounds__(GV_THREADS, 2) qgemv_kernel(const GemvParams p
             float bv = -INFINITY;
             int bi = 0x7fffffff;
             for (int w = 0; w < GV_WARPS; w++) {
-                const float v = s_amv[w][tid];
+                const float vv = s_amv[w][tid];
                 const int ix = s_ami[w][tid];
-                if (v > bv || (v == bv && ix < bi)) { bv = v; bi = ix; }
+                if (vv > bv || (vv == bv && ix < bi)) { bv = vv; bi = ix; }
             }
             p.am_val[(size_t)tid * gridDim.x + blockIdx.x] = bv;
             p.am_idx[(size_t)tid * gridDim.x + blockIdx.x] = bi;
@@ -345,30 +441,37 @@ __global__ void __launch_bounds__(GV_THREADS, 2) qgemv_kernel(const GemvParams p
     }
 }
 
-size_t gemv_smem_bytes(int qt, int mt, int64_t row_bytes)
+// ------------------------------------------------------------------ launch
+
+static constexpr int GV_D = 6;
+static constexpr int rw_of(int mt) { return mt == 1 ? 4 : 2; }
+
+static size_t ring_bytes(int mt) { return (size_t)GV_WARPS * GV_D * rw_of(mt) * 32 * 16; }
+
+static size_t x_bytes(int qt, int mt, int64_t row_bytes)
 {
     const int nchunk = (int)(row_bytes >> 4);
-    const int f4 = qt == Q_I4 ? 8 : qt == Q_I8 ? 4 : 2;
-    size_t b = (size_t)mt * nchunk * f4 * 16;
-    b += (qt == Q_I4 ? (size_t)mt * nchunk : (size_t)mt) * 4;
-    return b;
+    const int xu4 = qt == Q_I4 ? 7 : qt == Q_I8 ? 3 : 2;
+    return (size_t)mt * nchunk * xu4 * 16 + (qt == Q_I4 ? (size_t)mt * nchunk * 4 : 0);
 }
+
+size_t gemv_smem_bytes(int qt, int mt, int64_t row_bytes) { return ring_bytes(mt) + x_bytes(qt, mt, row_bytes); }
 
 static bool g_pdl = true;
 void gemv_set_pdl(bool on) { g_pdl = on; }
 bool pdl_enabled() { return g_pdl; }
 
+int gemv_rows_per_group(int M) { return rw_of(M <= 1 ? 1 : 2); }
+
 template <int QT, int MT>
 static int launch_mt(const GemvParams &p, int grid, size_t smem, cudaStream_t st)
 {
-    constexpr int RW = MT == 1 ? 4 : 2;
-    constexpr int D = MT >= 2 ? 3 : 4;
-    auto kern = qgemv_kernel<QT, MT, RW, D>;
+    auto kern = qgemv_kernel<QT, MT, rw_of(MT), GV_D>;
     static bool attr_set[64] = {};
     int dev = 0;
     cudaGetDevice(&dev);
     if (!attr_set[dev & 63]) {
-        DU_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
+        DU_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024));
         attr_set[dev & 63] = true;
     }
     cudaLaunchConfig_t cfg = {};
@@ -385,7 +488,15 @@ static int launch_mt(const GemvParams &p, int grid, size_t smem, cudaStream_t st
     return DU_OK;
 }
 
-int gemv_rows_per_group(int M) { return M == 1 ? 4 : 2; }
+// CTAs for N rows at token tile M: `want` (0 = as many as fit, at most 2 per SM),
+// never more than one per row group
+int gemv_grid_for(int N, int M, int want)
+{
+    const int RW = gemv_rows_per_group(M);
+    const int ng = (N + RW - 1) / RW;
+    const int grid = want > 0 ? want : 2 * num_sms();
+    return grid > ng ? ng : grid;
+}
 
 int launch_gemv(int qt, GemvParams p, cudaStream_t st)
 {
@@ -393,8 +504,10 @@ int launch_gemv(int qt, GemvParams p, cudaStream_t st)
     if (p.M > 8) return fail(DU_EINVAL, "gemv: M > 8 must be split by the caller");
     const int mt = p.M <= 1 ? 1 : p.M <= 2 ? 2 : p.M <= 4 ? 4 : 8;
     const size_t smem = gemv_smem_bytes(qt, mt, p.row_bytes);
-    if (smem > 200 * 1024) return fail(DU_EINVAL, "gemv: M*K too large for the shared-memory stage");
-    const int grid = gemv_grid_for(p.N, mt, p.grid);
+    if (smem > 220 * 1024) return fail(DU_EINVAL, "gemv: M*K too large for the shared-memory stage");
+    int want = p.grid;
+    if (want <= 0) want = (smem <= 110 * 1024 ? 2 : 1) * num_sms();
+    const int grid = gemv_grid_for(p.N, mt, want);
 #define DU_GV_CASE(Q, M_)                                        \
     if (qt == Q && mt == M_) return launch_mt<Q, M_>(p, grid, smem, st);
     DU_GV_CASE(Q_I4, 1) DU_GV_CASE(Q_I4, 2) DU_GV_CASE(Q_I4, 4) DU_GV_CASE(Q_I4, 8)
@@ -402,15 +515,6 @@ int launch_gemv(int qt, GemvParams p, cudaStream_t st)
     DU_GV_CASE(Q_F16, 1) DU_GV_CASE(Q_F16, 2) DU_GV_CASE(Q_F16, 4) DU_GV_CASE(Q_F16, 8)
 #undef DU_GV_CASE
     return fail(DU_EINVAL, "gemv: unsupported quant kind");
-}
-
-// CTAs for N rows at token tile M: `want` (0 = 2 per SM), at most one per row group
-int gemv_grid_for(int N, int M, int want)
-{
-    const int RW = gemv_rows_per_group(M);
-    const int ng = (N + RW - 1) / RW;
-    const int grid = want > 0 ? want : 2 * num_sms();
-    return grid > ng ? ng : grid;
 }
 
 }  // namespace du

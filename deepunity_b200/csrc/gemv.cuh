@@ -8,25 +8,26 @@
 // partials, G3CS:911-928).
 //
 // Design (B200, HBM-bound at M = 1):
-//  * The grid is 2 CTAs per SM; each CTA owns a contiguous range of row
-//    groups (RW = 4 rows at M <= 2, else 2) so every SM streams the same
-//    number of bytes.  Warps take the CTA's groups round-robin and never
-//    synchronise with each other after the prologue.
-//  * A warp streams a row group 512 bytes per row per step (one 128-bit
-//    L1-bypassing load per lane and row) through a 4-deep register ring: the
-//    loads of the next 3 steps are in flight while one step computes.  The
-//    first 3 steps are issued before griddepcontrol.wait, so under
-//    programmatic dependent launch the weight fetch overlaps the previous
-//    kernel's tail and this kernel's own activation prologue.
-//  * The activation vector is staged once per CTA in shared memory, already
-//    multiplied by a per-column power of two (bank-conflict-free swizzle).
-//    Each weight nibble / byte is then turned into an fp32 operand with ONE
-//    bitwise AND: a masked nibble (or byte, xor 0x80 so it is unsigned) read
-//    as a float is the exact subnormal n * 2^(p - 149), p = its bit position,
-//    so x' * that = x * n * 2^-50, rounded once, with two columns per packed
-//    fma.rn.f32x2.  The zero points (8 for INT4, 128 for INT8) come back out
-//    through per-chunk / per-token sums of x.  Cost per INT4 weight: ~1.1
-//    integer op + 0.5 FFMA2.
+//  * Each CTA owns a contiguous range of row groups (RW rows) so every SM
+//    streams the same number of bytes; its 8 warps take the groups
+//    round-robin and never synchronise with each other after the prologue.
+//  * A lane streams its 16-byte weight chunks (one per row of the group, 512
+//    contiguous bytes per row across the warp) through a private D-stage ring
+//    in shared memory with cp.async (L2 only), so D - 1 steps per warp are in
+//    flight without holding registers.  The first D - 1 steps are issued
+//    before griddepcontrol.wait: under programmatic dependent launch the
+//    weight fetch overlaps the previous kernel's tail and this kernel's
+//    activation prologue.
+//  * INT4 / INT8: the activation vector is turned, once per CTA, into 22-bit
+//    fixed point (per-token power-of-two scale, |x_int| < 2^22) split into
+//    three byte planes laid out to match the nibble / byte order of a weight
+//    word.  A weight word then costs dp4a per plane: exact integer products,
+//    3 dp4a per 4 INT8 weights, 6 dp4a + 3 integer ops per 8 INT4 weights.
+//    INT8 (signed, no zero point) accumulates the whole row exactly in int32
+//    per plane and applies the row scale once; INT4 folds its zero point (8)
+//    through per-chunk sums of x_int and applies its group scale per
+//    32-column chunk.
+//  * FP16 (lm_head): fp32 activations in smem, packed fma.rn.f32x2.
 //  * Each finished row group is folded with warp shuffles and its epilogue is
 //    run by the owning lanes.
 #pragma once
@@ -36,7 +37,7 @@
 namespace du {
 
 constexpr int GV_THREADS = 256;
-constexpr float GV_TWO50 = 1125899906842624.0f;   // 2^50
+constexpr int GV_WARPS = GV_THREADS / 32;
 
 enum GemvMap { MAP_IDENT = 0, MAP_ROPE_PAIR = 1, MAP_GATEUP = 2 };
 enum GemvEpi { EPI_STORE = 0, EPI_RESID = 1, EPI_QKV = 2, EPI_GATEUP = 3, EPI_LOGITS = 4 };
@@ -55,7 +56,7 @@ struct GemvParams {
     int K, N, M, group;
     int map, map_hd, map_I;
     int64_t row_off;        // added to the mapped physical row
-    int grid;               // CTAs (0 = 2 per SM); also the number of argmax partials
+    int grid;               // CTAs (0 = as many as fit); also the number of argmax partials
     // epilogue
     int epi;
     float *y;
@@ -75,35 +76,11 @@ struct GemvParams {
     int vocab_off;
 };
 
+// COLS: weight columns per 16-byte chunk; XU4: uint4s of staged activations per chunk
 template <int QT> struct GvTraits;
-template <> struct GvTraits<Q_I4> { static constexpr int COLS = 32, F4 = 8; };   // cols per 16 B chunk
-template <> struct GvTraits<Q_I8> { static constexpr int COLS = 16, F4 = 4; };
-template <> struct GvTraits<Q_F16> { static constexpr int COLS = 8, F4 = 2; };
-
-// 2^e as an exact fp32 constant, e in [-126, 127]
-__device__ __forceinline__ float gv_pow2(int e) { return __int_as_float((127 + e) << 23); }
-
-// power-of-two exponent applied to x at column position k (see header note)
-template <int QT>
-__device__ __forceinline__ int gv_xexp(int k)
-{
-    if (QT == Q_I4) {
-        const int p = k & 7;
-        const int e = p < 5 ? 4 * p : 4 * (p - 3);
-        return 99 - e;
-    } else if (QT == Q_I8) {
-        return (k & 1) ? 91 : 99;
-    }
-    return 0;
-}
-
-// physical float4 slot of logical float4 f of a token row (bank-conflict-free
-// for the lane-block reads of the main loop)
-template <int QT>
-__device__ __forceinline__ int gv_swz(int f)
-{
-    return f ^ ((f >> 3) & (GvTraits<QT>::F4 - 1));
-}
+template <> struct GvTraits<Q_I4> { static constexpr int COLS = 32, XU4 = 7; };   // 6 used + 1 pad (banks)
+template <> struct GvTraits<Q_I8> { static constexpr int COLS = 16, XU4 = 3; };
+template <> struct GvTraits<Q_F16> { static constexpr int COLS = 8, XU4 = 2; };   // fp32 x, swizzled
 
 __device__ __forceinline__ int64_t gv_map_row(const GemvParams &p, int lr)
 {
@@ -119,6 +96,38 @@ __device__ __forceinline__ int64_t gv_map_row(const GemvParams &p, int lr)
     return r + p.row_off;
 }
 
+// dp4a with explicit operand signedness (a: weights, b: activation plane)
+__device__ __forceinline__ int dp4a_uu(uint32_t a, uint32_t b, int c)
+{
+    int d;
+    asm("dp4a.u32.u32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+__device__ __forceinline__ int dp4a_us(uint32_t a, uint32_t b, int c)
+{
+    int d;
+    asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+__device__ __forceinline__ int dp4a_su(uint32_t a, uint32_t b, int c)
+{
+    int d;
+    asm("dp4a.s32.u32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+__device__ __forceinline__ int dp4a_ss(uint32_t a, uint32_t b, int c)
+{
+    int d;
+    asm("dp4a.s32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+
+// exact int -> float for |v| < 2^22 without the conversion unit
+__device__ __forceinline__ float gv_i2f_small(int v)
+{
+    return __int_as_float(v + 0x4B400000) - 12582912.0f;
+}
+
 // acc += a * b on two fp32 lanes with one packed FFMA2 (sm_100 fma.rn.f32x2)
 __device__ __forceinline__ void ffma2(float2 &acc, float a0, float a1, float b0, float b1)
 {
@@ -132,30 +141,21 @@ __device__ __forceinline__ void ffma2(float2 &acc, float a0, float a1, float b0,
         : "f"(a0), "f"(a1), "f"(b0), "f"(b1));
 }
 
-// 8 INT4 weights (one 32-bit word, nibble j = column k0 + j) against x'[0..7]
-__device__ __forceinline__ void gv_dot_i4(uint32_t w, float4 a, float4 b, float2 &acc)
-{
-    const uint32_t w12 = w >> 12;
-    ffma2(acc, __uint_as_float(w & 0x0000000Fu), __uint_as_float(w & 0x000000F0u), a.x, a.y);
-    ffma2(acc, __uint_as_float(w & 0x00000F00u), __uint_as_float(w & 0x0000F000u), a.z, a.w);
-    ffma2(acc, __uint_as_float(w & 0x000F0000u), __uint_as_float(w12 & 0x00000F00u), b.x, b.y);
-    ffma2(acc, __uint_as_float(w12 & 0x0000F000u), __uint_as_float(w12 & 0x000F0000u), b.z, b.w);
-}
-
-// 4 INT8 weights (byte j = column k0 + j), offset to unsigned (q + 128)
-__device__ __forceinline__ void gv_dot_i8(uint32_t w, float4 a, float2 &acc)
-{
-    const uint32_t u = w ^ 0x80808080u;
-    const uint32_t u16 = u >> 16;
-    ffma2(acc, __uint_as_float(u & 0x000000FFu), __uint_as_float(u & 0x0000FF00u), a.x, a.y);
-    ffma2(acc, __uint_as_float(u16 & 0x000000FFu), __uint_as_float(u16 & 0x0000FF00u), a.z, a.w);
-}
-
 __device__ __forceinline__ void gv_dot_f16(uint32_t w, float a, float b, float2 &acc)
 {
     __half2 h = *reinterpret_cast<__half2 *>(&w);
     const float2 f = __half22float2(h);
     ffma2(acc, f.x, f.y, a, b);
 }
+
+__device__ __forceinline__ void cp_async16_cg(void *smem, const void *gmem, bool valid)
+{
+    const unsigned s = (unsigned)__cvta_generic_to_shared(smem);
+    const int n = valid ? 16 : 0;
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(s), "l"(gmem), "r"(n) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit_group() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait_group() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 
 }  // namespace du
