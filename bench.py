@@ -50,6 +50,8 @@ def parse():
     ap.add_argument("--clock-sampler", choices=["nvml", "smi", "none"], default="nvml")
     ap.add_argument("--sweep", choices=["gemv", "attn"], default=None,
                     help="kernel sweeps (one JSON line per case): config-2 GEMV, config-3 flash-decode")
+    ap.add_argument("--case", default=None, help="--sweep gemv: only quant:N:K:M (e.g. int4:14336:4096:1)")
+    ap.add_argument("--reps", type=int, default=0, help="--sweep: timed launches per case (0 = auto)")
     ap.add_argument("--layers", type=int, default=0,
                     help="profiling only: keep the first N decoder layers (smaller device footprint)")
     return ap.parse_args()
@@ -397,14 +399,22 @@ def run_sweep_gemv(args):
     _lib.call("du_init", 0)
     peak, kind = peaks()
     g = torch.Generator(device="cuda").manual_seed(0)
+    only = None
+    if args.case:   # "int4:14336:4096:1" -> one sweep cell (profiling)
+        q_, n_, k_, m_ = args.case.split(":")
+        only = (q_, int(n_), int(k_), int(m_))
     for quant in ("int4", "int8"):
         for (N, K) in [(4096, 4096), (14336, 4096), (4096, 14336)]:
+            if only and (quant, N, K) != only[:3]:
+                continue
             wbytes = N * K // 2 if quant == "int4" else N * K
             sbytes = N * (K // 128) * 2 if quant == "int4" else N * 2
             copies = max(2, int(np.ceil(1.1e9 / (wbytes + sbytes))))
             W = torch.randint(0, 256, (copies, wbytes), dtype=torch.uint8, device="cuda", generator=g)
             Sc = (torch.rand((copies, sbytes // 2), device="cuda", generator=g) * 1e-3).half()
             for M in (1, 4, 16, 64, 512):
+                if only and M != only[3]:
+                    continue
                 x = torch.randn((M, K), device="cuda", generator=g).bfloat16()
                 y = torch.empty((M, N), device="cuda")
                 if quant == "int4":
@@ -415,7 +425,7 @@ def run_sweep_gemv(args):
                     f = lambda i: _lib.call("du_gemv_q8", C.c_void_p(y.data_ptr()), C.c_void_p(x.data_ptr()),
                                             _lib.DTYPE_BF16, C.c_void_p(W[i % copies].data_ptr()),
                                             C.c_void_p(Sc[i % copies].data_ptr()), _lib.DTYPE_F16, M, N, K, None)
-                reps = max(4, min(200, int(2e9 / ((wbytes + sbytes) * max(1, M // 8)))))
+                reps = args.reps or max(4, min(200, int(2e9 / ((wbytes + sbytes) * max(1, M // 8)))))
                 _events_ms(f, 3)
                 ms = _events_ms(f, reps)
                 byts = wbytes + sbytes + M * K * 2 + M * N * 4

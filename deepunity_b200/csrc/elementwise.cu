@@ -59,7 +59,7 @@ __device__ __forceinline__ bool am_better(float v, int i, float bv, int bi)
 }
 
 __global__ void argmax_final_kernel(const float *am_val, const int *am_idx, int nparts, int *out_ids,
-                                    int *feed_ids, float *pairs)
+                                    int *feed_ids, float *pairs, TokHist hist)
 {
     const int m = blockIdx.x;
     __shared__ float sv[32];
@@ -88,15 +88,16 @@ __global__ void argmax_final_kernel(const float *am_val, const int *am_idx, int 
         } else {
             out_ids[m] = bi;
             if (feed_ids) feed_ids[m] = bi;
+            if (hist.tok) hist.tok[(size_t)m * hist.cap + hist.cache_len[m]] = bi;
         }
     }
 }
 
 int launch_argmax_final(const float *am_val, const int *am_idx, int M, int nparts, int *out_ids, int *feed_ids,
-                        cudaStream_t st)
+                        TokHist hist, cudaStream_t st)
 {
     if (M <= 0) return DU_OK;
-    argmax_final_kernel<<<M, 256, 0, st>>>(am_val, am_idx, nparts, out_ids, feed_ids, nullptr);
+    argmax_final_kernel<<<M, 256, 0, st>>>(am_val, am_idx, nparts, out_ids, feed_ids, nullptr, hist);
     DU_CUDA_TRY(cudaGetLastError());
     return DU_OK;
 }
@@ -105,13 +106,14 @@ int launch_argmax_final_pairs(const float *am_val, const int *am_idx, int M, int
                               cudaStream_t st)
 {
     if (M <= 0) return DU_OK;
-    argmax_final_kernel<<<M, 256, 0, st>>>(am_val, am_idx, nparts, nullptr, nullptr, pairs);
+    argmax_final_kernel<<<M, 256, 0, st>>>(am_val, am_idx, nparts, nullptr, nullptr, pairs, TokHist{});
     DU_CUDA_TRY(cudaGetLastError());
     return DU_OK;
 }
 
 // gpairs [tp][maxb][2]: best (value, index) of each rank's vocab shard
-__global__ void argmax_pick_tp_kernel(const float *gpairs, int tp, int maxb, int M, int *out_ids, int *feed_ids)
+__global__ void argmax_pick_tp_kernel(const float *gpairs, int tp, int maxb, int M, int *out_ids, int *feed_ids,
+                                      TokHist hist)
 {
     const int m = blockIdx.x * blockDim.x + threadIdx.x;
     if (m >= M) return;
@@ -124,13 +126,14 @@ __global__ void argmax_pick_tp_kernel(const float *gpairs, int tp, int maxb, int
     }
     out_ids[m] = bi;
     if (feed_ids) feed_ids[m] = bi;
+    if (hist.tok) hist.tok[(size_t)m * hist.cap + hist.cache_len[m]] = bi;
 }
 
 int launch_argmax_pick_tp(const float *gpairs, int tp, int maxb, int M, int *out_ids, int *feed_ids,
-                          cudaStream_t st)
+                          TokHist hist, cudaStream_t st)
 {
     if (M <= 0) return DU_OK;
-    argmax_pick_tp_kernel<<<(M + 127) / 128, 128, 0, st>>>(gpairs, tp, maxb, M, out_ids, feed_ids);
+    argmax_pick_tp_kernel<<<(M + 127) / 128, 128, 0, st>>>(gpairs, tp, maxb, M, out_ids, feed_ids, hist);
     DU_CUDA_TRY(cudaGetLastError());
     return DU_OK;
 }

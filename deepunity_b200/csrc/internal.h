@@ -29,12 +29,19 @@ int launch_flash_decode(const float *q, const __half *kc, const __half *vc, cons
 int launch_embed(const int *ids, const __half *embed, float scale, int M, int H, float *out, cudaStream_t st);
 int launch_rmsnorm(const float *x, const __half *gamma_m1, int rows, int H, float eps, float *y,
                    cudaStream_t st);
+// Greedy-token history of the device-resident decode loop: the id chosen for
+// sequence m is also written at tok[m * cap + cache_len[m]] (its input position).
+struct TokHist {
+    int *tok = nullptr;
+    const int *cache_len = nullptr;
+    int cap = 0;
+};
 int launch_argmax_final(const float *am_val, const int *am_idx, int M, int nparts, int *out_ids,
-                        int *feed_ids, cudaStream_t st);
+                        int *feed_ids, TokHist hist, cudaStream_t st);
 int launch_argmax_final_pairs(const float *am_val, const int *am_idx, int M, int nparts, float *pairs,
                               cudaStream_t st);
 int launch_argmax_pick_tp(const float *gpairs, int tp, int maxb, int M, int *out_ids, int *feed_ids,
-                          cudaStream_t st);
+                          TokHist hist, cudaStream_t st);
 int launch_add_inplace(float *y, const float *x, size_t n, cudaStream_t st);
 int launch_quantize_int8(const float *w, int64_t rows, int64_t cols, int8_t *q, __half *s, cudaStream_t st);
 int launch_quantize_int4(const float *w, int64_t rows, int64_t cols, int group, uint8_t *p, __half *s,

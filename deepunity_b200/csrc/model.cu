@@ -60,7 +60,8 @@ struct du_model {
     // device state
     int *d_cache_len = nullptr;             // [maxb]
     int *d_ids = nullptr;                   // [max_tokens] input ids
-    int *d_next = nullptr;                  // [maxb] greedy ids
+    int *d_next = nullptr;                  // [max_tokens] greedy ids
+    int *d_hist = nullptr;                  // [maxb][cap] greedy id chosen at each input position
     int *d_pos = nullptr, *d_seq = nullptr, *d_kvlen = nullptr;   // per-token (prefill)
     float *x_res = nullptr;                 // [max_tokens][H]
     float *part = nullptr;                  // [max_tokens][H] TP partial sums
@@ -205,6 +206,7 @@ static int model_alloc(du_model *m)
     m->d_cache_len = (int *)dalloc(m, sizeof(int) * m->maxb, &rc);
     m->d_ids = (int *)dalloc(m, sizeof(int) * T, &rc);
     m->d_next = (int *)dalloc(m, sizeof(int) * T, &rc);
+    m->d_hist = (int *)dalloc(m, sizeof(int) * (size_t)m->maxb * m->cap, &rc);
     m->d_pos = (int *)dalloc(m, sizeof(int) * T, &rc);
     m->d_seq = (int *)dalloc(m, sizeof(int) * T, &rc);
     m->d_kvlen = (int *)dalloc(m, sizeof(int) * T, &rc);
@@ -577,8 +579,14 @@ static int enqueue_head(du_model *m, const StepIO &io)
         c.am_idx = m->am_idx + (size_t)t0 * nparts;
         if ((rc = launch_gemv(Q_F16, c, st))) return rc;
     }
+    TokHist hist;
+    if (io.advance) {   // decode: record the greedy id at each sequence's input position
+        hist.tok = m->d_hist;
+        hist.cache_len = m->d_cache_len;
+        hist.cap = m->cap;
+    }
     if (m->tp == 1) {
-        if ((rc = launch_argmax_final(m->am_val, m->am_idx, R, nparts, io.next_out, io.feed, st))) return rc;
+        if ((rc = launch_argmax_final(m->am_val, m->am_idx, R, nparts, io.next_out, io.feed, hist, st))) return rc;
     } else {
         // local best (val, idx) per row, exchange the pairs between ranks, pick the global best
         if ((rc = launch_argmax_final_pairs(m->am_val, m->am_idx, R, nparts, m->best_val, st))) return rc;
@@ -586,7 +594,8 @@ static int enqueue_head(du_model *m, const StepIO &io)
         if ((rc = nccl_check(m, api->AllGather(m->best_val, m->gbest_val, (size_t)m->max_tokens * 2, ncclFloat32,
                                                m->comm, st), "ncclAllGather")))
             return rc;
-        if ((rc = launch_argmax_pick_tp(m->gbest_val, m->tp, m->max_tokens, R, io.next_out, io.feed, st))) return rc;
+        if ((rc = launch_argmax_pick_tp(m->gbest_val, m->tp, m->max_tokens, R, io.next_out, io.feed, hist, st)))
+            return rc;
     }
     if (io.advance) {
         if ((rc = launch_step_advance(m->d_cache_len, M, st))) return rc;
@@ -995,17 +1004,18 @@ DU_API int du_decode_loop(du_model *m, const int32_t *ids, int batch, int n_step
     cudaGraphExec_t exec;
     if ((rc = get_graph(m, batch, &exec))) return rc;
     cudaStream_t st = m->stream;
-    int *hist = nullptr;
-    DU_CUDA_TRY(cudaMallocAsync((void **)&hist, sizeof(int) * (size_t)n_steps * batch, st));
     memcpy(m->h_pin_ids, ids, sizeof(int) * batch);
     DU_CUDA_TRY(cudaMemcpyAsync(m->d_ids, m->h_pin_ids, sizeof(int) * batch, cudaMemcpyHostToDevice, st));
-    for (int s = 0; s < n_steps; s++) {
-        DU_CUDA_TRY(cudaGraphLaunch(exec, st));
-        DU_CUDA_TRY(cudaMemcpyAsync(hist + (size_t)s * batch, m->d_next, sizeof(int) * batch, cudaMemcpyDeviceToDevice, st));
-    }
-    DU_CUDA_TRY(cudaMemcpyAsync(tokens_out, hist, sizeof(int) * (size_t)n_steps * batch, cudaMemcpyDeviceToHost, st));
-    DU_CUDA_TRY(cudaFreeAsync(hist, st));
+    // back-to-back graph replays; each step's argmax feeds the next step's input on
+    // the device and is recorded at its input position of the token history
+    for (int s = 0; s < n_steps; s++) DU_CUDA_TRY(cudaGraphLaunch(exec, st));
+    std::vector<int> h((size_t)batch * n_steps);
+    for (int b = 0; b < batch; b++)
+        DU_CUDA_TRY(cudaMemcpyAsync(h.data() + (size_t)b * n_steps, m->d_hist + (size_t)b * m->cap + m->h_cache_len[b],
+                                    sizeof(int) * n_steps, cudaMemcpyDeviceToHost, st));
     DU_CUDA_TRY(cudaStreamSynchronize(st));
+    for (int s = 0; s < n_steps; s++)
+        for (int b = 0; b < batch; b++) tokens_out[(size_t)s * batch + b] = h[(size_t)b * n_steps + s];
     for (int b = 0; b < batch; b++) m->h_cache_len[b] += n_steps;
     m->last_batch = batch;
     return DU_OK;
