@@ -8,32 +8,6 @@ namespace du {
 // (conflict-free for the lane-chunk reads of the main loop).
 __device__ __forceinline__ int gv_swz16(int f) { return f ^ ((f >> 3) & 1); }
 
-// Block-wide sum / max of one float per thread (all threads must call).
-__device__ __forceinline__ float block_sum(float v, float *red)
-{
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    v = warp_sum(v);
-    __syncthreads();
-    if (lane == 0) red[warp] = v;
-    __syncthreads();
-    float t = 0.0f;
-#pragma unroll
-    for (int i = 0; i < GV_WARPS; i++) t += red[i];
-    return t;
-}
-__device__ __forceinline__ float block_max(float v, float *red)
-{
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    v = warp_max(v);
-    __syncthreads();
-    if (lane == 0) red[warp] = v;
-    __syncthreads();
-    float t = red[0];
-#pragma unroll
-    for (int i = 1; i < GV_WARPS; i++) t = fmaxf(t, red[i]);
-    return t;
-}
-
 // x_k (optionally RMSNorm'd: x * rms * (1 + gamma'_k)), computed identically
 // wherever it is needed
 __device__ __forceinline__ float gv_xval(const GemvParams &p, const float *xr, float inv, int k)
@@ -54,13 +28,36 @@ __device__ void gv_stage_x(const GemvParams &p, uint4 *xq, float *xsumf, long lo
     for (int m = 0; m < MT; m++) {
         const float *xr = p.x + (size_t)m * p.ldx;
         const bool live = m < p.M;
+        // one pass: sum of squares (RMSNorm) and max |x * (1 + gamma')| (fixed-point range)
+        float ss = 0.0f, mx = 0.0f;
+        if (live) {
+            for (int k4 = tid; k4 < (p.K >> 2); k4 += GV_THREADS) {
+                const float4 v = reinterpret_cast<const float4 *>(xr)[k4];
+                float g0 = 1.0f, g1 = 1.0f, g2 = 1.0f, g3 = 1.0f;
+                if (p.gamma != nullptr) {
+                    const __half2 *g2p = reinterpret_cast<const __half2 *>(p.gamma) + 2 * k4;
+                    const float2 a = __half22float2(g2p[0]), b = __half22float2(g2p[1]);
+                    g0 = 1.0f + a.x; g1 = 1.0f + a.y; g2 = 1.0f + b.x; g3 = 1.0f + b.y;
+                }
+                ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+                mx = fmaxf(mx, fmaxf(fmaxf(fabsf(v.x * g0), fabsf(v.y * g1)), fmaxf(fabsf(v.z * g2), fabsf(v.w * g3))));
+            }
+        }
+        {
+            const int lane = tid & 31, warp = tid >> 5;
+            ss = warp_sum(ss);
+            mx = warp_max(mx);
+            __syncthreads();
+            if (lane == 0) { red[warp] = ss; red[GV_WARPS + warp] = mx; }
+            __syncthreads();
+            ss = 0.0f; mx = 0.0f;
+#pragma unroll
+            for (int i = 0; i < GV_WARPS; i++) { ss += red[i]; mx = fmaxf(mx, red[GV_WARPS + i]); }
+        }
         float inv = 1.0f;
         if (p.gamma != nullptr) {
-            float ss = 0.0f;
-            if (live)
-                for (int k = tid; k < p.K; k += GV_THREADS) ss += xr[k] * xr[k];
-            ss = block_sum(ss, red);
             inv = 1.0f / sqrtf(ss / (float)p.K + p.eps);
+            mx *= inv * 1.0000002f;     // bound on max |normalised x| (rounding of the product order)
         }
         if (QT == Q_F16) {
             float4 *xs = reinterpret_cast<float4 *>(xq) + (size_t)m * nchunk * 2;
@@ -76,11 +73,7 @@ __device__ void gv_stage_x(const GemvParams &p, uint4 *xq, float *xsumf, long lo
             }
             continue;
         }
-        // per-token power-of-two scale: max |x| * 2^s < 2^22
-        float mx = 0.0f;
-        if (live)
-            for (int k = tid; k < p.K; k += GV_THREADS) mx = fmaxf(mx, fabsf(gv_xval(p, xr, inv, k)));
-        mx = block_max(mx, red);
+        // per-token power-of-two scale: max |x| * 2^s < 2^22 (so |x_int| < 2^23 always)
         const int s = mx > 0.0f ? 21 - ilogbf(mx) : 0;
         const float sc = ldexpf(1.0f, s);
         if (tid == 0) xscale[m] = ldexpf(1.0f, -s);
@@ -200,10 +193,18 @@ __global__ void __launch_bounds__(GV_THREADS) qgemv_kernel(const GemvParams p)
     const int nchunk = (int)(p.row_bytes >> 4);
     const int S = (nchunk + 31) >> 5;                    // 512-byte segments per row
 
-    // ring: [warp][stage][row][lane] 16-byte slots, then the staged activations
+    // ring: [warp][stage][row][lane] 16-byte weight slots; INT4 also [warp][stage][row][lane]
+    // 4-byte slots holding the fp16 pair that contains the lane's group scale; then the
+    // staged activations
     uint4 *ring = reinterpret_cast<uint4 *>(gv_smem) + (size_t)warp * D * RW * 32 + lane;
-    uint4 *xq = reinterpret_cast<uint4 *>(gv_smem) + (size_t)GV_WARPS * D * RW * 32;
+    uint32_t *sring = reinterpret_cast<uint32_t *>(reinterpret_cast<uint4 *>(gv_smem) + (size_t)GV_WARPS * D * RW * 32) +
+                      (size_t)warp * D * RW * 32 + lane;
+    uint4 *xq = reinterpret_cast<uint4 *>(gv_smem) + (size_t)GV_WARPS * D * RW * 32 +
+                (QT == Q_I4 ? (size_t)GV_WARPS * D * RW * 32 / 4 : 0);
     float *xsumf = reinterpret_cast<float *>(xq + (size_t)MT * nchunk * T::XU4);
+    const uint8_t *sbase = reinterpret_cast<const uint8_t *>(p.scales);
+    const int gshift = QT == Q_I4 ? __ffs(p.group) - 1 : 0;        // group is a power of two
+    const int64_t srow_bytes = QT == Q_I4 ? ((int64_t)p.K >> gshift) * 2 : 0;
 
     // contiguous range of row groups for this CTA, round-robin over its warps
     const int NG = (p.N + RW - 1) / RW;
@@ -213,24 +214,32 @@ __global__ void __launch_bounds__(GV_THREADS) qgemv_kernel(const GemvParams p)
     const int nsteps = my_groups * S;
 
     // ---- issue side: (group, segment) of the next step to fetch
-    int is_g = g_begin + warp, is_s = 0;
+    int is_g = g_begin + warp, is_s = 0, is_stage = 0;
     const uint8_t *iw[RW];
+    const uint8_t *isw[RW];
     bool iv[RW];
     auto set_issue_rows = [&]() {
 #pragma unroll
         for (int j = 0; j < RW; j++) {
             const int lr = is_g * RW + j;
             iv[j] = lr < p.N;
-            iw[j] = p.w + (iv[j] ? gv_map_row(p, lr) : 0) * p.row_bytes + lane * 16;
+            const int64_t pr = iv[j] ? gv_map_row(p, lr) : 0;
+            iw[j] = p.w + pr * p.row_bytes + lane * 16;
+            if (QT == Q_I4) isw[j] = sbase + pr * srow_bytes;
         }
     };
     auto issue = [&](int i) {
         if (i < nsteps) {
-            const int stage = i % D;
-            const bool cv = is_s * 32 + lane < nchunk;
+            const int c = is_s * 32 + lane;
+            const bool cv = c < nchunk;
+            // 4-byte word holding the fp16 scale of group (c * 32) >> gshift
+            const int sw_off = (((c * 32) >> gshift) * 2) & ~3;
 #pragma unroll
-            for (int j = 0; j < RW; j++)
-                cp_async16_cg(ring + (stage * RW + j) * 32, iw[j] + (int64_t)is_s * 512, cv && iv[j]);
+            for (int j = 0; j < RW; j++) {
+                cp_async16_cg(ring + (is_stage * RW + j) * 32, iw[j] + (int64_t)is_s * 512, cv && iv[j]);
+                if (QT == Q_I4) cp_async4_ca(sring + (is_stage * RW + j) * 32, isw[j] + sw_off, cv && iv[j]);
+            }
+            if (++is_stage == D) is_stage = 0;
             if (++is_s == S) {
                 is_s = 0;
                 is_g += GV_WARPS;
@@ -248,9 +257,6 @@ __global__ void __launch_bounds__(GV_THREADS) qgemv_kernel(const GemvParams p)
     gv_stage_x<QT, MT>(p, xq, xsumf, s_xsum64, s_xscale, nchunk, s_red);
     pdl_trigger();
 
-    const __half *sc4 = reinterpret_cast<const __half *>(p.scales);
-    const int64_t spr = QT == Q_I4 ? (int64_t)p.K / p.group : 0;
-
     // accumulators: INT8 exact int32 plane sums; INT4 / FP16 fp32
     int s8[RW][MT][3];
     float acc[RW][MT];
@@ -266,23 +272,13 @@ __global__ void __launch_bounds__(GV_THREADS) qgemv_kernel(const GemvParams p)
 #pragma unroll
     for (int m = 0; m < MT; m++) { am_v[m] = -INFINITY; am_i[m] = 0x7fffffff; }
 
-    int cs_g = g_begin + warp, cs_s = 0;     // compute side (group, segment)
-    int64_t srow[RW];                        // INT4: scale row bases of the group being computed
-    auto set_compute_rows = [&]() {
-        if (QT == Q_I4) {
-#pragma unroll
-            for (int j = 0; j < RW; j++) {
-                const int lr = cs_g * RW + j;
-                srow[j] = (lr < p.N ? gv_map_row(p, lr) : 0) * spr;
-            }
-        }
-    };
-    set_compute_rows();
+    int cs_g = g_begin + warp, cs_s = 0, cs_stage = 0;     // compute side (group, segment, ring slot)
 
     for (int i = 0; i < nsteps; i++) {
         issue(i + D - 1);
         cp_async_wait_group<D - 1>();
-        const int stage = i % D;
+        const int stage = cs_stage;
+        if (++cs_stage == D) cs_stage = 0;
         uint4 wv[RW];
 #pragma unroll
         for (int j = 0; j < RW; j++) wv[j] = ring[(stage * RW + j) * 32];
@@ -290,8 +286,10 @@ __global__ void __launch_bounds__(GV_THREADS) qgemv_kernel(const GemvParams p)
         if (c < nchunk) {
             if (QT == Q_I4) {
                 float d[RW];
+                const int hsel = (((c * 32) >> gshift) & 1) * 16;
 #pragma unroll
-                for (int j = 0; j < RW; j++) d[j] = __half2float(sc4[srow[j] + (c * 32) / p.group]);
+                for (int j = 0; j < RW; j++)
+                    d[j] = __half2float(__ushort_as_half((unsigned short)(sring[(stage * RW + j) * 32] >> hsel)));
 #pragma unroll
                 for (int m = 0; m < MT; m++) {
                     const uint4 *xp = xq + ((size_t)m * nchunk + c) * T::XU4;
@@ -304,21 +302,23 @@ __global__ void __launch_bounds__(GV_THREADS) qgemv_kernel(const GemvParams p)
                     const float xs8 = xsumf[(size_t)m * nchunk + c];
 #pragma unroll
                     for (int j = 0; j < RW; j++) {
-                        int a0 = 0, a1 = 0, a2 = 0;
+                        // even / odd nibble streams accumulate separately (shorter dependency chains)
+                        int a0 = 0, a1 = 0, a2 = 0, b0 = 0, b1 = 0, b2 = 0;
 #pragma unroll
                         for (int wd = 0; wd < 4; wd++) {
                             const uint32_t w = wd == 0 ? wv[j].x : wd == 1 ? wv[j].y : wd == 2 ? wv[j].z : wv[j].w;
                             const uint32_t lo = w & 0x0F0F0F0Fu, hi = (w >> 4) & 0x0F0F0F0Fu;
                             a0 = dp4a_uu(lo, xw[wd * 6 + 0], a0);
-                            a0 = dp4a_uu(hi, xw[wd * 6 + 1], a0);
+                            b0 = dp4a_uu(hi, xw[wd * 6 + 1], b0);
                             a1 = dp4a_uu(lo, xw[wd * 6 + 2], a1);
-                            a1 = dp4a_uu(hi, xw[wd * 6 + 3], a1);
+                            b1 = dp4a_uu(hi, xw[wd * 6 + 3], b1);
                             a2 = dp4a_us(lo, xw[wd * 6 + 4], a2);
-                            a2 = dp4a_us(hi, xw[wd * 6 + 5], a2);
+                            b2 = dp4a_us(hi, xw[wd * 6 + 5], b2);
                         }
-                        // sum n * x_int - 8 * sum x_int, exact planes, one rounding per term
-                        const float f = fmaf(gv_i2f_small(a2), 65536.0f,
-                                             fmaf(gv_i2f_small(a1), 256.0f, gv_i2f_small(a0))) - xs8;
+                        // sum n * x_int - 8 * sum x_int: planes 0 and 1 join exactly in int32
+                        // (< 2^25), plane 2 (< 2^19 in magnitude) is exact in fp32
+                        const int p01 = (a0 + b0) + ((a1 + b1) << 8);
+                        const float f = fmaf((float)(a2 + b2), 65536.0f, (float)p01) - xs8;
                         acc[j][m] = fmaf(d[j], f, acc[j][m]);
                     }
                 }
@@ -416,7 +416,6 @@ __global__ void __launch_bounds__(GV_THREADS) qgemv_kernel(const GemvParams p)
             }
             cs_s = 0;
             cs_g += GV_WARPS;
-            set_compute_rows();
         }
     }
     cp_async_wait_group<0>();
@@ -443,10 +442,16 @@ __global__ void __launch_bounds__(GV_THREADS) qgemv_kernel(const GemvParams p)
 
 // ------------------------------------------------------------------ launch
 
-static constexpr int GV_D = 6;
+// Ring depth D: 4 when two CTAs per SM fit in shared memory, else 3 if that
+// makes two fit (large K), else 4 with one CTA per SM.
 static constexpr int rw_of(int mt) { return mt == 1 ? 4 : 2; }
+static constexpr size_t SMEM_PER_SM = 227 * 1024;
 
-static size_t ring_bytes(int mt) { return (size_t)GV_WARPS * GV_D * rw_of(mt) * 32 * 16; }
+static size_t ring_bytes(int qt, int mt, int d)
+{
+    const size_t slots = (size_t)GV_WARPS * d * rw_of(mt) * 32;
+    return slots * 16 + (qt == Q_I4 ? slots * 4 : 0);
+}
 
 static size_t x_bytes(int qt, int mt, int64_t row_bytes)
 {
@@ -455,7 +460,21 @@ static size_t x_bytes(int qt, int mt, int64_t row_bytes)
     return (size_t)mt * nchunk * xu4 * 16 + (qt == Q_I4 ? (size_t)mt * nchunk * 4 : 0);
 }
 
-size_t gemv_smem_bytes(int qt, int mt, int64_t row_bytes) { return ring_bytes(mt) + x_bytes(qt, mt, row_bytes); }
+static int choose_depth(int qt, int mt, int64_t row_bytes, int *cps)
+{
+    const size_t x = x_bytes(qt, mt, row_bytes);
+    for (int d = 4; d >= 3; d--)
+        if (2 * (ring_bytes(qt, mt, d) + x + 1024) <= SMEM_PER_SM) { *cps = 2; return d; }
+    *cps = 1;
+    return 4;
+}
+
+size_t gemv_smem_bytes(int qt, int mt, int64_t row_bytes)
+{
+    int cps = 1;
+    const int d = choose_depth(qt, mt, row_bytes, &cps);
+    return ring_bytes(qt, mt, d) + x_bytes(qt, mt, row_bytes);
+}
 
 static bool g_pdl = true;
 void gemv_set_pdl(bool on) { g_pdl = on; }
@@ -463,10 +482,10 @@ bool pdl_enabled() { return g_pdl; }
 
 int gemv_rows_per_group(int M) { return rw_of(M <= 1 ? 1 : 2); }
 
-template <int QT, int MT>
-static int launch_mt(const GemvParams &p, int grid, size_t smem, cudaStream_t st)
+template <int QT, int MT, int D>
+static int launch_kernel(const GemvParams &p, int grid, size_t smem, cudaStream_t st)
 {
-    auto kern = qgemv_kernel<QT, MT, rw_of(MT), GV_D>;
+    auto kern = qgemv_kernel<QT, MT, rw_of(MT), D>;
     static bool attr_set[64] = {};
     int dev = 0;
     cudaGetDevice(&dev);
@@ -488,8 +507,13 @@ static int launch_mt(const GemvParams &p, int grid, size_t smem, cudaStream_t st
     return DU_OK;
 }
 
-// CTAs for N rows at token tile M: `want` (0 = as many as fit, at most 2 per SM),
-// never more than one per row group
+template <int QT, int MT>
+static int launch_mt(const GemvParams &p, int grid, int depth, size_t smem, cudaStream_t st)
+{
+    return depth == 3 ? launch_kernel<QT, MT, 3>(p, grid, smem, st) : launch_kernel<QT, MT, 4>(p, grid, smem, st);
+}
+
+// CTAs for N rows at token tile M: `want` (0 = 2 per SM), never more than one per row group
 int gemv_grid_for(int N, int M, int want)
 {
     const int RW = gemv_rows_per_group(M);
@@ -502,14 +526,16 @@ int launch_gemv(int qt, GemvParams p, cudaStream_t st)
 {
     if (p.M <= 0 || p.N <= 0) return DU_OK;
     if (p.M > 8) return fail(DU_EINVAL, "gemv: M > 8 must be split by the caller");
+    if (qt == Q_I4 && (p.group < 32 || (p.group & (p.group - 1)) || ((p.K / p.group) & 1)))
+        return fail(DU_EINVAL, "gemv: int4 group must be a power of two >= 32 with an even number of groups per row");
     const int mt = p.M <= 1 ? 1 : p.M <= 2 ? 2 : p.M <= 4 ? 4 : 8;
-    const size_t smem = gemv_smem_bytes(qt, mt, p.row_bytes);
+    int cps = 1;
+    const int depth = choose_depth(qt, mt, p.row_bytes, &cps);
+    const size_t smem = ring_bytes(qt, mt, depth) + x_bytes(qt, mt, p.row_bytes);
     if (smem > 220 * 1024) return fail(DU_EINVAL, "gemv: M*K too large for the shared-memory stage");
-    int want = p.grid;
-    if (want <= 0) want = (smem <= 110 * 1024 ? 2 : 1) * num_sms();
-    const int grid = gemv_grid_for(p.N, mt, want);
+    const int grid = gemv_grid_for(p.N, mt, p.grid > 0 ? p.grid : cps * num_sms());
 #define DU_GV_CASE(Q, M_)                                        \
-    if (qt == Q && mt == M_) return launch_mt<Q, M_>(p, grid, smem, st);
+    if (qt == Q && mt == M_) return launch_mt<Q, M_>(p, grid, depth, smem, st);
     DU_GV_CASE(Q_I4, 1) DU_GV_CASE(Q_I4, 2) DU_GV_CASE(Q_I4, 4) DU_GV_CASE(Q_I4, 8)
     DU_GV_CASE(Q_I8, 1) DU_GV_CASE(Q_I8, 2) DU_GV_CASE(Q_I8, 4) DU_GV_CASE(Q_I8, 8)
     DU_GV_CASE(Q_F16, 1) DU_GV_CASE(Q_F16, 2) DU_GV_CASE(Q_F16, 4) DU_GV_CASE(Q_F16, 8)

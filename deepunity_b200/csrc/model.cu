@@ -159,7 +159,10 @@ static int check_cfg(const du_model_config &c)
     DU_CHECK_ARG(c.intermediate_size % tp == 0 && c.vocab_size % tp == 0, "config: intermediate/vocab % tp");
     const int H = c.hidden_size, I_l = c.intermediate_size / tp, K_o = c.num_heads_q / tp * c.head_dim;
     if (c.quant == DU_QUANT_INT4) {
-        DU_CHECK_ARG(c.group_size > 0 && c.group_size % 32 == 0, "config: int4 group must be a multiple of 32");
+        DU_CHECK_ARG(c.group_size >= 32 && (c.group_size & (c.group_size - 1)) == 0,
+                     "config: int4 group must be a power of two >= 32");
+        DU_CHECK_ARG((H / c.group_size) % 2 == 0 && (I_l / c.group_size) % 2 == 0 && (K_o / c.group_size) % 2 == 0,
+                     "config: every (sharded) K must hold an even number of int4 groups");
         DU_CHECK_ARG(H % c.group_size == 0 && I_l % c.group_size == 0 && K_o % c.group_size == 0,
                      "config: every (sharded) K must be a multiple of the int4 group");
     }
