@@ -59,6 +59,7 @@ SIGNATURES = {
     "du_gemv_q4": (I, [P, P, I, P, P, I, I, I, I, P]),
     "du_gemv_f16": (I, [P, P, I, P, I, I, I, P]),
     "du_flash_decode": (I, [P, P, P, P, P, I, I, I, I, I, F, P]),
+    "du_flash_decode_noalloc": (I, [P, P, P, P, P, I, I, I, I, I, F, P]),
     "du_quantize_int8": (I, [P, I64, I64, P, P, P]),
     "du_quantize_int4": (I, [P, I64, I64, I, P, P, P]),
     "du_rmsnorm": (I, [P, P, P, I, I, F, P]),

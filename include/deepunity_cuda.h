@@ -184,6 +184,22 @@ DU_API int du_flash_decode(float *out, const float *q, const uint16_t *k_cache,
                            const uint16_t *v_cache, const int32_t *kv_len, int batch, int hq,
                            int hkv, int hd, int capacity, float scale, void *stream);
 
+/* Same computation as du_flash_decode, but it allocates nothing: for callers
+ * that must not call cudaMalloc / cudaFree, such as a game engine plugin
+ * running on the engine's render or job thread (the engine owns the GPU memory
+ * budget, and allocation can synchronise the whole device mid-frame).  No
+ * counterpart in the reference.  Its scratch is a fixed device array of
+ * 1048576 floats plus 8192 split counters (about 4 MiB), held by every GPU that
+ * loads the library until exit; calls needing more (batch * num_heads_q *
+ * (head_dim + 2) > 1048576, or batch * num_heads_kv > 8192) fail with DU_EINVAL.
+ * The split count is reduced to fit the array.  The first call on a device
+ * resolves the array's device address (cudaGetSymbolAddress) for that device;
+ * make that first call before any stream capture.  Every call shares the array
+ * and clears its counters first; calls whose kernels overlap on the GPU race. */
+DU_API int du_flash_decode_noalloc(float *out, const float *q, const uint16_t *k_cache,
+                                   const uint16_t *v_cache, const int32_t *kv_len, int batch, int hq,
+                                   int hkv, int hd, int capacity, float scale, void *stream);
+
 /* IMP quantizers on the device, bit-exact with quantize_int8 / quantize_int4
  * (IMP:229-248); group is a parameter (reference G4 = 32). */
 DU_API int du_quantize_int8(const float *w, int64_t rows, int64_t cols, int8_t *q,
