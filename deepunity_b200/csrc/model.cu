@@ -293,7 +293,49 @@ static int copy2d(void *dst, size_t dst_pitch, const void *src, size_t src_pitch
     return DU_OK;
 }
 
-enum TensorKind { T_NONE, T_Q, T_K, T_V, T_O, T_GATE, T_UP, T_DOWN };
+enum TensorKind { T_NONE, T_Q, T_K, T_V, T_O, T_GATE, T_UP, T_DOWN, T_LMHEAD };
+
+// Tensor-parallel partition of one global tensor: its shape [rows, cols], the
+// window [r0, r1) x [c0, c1) this rank keeps, and where the window lands in the
+// rank's concatenated buffer (first row drow, row length dcols).
+//   q / k / v, gate / up : whole heads / rows, split by output rows
+//   o / down             : split by input columns (every row kept)
+//   lm_head              : vocab rows
+struct ShardWindow {
+    int64_t rows, cols, r0, r1, c0, c1, drow, dcols;
+};
+
+static int shard_window(const du_model_config &c, int tk, ShardWindow *w)
+{
+    const int tp = c.tp_size <= 0 ? 1 : c.tp_size, r = c.tp_rank;
+    const int64_t H = c.hidden_size, hd = c.head_dim, I = c.intermediate_size;
+    const int64_t hq_l = c.num_heads_q / tp, hkv_l = c.num_heads_kv / tp, I_l = I / tp, V_l = c.vocab_size / tp;
+    ShardWindow s = {};
+    switch (tk) {
+    case T_Q: s = {c.num_heads_q * hd, H, r * hq_l * hd, (r + 1) * hq_l * hd, 0, H, 0, H}; break;
+    case T_K: s = {c.num_heads_kv * hd, H, r * hkv_l * hd, (r + 1) * hkv_l * hd, 0, H, hq_l * hd, H}; break;
+    case T_V: s = {c.num_heads_kv * hd, H, r * hkv_l * hd, (r + 1) * hkv_l * hd, 0, H, (hq_l + hkv_l) * hd, H}; break;
+    case T_O: s = {H, c.num_heads_q * hd, 0, H, r * hq_l * hd, (r + 1) * hq_l * hd, 0, hq_l * hd}; break;
+    case T_GATE: s = {I, H, r * I_l, (r + 1) * I_l, 0, H, 0, H}; break;
+    case T_UP: s = {I, H, r * I_l, (r + 1) * I_l, 0, H, I_l, H}; break;
+    case T_DOWN: s = {H, I, 0, H, r * I_l, (r + 1) * I_l, 0, I_l}; break;
+    case T_LMHEAD: s = {c.vocab_size, H, r * V_l, (r + 1) * V_l, 0, H, 0, H}; break;
+    default: return fail(DU_ENOTFOUND, "unknown tensor kind");
+    }
+    *w = s;
+    return DU_OK;
+}
+
+static int tensor_kind_of(const char *stem)
+{
+    static const struct { const char *stem; int k; } stems[] = {
+        {"self_attn_q_proj", T_Q}, {"self_attn_k_proj", T_K}, {"self_attn_v_proj", T_V},
+        {"self_attn_o_proj", T_O}, {"mlp_gate_proj", T_GATE}, {"mlp_up_proj", T_UP}, {"mlp_down_proj", T_DOWN},
+        {"lm_head", T_LMHEAD}};
+    for (auto &s : stems)
+        if (strcmp(stem, s.stem) == 0) return s.k;
+    return T_NONE;
+}
 
 // Places one IMP tensor (weights, or its scales) into the sharded device layout.
 static int place_tensor(du_model *m, const char *name, const void *src, size_t bytes, cudaMemcpyKind kind)
@@ -354,27 +396,20 @@ static int place_tensor(du_model *m, const char *name, const void *src, size_t b
     if (is_scale && m->quant == DU_QUANT_FP16) return fail(DU_EINVAL, "fp16 model has no scales");
 
     // global shape [rows, cols], this rank's row/col window, destination
-    int64_t rows = 0, cols = 0, r0 = 0, r1 = 0, c0 = 0, c1 = 0, drow = 0;
+    ShardWindow sw;
+    int rc = shard_window(m->cfg, tk, &sw);
+    if (rc) return rc;
+    const int64_t rows = sw.rows, cols = sw.cols, r0 = sw.r0, r1 = sw.r1, c0 = sw.c0, c1 = sw.c1;
+    const int64_t drow = sw.drow, dcols = sw.dcols;
     uint8_t *dw = nullptr;
     __half *ds = nullptr;
-    int64_t dcols = 0;   // destination row length (elements)
     switch (tk) {
-    case T_Q: rows = (int64_t)m->hq * hd; cols = H; r0 = (int64_t)r * m->hq_l * hd; r1 = r0 + (int64_t)m->hq_l * hd;
-        c0 = 0; c1 = H; dw = ly.w_qkv; ds = ly.s_qkv; drow = 0; dcols = H; break;
-    case T_K: rows = (int64_t)m->hkv * hd; cols = H; r0 = (int64_t)r * m->hkv_l * hd; r1 = r0 + (int64_t)m->hkv_l * hd;
-        c0 = 0; c1 = H; dw = ly.w_qkv; ds = ly.s_qkv; drow = (int64_t)m->hq_l * hd; dcols = H; break;
-    case T_V: rows = (int64_t)m->hkv * hd; cols = H; r0 = (int64_t)r * m->hkv_l * hd; r1 = r0 + (int64_t)m->hkv_l * hd;
-        c0 = 0; c1 = H; dw = ly.w_qkv; ds = ly.s_qkv; drow = (int64_t)(m->hq_l + m->hkv_l) * hd; dcols = H; break;
-    case T_O: rows = H; cols = (int64_t)m->hq * hd; r0 = 0; r1 = H; c0 = (int64_t)r * m->hq_l * hd;
-        c1 = c0 + (int64_t)m->hq_l * hd; dw = ly.w_o; ds = ly.s_o; drow = 0; dcols = (int64_t)m->hq_l * hd; break;
-    case T_GATE: rows = m->I; cols = H; r0 = (int64_t)r * m->I_l; r1 = r0 + m->I_l; c0 = 0; c1 = H;
-        dw = ly.w_gu; ds = ly.s_gu; drow = 0; dcols = H; break;
-    case T_UP: rows = m->I; cols = H; r0 = (int64_t)r * m->I_l; r1 = r0 + m->I_l; c0 = 0; c1 = H;
-        dw = ly.w_gu; ds = ly.s_gu; drow = m->I_l; dcols = H; break;
-    case T_DOWN: rows = H; cols = m->I; r0 = 0; r1 = H; c0 = (int64_t)r * m->I_l; c1 = c0 + m->I_l;
-        dw = ly.w_d; ds = ly.s_d; drow = 0; dcols = m->I_l; break;
-    default: break;
+    case T_Q: case T_K: case T_V: dw = ly.w_qkv; ds = ly.s_qkv; break;
+    case T_O: dw = ly.w_o; ds = ly.s_o; break;
+    case T_GATE: case T_UP: dw = ly.w_gu; ds = ly.s_gu; break;
+    default: dw = ly.w_d; ds = ly.s_d; break;
     }
+    (void)hd; (void)r;
     if (!is_scale) {
         const int64_t need = qbytes(m->quant, rows, cols);
         DU_CHECK_ARG((int64_t)bytes == need, (std::string("size mismatch for ") + name).c_str());
@@ -1053,6 +1088,19 @@ DU_API int du_model_weight_bytes(du_model *m, uint64_t *out)
 {
     DU_CHECK_ARG(m && out, "du_model_weight_bytes: null argument");
     *out = m->weight_bytes;
+    return DU_OK;
+}
+
+DU_API int du_tp_shard_window(const du_model_config *cfg, const char *tensor, int64_t *out6)
+{
+    DU_CHECK_ARG(cfg && tensor && out6, "du_tp_shard_window: null argument");
+    int rc = check_cfg(*cfg);
+    if (rc) return rc;
+    const int tk = tensor_kind_of(tensor);
+    if (tk == T_NONE) return fail(DU_ENOTFOUND, std::string("du_tp_shard_window: unknown tensor ") + tensor);
+    ShardWindow w;
+    if ((rc = shard_window(*cfg, tk, &w))) return rc;
+    out6[0] = w.rows; out6[1] = w.cols; out6[2] = w.r0; out6[3] = w.r1; out6[4] = w.c0; out6[5] = w.c1;
     return DU_OK;
 }
 

@@ -112,6 +112,13 @@ DU_API int du_nccl_unique_id(void *out128);
  * polled against timeout_ms. */
 DU_API int du_tp_init(du_model *m, const void *nccl_unique_id, int timeout_ms);
 
+/* Host-only (no device work): the slice of a global tensor that rank
+ * cfg->tp_rank keeps.  tensor is a stem of IMP's file names
+ * ("self_attn_q_proj", ..., "mlp_down_proj") or "lm_head"; out6 = {rows, cols,
+ * r0, r1, c0, c1}: the global shape and the kept window [r0, r1) x [c0, c1).
+ * No reference counterpart (the reference is single-GPU). */
+DU_API int du_tp_shard_window(const du_model_config *cfg, const char *tensor, int64_t *out6);
+
 /* MiniCPM5Model.Forward(ids, useCache, lastPosOnly) (M5M:531-549): runs
  * `seq_len` tokens of each of `batch` sequences (ids [batch, seq_len], host),
  * appending to the KV cache when use_cache != 0.  logits_out (host, may be
