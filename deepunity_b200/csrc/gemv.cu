@@ -403,8 +403,8 @@ __global__ void __launch_bounds__(GV_THREADS) qgemv_kernel(const GemvParams p)
                             if (p.epi == EPI_LOGITS) {
                                 const float f = v[j][m];
                                 if (f > am_v[m]) { am_v[m] = f; am_i[m] = p.vocab_off + lr; }
-                                if (lane == j * MT + m && p.logits)
-                                    p.logits[(size_t)m * p.ldl + p.vocab_off + lr] = f;
+                                if (lane == j * MT + m && p.logits)   // local shard; the index carries the offset
+                                    p.logits[(size_t)m * p.ldl + lr] = f;
                             } else if (lane == j * MT + m) {
                                 float f = v[j][m];
                                 if (QT == Q_I8) f *= gv_row_scale<QT>(p, lr);

@@ -68,7 +68,8 @@ struct GemvParams {
     const int *seq_of;      // [M] sequence per token (nullptr: token m -> sequence m)
     int hq, hkv, hd, cap;
     const __half *rope_cos, *rope_sin;  // [cap][hd/2]
-    // EPI_LOGITS: logits[m][vocab_off + row] (optional) + per-CTA (max, argmax)
+    // EPI_LOGITS: logits[m][row] of this rank's vocab shard (optional) + per-CTA
+    // (max, argmax) with the global vocab index vocab_off + row
     float *logits;
     int ldl;
     float *am_val;          // [M][gridDim.x]
