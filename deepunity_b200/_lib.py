@@ -15,6 +15,7 @@ LIB_PATH = os.path.join(HERE, "libdeepunity_cuda.so")
 DU_OK, DU_EINVAL, DU_ECUDA, DU_ENOMEM, DU_EBUSY, DU_ENCCL, DU_ENOTFOUND, DU_ESTATE = range(8)
 QUANT_FP16, QUANT_INT8, QUANT_INT4 = 0, 1, 2
 DTYPE_F32, DTYPE_F16, DTYPE_BF16 = 0, 1, 2
+FLAG_NO_PERSISTENT = 1
 
 
 class DUError(RuntimeError):
@@ -30,7 +31,8 @@ class ModelConfig(C.Structure):
                 ("vocab_size", C.c_int32), ("rms_eps", C.c_float), ("rope_theta", C.c_float),
                 ("embed_scale", C.c_float), ("quant", C.c_int32), ("group_size", C.c_int32),
                 ("kv_capacity", C.c_int32), ("max_batch", C.c_int32), ("tp_rank", C.c_int32),
-                ("tp_size", C.c_int32), ("tie_embedding", C.c_int32), ("reserved", C.c_int32 * 5)]
+                ("tp_size", C.c_int32), ("tie_embedding", C.c_int32), ("flags", C.c_int32),
+                ("reserved", C.c_int32 * 4)]
 
 
 # name -> (restype, argtypes); every symbol of include/deepunity_cuda.h

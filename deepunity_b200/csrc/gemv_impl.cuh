@@ -1,0 +1,480 @@
+// gemv_impl.cuh -- device implementation of the decode GEMV (design notes in
+// gemv.cuh), shared by the standalone kernel (gemv.cu) and the persistent
+// decode-step kernel (decode_step.cu).
+//
+// A GEMV runs in two phases so that a persistent kernel can overlap them with a
+// grid barrier:
+//   prefetch(): compute this CTA / warp's share of the rows and issue the first
+//               D - 1 ring stages of weight (and INT4 scale) loads;
+//   run():      stage the activations (needs the producer's output), stream the
+//               rest of the weights through the ring, run the epilogues.
+#pragma once
+
+#include "gemv.cuh"
+
+namespace du {
+
+// FP16 path: physical float4 slot of logical float4 f of a token row
+// (conflict-free for the lane-chunk reads of the main loop).
+__device__ __forceinline__ int gv_swz16(int f) { return f ^ ((f >> 3) & 1); }
+
+// x_k (optionally RMSNorm'd: x * rms * (1 + gamma'_k)), computed identically
+// wherever it is needed
+__device__ __forceinline__ float gv_xval(const GemvParams &p, const float *xr, float inv, int k)
+{
+    float v = xr[k];
+    if (p.gamma != nullptr) v = v * inv * (1.0f + __half2float(p.gamma[k]));
+    return v;
+}
+
+// Stages the activations of the MT tokens in shared memory.
+//  INT4 / INT8: 22-bit fixed-point byte planes + zero-point sums, per-token shift
+//  FP16: fp32, swizzled
+template <int QT, int MT>
+__device__ void gv_stage_x(const GemvParams &p, uint4 *xq, float *xsumf, long long *xsum64, float *xscale,
+                           int nchunk, float *red)
+{
+    const int tid = threadIdx.x;
+    for (int m = 0; m < MT; m++) {
+        const float *xr = p.x + (size_t)m * p.ldx;
+        const bool live = m < p.M;
+        // one pass: sum of squares (RMSNorm) and max |x * (1 + gamma')| (fixed-point range)
+        float ss = 0.0f, mx = 0.0f;
+        if (live) {
+            for (int k4 = tid; k4 < (p.K >> 2); k4 += GV_THREADS) {
+                const float4 v = reinterpret_cast<const float4 *>(xr)[k4];
+                float g0 = 1.0f, g1 = 1.0f, g2 = 1.0f, g3 = 1.0f;
+                if (p.gamma != nullptr) {
+                    const __half2 *g2p = reinterpret_cast<const __half2 *>(p.gamma) + 2 * k4;
+                    const float2 a = __half22float2(g2p[0]), b = __half22float2(g2p[1]);
+                    g0 = 1.0f + a.x; g1 = 1.0f + a.y; g2 = 1.0f + b.x; g3 = 1.0f + b.y;
+                }
+                ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+                mx = fmaxf(mx, fmaxf(fmaxf(fabsf(v.x * g0), fabsf(v.y * g1)), fmaxf(fabsf(v.z * g2), fabsf(v.w * g3))));
+            }
+        }
+        {
+            const int lane = tid & 31, warp = tid >> 5;
+            ss = warp_sum(ss);
+            mx = warp_max(mx);
+            __syncthreads();
+            if (lane == 0) { red[warp] = ss; red[GV_WARPS + warp] = mx; }
+            __syncthreads();
+            ss = 0.0f; mx = 0.0f;
+#pragma unroll
+            for (int i = 0; i < GV_WARPS; i++) { ss += red[i]; mx = fmaxf(mx, red[GV_WARPS + i]); }
+        }
+        float inv = 1.0f;
+        if (p.gamma != nullptr) {
+            inv = 1.0f / sqrtf(ss / (float)p.K + p.eps);
+            mx *= inv * 1.0000002f;     // bound on max |normalised x| (rounding of the product order)
+        }
+        if (QT == Q_F16) {
+            float4 *xs = reinterpret_cast<float4 *>(xq) + (size_t)m * nchunk * 2;
+            for (int f = tid; f < nchunk * 2; f += GV_THREADS) {
+                float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+                if (live) {
+                    v.x = gv_xval(p, xr, inv, 4 * f);
+                    v.y = gv_xval(p, xr, inv, 4 * f + 1);
+                    v.z = gv_xval(p, xr, inv, 4 * f + 2);
+                    v.w = gv_xval(p, xr, inv, 4 * f + 3);
+                }
+                xs[gv_swz16(f)] = v;
+            }
+            continue;
+        }
+        // per-token power-of-two scale: max |x| * 2^s < 2^22 (so |x_int| < 2^23 always)
+        const int s = mx > 0.0f ? 21 - ilogbf(mx) : 0;
+        const float sc = ldexpf(1.0f, s);
+        if (tid == 0) xscale[m] = ldexpf(1.0f, -s);
+        uint32_t *xw = reinterpret_cast<uint32_t *>(xq) + (size_t)m * nchunk * GvTraits<QT>::XU4 * 4;
+        if (QT == Q_I4) {
+            // word-group g = 8 columns; chunk c = g / 4, slot wd = g % 4; words
+            // [P0 even, P0 odd, P1 even, P1 odd, P2 even, P2 odd] (even = columns 0,2,4,6)
+            const int ngroups = nchunk * 4;
+            for (int g0 = 0; g0 < ngroups; g0 += GV_THREADS) {
+                const int g = g0 + tid;
+                int part = 0;
+                if (g < ngroups) {
+                    uint32_t pe[3] = {0, 0, 0}, po[3] = {0, 0, 0};
+#pragma unroll
+                    for (int j = 0; j < 8; j++) {
+                        const int v = live ? __float2int_rn(gv_xval(p, xr, inv, 8 * g + j) * sc) : 0;
+                        part += v;
+                        const int sh = 8 * (j >> 1);
+                        uint32_t *dst = (j & 1) ? po : pe;
+                        dst[0] |= (uint32_t)(v & 0xFF) << sh;
+                        dst[1] |= (uint32_t)((v >> 8) & 0xFF) << sh;
+                        dst[2] |= (uint32_t)((v >> 16) & 0xFF) << sh;
+                    }
+                    const int c = g >> 2, wd = g & 3;
+                    uint32_t *o = xw + (size_t)c * GvTraits<QT>::XU4 * 4 + wd * 6;
+                    o[0] = pe[0]; o[1] = po[0]; o[2] = pe[1]; o[3] = po[1]; o[4] = pe[2]; o[5] = po[2];
+                }
+                // chunk sum over the 4 word-groups held by 4 consecutive lanes
+                part += __shfl_xor_sync(0xffffffffu, part, 1);
+                part += __shfl_xor_sync(0xffffffffu, part, 2);
+                if (g < ngroups && (g & 3) == 0) xsumf[(size_t)m * nchunk + (g >> 2)] = 8.0f * (float)part;
+            }
+        } else {
+            // word-group g = 4 columns; chunk c = g / 4, slot wd = g % 4; words [P0, P1, P2]
+            const int ngroups = nchunk * 4;
+            long long tot = 0;
+            for (int g = tid; g < ngroups; g += GV_THREADS) {
+                uint32_t pw[3] = {0, 0, 0};
+#pragma unroll
+                for (int j = 0; j < 4; j++) {
+                    const int v = live ? __float2int_rn(gv_xval(p, xr, inv, 4 * g + j) * sc) : 0;
+                    tot += v;
+                    pw[0] |= (uint32_t)(v & 0xFF) << (8 * j);
+                    pw[1] |= (uint32_t)((v >> 8) & 0xFF) << (8 * j);
+                    pw[2] |= (uint32_t)((v >> 16) & 0xFF) << (8 * j);
+                }
+                const int c = g >> 2, wd = g & 3;
+                uint32_t *o = xw + (size_t)c * GvTraits<QT>::XU4 * 4 + wd * 3;
+                o[0] = pw[0]; o[1] = pw[1]; o[2] = pw[2];
+            }
+            // exact block sum of the int64 totals (two 32-bit halves through fp-free shuffles)
+            for (int o = 16; o > 0; o >>= 1) tot += __shfl_xor_sync(0xffffffffu, tot, o);
+            __syncthreads();
+            long long *r64 = reinterpret_cast<long long *>(red);
+            if ((tid & 31) == 0) r64[tid >> 5] = tot;
+            __syncthreads();
+            if (tid == 0) {
+                long long t = 0;
+                for (int i = 0; i < GV_WARPS; i++) t += r64[i];
+                xsum64[m] = t;
+            }
+        }
+    }
+    __syncthreads();
+}
+
+__device__ __forceinline__ void gv_epi_pair(const GemvParams &p, int lr0, int m, float x1, float x2)
+{
+    if (p.epi == EPI_GATEUP) {
+        p.y[(size_t)m * p.ldy + (lr0 >> 1)] = (x1 / (1.0f + expf(-x1))) * x2;
+        return;
+    }
+    // EPI_QKV: rows (lr0, lr0 + 1) are the RoPE pair (i, i + hd/2) of one head
+    const int hd = p.hd, head = lr0 / hd, i = (lr0 - head * hd) >> 1;
+    const int pos = p.pos[m];
+    const int seq = p.seq_of ? p.seq_of[m] : m;
+    if (head < p.hq + p.hkv) {
+        const float c = __half2float(p.rope_cos[(size_t)pos * (hd >> 1) + i]);
+        const float s = __half2float(p.rope_sin[(size_t)pos * (hd >> 1) + i]);
+        const float r1 = x1 * c - x2 * s;
+        const float r2 = x2 * c + x1 * s;
+        x1 = r1;
+        x2 = r2;
+    }
+    if (head < p.hq) {
+        float *qo = p.q_out + (size_t)m * p.hq * hd + (size_t)head * hd;
+        qo[i] = x1;
+        qo[i + (hd >> 1)] = x2;
+    } else {
+        const bool isk = head < p.hq + p.hkv;
+        const int kh = isk ? head - p.hq : head - p.hq - p.hkv;
+        __half *dst = (isk ? p.k_cache : p.v_cache) + (((size_t)seq * p.cap + pos) * p.hkv + kh) * hd;
+        dst[i] = __float2half_rn(x1);
+        dst[i + (hd >> 1)] = __float2half_rn(x2);
+    }
+}
+
+template <int QT>
+__device__ __forceinline__ float gv_row_scale(const GemvParams &p, int lr)
+{
+    const int64_t pr = gv_map_row(p, lr);
+    return p.scale_f32 ? reinterpret_cast<const float *>(p.scales)[pr]
+                       : __half2float(reinterpret_cast<const __half *>(p.scales)[pr]);
+}
+
+
+// Shared-memory scratch a GEMV run needs besides the ring and activation stage.
+template <int MT>
+struct GemvShared {
+    float red[2 * GV_WARPS];
+    float xscale[MT];
+    long long xsum64[MT];
+    float amv[GV_WARPS][MT];
+    int ami[GV_WARPS][MT];
+};
+
+// Bytes of the per-CTA weight ring (all warps) for depth D.
+template <int QT, int RW, int D>
+__host__ __device__ constexpr size_t gemv_ring_bytes()
+{
+    return (size_t)GV_WARPS * D * RW * 32 * 16 + (QT == Q_I4 ? (size_t)GV_WARPS * D * RW * 32 * 4 : 0);
+}
+
+template <int QT, int MT, int RW, int D>
+struct GemvStream {
+    using T = GvTraits<QT>;
+    int lane, warp, nchunk, S, nsteps, g_begin, gshift;
+    int64_t srow_bytes;
+    uint4 *ring;          // this lane's slot 0 (weights)
+    uint32_t *sring;      // this lane's slot 0 (INT4 scales)
+    // issue side: (group, segment, ring slot) of the next step to fetch
+    int is_g, is_s, is_stage;
+    const uint8_t *iw[RW];
+    const uint8_t *isw[RW];
+    bool iv[RW];
+
+    __device__ __forceinline__ void set_issue_rows(const GemvParams &p)
+    {
+        const uint8_t *sbase = reinterpret_cast<const uint8_t *>(p.scales);
+#pragma unroll
+        for (int j = 0; j < RW; j++) {
+            const int lr = is_g * RW + j;
+            iv[j] = lr < p.N;
+            const int64_t pr = iv[j] ? gv_map_row(p, lr) : 0;
+            iw[j] = p.w + pr * p.row_bytes + lane * 16;
+            if (QT == Q_I4) isw[j] = sbase + pr * srow_bytes;
+        }
+    }
+
+    __device__ __forceinline__ void issue(const GemvParams &p, int i)
+    {
+        if (i < nsteps) {
+            const int c = is_s * 32 + lane;
+            const bool cv = c < nchunk;
+            // 4-byte word holding the fp16 scale of group (c * 32) >> gshift
+            const int sw_off = (((c * 32) >> gshift) * 2) & ~3;
+#pragma unroll
+            for (int j = 0; j < RW; j++) {
+                cp_async16_cg(ring + (is_stage * RW + j) * 32, iw[j] + (int64_t)is_s * 512, cv && iv[j]);
+                if (QT == Q_I4) cp_async4_ca(sring + (is_stage * RW + j) * 32, isw[j] + sw_off, cv && iv[j]);
+            }
+            if (++is_stage == D) is_stage = 0;
+            if (++is_s == S) {
+                is_s = 0;
+                is_g += GV_WARPS;
+                set_issue_rows(p);
+            }
+        }
+        cp_async_commit_group();
+    }
+
+    // Phase 1: work split (CTA `cta` of `ncta`) and the first D - 1 ring stages.
+    __device__ __forceinline__ void prefetch(const GemvParams &p, unsigned char *ring_smem, int cta, int ncta)
+    {
+        lane = threadIdx.x & 31;
+        warp = threadIdx.x >> 5;
+        nchunk = (int)(p.row_bytes >> 4);
+        S = (nchunk + 31) >> 5;                         // 512-byte segments per row
+        ring = reinterpret_cast<uint4 *>(ring_smem) + (size_t)warp * D * RW * 32 + lane;
+        sring = reinterpret_cast<uint32_t *>(reinterpret_cast<uint4 *>(ring_smem) + (size_t)GV_WARPS * D * RW * 32) +
+                (size_t)warp * D * RW * 32 + lane;
+        gshift = QT == Q_I4 ? __ffs(p.group) - 1 : 0;   // group is a power of two
+        srow_bytes = QT == Q_I4 ? ((int64_t)p.K >> gshift) * 2 : 0;
+        // contiguous range of row groups for this CTA, round-robin over its warps
+        const int NG = (p.N + RW - 1) / RW;
+        g_begin = (int)(((int64_t)cta * NG) / ncta);
+        const int g_end = (int)(((int64_t)(cta + 1) * NG) / ncta);
+        const int my_groups = g_end - g_begin > warp ? (g_end - g_begin - warp + GV_WARPS - 1) / GV_WARPS : 0;
+        nsteps = my_groups * S;
+        is_g = g_begin + warp;
+        is_s = 0;
+        is_stage = 0;
+        set_issue_rows(p);
+#pragma unroll
+        for (int j = 0; j < D - 1; j++) issue(p, j);
+    }
+
+    // Phase 2: activations -> smem, stream, epilogue.  All threads of the CTA call it.
+    // `after_stage` runs once the activations are staged (PDL trigger in the standalone kernel).
+    template <typename AfterStage>
+    __device__ __forceinline__ void run(const GemvParams &p, unsigned char *x_smem, GemvShared<MT> &sh, int cta,
+                                        int ncta, AfterStage after_stage)
+    {
+        uint4 *xq = reinterpret_cast<uint4 *>(x_smem);
+        float *xsumf = reinterpret_cast<float *>(xq + (size_t)MT * nchunk * T::XU4);
+        gv_stage_x<QT, MT>(p, xq, xsumf, sh.xsum64, sh.xscale, nchunk, sh.red);
+        after_stage();
+
+        // accumulators: INT8 exact int32 plane sums; INT4 / FP16 fp32
+        int s8[RW][MT][3];
+        float acc[RW][MT];
+#pragma unroll
+        for (int j = 0; j < RW; j++)
+#pragma unroll
+            for (int m = 0; m < MT; m++) {
+                acc[j][m] = 0.0f;
+                s8[j][m][0] = s8[j][m][1] = s8[j][m][2] = 0;
+            }
+        float am_v[MT];
+        int am_i[MT];
+#pragma unroll
+        for (int m = 0; m < MT; m++) { am_v[m] = -INFINITY; am_i[m] = 0x7fffffff; }
+
+        int cs_g = g_begin + warp, cs_s = 0, cs_stage = 0;     // compute side (group, segment, ring slot)
+        for (int i = 0; i < nsteps; i++) {
+            issue(p, i + D - 1);
+            cp_async_wait_group<D - 1>();
+            const int stage = cs_stage;
+            if (++cs_stage == D) cs_stage = 0;
+            uint4 wv[RW];
+#pragma unroll
+            for (int j = 0; j < RW; j++) wv[j] = ring[(stage * RW + j) * 32];
+            const int c = cs_s * 32 + lane;
+            if (c < nchunk) {
+                if (QT == Q_I4) {
+                    float d[RW];
+                    const int hsel = (((c * 32) >> gshift) & 1) * 16;
+#pragma unroll
+                    for (int j = 0; j < RW; j++)
+                        d[j] = __half2float(__ushort_as_half((unsigned short)(sring[(stage * RW + j) * 32] >> hsel)));
+#pragma unroll
+                    for (int m = 0; m < MT; m++) {
+                        const uint4 *xp = xq + ((size_t)m * nchunk + c) * T::XU4;
+                        uint32_t xw[24];
+#pragma unroll
+                        for (int q = 0; q < 6; q++) {
+                            const uint4 t = xp[q];
+                            xw[4 * q] = t.x; xw[4 * q + 1] = t.y; xw[4 * q + 2] = t.z; xw[4 * q + 3] = t.w;
+                        }
+                        const float xs8 = xsumf[(size_t)m * nchunk + c];
+#pragma unroll
+                        for (int j = 0; j < RW; j++) {
+                            // even / odd nibble streams accumulate separately (shorter dependency chains)
+                            int a0 = 0, a1 = 0, a2 = 0, b0 = 0, b1 = 0, b2 = 0;
+#pragma unroll
+                            for (int wd = 0; wd < 4; wd++) {
+                                const uint32_t w = wd == 0 ? wv[j].x : wd == 1 ? wv[j].y : wd == 2 ? wv[j].z : wv[j].w;
+                                const uint32_t lo = w & 0x0F0F0F0Fu, hi = (w >> 4) & 0x0F0F0F0Fu;
+                                a0 = dp4a_uu(lo, xw[wd * 6 + 0], a0);
+                                b0 = dp4a_uu(hi, xw[wd * 6 + 1], b0);
+                                a1 = dp4a_uu(lo, xw[wd * 6 + 2], a1);
+                                b1 = dp4a_uu(hi, xw[wd * 6 + 3], b1);
+                                a2 = dp4a_us(lo, xw[wd * 6 + 4], a2);
+                                b2 = dp4a_us(hi, xw[wd * 6 + 5], b2);
+                            }
+                            // sum n * x_int - 8 * sum x_int: planes 0 and 1 join exactly in int32
+                            // (< 2^25), plane 2 (< 2^19 in magnitude) is exact in fp32
+                            const int p01 = (a0 + b0) + ((a1 + b1) << 8);
+                            const float f = fmaf((float)(a2 + b2), 65536.0f, (float)p01) - xs8;
+                            acc[j][m] = fmaf(d[j], f, acc[j][m]);
+                        }
+                    }
+                } else if (QT == Q_I8) {
+#pragma unroll
+                    for (int m = 0; m < MT; m++) {
+                        const uint4 *xp = xq + ((size_t)m * nchunk + c) * T::XU4;
+                        const uint4 t0 = xp[0], t1 = xp[1], t2 = xp[2];
+                        const uint32_t xw[12] = {t0.x, t0.y, t0.z, t0.w, t1.x, t1.y, t1.z, t1.w, t2.x, t2.y, t2.z, t2.w};
+#pragma unroll
+                        for (int j = 0; j < RW; j++)
+#pragma unroll
+                            for (int wd = 0; wd < 4; wd++) {
+                                const uint32_t w = wd == 0 ? wv[j].x : wd == 1 ? wv[j].y : wd == 2 ? wv[j].z : wv[j].w;
+                                s8[j][m][0] = dp4a_su(w, xw[wd * 3 + 0], s8[j][m][0]);
+                                s8[j][m][1] = dp4a_su(w, xw[wd * 3 + 1], s8[j][m][1]);
+                                s8[j][m][2] = dp4a_ss(w, xw[wd * 3 + 2], s8[j][m][2]);
+                            }
+                    }
+                } else {
+#pragma unroll
+                    for (int m = 0; m < MT; m++) {
+                        const float4 *xm = reinterpret_cast<const float4 *>(xq) + (size_t)m * nchunk * 2;
+                        const float4 a = xm[gv_swz16(c * 2)];
+                        const float4 b = xm[gv_swz16(c * 2 + 1)];
+#pragma unroll
+                        for (int j = 0; j < RW; j++) {
+                            float2 part = make_float2(0.f, 0.f);
+                            gv_dot_f16(wv[j].x, a.x, a.y, part);
+                            gv_dot_f16(wv[j].y, a.z, a.w, part);
+                            gv_dot_f16(wv[j].z, b.x, b.y, part);
+                            gv_dot_f16(wv[j].w, b.z, b.w, part);
+                            acc[j][m] += part.x + part.y;
+                        }
+                    }
+                }
+            }
+            if (++cs_s == S) {
+                // ---- row group done: fold the lanes, epilogue, reset
+                float v[RW][MT];
+#pragma unroll
+                for (int j = 0; j < RW; j++)
+#pragma unroll
+                    for (int m = 0; m < MT; m++) {
+                        if (QT == Q_I8) {
+                            long long t0 = s8[j][m][0], t1 = s8[j][m][1], t2 = s8[j][m][2];
+#pragma unroll
+                            for (int o = 16; o > 0; o >>= 1) {
+                                t0 += __shfl_xor_sync(0xffffffffu, t0, o);
+                                t1 += __shfl_xor_sync(0xffffffffu, t1, o);
+                                t2 += __shfl_xor_sync(0xffffffffu, t2, o);
+                            }
+                            const long long tot = t0 + (t1 << 8) + (t2 << 16);   // exact sum q * x_int
+                            v[j][m] = (float)tot * sh.xscale[m];
+                            s8[j][m][0] = s8[j][m][1] = s8[j][m][2] = 0;
+                        } else {
+                            v[j][m] = warp_sum(acc[j][m]) * (QT == Q_I4 ? sh.xscale[m] : 1.0f);
+                            acc[j][m] = 0.0f;
+                        }
+                    }
+                const int lr0 = cs_g * RW;
+                if (p.epi == EPI_QKV || p.epi == EPI_GATEUP) {
+#pragma unroll
+                    for (int jp = 0; jp < RW; jp += 2)
+#pragma unroll
+                        for (int m = 0; m < MT; m++)
+                            if (lane == (jp / 2) * MT + m && m < p.M && lr0 + jp + 1 < p.N) {
+                                float x1 = v[jp][m], x2 = v[jp + 1][m];
+                                if (QT == Q_I8) {
+                                    x1 *= gv_row_scale<QT>(p, lr0 + jp);
+                                    x2 *= gv_row_scale<QT>(p, lr0 + jp + 1);
+                                }
+                                gv_epi_pair(p, lr0 + jp, m, x1, x2);
+                            }
+                } else {
+#pragma unroll
+                    for (int j = 0; j < RW; j++)
+#pragma unroll
+                        for (int m = 0; m < MT; m++) {
+                            const int lr = lr0 + j;
+                            if (m < p.M && lr < p.N) {
+                                if (p.epi == EPI_LOGITS) {
+                                    const float f = v[j][m];
+                                    if (f > am_v[m]) { am_v[m] = f; am_i[m] = p.vocab_off + lr; }
+                                    if (lane == j * MT + m && p.logits)   // local shard; the index carries the offset
+                                        p.logits[(size_t)m * p.ldl + lr] = f;
+                                } else if (lane == j * MT + m) {
+                                    float f = v[j][m];
+                                    if (QT == Q_I8) f *= gv_row_scale<QT>(p, lr);
+                                    if (p.epi == EPI_STORE) p.y[(size_t)m * p.ldy + lr] = f;
+                                    else p.y[(size_t)m * p.ldy + lr] += f;      // EPI_RESID
+                                }
+                            }
+                        }
+                }
+                cs_s = 0;
+                cs_g += GV_WARPS;
+            }
+        }
+        cp_async_wait_group<0>();
+
+        if (p.epi == EPI_LOGITS) {
+            // per-CTA (max, argmax): rows ascend within a warp, so '>' keeps the lowest index on ties
+            if (lane == 0)
+#pragma unroll
+                for (int m = 0; m < MT; m++) { sh.amv[warp][m] = am_v[m]; sh.ami[warp][m] = am_i[m]; }
+            __syncthreads();
+            const int tid = threadIdx.x;
+            if (tid < p.M && tid < MT) {
+                float bv = -INFINITY;
+                int bi = 0x7fffffff;
+                for (int w = 0; w < GV_WARPS; w++) {
+                    const float vv = sh.amv[w][tid];
+                    const int ix = sh.ami[w][tid];
+                    if (vv > bv || (vv == bv && ix < bi)) { bv = vv; bi = ix; }
+                }
+                p.am_val[(size_t)tid * ncta + cta] = bv;
+                p.am_idx[(size_t)tid * ncta + cta] = bi;
+            }
+            __syncthreads();
+        }
+    }
+};
+
+}  // namespace du

@@ -22,9 +22,11 @@
 #include <chrono>
 #include <vector>
 
+#include "attn_impl.cuh"
 #include "gemv.cuh"
 #include "internal.h"
 #include "nccl_shim.h"
+#include "step_plan.h"
 
 namespace du {
 
@@ -39,6 +41,8 @@ struct Layer {
 struct Graph {
     cudaGraph_t g = nullptr;
     cudaGraphExec_t exec = nullptr;
+    StepStage *d_stages = nullptr;   // stage list of the persistent decode-step kernel (device)
+    bool persistent = false;
 };
 
 }  // namespace du
@@ -78,6 +82,9 @@ struct du_model {
     int fd_nsplit_decode = 1;
     size_t fd_scratch_fl = 0;
     int *h_pin_ids = nullptr, *h_pin_next = nullptr;
+    unsigned *d_barrier = nullptr;          // grid-barrier counter of the persistent step kernel
+    int *d_err = nullptr;                   // its error word (barrier timeout)
+    int *h_pin_err = nullptr;
     std::vector<int> h_cache_len;
     std::map<int, du::Graph> graphs;
     int last_batch = 0, last_rows = 0;      // rows of logits written by the last call
@@ -236,7 +243,10 @@ static int model_alloc(du_model *m)
     }
     m->fd_scratch = (float *)dalloc(m, sizeof(float) * m->fd_scratch_fl, &rc);
     m->fd_counters = (unsigned *)dalloc(m, sizeof(unsigned) * (size_t)T * m->hkv_l, &rc);
+    m->d_barrier = (unsigned *)dalloc(m, sizeof(unsigned), &rc);
+    m->d_err = (int *)dalloc(m, sizeof(int), &rc);
     if (rc) return rc;
+    DU_CUDA_TRY(cudaMallocHost(&m->h_pin_err, sizeof(int)));
     DU_CUDA_TRY(cudaMallocHost(&m->h_pin_ids, sizeof(int) * T));
     DU_CUDA_TRY(cudaMallocHost(&m->h_pin_next, sizeof(int) * m->maxb));
     m->h_cache_len.assign(m->maxb, 0);
@@ -264,7 +274,10 @@ static void model_free(du_model *m)
     for (auto &kv : m->graphs) {
         if (kv.second.exec) cudaGraphExecDestroy(kv.second.exec);
         if (kv.second.g) cudaGraphDestroy(kv.second.g);
+        if (kv.second.d_stages) cudaFree(kv.second.d_stages);
     }
+    if (m->h_pin_err) cudaFreeHost(m->h_pin_err);
+    m->h_pin_err = nullptr;
     m->graphs.clear();
     if (m->comm) {
         const NcclApi *n = nccl_api();
@@ -524,31 +537,27 @@ enum Stage { ST_QKV = 0, ST_ATTN = 1, ST_O = 2, ST_GATEUP = 3, ST_DOWN = 4 };
 // One stage of layer l for the token rows of `io`.  With tensor parallelism
 // the O and down stages end in an allreduce of the partial sums plus the
 // residual add (collective = false leaves both out, for kernel timing).
-static int enqueue_stage(du_model *m, const StepIO &io, int l, int stage, bool collective)
+// GEMV parameters of stage `stage` of layer l for the token rows of `io`
+// (shared by the per-kernel path and the persistent decode-step plan).
+static GemvParams stage_gemv_params(du_model *m, const StepIO &io, int l, int stage)
 {
-    const int H = m->H, hd = m->hd, M = io.M, qt = qt_of(m->quant);
-    cudaStream_t st = m->stream;
+    const int H = m->H, hd = m->hd;
     const int64_t Ko = (int64_t)m->hq_l * hd;
     const Layer &ly = m->layers[l];
-    __half *kc = m->k_cache + (size_t)l * m->kv_layer_elems;
-    __half *vc = m->v_cache + (size_t)l * m->kv_layer_elems;
-    int rc = DU_OK;
     GemvParams p;
     switch (stage) {
     case ST_QKV:   // RMSNorm(ln1) -> QKV GEMV -> RoPE -> q, fp16 K/V into the cache
         p = gp_base(m, ly.w_qkv, ly.s_qkv, H);
         p.x = m->x_res; p.ldx = H; p.gamma = ly.ln1; p.eps = m->cfg.rms_eps;
         p.N = m->qkv_rows; p.map = MAP_ROPE_PAIR; p.map_hd = hd;
-        p.epi = EPI_QKV; p.q_out = m->q; p.k_cache = kc; p.v_cache = vc;
+        p.epi = EPI_QKV; p.q_out = m->q;
+        p.k_cache = m->k_cache + (size_t)l * m->kv_layer_elems;
+        p.v_cache = m->v_cache + (size_t)l * m->kv_layer_elems;
         p.pos = io.pos; p.seq_of = io.seq_of; p.hq = m->hq_l; p.hkv = m->hkv_l; p.hd = hd; p.cap = m->cap;
         p.rope_cos = m->rope_cos; p.rope_sin = m->rope_sin;
-        return run_gemv(m, qt, p, M);
-    case ST_ATTN:
-        return launch_flash_decode(m->q, kc, vc, io.seq_of, io.kv_len, io.kv_len_add, M, m->hq_l, m->hkv_l, hd,
-                                   m->cap, powf((float)hd, -0.5f), m->att, m->fd_scratch, m->fd_counters,
-                                   io.fd_nsplit, st);
+        break;
     case ST_O:
-    case ST_DOWN:  // O / down GEMV -> residual add (TP1) or partial sum -> allreduce -> add
+    case ST_DOWN:  // O / down GEMV -> residual add (TP1) or partial sum for the allreduce
         if (stage == ST_O) {
             p = gp_base(m, ly.w_o, ly.s_o, Ko);
             p.x = m->att; p.ldx = (int)Ko;
@@ -559,21 +568,78 @@ static int enqueue_stage(du_model *m, const StepIO &io, int l, int stage, bool c
         p.N = H; p.map = MAP_IDENT;
         if (m->tp == 1) { p.epi = EPI_RESID; p.y = m->x_res; p.ldy = H; }
         else { p.epi = EPI_STORE; p.y = m->part; p.ldy = H; }
-        if ((rc = run_gemv(m, qt, p, M))) return rc;
-        if (m->tp > 1 && collective) {
-            if ((rc = allreduce_sum(m, m->part, (size_t)M * H))) return rc;
-            if ((rc = launch_add_inplace(m->x_res, m->part, (size_t)M * H, st))) return rc;
-        }
-        return DU_OK;
-    case ST_GATEUP:  // RMSNorm(ln2) -> gate|up GEMV -> SiLU(g) * u
+        break;
+    default:       // ST_GATEUP: RMSNorm(ln2) -> gate|up GEMV -> SiLU(g) * u
         p = gp_base(m, ly.w_gu, ly.s_gu, H);
         p.x = m->x_res; p.ldx = H; p.gamma = ly.ln2; p.eps = m->cfg.rms_eps;
         p.N = 2 * m->I_l; p.map = MAP_GATEUP; p.map_I = m->I_l;
         p.epi = EPI_GATEUP; p.y = m->inter; p.ldy = m->I_l;
-        return run_gemv(m, qt, p, M);
-    default:
-        return fail(DU_EINVAL, "unknown stage");
+        break;
     }
+    p.M = io.M;
+    return p;
+}
+
+// Attention parameters of layer l (scratch split for `nsplit` splits of io.M rows).
+static FdParams stage_attn_params(du_model *m, const StepIO &io, int l, int nsplit, int *G)
+{
+    FdParams a;
+    const int g = m->hq_l / m->hkv_l;
+    a.q = m->q;
+    a.k_cache = m->k_cache + (size_t)l * m->kv_layer_elems;
+    a.v_cache = m->v_cache + (size_t)l * m->kv_layer_elems;
+    a.seq_of = io.seq_of;
+    a.kv_len = io.kv_len;
+    a.kv_len_add = io.kv_len_add;
+    a.hq = m->hq_l; a.hkv = m->hkv_l; a.cap = m->cap;
+    a.scale = powf((float)m->hd, -0.5f);
+    a.out = m->att;
+    a.part_o = m->fd_scratch;
+    a.part_ml = m->fd_scratch + (size_t)io.M * m->hkv_l * nsplit * g * m->hd;
+    a.counters = m->fd_counters;
+    *G = g;
+    return a;
+}
+
+// One stage of layer l for the token rows of `io`.  With tensor parallelism
+// the O and down stages end in an allreduce of the partial sums plus the
+// residual add (collective = false leaves both out, for kernel timing).
+static int enqueue_stage(du_model *m, const StepIO &io, int l, int stage, bool collective)
+{
+    const int H = m->H, hd = m->hd, M = io.M, qt = qt_of(m->quant);
+    cudaStream_t st = m->stream;
+    int rc = DU_OK;
+    if (stage == ST_ATTN) {
+        __half *kc = m->k_cache + (size_t)l * m->kv_layer_elems;
+        __half *vc = m->v_cache + (size_t)l * m->kv_layer_elems;
+        return launch_flash_decode(m->q, kc, vc, io.seq_of, io.kv_len, io.kv_len_add, M, m->hq_l, m->hkv_l, hd,
+                                   m->cap, powf((float)hd, -0.5f), m->att, m->fd_scratch, m->fd_counters,
+                                   io.fd_nsplit, st);
+    }
+    if (stage < ST_QKV || stage > ST_DOWN) return fail(DU_EINVAL, "unknown stage");
+    if ((rc = run_gemv(m, qt, stage_gemv_params(m, io, l, stage), M))) return rc;
+    if ((stage == ST_O || stage == ST_DOWN) && m->tp > 1 && collective) {
+        if ((rc = allreduce_sum(m, m->part, (size_t)M * H))) return rc;
+        if ((rc = launch_add_inplace(m->x_res, m->part, (size_t)M * H, st))) return rc;
+    }
+    return DU_OK;
+}
+
+// final RMSNorm + lm_head GEMV with logits and per-CTA argmax partials.  The
+// selected rows (every token, or the last token of each sequence) are read in
+// place: row i of the head input is x_res[logit_first + i * logit_stride].
+static GemvParams head_gemv_params(du_model *m, const StepIO &io)
+{
+    const int H = m->H;
+    GemvParams p = gp_base(m, (const uint8_t *)m->lm_head, nullptr, H);
+    p.row_bytes = 2LL * H;
+    p.x = m->x_res + (size_t)io.logit_first * H;
+    p.ldx = H * io.logit_stride;
+    p.gamma = m->final_norm; p.eps = m->cfg.rms_eps;
+    p.N = m->V_l; p.map = MAP_IDENT; p.epi = EPI_LOGITS;
+    p.logits = m->logits; p.ldl = m->V_l; p.vocab_off = m->rank * m->V_l;
+    p.M = io.logits_rows;
+    return p;
 }
 
 static int enqueue_head(du_model *m, const StepIO &io);
@@ -596,15 +662,7 @@ static int enqueue_head(du_model *m, const StepIO &io)
     cudaStream_t st = m->stream;
     int rc = DU_OK;
     const int R = io.logits_rows;
-    // the selected rows (every token, or the last token of each sequence) are read
-    // in place: row i of the head input is x_res[logit_first + i * logit_stride]
-    GemvParams p = gp_base(m, (const uint8_t *)m->lm_head, nullptr, H);
-    p.row_bytes = 2LL * H;
-    p.x = m->x_res + (size_t)io.logit_first * H;
-    p.ldx = H * io.logit_stride;
-    p.gamma = m->final_norm; p.eps = m->cfg.rms_eps;
-    p.N = m->V_l; p.map = MAP_IDENT; p.epi = EPI_LOGITS;
-    p.logits = m->logits; p.ldl = m->V_l; p.vocab_off = m->rank * m->V_l;
+    GemvParams p = head_gemv_params(m, io);
     const int nparts = gemv_grid_for(p.N, 1, m->am_parts);   // same CTA count for every token tile
     p.grid = nparts;
     const int mt = gemv_max_tokens(Q_F16, p.row_bytes);
@@ -689,6 +747,99 @@ static StepIO decode_io(du_model *m, int batch)
     return io;
 }
 
+// Stage list of the persistent decode-step kernel for the decode rows of `io`.
+// Fails (and the caller falls back to per-stage kernels) when the model asks for
+// that (DU_FLAG_NO_PERSISTENT), runs tensor-parallel, or the batch does not fit
+// one token tile / the shared-memory budget.
+static int build_step_plan(du_model *m, const StepIO &io, StepPlan *plan, int *qt_out, int *mt_out, size_t *smem_out,
+                           StepStage **d_stages)
+{
+    *d_stages = nullptr;
+    if ((m->cfg.flags & DU_FLAG_NO_PERSISTENT) || m->tp > 1 || io.M > 8) return DU_ESTATE;
+    const int qt = qt_of(m->quant);
+    const int mt = io.M <= 1 ? 1 : io.M <= 2 ? 2 : io.M <= 4 ? 4 : 8;
+    std::vector<StepStage> st;
+    StepStage s0 = {};
+    s0.type = SG_EMBED;
+    st.push_back(s0);
+    int nsplit = num_sms() / (io.M * m->hkv_l);
+    if (nsplit < 1) nsplit = 1;
+    if (nsplit > FD_MAXSPLIT) nsplit = FD_MAXSPLIT;
+    size_t xmax = (size_t)4 * FD_TILE * (m->hd + 8) * sizeof(__half);     // attention tiles alias the x stage
+    for (int l = 0; l < m->L; l++)
+        for (int sg = ST_QKV; sg <= ST_DOWN; sg++) {
+            StepStage s = {};
+            if (sg == ST_ATTN) {
+                s.type = SG_ATTN;
+                s.a = stage_attn_params(m, io, l, nsplit, &s.G);
+                s.nsplit = nsplit;
+                s.nq = io.M;
+            } else {
+                s.type = SG_GEMV;
+                s.qt = qt;
+                s.g = stage_gemv_params(m, io, l, sg);
+                const size_t xb = gemv_x_bytes(qt, mt, s.g.row_bytes);
+                if (xb > xmax) xmax = xb;
+            }
+            st.push_back(s);
+        }
+    StepStage hs = {};
+    hs.type = SG_GEMV;
+    hs.qt = Q_F16;
+    hs.g = head_gemv_params(m, io);
+    hs.g.am_val = m->am_val;
+    hs.g.am_idx = m->am_idx;
+    if (gemv_x_bytes(Q_F16, mt, hs.g.row_bytes) > xmax) xmax = gemv_x_bytes(Q_F16, mt, hs.g.row_bytes);
+    st.push_back(hs);
+    StepStage as = {};
+    as.type = SG_ARGMAX;
+    st.push_back(as);
+
+    const size_t ring = step_ring_bytes(qt, mt) > step_ring_bytes(Q_F16, mt) ? step_ring_bytes(qt, mt)
+                                                                             : step_ring_bytes(Q_F16, mt);
+    const size_t smem = ring + xmax;
+    if (smem > 200 * 1024) return DU_ESTATE;
+    if (qt == Q_I4 && ((m->H / m->group) % 2 || (m->I_l / m->group) % 2)) return DU_ESTATE;
+
+    DU_CUDA_TRY(cudaMalloc(d_stages, sizeof(StepStage) * st.size()));
+    DU_CUDA_TRY(cudaMemcpy(*d_stages, st.data(), sizeof(StepStage) * st.size(), cudaMemcpyHostToDevice));
+    StepPlan p = {};
+    p.nstages = (int)st.size();
+    p.stages = *d_stages;
+    p.ring_bytes = ring;
+    p.ids = io.ids;
+    p.embed = m->embed;
+    p.embed_scale = m->cfg.embed_scale;
+    p.M = io.M;
+    p.H = m->H;
+    p.x_res = m->x_res;
+    p.am_val = m->am_val;
+    p.am_idx = m->am_idx;
+    p.nparts = num_sms();
+    p.next_out = io.next_out;
+    p.feed = io.feed;
+    p.hist = m->d_hist;
+    p.cache_len = m->d_cache_len;
+    p.cap = m->cap;
+    p.advance = io.advance ? 1 : 0;
+    p.barrier = m->d_barrier;
+    p.err = m->d_err;
+    *plan = p;
+    *qt_out = qt;
+    *mt_out = mt;
+    *smem_out = smem;
+    return DU_OK;
+}
+
+// Reports (and clears) a barrier timeout of the persistent step kernel.
+static int check_step_error(du_model *m)
+{
+    if (*m->h_pin_err == 0) return DU_OK;
+    *m->h_pin_err = 0;
+    cudaMemset(m->d_err, 0, sizeof(int));
+    return fail(DU_ECUDA, "decode step: grid barrier timed out (kernel aborted)");
+}
+
 static int get_graph(du_model *m, int batch, cudaGraphExec_t *out, Graph **gout = nullptr)
 {
     auto it = m->graphs.find(batch);
@@ -699,11 +850,24 @@ static int get_graph(du_model *m, int batch, cudaGraphExec_t *out, Graph **gout 
     }
     const StepIO io = decode_io(m, batch);
     Graph g;
+    StepPlan plan;
+    int qt = 0, mt = 0;
+    size_t smem = 0;
+    const bool persistent = build_step_plan(m, io, &plan, &qt, &mt, &smem, &g.d_stages) == DU_OK;
     DU_CUDA_TRY(cudaStreamBeginCapture(m->stream, cudaStreamCaptureModeThreadLocal));
-    int rc = enqueue_forward(m, io);
+    int rc;
+    if (persistent) {
+        cudaError_t me = cudaMemsetAsync(m->d_barrier, 0, sizeof(unsigned), m->stream);
+        rc = me == cudaSuccess ? launch_decode_step(plan, qt, mt, m->hd, smem, m->stream)
+                               : cuda_fail(me, "cudaMemsetAsync");
+    } else {
+        rc = enqueue_forward(m, io);
+    }
     cudaError_t e = cudaStreamEndCapture(m->stream, &g.g);
+    g.persistent = persistent;
     if (rc) {
         if (g.g) cudaGraphDestroy(g.g);
+        if (g.d_stages) cudaFree(g.d_stages);
         return rc;
     }
     if (e != cudaSuccess) return cuda_fail(e, "cudaStreamEndCapture");
@@ -1022,7 +1186,13 @@ DU_API int du_decode_step(du_model *m, const int32_t *ids, int batch, int32_t *n
     DU_CUDA_TRY(cudaMemcpyAsync(m->d_ids, m->h_pin_ids, sizeof(int) * batch, cudaMemcpyHostToDevice, st));
     DU_CUDA_TRY(cudaGraphLaunch(exec, st));
     DU_CUDA_TRY(cudaMemcpyAsync(m->h_pin_next, m->d_next, sizeof(int) * batch, cudaMemcpyDeviceToHost, st));
+    DU_CUDA_TRY(cudaMemcpyAsync(m->h_pin_err, m->d_err, sizeof(int), cudaMemcpyDeviceToHost, st));
     DU_CUDA_TRY(cudaStreamSynchronize(st));
+    if ((rc = check_step_error(m))) {
+        sync_cache_len(m);   // the aborted step may or may not have advanced the device copy
+        cudaStreamSynchronize(st);
+        return rc;
+    }
     memcpy(next_ids, m->h_pin_next, sizeof(int) * batch);
     for (int b = 0; b < batch; b++) m->h_cache_len[b] += 1;
     m->last_batch = batch;
@@ -1051,7 +1221,13 @@ DU_API int du_decode_loop(du_model *m, const int32_t *ids, int batch, int n_step
     for (int b = 0; b < batch; b++)
         DU_CUDA_TRY(cudaMemcpyAsync(h.data() + (size_t)b * n_steps, m->d_hist + (size_t)b * m->cap + m->h_cache_len[b],
                                     sizeof(int) * n_steps, cudaMemcpyDeviceToHost, st));
+    DU_CUDA_TRY(cudaMemcpyAsync(m->h_pin_err, m->d_err, sizeof(int), cudaMemcpyDeviceToHost, st));
     DU_CUDA_TRY(cudaStreamSynchronize(st));
+    if ((rc = check_step_error(m))) {
+        sync_cache_len(m);
+        cudaStreamSynchronize(st);
+        return rc;
+    }
     for (int s = 0; s < n_steps; s++)
         for (int b = 0; b < batch; b++) tokens_out[(size_t)s * batch + b] = h[(size_t)b * n_steps + s];
     for (int b = 0; b < batch; b++) m->h_cache_len[b] += n_steps;

@@ -81,7 +81,7 @@ class LlamaForCausalLM(LLM):
     def __init__(self, config: LlamaConfig, quant: LLMQuant = LLMQuant.INT8, kv_quant: KVQuant = KVQuant.FP16,
                  max_context_length: int = 8192, max_batch: int = 1, params_path: Optional[str] = None,
                  seed: Optional[int] = 0, init_std: float = 0.02, device: int = 0,
-                 tp_rank: int = 0, tp_size: int = 1):
+                 tp_rank: int = 0, tp_size: int = 1, flags: int = 0):
         if kv_quant != KVQuant.FP16:
             raise NotImplementedError("only the fp16 KV cache is implemented (KVQuant.FP16)")
         self.config = config
@@ -98,6 +98,7 @@ class LlamaForCausalLM(LLM):
         cfg.quant, cfg.group_size = int(self.quant), config.group_size
         cfg.kv_capacity, cfg.max_batch = max_context_length, max_batch
         cfg.tp_rank, cfg.tp_size, cfg.tie_embedding = tp_rank, tp_size, int(config.tie_embedding)
+        cfg.flags = flags     # FLAG_NO_PERSISTENT: per-stage kernels instead of the persistent step kernel
         h = C.c_void_p()
         _lib.call("du_model_create", C.byref(cfg), C.byref(h))
         self._h = h

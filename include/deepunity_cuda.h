@@ -66,8 +66,15 @@ typedef struct du_model_config {
     int32_t tp_rank;         /* tensor-parallel rank / size (1 = single GPU) */
     int32_t tp_size;
     int32_t tie_embedding;   /* 1: lm_head = embedding */
-    int32_t reserved[5];
+    int32_t flags;           /* DU_FLAG_* */
+    int32_t reserved[4];
 } du_model_config;
+
+/* du_model_config.flags */
+enum {
+    DU_FLAG_NO_PERSISTENT = 1   /* decode steps as a graph of per-stage kernels instead of the
+                                   persistent decode-step kernel */
+};
 
 typedef struct du_model du_model;
 

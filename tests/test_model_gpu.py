@@ -9,7 +9,7 @@ import numpy as np
 import pytest
 import torch
 
-from deepunity_b200 import DUError, LlamaForCausalLM, LLMQuant
+from deepunity_b200 import DUError, LlamaForCausalLM, LLMQuant, _lib
 from oracle import oracle as orc
 from tests.modelgen import C4, MID, SMALL, ModelWeights, TestConfig
 
@@ -28,12 +28,16 @@ def relerr(a, b):
     return float(np.max(np.abs(a - b)) / max(np.max(np.abs(b)), 1e-30))
 
 
-def build(cfg: TestConfig, seed=0, cap=128, max_batch=1):
+def build(cfg: TestConfig, seed=0, cap=128, max_batch=1, flags=0):
     w = ModelWeights(cfg, seed=seed)
     q = {"int8": LLMQuant.INT8, "int4": LLMQuant.INT4, "fp16": LLMQuant.FP16}[cfg.quant]
-    m = LlamaForCausalLM(cfg.du_kwargs(), q, max_context_length=cap, max_batch=max_batch, seed=None)
+    m = LlamaForCausalLM(cfg.du_kwargs(), q, max_context_length=cap, max_batch=max_batch, seed=None, flags=flags)
     w.load_into(m)
     return w, m
+
+
+# decode steps: the persistent decode-step kernel (default) and the graph of per-stage kernels
+PATHS = {"persistent": 0, "per_stage": _lib.FLAG_NO_PERSISTENT}
 
 
 VARIANTS = [SMALL, MID,
@@ -42,9 +46,10 @@ VARIANTS = [SMALL, MID,
             TestConfig(256, 512, 2, 4, 4, 64, 1024, quant="fp16")]
 
 
+@pytest.mark.parametrize("path", list(PATHS))
 @pytest.mark.parametrize("cfg", VARIANTS, ids=lambda c: f"{c.quant}-h{c.hidden}-hd{c.hd}-g{c.group}")
-def test_prefill_then_greedy_64_matches_oracle(cfg):
-    w, m = build(cfg, cap=128)
+def test_prefill_then_greedy_64_matches_oracle(cfg, path):
+    w, m = build(cfg, cap=128, flags=PATHS[path])
     om = orc.OracleModel(w, capacity=128)
     prompt = np.random.default_rng(7).integers(0, cfg.vocab, 16).astype(np.int32)
     logits, nxt = m.forward(prompt[None, :])
