@@ -150,12 +150,12 @@ template <int QT, int MT, int HD>
 static int ds_launch(const StepPlan &plan, size_t smem, cudaStream_t st)
 {
     auto kern = decode_step_kernel<QT, MT, HD>;
-    static bool attr_set[64] = {};
+    static size_t attr_set[64] = {};        // dynamic smem already allowed, per device
     int dev = 0;
     cudaGetDevice(&dev);
-    if (!attr_set[dev & 63]) {
-        DU_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024));
-        attr_set[dev & 63] = true;
+    if (attr_set[dev & 63] < smem) {
+        DU_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+        attr_set[dev & 63] = smem;
     }
     int per_sm = 0;
     DU_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, DS_THREADS, smem));
