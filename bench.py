@@ -314,7 +314,22 @@ def run_ours(args):
     barrier()
     ms_e2e = max_over_ranks(max(ev0.elapsed_time(ev1), 1000.0 * t_host))
 
-    # ---- per-kernel device times (CUDA events on the model stream, all layers' weights)
+    # ---- stage times of the last step when it ran as the persistent decode-step kernel:
+    # globaltimer stamps at each grid-barrier exit (embed, L x [qkv, attn, o, gate|up, down], lm_head, argmax)
+    L = cfg.num_layers
+    st_buf = (C.c_float * (5 * L + 8))()
+    n_st = C.c_int()
+    _lib.call("du_model_stage_times", m.handle, st_buf, len(st_buf), C.byref(n_st))
+    stage_us = None
+    if n_st.value == 5 * L + 3:
+        v = [float(x) for x in st_buf[:n_st.value]]
+        per = [v[1 + 5 * l:1 + 5 * l + 5] for l in range(L)]
+        avg = lambda i: sum(p[i] for p in per) / L
+        stage_us = {"embed": round(v[0], 2), "qkv": round(avg(0), 2), "attn": round(avg(1), 2),
+                    "o_proj": round(avg(2), 2), "gate_up": round(avg(3), 2), "down": round(avg(4), 2),
+                    "lm_head": round(v[-2], 2), "argmax": round(v[-1], 2)}
+
+    # ---- per-kernel device times of the per-stage path (CUDA events, all layers' weights)
     kt = (C.c_float * 6)()
     _lib.call("du_model_kernel_times", m.handle, B, 2, kt)
     kt = [float(v) for v in kt]
@@ -325,7 +340,13 @@ def run_ours(args):
     I_l, H = cfg.intermediate_size // world, cfg.hidden_size
     g = cfg.group_size
     gu_bytes = 2 * I_l * H // 2 + 2 * I_l * (H // g) * 2 + B * H * 4 + B * I_l * 4
-    achieved = gu_bytes / (kt[3] / 1000.0) / 1e9
+    if stage_us is not None:
+        gu_ms = stage_us["gate_up"] / 1000.0
+        roof_kernel = "decode_step_kernel (persistent), gate|up INT4 GEMV stage incl. its grid barrier"
+    else:
+        gu_ms = kt[3]
+        roof_kernel = "qgemv_kernel gate|up INT4 GEMV (RMSNorm prologue, SiLU epilogue)"
+    achieved = gu_bytes / (gu_ms / 1000.0) / 1e9
     step_bytes = m.weight_bytes() + 2 * cfg.num_layers * B * (args.prompt + args.warmup + args.steps) * \
         (cfg.num_heads_kv // world) * cfg.head_dim * 2
     traffic = None
@@ -353,7 +374,9 @@ def run_ours(args):
                        "model": CONFIG if not args.layers else f"{CONFIG} (first {args.layers} layers, profiling)",
                        "global_batch": B, "seq_len": args.prompt,
                        "parallelism": f"tp{world}", "l2": "no flush: ~4.8 GB streamed per step >> 126 MB L2"},
-            "roofline": {"bound": "hbm", "kernel": "gate|up INT4 GEMV (RMSNorm prologue, SiLU epilogue)",
+            "decode_path": "persistent decode-step kernel" if stage_us else "graph of per-stage kernels",
+            "stage_us": stage_us,
+            "roofline": {"bound": "hbm", "kernel": roof_kernel,
                          "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "peak_kind": peak_kind, "traffic": traffic,
                          "algorithmic_bytes_per_launch": gu_bytes},

@@ -58,6 +58,7 @@ SIGNATURES = {
     "du_model_destroy": (I, [P]),
     "du_model_graph_info": (I, [P, I, C.POINTER(C.c_int), C.POINTER(C.c_int)]),
     "du_model_kernel_times": (I, [P, I, I, C.POINTER(C.c_float)]),
+    "du_model_stage_times": (I, [P, C.POINTER(C.c_float), I, C.POINTER(C.c_int)]),
     "du_gemv_q8": (I, [P, P, I, P, P, I, I, I, I, P]),
     "du_gemv_q4": (I, [P, P, I, P, P, I, I, I, I, P]),
     "du_gemv_f16": (I, [P, P, I, P, I, I, I, P]),

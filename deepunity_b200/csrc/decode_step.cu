@@ -30,6 +30,13 @@ constexpr int DS_THREADS = GV_THREADS;    // 8 warps
 constexpr int DS_D = 4;                   // ring depth
 constexpr unsigned DS_SPIN_LIMIT = 1u << 22;     // ~1-2 s of polling before giving up
 
+__device__ __forceinline__ unsigned long long globaltimer_ns()
+{
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+    return t;
+}
+
 __device__ __forceinline__ bool ds_grid_sync(unsigned *ctr, unsigned target, int *err)
 {
     __syncthreads();
@@ -68,6 +75,7 @@ __global__ void __launch_bounds__(DS_THREADS, 1) decode_step_kernel(const StepPl
     GemvStream<QT, MT, RW, DS_D> gq;       // weight stream of the model's linears
     bool gq_ready = false;                 // gq holds the prefetched next stage
     unsigned nbar = 0;
+    if (cta == 0 && tid == 0 && plan.stamps) plan.stamps[0] = globaltimer_ns();
 
     for (int s = 0; s < plan.nstages; s++) {
         const StepStage &st = plan.stages[s];
@@ -140,6 +148,7 @@ __global__ void __launch_bounds__(DS_THREADS, 1) decode_step_kernel(const StepPl
             nbar++;
             if (!ds_grid_sync(plan.barrier, nbar * (unsigned)ncta, plan.err)) break;
         }
+        if (cta == 0 && tid == 0 && plan.stamps) plan.stamps[s + 1] = globaltimer_ns();
     }
     asm volatile("cp.async.wait_all;" ::: "memory");
 }

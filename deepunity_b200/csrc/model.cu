@@ -85,6 +85,8 @@ struct du_model {
     unsigned *d_barrier = nullptr;          // grid-barrier counter of the persistent step kernel
     int *d_err = nullptr;                   // its error word (barrier timeout)
     int *h_pin_err = nullptr;
+    unsigned long long *d_stamps = nullptr; // per-stage timestamps of the last persistent step
+    int stamp_stages = 0;                   // stages of the step that wrote them
     std::vector<int> h_cache_len;
     std::map<int, du::Graph> graphs;
     int last_batch = 0, last_rows = 0;      // rows of logits written by the last call
@@ -245,6 +247,7 @@ static int model_alloc(du_model *m)
     m->fd_counters = (unsigned *)dalloc(m, sizeof(unsigned) * (size_t)T * m->hkv_l, &rc);
     m->d_barrier = (unsigned *)dalloc(m, sizeof(unsigned), &rc);
     m->d_err = (int *)dalloc(m, sizeof(int), &rc);
+    m->d_stamps = (unsigned long long *)dalloc(m, sizeof(unsigned long long) * (5 * (size_t)m->L + 8), &rc);
     if (rc) return rc;
     DU_CUDA_TRY(cudaMallocHost(&m->h_pin_err, sizeof(int)));
     DU_CUDA_TRY(cudaMallocHost(&m->h_pin_ids, sizeof(int) * T));
@@ -824,6 +827,8 @@ static int build_step_plan(du_model *m, const StepIO &io, StepPlan *plan, int *q
     p.advance = io.advance ? 1 : 0;
     p.barrier = m->d_barrier;
     p.err = m->d_err;
+    p.stamps = m->d_stamps;
+    m->stamp_stages = p.nstages;
     *plan = p;
     *qt_out = qt;
     *mt_out = mt;
@@ -1301,6 +1306,20 @@ DU_API int du_model_graph_info(du_model *m, int batch, int *kernel_nodes, int *t
     }
     *kernel_nodes = k;
     *total_nodes = (int)n;
+    return DU_OK;
+}
+
+DU_API int du_model_stage_times(du_model *m, float *us_out, int max_stages, int *n_out)
+{
+    DU_GUARD(m);
+    DU_CHECK_ARG(us_out && n_out && max_stages >= 0, "du_model_stage_times: bad arguments");
+    *n_out = 0;
+    if (m->stamp_stages <= 0) return DU_OK;
+    std::vector<unsigned long long> ts((size_t)m->stamp_stages + 1);
+    DU_CUDA_TRY(cudaMemcpy(ts.data(), m->d_stamps, sizeof(unsigned long long) * ts.size(), cudaMemcpyDeviceToHost));
+    const int n = m->stamp_stages < max_stages ? m->stamp_stages : max_stages;
+    for (int s = 0; s < n; s++) us_out[s] = (float)((double)(ts[s + 1] - ts[s]) * 1e-3);
+    *n_out = n;
     return DU_OK;
 }
 

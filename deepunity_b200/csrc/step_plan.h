@@ -36,6 +36,8 @@ struct StepPlan {
     // grid barrier
     unsigned *barrier;
     int *err;
+    // globaltimer (ns) when CTA 0 leaves each barrier: [0] kernel start, [s + 1] end of stage s
+    unsigned long long *stamps;
 };
 
 size_t step_ring_bytes(int qt, int mt);

@@ -170,6 +170,11 @@ DU_API int du_model_destroy(du_model *m);
  * rewrites the KV slot of the next position, which the next decode step
  * overwrites anyway. */
 DU_API int du_model_graph_info(du_model *m, int batch, int *kernel_nodes, int *total_nodes);
+/* Stage durations (microseconds, between consecutive grid-barrier exits of
+ * CTA 0) of the most recent decode step that ran as the persistent decode-step
+ * kernel: embed, then per layer QKV, attention, O, gate|up, down, then lm_head
+ * and argmax.  n_out = stages written (0 if no persistent step ran). */
+DU_API int du_model_stage_times(du_model *m, float *us_out, int max_stages, int *n_out);
 DU_API int du_model_kernel_times(du_model *m, int batch, int reps, float *ms_out);
 
 /* ------------------------------------------------ kernel-level entry points
