@@ -30,7 +30,7 @@ struct FdParams {
 
 // Shared memory of one unit: K/V tiles (dynamic, 4 * FD_TILE * (HD + 8) halves) + these.
 template <int HD>
-struct FdShared {
+struct __align__(16) FdShared {     // qs is read as float4
     float qs[FD_MAXG][HD];
     float ps[FD_TILE][FD_MAXG];              // scores, then probabilities
     float m[FD_MAXG], l[FD_MAXG], alpha[FD_MAXG];
@@ -48,47 +48,87 @@ __device__ __forceinline__ void fd_cp_commit() { asm volatile("cp.async.commit_g
 template <int N>
 __device__ __forceinline__ void fd_cp_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 
+// Positions of unit (row, kv head, split).
+struct FdGeom {
+    int kv_len, ns_act, start, end, ntiles;
+    const __half *kbase, *vbase;
+};
+
+template <int HD>
+__device__ __forceinline__ FdGeom fd_geom(const FdParams &p, int row, int kvh, int split, int nsplit)
+{
+    FdGeom g;
+    const int seq = p.seq_of ? p.seq_of[row] : row;
+    g.kv_len = p.kv_len[row] + p.kv_len_add;
+    // splits actually used for this length: at least one tile each
+    g.ns_act = max(1, min(nsplit, (g.kv_len + FD_TILE - 1) / FD_TILE));
+    int chunk = (g.kv_len + g.ns_act - 1) / g.ns_act;
+    chunk = (chunk + FD_TILE - 1) & ~(FD_TILE - 1);
+    g.start = split * chunk;
+    g.end = split < g.ns_act ? min(g.start + chunk, g.kv_len) : g.start;
+    g.ntiles = g.end > g.start ? (g.end - g.start + FD_TILE - 1) / FD_TILE : 0;
+    g.kbase = p.k_cache + ((size_t)seq * p.cap * p.hkv + kvh) * HD;
+    g.vbase = p.v_cache + ((size_t)seq * p.cap * p.hkv + kvh) * HD;
+    return g;
+}
+
+// cp.async of the K/V rows of tile t at positions [lo, hi) into buffer buf
+// (rows past the unit's end are zero-filled); one commit group.
+template <int HD, int NT>
+__device__ __forceinline__ void fd_load_rows(const FdParams &p, const FdGeom &g, int t, int buf, int lo, int hi,
+                                             unsigned char *tiles)
+{
+    constexpr int LDS = HD + 8;
+    constexpr int CPR = HD / 8;
+    auto Ks = reinterpret_cast<__half (*)[FD_TILE][LDS]>(tiles);
+    auto Vs = reinterpret_cast<__half (*)[FD_TILE][LDS]>(tiles + 2 * FD_TILE * LDS * 2);
+    const size_t pos_stride = (size_t)p.hkv * HD;
+    const int p0 = g.start + t * FD_TILE;
+    lo = max(lo, p0);
+    hi = min(hi, p0 + FD_TILE);
+    for (int i = threadIdx.x; i < (hi - lo) * CPR; i += NT) {
+        const int j = lo - p0 + i / CPR, c = i % CPR;
+        const int pos = p0 + j;
+        const bool ok = pos < g.end;
+        const size_t off = (size_t)(ok ? pos : 0) * pos_stride + c * 8;
+        fd_cp_async16(&Ks[buf][j][c * 8], g.kbase + off, ok);
+        fd_cp_async16(&Vs[buf][j][c * 8], g.vbase + off, ok);
+    }
+    fd_cp_commit();
+}
+
+// Loads, ahead of the producer of this step's K/V rows, the rows of tile 0 that
+// earlier steps wrote (positions below kv_len - new_rows).  The unit is then
+// run with pre_new = new_rows.
+template <int HD, int NT>
+__device__ __forceinline__ void fd_prefetch(const FdParams &p, int row, int kvh, int split, int nsplit, int new_rows,
+                                            unsigned char *tiles)
+{
+    const FdGeom g = fd_geom<HD>(p, row, kvh, split, nsplit);
+    if (g.ntiles > 0) fd_load_rows<HD, NT>(p, g, 0, 0, g.start, g.kv_len - new_rows, tiles);
+}
+
 // Processes unit (row, kvh, split) of a launch with `nsplit` splits per
 // (row, kv head).  The CTA that finishes the last split of a (row, kv head)
-// merges all splits into p.out.  All NT threads must call it.
+// merges all splits into p.out.  All NT threads must call it.  pre_new < 0:
+// nothing was prefetched; else fd_prefetch(..., new_rows = pre_new) ran and
+// only tile 0's rows from kv_len - pre_new on are loaded here.
 template <int HD, int NT>
 __device__ void fd_unit(const FdParams &p, int G, int row, int kvh, int split, int nsplit, unsigned char *tiles,
-                        FdShared<HD> &sh)
+                        FdShared<HD> &sh, int pre_new = -1)
 {
     constexpr int LDS = HD + 8;               // padded row (halves): conflict-free 16 B reads
-    constexpr int CPR = HD / 8;               // 16 B chunks per row
     constexpr int NW = NT / 32;
+    constexpr size_t TILE_BYTES = 4 * FD_TILE * LDS * 2;
     auto Ks = reinterpret_cast<__half (*)[FD_TILE][LDS]>(tiles);
     auto Vs = reinterpret_cast<__half (*)[FD_TILE][LDS]>(tiles + 2 * FD_TILE * LDS * 2);
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
 
-    const int seq = p.seq_of ? p.seq_of[row] : row;
-    const int kv_len = p.kv_len[row] + p.kv_len_add;
-    // splits actually used for this length: at least one tile each
-    const int ns_act = max(1, min(nsplit, (kv_len + FD_TILE - 1) / FD_TILE));
-    int chunk = (kv_len + ns_act - 1) / ns_act;
-    chunk = (chunk + FD_TILE - 1) & ~(FD_TILE - 1);
-    const int start = split * chunk;
-    const int end = split < ns_act ? min(start + chunk, kv_len) : start;
-    const int ntiles = end > start ? (end - start + FD_TILE - 1) / FD_TILE : 0;
+    const FdGeom geo = fd_geom<HD>(p, row, kvh, split, nsplit);
+    const int ns_act = geo.ns_act, start = geo.start, end = geo.end, ntiles = geo.ntiles;
 
-    const size_t pos_stride = (size_t)p.hkv * HD;
-    const __half *kbase = p.k_cache + ((size_t)seq * p.cap * p.hkv + kvh) * HD;
-    const __half *vbase = p.v_cache + ((size_t)seq * p.cap * p.hkv + kvh) * HD;
-    auto load_tile = [&](int t, int buf) {
-        const int p0 = start + t * FD_TILE;
-        for (int i = tid; i < FD_TILE * CPR; i += NT) {
-            const int j = i / CPR, c = i - j * CPR;
-            const int pos = p0 + j;
-            const bool ok = pos < end;
-            const size_t off = (size_t)(ok ? pos : 0) * pos_stride + c * 8;
-            fd_cp_async16(&Ks[buf][j][c * 8], kbase + off, ok);
-            fd_cp_async16(&Vs[buf][j][c * 8], vbase + off, ok);
-        }
-        fd_cp_commit();
-    };
-
-    if (ntiles > 0) load_tile(0, 0);
+    if (ntiles > 0)
+        fd_load_rows<HD, NT>(p, geo, 0, 0, pre_new < 0 ? start : geo.kv_len - pre_new, 0x7fffffff, tiles);
     for (int i = tid; i < G * HD; i += NT) {
         const int g = i / HD, d = i - g * HD;
         sh.qs[g][d] = p.q[((size_t)row * p.hq + kvh * G + g) * HD + d] * p.scale;
@@ -112,7 +152,7 @@ __device__ void fd_unit(const FdParams &p, int G, int row, int kvh, int split, i
 
     for (int t = 0; t < ntiles; t++) {
         const int buf = t & 1;
-        if (t + 1 < ntiles) { load_tile(t + 1, buf ^ 1); fd_cp_wait<1>(); }
+        if (t + 1 < ntiles) { fd_load_rows<HD, NT>(p, geo, t + 1, buf ^ 1, 0, 0x7fffffff, tiles); fd_cp_wait<1>(); }
         else { fd_cp_wait<0>(); }
         __syncthreads();
 
@@ -213,28 +253,42 @@ __device__ void fd_unit(const FdParams &p, int G, int row, int kvh, int split, i
         pm[0] = sh.m[tid];
         pm[1] = sh.l[tid];
     }
-    __threadfence();
+    // publish: the CTA's stores are ordered before thread 0's acq_rel add (bar.sync
+    // then atom.acq_rel.gpu); the last CTA's add also acquires the other splits' stores
     __syncthreads();
     if (tid == 0) {
-        const unsigned prev = atomicAdd(&p.counters[rk], 1u);
+        unsigned prev;
+        asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(prev) : "l"(&p.counters[rk]) : "memory");
         sh.last = (prev == (unsigned)nsplit - 1) ? 1u : 0u;
     }
     __syncthreads();
     if (!sh.last) return;
-    __threadfence();
 
     // ---- last CTA of this (row, kv head): log-sum-exp combine, fixed split order
     const float *pmb = p.part_ml + rk * nsplit * G * 2;
     const float *pob = p.part_o + rk * nsplit * G * HD;
+    const int per = G * HD;
+    if ((size_t)ns_act * (per + 2 * G) * 4 <= TILE_BYTES) {
+        // every split's (o, m, l) in one round of copies (the tiles are free now)
+        float *so = reinterpret_cast<float *>(tiles);
+        float *sml = so + (size_t)ns_act * per;
+        for (int i = tid; i < ns_act * per / 4; i += NT) fd_cp_async16(so + 4 * i, pob + 4 * i, true);
+        for (int i = tid; i < ns_act * G * 2; i += NT) sml[i] = __ldcg(pmb + i);
+        fd_cp_commit();
+        fd_cp_wait<0>();
+        __syncthreads();
+        pmb = sml;
+        pob = so;
+    }
     for (int g = warp; g < G; g += NW) {
         float M = FD_NEG;
-        for (int s = lane; s < ns_act; s += 32) M = fmaxf(M, __ldcg(&pmb[(s * G + g) * 2]));
+        for (int s = lane; s < ns_act; s += 32) M = fmaxf(M, pmb[(s * G + g) * 2]);
         M = warp_max(M);
         float L = 0.0f;
         for (int s = lane; s < ns_act; s += 32) {
-            const float w = expf(__ldcg(&pmb[(s * G + g) * 2]) - M);
+            const float w = expf(pmb[(s * G + g) * 2] - M);
             sh.w[g][s] = w;
-            L = fmaf(__ldcg(&pmb[(s * G + g) * 2 + 1]), w, L);
+            L = fmaf(pmb[(s * G + g) * 2 + 1], w, L);
         }
         L = warp_sum(L);
         if (lane == 0) sh.inv[g] = 1.0f / fmaxf(L, 1e-12f);
@@ -245,7 +299,7 @@ __device__ void fd_unit(const FdParams &p, int G, int row, int kvh, int split, i
         const float *po_gd = pob + g * HD + d;
         float O = 0.0f;
 #pragma unroll 4
-        for (int s = 0; s < ns_act; s++) O = fmaf(__ldcg(po_gd + (size_t)s * G * HD), sh.w[g][s], O);
+        for (int s = 0; s < ns_act; s++) O = fmaf(po_gd[(size_t)s * per], sh.w[g][s], O);
         p.out[((size_t)row * p.hq + kvh * G + g) * HD + d] = O * sh.inv[g];
     }
     if (tid == 0) p.counters[rk] = 0u;   // ready for the next launch / graph replay

@@ -33,7 +33,7 @@ static size_t x_bytes(int qt, int mt, int64_t row_bytes)
 {
     const int nchunk = (int)(row_bytes >> 4);
     const int xu4 = qt == Q_I4 ? 7 : qt == Q_I8 ? 3 : 2;
-    return (size_t)mt * nchunk * xu4 * 16 + (qt == Q_I4 ? (size_t)mt * nchunk * 4 : 0);
+    return (size_t)mt * nchunk * xu4 * 16;
 }
 
 static int choose_depth(int qt, int mt, int64_t row_bytes, int *cps)

@@ -19,14 +19,19 @@
 //    weight fetch overlaps the previous kernel's tail and this kernel's
 //    activation prologue.
 //  * INT4 / INT8: the activation vector is turned, once per CTA, into 22-bit
-//    fixed point (per-token power-of-two scale, |x_int| < 2^22) split into
-//    three byte planes laid out to match the nibble / byte order of a weight
-//    word.  A weight word then costs dp4a per plane: exact integer products,
-//    3 dp4a per 4 INT8 weights, 6 dp4a + 3 integer ops per 8 INT4 weights.
-//    INT8 (signed, no zero point) accumulates the whole row exactly in int32
-//    per plane and applies the row scale once; INT4 folds its zero point (8)
-//    through per-chunk sums of x_int and applies its group scale per
-//    32-column chunk.
+//    fixed point split into three byte planes laid out to match the nibble /
+//    byte order of a weight word.  A weight word then costs dp4a per plane:
+//    exact integer products, 3 dp4a per 4 INT8 weights, 6 dp4a + 3 integer
+//    ops per 8 INT4 weights.
+//    INT8 (signed, no zero point) uses one power-of-two scale per token,
+//    accumulates the whole row exactly in int32 per plane and applies the row
+//    scale once.  INT4 uses one power-of-two scale per 32-column chunk (found
+//    by the four lanes that convert the chunk, so staging is a single pass
+//    with no block-wide reduction), folds its zero point (8) through per-chunk
+//    sums of x_int and applies group scale x chunk scale per chunk.
+//  * RMSNorm (INT4 / FP16): x * (1 + gamma') is staged and the per-token
+//    1 / rms, a scalar, multiplies the folded dot product in the epilogue;
+//    the sum of squares is reduced alongside the conversion.
 //  * FP16 (lm_head): fp32 activations in smem, packed fma.rn.f32x2.
 //  * Each finished row group is folded with warp shuffles and its epilogue is
 //    run by the owning lanes.
@@ -161,6 +166,14 @@ __device__ __forceinline__ void cp_async4_ca(void *smem, const void *gmem, bool 
     const int n = valid ? 4 : 0;
     asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(s), "l"(gmem), "r"(n) : "memory");
 }
+// Round-to-nearest-even of v * sc for |v * sc| <= 2^22, sc a power of two:
+// the single rounding of v * sc + 1.5 * 2^23 leaves the integer in the low
+// mantissa bits (the same result as __float2int_rn(v * sc)).
+__device__ __forceinline__ int gv_rint_small(float v, float sc)
+{
+    return __float_as_int(fmaf(v, sc, 12582912.0f)) - 0x4B400000;
+}
+
 __device__ __forceinline__ void cp_async_commit_group() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 template <int N>
 __device__ __forceinline__ void cp_async_wait_group() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }

@@ -27,105 +27,69 @@ __device__ __forceinline__ float gv_xval(const GemvParams &p, const float *xr, f
     return v;
 }
 
+// Shared-memory scratch a GEMV run needs besides the ring and activation stage.
+template <int MT, int NW = GV_WARPS>
+struct __align__(16) GemvShared {
+    float red[2 * NW];
+    float ssq[NW][MT];   // per-warp sums of squares (RMSNorm)
+    float xscale[MT];          // per-token factor of the folded dot product
+    float amv[NW][MT];
+    int ami[NW][MT];
+};
+
 // Stages the activations of the MT tokens in shared memory.
-//  INT4 / INT8: 22-bit fixed-point byte planes + zero-point sums, per-token shift
-//  FP16: fp32, swizzled
-template <int QT, int MT>
-__device__ void gv_stage_x(const GemvParams &p, uint4 *xq, float *xsumf, long long *xsum64, float *xscale,
-                           int nchunk, float *red)
+//  INT4: one pass; per 32-column chunk 6 plane words x 4 word groups, then
+//        (8 * sum x_int, 2^-s) in the pad words 24, 25; xscale = 1 / rms (or 1)
+//  INT8: per-token power-of-two scale over the normalised x; xscale = 2^-s
+//  FP16: x * (1 + gamma') in fp32, swizzled; xscale = 1 / rms (or 1)
+template <int QT, int MT, int NW>
+__device__ void gv_stage_x(const GemvParams &p, uint4 *xq, GemvShared<MT, NW> &sh, int nchunk)
 {
-    const int tid = threadIdx.x;
-    for (int m = 0; m < MT; m++) {
-        const float *xr = p.x + (size_t)m * p.ldx;
-        const bool live = m < p.M;
-        // one pass: sum of squares (RMSNorm) and max |x * (1 + gamma')| (fixed-point range)
-        float ss = 0.0f, mx = 0.0f;
-        if (live) {
-            for (int k4 = tid; k4 < (p.K >> 2); k4 += GV_THREADS) {
-                const float4 v = reinterpret_cast<const float4 *>(xr)[k4];
-                float g0 = 1.0f, g1 = 1.0f, g2 = 1.0f, g3 = 1.0f;
-                if (p.gamma != nullptr) {
-                    const __half2 *g2p = reinterpret_cast<const __half2 *>(p.gamma) + 2 * k4;
-                    const float2 a = __half22float2(g2p[0]), b = __half22float2(g2p[1]);
-                    g0 = 1.0f + a.x; g1 = 1.0f + a.y; g2 = 1.0f + b.x; g3 = 1.0f + b.y;
+    constexpr int NT = NW * 32;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    if (QT == Q_I8) {
+        for (int m = 0; m < MT; m++) {
+            const float *xr = p.x + (size_t)m * p.ldx;
+            const bool live = m < p.M;
+            // sum of squares (RMSNorm) and max |x * (1 + gamma')| (fixed-point range)
+            float ss = 0.0f, mx = 0.0f;
+            if (live) {
+                for (int k4 = tid; k4 < (p.K >> 2); k4 += NT) {
+                    const float4 v = reinterpret_cast<const float4 *>(xr)[k4];
+                    float g0 = 1.0f, g1 = 1.0f, g2 = 1.0f, g3 = 1.0f;
+                    if (p.gamma != nullptr) {
+                        const __half2 *g2p = reinterpret_cast<const __half2 *>(p.gamma) + 2 * k4;
+                        const float2 a = __half22float2(g2p[0]), b = __half22float2(g2p[1]);
+                        g0 = 1.0f + a.x; g1 = 1.0f + a.y; g2 = 1.0f + b.x; g3 = 1.0f + b.y;
+                    }
+                    ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+                    mx = fmaxf(mx, fmaxf(fmaxf(fabsf(v.x * g0), fabsf(v.y * g1)), fmaxf(fabsf(v.z * g2), fabsf(v.w * g3))));
                 }
-                ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
-                mx = fmaxf(mx, fmaxf(fmaxf(fabsf(v.x * g0), fabsf(v.y * g1)), fmaxf(fabsf(v.z * g2), fabsf(v.w * g3))));
             }
-        }
-        {
-            const int lane = tid & 31, warp = tid >> 5;
             ss = warp_sum(ss);
             mx = warp_max(mx);
             __syncthreads();
-            if (lane == 0) { red[warp] = ss; red[GV_WARPS + warp] = mx; }
+            if (lane == 0) { sh.red[warp] = ss; sh.red[NW + warp] = mx; }
             __syncthreads();
             ss = 0.0f; mx = 0.0f;
 #pragma unroll
-            for (int i = 0; i < GV_WARPS; i++) { ss += red[i]; mx = fmaxf(mx, red[GV_WARPS + i]); }
-        }
-        float inv = 1.0f;
-        if (p.gamma != nullptr) {
-            inv = 1.0f / sqrtf(ss / (float)p.K + p.eps);
-            mx *= inv * 1.0000002f;     // bound on max |normalised x| (rounding of the product order)
-        }
-        if (QT == Q_F16) {
-            float4 *xs = reinterpret_cast<float4 *>(xq) + (size_t)m * nchunk * 2;
-            for (int f = tid; f < nchunk * 2; f += GV_THREADS) {
-                float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-                if (live) {
-                    v.x = gv_xval(p, xr, inv, 4 * f);
-                    v.y = gv_xval(p, xr, inv, 4 * f + 1);
-                    v.z = gv_xval(p, xr, inv, 4 * f + 2);
-                    v.w = gv_xval(p, xr, inv, 4 * f + 3);
-                }
-                xs[gv_swz16(f)] = v;
+            for (int i = 0; i < NW; i++) { ss += sh.red[i]; mx = fmaxf(mx, sh.red[NW + i]); }
+            float inv = 1.0f;
+            if (p.gamma != nullptr) {
+                inv = 1.0f / sqrtf(ss / (float)p.K + p.eps);
+                mx *= inv * 1.0000002f;     // bound on max |normalised x| (rounding of the product order)
             }
-            continue;
-        }
-        // per-token power-of-two scale: max |x| * 2^s < 2^22 (so |x_int| < 2^23 always)
-        const int s = mx > 0.0f ? 21 - ilogbf(mx) : 0;
-        const float sc = ldexpf(1.0f, s);
-        if (tid == 0) xscale[m] = ldexpf(1.0f, -s);
-        uint32_t *xw = reinterpret_cast<uint32_t *>(xq) + (size_t)m * nchunk * GvTraits<QT>::XU4 * 4;
-        if (QT == Q_I4) {
-            // word-group g = 8 columns; chunk c = g / 4, slot wd = g % 4; words
-            // [P0 even, P0 odd, P1 even, P1 odd, P2 even, P2 odd] (even = columns 0,2,4,6)
-            const int ngroups = nchunk * 4;
-            for (int g0 = 0; g0 < ngroups; g0 += GV_THREADS) {
-                const int g = g0 + tid;
-                int part = 0;
-                if (g < ngroups) {
-                    uint32_t pe[3] = {0, 0, 0}, po[3] = {0, 0, 0};
-#pragma unroll
-                    for (int j = 0; j < 8; j++) {
-                        const int v = live ? __float2int_rn(gv_xval(p, xr, inv, 8 * g + j) * sc) : 0;
-                        part += v;
-                        const int sh = 8 * (j >> 1);
-                        uint32_t *dst = (j & 1) ? po : pe;
-                        dst[0] |= (uint32_t)(v & 0xFF) << sh;
-                        dst[1] |= (uint32_t)((v >> 8) & 0xFF) << sh;
-                        dst[2] |= (uint32_t)((v >> 16) & 0xFF) << sh;
-                    }
-                    const int c = g >> 2, wd = g & 3;
-                    uint32_t *o = xw + (size_t)c * GvTraits<QT>::XU4 * 4 + wd * 6;
-                    o[0] = pe[0]; o[1] = po[0]; o[2] = pe[1]; o[3] = po[1]; o[4] = pe[2]; o[5] = po[2];
-                }
-                // chunk sum over the 4 word-groups held by 4 consecutive lanes
-                part += __shfl_xor_sync(0xffffffffu, part, 1);
-                part += __shfl_xor_sync(0xffffffffu, part, 2);
-                if (g < ngroups && (g & 3) == 0) xsumf[(size_t)m * nchunk + (g >> 2)] = 8.0f * (float)part;
-            }
-        } else {
+            // per-token power-of-two scale: max |x| * 2^s < 2^22
+            const int s = mx > 0.0f ? 21 - ilogbf(mx) : 0;
+            const float sc = ldexpf(1.0f, s);
+            if (tid == 0) sh.xscale[m] = ldexpf(1.0f, -s);
+            uint32_t *xw = reinterpret_cast<uint32_t *>(xq) + (size_t)m * nchunk * GvTraits<QT>::XU4 * 4;
             // word-group g = 4 columns; chunk c = g / 4, slot wd = g % 4; words [P0, P1, P2]
-            const int ngroups = nchunk * 4;
-            long long tot = 0;
-            for (int g = tid; g < ngroups; g += GV_THREADS) {
+            for (int g = tid; g < nchunk * 4; g += NT) {
                 uint32_t pw[3] = {0, 0, 0};
 #pragma unroll
                 for (int j = 0; j < 4; j++) {
                     const int v = live ? __float2int_rn(gv_xval(p, xr, inv, 4 * g + j) * sc) : 0;
-                    tot += v;
                     pw[0] |= (uint32_t)(v & 0xFF) << (8 * j);
                     pw[1] |= (uint32_t)((v >> 8) & 0xFF) << (8 * j);
                     pw[2] |= (uint32_t)((v >> 16) & 0xFF) << (8 * j);
@@ -134,18 +98,122 @@ __device__ void gv_stage_x(const GemvParams &p, uint4 *xq, float *xsumf, long lo
                 uint32_t *o = xw + (size_t)c * GvTraits<QT>::XU4 * 4 + wd * 3;
                 o[0] = pw[0]; o[1] = pw[1]; o[2] = pw[2];
             }
-            // exact block sum of the int64 totals (two 32-bit halves through fp-free shuffles)
-            for (int o = 16; o > 0; o >>= 1) tot += __shfl_xor_sync(0xffffffffu, tot, o);
-            __syncthreads();
-            long long *r64 = reinterpret_cast<long long *>(red);
-            if ((tid & 31) == 0) r64[tid >> 5] = tot;
-            __syncthreads();
-            if (tid == 0) {
-                long long t = 0;
-                for (int i = 0; i < GV_WARPS; i++) t += r64[i];
-                xsum64[m] = t;
+        }
+        __syncthreads();
+        return;
+    }
+
+    float ss[MT];
+#pragma unroll
+    for (int m = 0; m < MT; m++) {
+        ss[m] = 0.0f;
+        const float *xr = p.x + (size_t)m * p.ldx;
+        const bool live = m < p.M;
+        if (QT == Q_F16) {
+            float4 *xs = reinterpret_cast<float4 *>(xq) + (size_t)m * nchunk * 2;
+#pragma unroll 4
+            for (int f = tid; f < nchunk * 2; f += NT) {
+                float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+                if (live) {
+                    v = reinterpret_cast<const float4 *>(xr)[f];
+                    ss[m] += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+                    if (p.gamma != nullptr) {
+                        const __half2 *g2p = reinterpret_cast<const __half2 *>(p.gamma) + 2 * f;
+                        const float2 a = __half22float2(g2p[0]), b = __half22float2(g2p[1]);
+                        v.x *= 1.0f + a.x; v.y *= 1.0f + a.y; v.z *= 1.0f + b.x; v.w *= 1.0f + b.y;
+                    }
+                }
+                xs[gv_swz16(f)] = v;
+            }
+            continue;
+        }
+        // INT4: word-group g = 8 columns, 4 consecutive lanes convert one 32-column chunk.
+        // The loads of up to SB groups per thread are issued together (one round trip).
+        uint32_t *xw = reinterpret_cast<uint32_t *>(xq) + (size_t)m * nchunk * GvTraits<QT>::XU4 * 4;
+        const int ngroups = nchunk * 4;
+        constexpr int SB = 4;
+        for (int g0 = 0; g0 < ngroups; g0 += SB * NT) {
+            float4 xa[SB], xb[SB];
+            uint4 gw[SB];
+#pragma unroll
+            for (int b = 0; b < SB; b++) {
+                const int g = g0 + b * NT + tid;
+                xa[b] = xb[b] = make_float4(0.f, 0.f, 0.f, 0.f);
+                gw[b] = make_uint4(0u, 0u, 0u, 0u);     // gamma' = 0
+                if (live && g < ngroups) {
+                    xa[b] = reinterpret_cast<const float4 *>(xr)[2 * g];
+                    xb[b] = reinterpret_cast<const float4 *>(xr)[2 * g + 1];
+                    if (p.gamma != nullptr) gw[b] = reinterpret_cast<const uint4 *>(p.gamma)[g];
+                }
+            }
+#pragma unroll
+            for (int b = 0; b < SB; b++) {
+                const int g = g0 + b * NT + tid;
+                if (g0 + b * NT >= ngroups) break;      // uniform across the CTA
+                float v[8] = {xa[b].x, xa[b].y, xa[b].z, xa[b].w, xb[b].x, xb[b].y, xb[b].z, xb[b].w};
+#pragma unroll
+                for (int j = 0; j < 8; j++) ss[m] += v[j] * v[j];
+                if (p.gamma != nullptr) {
+                    const uint32_t gv4[4] = {gw[b].x, gw[b].y, gw[b].z, gw[b].w};
+#pragma unroll
+                    for (int j = 0; j < 4; j++) {
+                        const float2 gg = __half22float2(*reinterpret_cast<const __half2 *>(&gv4[j]));
+                        v[2 * j] *= 1.0f + gg.x;
+                        v[2 * j + 1] *= 1.0f + gg.y;
+                    }
+                }
+                float mx = 0.0f;
+#pragma unroll
+                for (int j = 0; j < 8; j++) mx = fmaxf(mx, fabsf(v[j]));
+                mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+                mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+                // chunk scale 2^s with max |v| * 2^s < 2^22 (s capped so 2^s and 2^-s stay normal)
+                int s = mx > 0.0f ? 21 - ilogbf(mx) : 0;
+                if (s > 126) s = 126;
+                const float sc = __int_as_float((127 + s) << 23);
+                int n[8], part = 0;
+#pragma unroll
+                for (int j = 0; j < 8; j++) {
+                    n[j] = gv_rint_small(v[j], sc);
+                    part += n[j];
+                }
+                part += __shfl_xor_sync(0xffffffffu, part, 1);
+                part += __shfl_xor_sync(0xffffffffu, part, 2);
+                if (g < ngroups) {
+                    // byte planes of the even (0,2,4,6) and odd (1,3,5,7) columns
+                    const uint32_t e01 = __byte_perm(n[0], n[2], 0x5140), e23 = __byte_perm(n[4], n[6], 0x5140);
+                    const uint32_t o01 = __byte_perm(n[1], n[3], 0x5140), o23 = __byte_perm(n[5], n[7], 0x5140);
+                    const uint32_t e2 = __byte_perm(__byte_perm(n[0], n[2], 0x0062), __byte_perm(n[4], n[6], 0x0062), 0x5410);
+                    const uint32_t o2 = __byte_perm(__byte_perm(n[1], n[3], 0x0062), __byte_perm(n[5], n[7], 0x0062), 0x5410);
+                    const int c = g >> 2, wd = g & 3;
+                    uint32_t *o = xw + (size_t)c * GvTraits<QT>::XU4 * 4 + wd * 6;
+                    o[0] = __byte_perm(e01, e23, 0x5410);
+                    o[1] = __byte_perm(o01, o23, 0x5410);
+                    o[2] = __byte_perm(e01, e23, 0x7632);
+                    o[3] = __byte_perm(o01, o23, 0x7632);
+                    o[4] = e2;
+                    o[5] = o2;
+                    if (wd == 0) {
+                        uint32_t *pad = xw + (size_t)c * GvTraits<QT>::XU4 * 4 + 24;
+                        pad[0] = __float_as_uint(8.0f * (float)part);
+                        pad[1] = __float_as_uint(__int_as_float((127 - s) << 23));
+                    }
+                }
             }
         }
+    }
+    // 1 / rms per token for the epilogue
+#pragma unroll
+    for (int m = 0; m < MT; m++) {
+        const float w = warp_sum(ss[m]);
+        if (lane == 0) sh.ssq[warp][m] = w;
+    }
+    __syncthreads();
+    if (tid < MT) {
+        float t = 0.0f;
+#pragma unroll
+        for (int i = 0; i < NW; i++) t += sh.ssq[i][tid];
+        sh.xscale[tid] = p.gamma != nullptr ? 1.0f / sqrtf(t / (float)p.K + p.eps) : 1.0f;
     }
     __syncthreads();
 }
@@ -190,46 +258,34 @@ __device__ __forceinline__ float gv_row_scale(const GemvParams &p, int lr)
 }
 
 
-// Shared-memory scratch a GEMV run needs besides the ring and activation stage.
-template <int MT>
-struct GemvShared {
-    float red[2 * GV_WARPS];
-    float xscale[MT];
-    long long xsum64[MT];
-    float amv[GV_WARPS][MT];
-    int ami[GV_WARPS][MT];
-};
 
 // Bytes of the per-CTA weight ring (all warps) for depth D.
-template <int QT, int RW, int D>
+template <int QT, int RW, int D, int NW = GV_WARPS>
 __host__ __device__ constexpr size_t gemv_ring_bytes()
 {
-    return (size_t)GV_WARPS * D * RW * 32 * 16 + (QT == Q_I4 ? (size_t)GV_WARPS * D * RW * 32 * 4 : 0);
+    return (size_t)NW * D * RW * 32 * 16 + (QT == Q_I4 ? (size_t)NW * D * RW * 32 * 4 : 0);
 }
 
-template <int QT, int MT, int RW, int D>
+template <int QT, int MT, int RW, int D, int NW = GV_WARPS>
 struct GemvStream {
     using T = GvTraits<QT>;
     int lane, warp, nchunk, S, nsteps, g_begin, gshift;
-    int64_t srow_bytes;
+    int row_bytes, srow_bytes;
+    const uint8_t *wbase;  // this lane's 16 bytes of physical row 0
+    const uint8_t *sbase;  // INT4 scales
     uint4 *ring;          // this lane's slot 0 (weights)
     uint32_t *sring;      // this lane's slot 0 (INT4 scales)
-    // issue side: (group, segment, ring slot) of the next step to fetch
+    // issue side: (group, segment, ring slot) of the next step to fetch, and the
+    // physical rows of that group (-1 past the last row)
     int is_g, is_s, is_stage;
-    const uint8_t *iw[RW];
-    const uint8_t *isw[RW];
-    bool iv[RW];
+    int ipr[RW];
 
     __device__ __forceinline__ void set_issue_rows(const GemvParams &p)
     {
-        const uint8_t *sbase = reinterpret_cast<const uint8_t *>(p.scales);
 #pragma unroll
         for (int j = 0; j < RW; j++) {
             const int lr = is_g * RW + j;
-            iv[j] = lr < p.N;
-            const int64_t pr = iv[j] ? gv_map_row(p, lr) : 0;
-            iw[j] = p.w + pr * p.row_bytes + lane * 16;
-            if (QT == Q_I4) isw[j] = sbase + pr * srow_bytes;
+            ipr[j] = lr < p.N ? (int)gv_map_row(p, lr) : -1;
         }
     }
 
@@ -242,13 +298,15 @@ struct GemvStream {
             const int sw_off = (((c * 32) >> gshift) * 2) & ~3;
 #pragma unroll
             for (int j = 0; j < RW; j++) {
-                cp_async16_cg(ring + (is_stage * RW + j) * 32, iw[j] + (int64_t)is_s * 512, cv && iv[j]);
-                if (QT == Q_I4) cp_async4_ca(sring + (is_stage * RW + j) * 32, isw[j] + sw_off, cv && iv[j]);
+                const int64_t r = ipr[j] < 0 ? 0 : ipr[j];
+                cp_async16_cg(ring + (is_stage * RW + j) * 32, wbase + r * row_bytes + is_s * 512, cv && ipr[j] >= 0);
+                if (QT == Q_I4)
+                    cp_async4_ca(sring + (is_stage * RW + j) * 32, sbase + r * srow_bytes + sw_off, cv && ipr[j] >= 0);
             }
             if (++is_stage == D) is_stage = 0;
             if (++is_s == S) {
                 is_s = 0;
-                is_g += GV_WARPS;
+                is_g += NW;
                 set_issue_rows(p);
             }
         }
@@ -263,15 +321,18 @@ struct GemvStream {
         nchunk = (int)(p.row_bytes >> 4);
         S = (nchunk + 31) >> 5;                         // 512-byte segments per row
         ring = reinterpret_cast<uint4 *>(ring_smem) + (size_t)warp * D * RW * 32 + lane;
-        sring = reinterpret_cast<uint32_t *>(reinterpret_cast<uint4 *>(ring_smem) + (size_t)GV_WARPS * D * RW * 32) +
+        sring = reinterpret_cast<uint32_t *>(reinterpret_cast<uint4 *>(ring_smem) + (size_t)NW * D * RW * 32) +
                 (size_t)warp * D * RW * 32 + lane;
         gshift = QT == Q_I4 ? __ffs(p.group) - 1 : 0;   // group is a power of two
-        srow_bytes = QT == Q_I4 ? ((int64_t)p.K >> gshift) * 2 : 0;
+        row_bytes = (int)p.row_bytes;
+        srow_bytes = QT == Q_I4 ? (p.K >> gshift) * 2 : 0;
+        wbase = p.w + lane * 16;
+        sbase = reinterpret_cast<const uint8_t *>(p.scales);
         // contiguous range of row groups for this CTA, round-robin over its warps
         const int NG = (p.N + RW - 1) / RW;
         g_begin = (int)(((int64_t)cta * NG) / ncta);
         const int g_end = (int)(((int64_t)(cta + 1) * NG) / ncta);
-        const int my_groups = g_end - g_begin > warp ? (g_end - g_begin - warp + GV_WARPS - 1) / GV_WARPS : 0;
+        const int my_groups = g_end - g_begin > warp ? (g_end - g_begin - warp + NW - 1) / NW : 0;
         nsteps = my_groups * S;
         is_g = g_begin + warp;
         is_s = 0;
@@ -284,12 +345,11 @@ struct GemvStream {
     // Phase 2: activations -> smem, stream, epilogue.  All threads of the CTA call it.
     // `after_stage` runs once the activations are staged (PDL trigger in the standalone kernel).
     template <typename AfterStage>
-    __device__ __forceinline__ void run(const GemvParams &p, unsigned char *x_smem, GemvShared<MT> &sh, int cta,
+    __device__ __forceinline__ void run(const GemvParams &p, unsigned char *x_smem, GemvShared<MT, NW> &sh, int cta,
                                         int ncta, AfterStage after_stage)
     {
         uint4 *xq = reinterpret_cast<uint4 *>(x_smem);
-        float *xsumf = reinterpret_cast<float *>(xq + (size_t)MT * nchunk * T::XU4);
-        gv_stage_x<QT, MT>(p, xq, xsumf, sh.xsum64, sh.xscale, nchunk, sh.red);
+        gv_stage_x<QT, MT, NW>(p, xq, sh, nchunk);
         after_stage();
 
         // accumulators: INT8 exact int32 plane sums; INT4 / FP16 fp32
@@ -333,7 +393,8 @@ struct GemvStream {
                             const uint4 t = xp[q];
                             xw[4 * q] = t.x; xw[4 * q + 1] = t.y; xw[4 * q + 2] = t.z; xw[4 * q + 3] = t.w;
                         }
-                        const float xs8 = xsumf[(size_t)m * nchunk + c];
+                        const uint2 pad = *reinterpret_cast<const uint2 *>(xp + 6);
+                        const float xs8 = __uint_as_float(pad.x), xcs = __uint_as_float(pad.y);
 #pragma unroll
                         for (int j = 0; j < RW; j++) {
                             // even / odd nibble streams accumulate separately (shorter dependency chains)
@@ -353,7 +414,7 @@ struct GemvStream {
                             // (< 2^25), plane 2 (< 2^19 in magnitude) is exact in fp32
                             const int p01 = (a0 + b0) + ((a1 + b1) << 8);
                             const float f = fmaf((float)(a2 + b2), 65536.0f, (float)p01) - xs8;
-                            acc[j][m] = fmaf(d[j], f, acc[j][m]);
+                            acc[j][m] = fmaf(d[j], f * xcs, acc[j][m]);
                         }
                     }
                 } else if (QT == Q_I8) {
@@ -409,7 +470,7 @@ struct GemvStream {
                             v[j][m] = (float)tot * sh.xscale[m];
                             s8[j][m][0] = s8[j][m][1] = s8[j][m][2] = 0;
                         } else {
-                            v[j][m] = warp_sum(acc[j][m]) * (QT == Q_I4 ? sh.xscale[m] : 1.0f);
+                            v[j][m] = warp_sum(acc[j][m]) * sh.xscale[m];
                             acc[j][m] = 0.0f;
                         }
                     }
@@ -449,7 +510,7 @@ struct GemvStream {
                         }
                 }
                 cs_s = 0;
-                cs_g += GV_WARPS;
+                cs_g += NW;
             }
         }
         cp_async_wait_group<0>();
@@ -464,7 +525,7 @@ struct GemvStream {
             if (tid < p.M && tid < MT) {
                 float bv = -INFINITY;
                 int bi = 0x7fffffff;
-                for (int w = 0; w < GV_WARPS; w++) {
+                for (int w = 0; w < NW; w++) {
                     const float vv = sh.amv[w][tid];
                     const int ix = sh.ami[w][tid];
                     if (vv > bv || (vv == bv && ix < bi)) { bv = vv; bi = ix; }

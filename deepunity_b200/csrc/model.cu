@@ -768,7 +768,7 @@ static int build_step_plan(du_model *m, const StepIO &io, StepPlan *plan, int *q
     int nsplit = num_sms() / (io.M * m->hkv_l);
     if (nsplit < 1) nsplit = 1;
     if (nsplit > FD_MAXSPLIT) nsplit = FD_MAXSPLIT;
-    size_t xmax = (size_t)4 * FD_TILE * (m->hd + 8) * sizeof(__half);     // attention tiles alias the x stage
+    size_t xmax = 16;
     for (int l = 0; l < m->L; l++)
         for (int sg = ST_QKV; sg <= ST_DOWN; sg++) {
             StepStage s = {};
@@ -777,6 +777,7 @@ static int build_step_plan(du_model *m, const StepIO &io, StepPlan *plan, int *q
                 s.a = stage_attn_params(m, io, l, nsplit, &s.G);
                 s.nsplit = nsplit;
                 s.nq = io.M;
+                s.a_new = 1;
             } else {
                 s.type = SG_GEMV;
                 s.qt = qt;
@@ -798,10 +799,13 @@ static int build_step_plan(du_model *m, const StepIO &io, StepPlan *plan, int *q
     as.type = SG_ARGMAX;
     st.push_back(as);
 
-    const size_t ring = step_ring_bytes(qt, mt) > step_ring_bytes(Q_F16, mt) ? step_ring_bytes(qt, mt)
-                                                                             : step_ring_bytes(Q_F16, mt);
+    const size_t ring_l = step_ring_bytes(qt, mt, ds_depth(mt));          // the layers' linears
+    const size_t ring_h = step_ring_bytes(Q_F16, mt, ds_head_depth(mt));  // lm_head
+    const size_t tiles = (size_t)4 * FD_TILE * (m->hd + 8) * sizeof(__half);    // attention K/V tiles alias the ring
+    size_t ring = ring_l > ring_h ? ring_l : ring_h;
+    if (tiles > ring) ring = tiles;
     const size_t smem = ring + xmax;
-    if (smem > 200 * 1024) return DU_ESTATE;
+    if (smem > step_smem_limit(qt, mt, m->hd)) return DU_ESTATE;
     if (qt == Q_I4 && ((m->H / m->group) % 2 || (m->I_l / m->group) % 2)) return DU_ESTATE;
 
     DU_CUDA_TRY(cudaMalloc(d_stages, sizeof(StepStage) * st.size()));

@@ -14,12 +14,13 @@ struct StepStage {
     GemvParams g;        // SG_GEMV
     FdParams a;          // SG_ATTN
     int G, nsplit, nq;   // SG_ATTN
+    int a_new;           // SG_ATTN: K/V rows per query row written by this step (loaded after the barrier)
 };
 
 struct StepPlan {
     int nstages;
     const StepStage *stages;     // device array
-    size_t ring_bytes;           // offset of the activation / attention-tile region
+    size_t ring_bytes;           // bytes of the ring / attention-tile region (the activation stage follows)
     // SG_EMBED
     const int *ids;
     const __half *embed;
@@ -40,7 +41,20 @@ struct StepPlan {
     unsigned long long *stamps;
 };
 
-size_t step_ring_bytes(int qt, int mt);
+// weight-ring depths of the persistent kernel: the model's linears per token
+// tile, and the fp16 lm_head
+#ifndef DU_STEP_RING_DEPTH
+#define DU_STEP_RING_DEPTH 4
+#endif
+#ifndef DU_STEP_HEAD_DEPTH
+#define DU_STEP_HEAD_DEPTH 4
+#endif
+__host__ __device__ constexpr int ds_depth(int) { return DU_STEP_RING_DEPTH; }
+__host__ __device__ constexpr int ds_head_depth(int) { return DU_STEP_HEAD_DEPTH; }
+
+size_t step_ring_bytes(int qt, int mt, int depth);
+// dynamic shared memory the persistent kernel of this configuration can be given
+size_t step_smem_limit(int qt, int mt, int hd);
 int launch_decode_step(const StepPlan &plan, int qt, int mt, int hd, size_t smem, cudaStream_t st);
 
 }  // namespace du
