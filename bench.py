@@ -47,6 +47,8 @@ def parse():
     ap.add_argument("--prompt", type=int, default=PROMPT)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--path", choices=["persistent", "per_stage"], default="persistent",
+                    help="decode step as one persistent kernel, or as a graph of per-stage kernels")
     ap.add_argument("--clock-sampler", choices=["nvml", "smi", "none"], default="nvml")
     ap.add_argument("--sweep", choices=["gemv", "attn"], default=None,
                     help="kernel sweeps (one JSON line per case): config-2 GEMV, config-3 flash-decode")
@@ -254,7 +256,8 @@ def run_ours(args):
     B = args.batch
     need = args.prompt + args.warmup + 2 * args.steps + 4
     m = LlamaForCausalLM(cfg, LLMQuant.INT4, max_context_length=max(CAPACITY, need), max_batch=B, seed=0,
-                         device=local, tp_rank=rank, tp_size=world)
+                         device=local, tp_rank=rank, tp_size=world,
+                         flags=_lib.FLAG_NO_PERSISTENT if args.path == "per_stage" else 0)
     if world > 1:
         uid = [None]
         if rank == 0:
@@ -340,22 +343,33 @@ def run_ours(args):
     I_l, H = cfg.intermediate_size // world, cfg.hidden_size
     g = cfg.group_size
     gu_bytes = 2 * I_l * H // 2 + 2 * I_l * (H // g) * 2 + B * H * 4 + B * I_l * 4
+    kv_read = 2 * cfg.num_layers * B * (args.prompt + args.warmup + args.steps) * \
+        (cfg.num_heads_kv // world) * cfg.head_dim * 2        # K and V rows read per step (mean length)
+    step_bytes = m.weight_bytes() + kv_read
+    step_ms = ms / args.steps
     if stage_us is not None:
-        gu_ms = stage_us["gate_up"] / 1000.0
-        roof_kernel = "decode_step_kernel (persistent), gate|up INT4 GEMV stage incl. its grid barrier"
+        # one launch per step: the roofline is the whole persistent kernel
+        roof_kernel = "decode_step_kernel (persistent; one launch = one decode step)"
+        roof_bytes, roof_ms = step_bytes, step_ms
     else:
-        gu_ms = kt[3]
         roof_kernel = "qgemv_kernel gate|up INT4 GEMV (RMSNorm prologue, SiLU epilogue)"
-    achieved = gu_bytes / (gu_ms / 1000.0) / 1e9
-    step_bytes = m.weight_bytes() + 2 * cfg.num_layers * B * (args.prompt + args.warmup + args.steps) * \
-        (cfg.num_heads_kv // world) * cfg.head_dim * 2
+        roof_bytes, roof_ms = gu_bytes, kt[3]
+    achieved = roof_bytes / (roof_ms / 1000.0) / 1e9
+    # DRAM bytes per launch of decode_step_kernel from ncu captures at two layer counts
+    # (traffic = fixed + per_layer * layers), scaled to this run's layer count
     traffic = None
-    prof = os.path.join(ROOT, "profiles", "gateup_gemv_traffic.json")
-    if os.path.exists(prof):
+    prof = os.path.join(ROOT, "profiles", "decode_step_traffic.json")
+    if stage_us is not None and os.path.exists(prof):
         try:
-            traffic = json.load(open(prof)).get("bytes_per_launch")
+            tj = json.load(open(prof))
+            traffic = int(tj["fixed_bytes"] + tj["per_layer_bytes"] * cfg.num_layers)
         except Exception:
             traffic = None
+    stage_roof = None
+    if stage_us is not None:
+        stage_roof = {"stage": "gate|up INT4 GEMV inside the persistent kernel (incl. its grid barrier)",
+                      "bytes": gu_bytes, "us": stage_us["gate_up"],
+                      "achieved_gbs": round(gu_bytes / (stage_us["gate_up"] * 1e-6) / 1e9, 1)}
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -379,10 +393,8 @@ def run_ours(args):
             "roofline": {"bound": "hbm", "kernel": roof_kernel,
                          "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "peak_kind": peak_kind, "traffic": traffic,
-                         "algorithmic_bytes_per_launch": gu_bytes},
-            "step_roofline": {"bytes_per_step_per_gpu": step_bytes,
-                              "achieved_gbs": round(step_bytes / (ms / args.steps / 1000.0) / 1e9, 1),
-                              "frac": round(step_bytes / (ms / args.steps / 1000.0) / 1e9 / peak, 4)},
+                         "algorithmic_bytes_per_launch": roof_bytes, "launch_ms": round(roof_ms, 5)},
+            "stage_roofline": stage_roof,
             "kernel_ms": dict(zip(["qkv", "attn", "o_proj", "gate_up", "down", "lm_head"],
                                   [round(v, 5) for v in kt])),
             "e2e": {"value": round(e2e, 2), "unit": "tok/s", "h2d_bytes_per_step": 4 * B,
