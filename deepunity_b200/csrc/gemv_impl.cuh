@@ -35,6 +35,7 @@ struct __align__(16) GemvShared {
     float xscale[MT];          // per-token factor of the folded dot product
     float amv[NW][MT];
     int ami[NW][MT];
+    float pbuf[NW][2][(MT == 1 ? 4 : 2) * MT];   // partial row groups split between warps (first / last)
 };
 
 // Stages the activations of the MT tokens in shared memory.
@@ -266,19 +267,29 @@ __host__ __device__ constexpr size_t gemv_ring_bytes()
     return (size_t)NW * D * RW * 32 * 16 + (QT == Q_I4 ? (size_t)NW * D * RW * 32 * 4 : 0);
 }
 
+// Work split: a CTA owns a contiguous range of row groups; their (group,
+// 512-byte segment) units, group-major, are cut into NW contiguous, equal
+// ranges, one per warp (split-K inside the CTA).  A group whose units fall to
+// several warps leaves per-warp partial sums in shared memory; the warp that
+// holds its last unit adds them in warp order (deterministic) and runs the
+// epilogue.
 template <int QT, int MT, int RW, int D, int NW = GV_WARPS>
 struct GemvStream {
     using T = GvTraits<QT>;
-    int lane, warp, nchunk, S, nsteps, g_begin, gshift;
+    int lane, warp, nchunk, S, gshift;
     int row_bytes, srow_bytes;
     const uint8_t *wbase;  // this lane's 16 bytes of physical row 0
     const uint8_t *sbase;  // INT4 scales
     uint4 *ring;          // this lane's slot 0 (weights)
     uint32_t *sring;      // this lane's slot 0 (INT4 scales)
-    // issue side: (group, segment, ring slot) of the next step to fetch, and the
-    // physical rows of that group (-1 past the last row)
-    int is_g, is_s, is_stage;
+    int g_begin, U;       // the CTA's first row group and its number of units
+    int u0, u1;           // this warp's units
+    // issue side: (group, segment, ring slot) of the next unit to fetch, units left,
+    // and the physical rows of that group (-1 past the last row)
+    int is_g, is_s, is_stage, is_left;
     int ipr[RW];
+
+    __device__ __forceinline__ int unit_lo(int w) const { return (int)(((int64_t)w * U) / NW); }
 
     __device__ __forceinline__ void set_issue_rows(const GemvParams &p)
     {
@@ -289,9 +300,9 @@ struct GemvStream {
         }
     }
 
-    __device__ __forceinline__ void issue(const GemvParams &p, int i)
+    __device__ __forceinline__ void issue(const GemvParams &p)
     {
-        if (i < nsteps) {
+        if (is_left > 0) {
             const int c = is_s * 32 + lane;
             const bool cv = c < nchunk;
             // 4-byte word holding the fp16 scale of group (c * 32) >> gshift
@@ -303,11 +314,12 @@ struct GemvStream {
                 if (QT == Q_I4)
                     cp_async4_ca(sring + (is_stage * RW + j) * 32, sbase + r * srow_bytes + sw_off, cv && ipr[j] >= 0);
             }
+            is_left--;
             if (++is_stage == D) is_stage = 0;
             if (++is_s == S) {
                 is_s = 0;
-                is_g += NW;
-                set_issue_rows(p);
+                is_g++;
+                if (is_left > 0) set_issue_rows(p);
             }
         }
         cp_async_commit_group();
@@ -328,18 +340,59 @@ struct GemvStream {
         srow_bytes = QT == Q_I4 ? (p.K >> gshift) * 2 : 0;
         wbase = p.w + lane * 16;
         sbase = reinterpret_cast<const uint8_t *>(p.scales);
-        // contiguous range of row groups for this CTA, round-robin over its warps
         const int NG = (p.N + RW - 1) / RW;
         g_begin = (int)(((int64_t)cta * NG) / ncta);
         const int g_end = (int)(((int64_t)(cta + 1) * NG) / ncta);
-        const int my_groups = g_end - g_begin > warp ? (g_end - g_begin - warp + NW - 1) / NW : 0;
-        nsteps = my_groups * S;
-        is_g = g_begin + warp;
-        is_s = 0;
+        U = (g_end - g_begin) * S;
+        u0 = unit_lo(warp);
+        u1 = unit_lo(warp + 1);
+        is_g = g_begin + u0 / S;
+        is_s = u0 % S;
+        is_left = u1 - u0;
         is_stage = 0;
-        set_issue_rows(p);
+        if (is_left > 0) set_issue_rows(p);
 #pragma unroll
-        for (int j = 0; j < D - 1; j++) issue(p, j);
+        for (int j = 0; j < D - 1; j++) issue(p);
+    }
+
+    // Epilogue of the finished row group starting at logical row lr0 (v: every lane holds every value).
+    __device__ __forceinline__ void epilogue(const GemvParams &p, int lr0, const float (&v)[RW][MT], float *am_v,
+                                             int *am_i) const
+    {
+        if (p.epi == EPI_QKV || p.epi == EPI_GATEUP) {
+#pragma unroll
+            for (int jp = 0; jp < RW; jp += 2)
+#pragma unroll
+                for (int m = 0; m < MT; m++)
+                    if (lane == (jp / 2) * MT + m && m < p.M && lr0 + jp + 1 < p.N) {
+                        float x1 = v[jp][m], x2 = v[jp + 1][m];
+                        if (QT == Q_I8) {
+                            x1 *= gv_row_scale<QT>(p, lr0 + jp);
+                            x2 *= gv_row_scale<QT>(p, lr0 + jp + 1);
+                        }
+                        gv_epi_pair(p, lr0 + jp, m, x1, x2);
+                    }
+        } else {
+#pragma unroll
+            for (int j = 0; j < RW; j++)
+#pragma unroll
+                for (int m = 0; m < MT; m++) {
+                    const int lr = lr0 + j;
+                    if (m < p.M && lr < p.N) {
+                        if (p.epi == EPI_LOGITS) {
+                            const float f = v[j][m];
+                            const int ix = p.vocab_off + lr;    // global index; the shard write is local
+                            if (f > am_v[m] || (f == am_v[m] && ix < am_i[m])) { am_v[m] = f; am_i[m] = ix; }
+                            if (lane == j * MT + m && p.logits) p.logits[(size_t)m * p.ldl + lr] = f;
+                        } else if (lane == j * MT + m) {
+                            float f = v[j][m];
+                            if (QT == Q_I8) f *= gv_row_scale<QT>(p, lr);
+                            if (p.epi == EPI_STORE) p.y[(size_t)m * p.ldy + lr] = f;
+                            else p.y[(size_t)m * p.ldy + lr] += f;      // EPI_RESID
+                        }
+                    }
+                }
+        }
     }
 
     // Phase 2: activations -> smem, stream, epilogue.  All threads of the CTA call it.
@@ -367,9 +420,13 @@ struct GemvStream {
 #pragma unroll
         for (int m = 0; m < MT; m++) { am_v[m] = -INFINITY; am_i[m] = 0x7fffffff; }
 
-        int cs_g = g_begin + warp, cs_s = 0, cs_stage = 0;     // compute side (group, segment, ring slot)
-        for (int i = 0; i < nsteps; i++) {
-            issue(p, i + D - 1);
+        // compute side (group, segment, ring slot)
+        int cs_g = g_begin + u0 / S, cs_s = u0 % S, cs_stage = 0;
+        const int first_g = cs_g;
+        const bool first_whole = cs_s == 0;       // this warp starts its first group at segment 0
+        const int n = u1 - u0;
+        for (int i = 0; i < n; i++) {
+            issue(p);
             cp_async_wait_group<D - 1>();
             const int stage = cs_stage;
             if (++cs_stage == D) cs_stage = 0;
@@ -451,8 +508,9 @@ struct GemvStream {
                     }
                 }
             }
-            if (++cs_s == S) {
-                // ---- row group done: fold the lanes, epilogue, reset
+            const bool end_g = ++cs_s == S;
+            if (end_g || i == n - 1) {
+                // ---- this warp's part of row group cs_g is done: fold the lanes, reset
                 float v[RW][MT];
 #pragma unroll
                 for (int j = 0; j < RW; j++)
@@ -474,49 +532,47 @@ struct GemvStream {
                             acc[j][m] = 0.0f;
                         }
                     }
-                const int lr0 = cs_g * RW;
-                if (p.epi == EPI_QKV || p.epi == EPI_GATEUP) {
-#pragma unroll
-                    for (int jp = 0; jp < RW; jp += 2)
-#pragma unroll
-                        for (int m = 0; m < MT; m++)
-                            if (lane == (jp / 2) * MT + m && m < p.M && lr0 + jp + 1 < p.N) {
-                                float x1 = v[jp][m], x2 = v[jp + 1][m];
-                                if (QT == Q_I8) {
-                                    x1 *= gv_row_scale<QT>(p, lr0 + jp);
-                                    x2 *= gv_row_scale<QT>(p, lr0 + jp + 1);
-                                }
-                                gv_epi_pair(p, lr0 + jp, m, x1, x2);
-                            }
-                } else {
+                if (end_g && (cs_g != first_g || first_whole)) {
+                    epilogue(p, cs_g * RW, v, am_v, am_i);            // the whole group was this warp's
+                } else if (lane == 0) {
+                    float *pb = sh.pbuf[warp][cs_g == first_g ? 0 : 1];
 #pragma unroll
                     for (int j = 0; j < RW; j++)
 #pragma unroll
-                        for (int m = 0; m < MT; m++) {
-                            const int lr = lr0 + j;
-                            if (m < p.M && lr < p.N) {
-                                if (p.epi == EPI_LOGITS) {
-                                    const float f = v[j][m];
-                                    if (f > am_v[m]) { am_v[m] = f; am_i[m] = p.vocab_off + lr; }
-                                    if (lane == j * MT + m && p.logits)   // local shard; the index carries the offset
-                                        p.logits[(size_t)m * p.ldl + lr] = f;
-                                } else if (lane == j * MT + m) {
-                                    float f = v[j][m];
-                                    if (QT == Q_I8) f *= gv_row_scale<QT>(p, lr);
-                                    if (p.epi == EPI_STORE) p.y[(size_t)m * p.ldy + lr] = f;
-                                    else p.y[(size_t)m * p.ldy + lr] += f;      // EPI_RESID
-                                }
-                            }
-                        }
+                        for (int m = 0; m < MT; m++) pb[j * MT + m] = v[j][m];
                 }
-                cs_s = 0;
-                cs_g += NW;
+                if (end_g) {
+                    cs_s = 0;
+                    cs_g++;
+                }
             }
         }
         cp_async_wait_group<0>();
 
+        // groups split between warps: the holder of a group's last unit (which started the
+        // group past segment 0) adds the parts of every contributing warp in warp order
+        __syncthreads();
+        if (n > 0 && !first_whole && u1 > (u0 / S) * S + S - 1) {
+            const int gl = u0 / S;
+            float v[RW][MT];
+#pragma unroll
+            for (int j = 0; j < RW; j++)
+#pragma unroll
+                for (int m = 0; m < MT; m++) v[j][m] = 0.0f;
+            for (int w = 0; w <= warp; w++) {
+                const int lo = unit_lo(w), hi = unit_lo(w + 1);
+                if (hi <= lo || hi <= gl * S || lo >= gl * S + S) continue;    // empty, or not in this group
+                const float *pb = sh.pbuf[w][lo / S == gl ? 0 : 1];
+#pragma unroll
+                for (int j = 0; j < RW; j++)
+#pragma unroll
+                    for (int m = 0; m < MT; m++) v[j][m] += pb[j * MT + m];
+            }
+            epilogue(p, (g_begin + gl) * RW, v, am_v, am_i);
+        }
+
         if (p.epi == EPI_LOGITS) {
-            // per-CTA (max, argmax): rows ascend within a warp, so '>' keeps the lowest index on ties
+            // per-CTA (max, argmax); ties keep the lowest index
             if (lane == 0)
 #pragma unroll
                 for (int m = 0; m < MT; m++) { sh.amv[warp][m] = am_v[m]; sh.ami[warp][m] = am_i[m]; }

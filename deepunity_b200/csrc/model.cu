@@ -831,6 +831,7 @@ static int build_step_plan(du_model *m, const StepIO &io, StepPlan *plan, int *q
     p.advance = io.advance ? 1 : 0;
     p.barrier = m->d_barrier;
     p.err = m->d_err;
+
     p.stamps = m->d_stamps;
     m->stamp_stages = p.nstages;
     *plan = p;
