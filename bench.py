@@ -47,12 +47,12 @@ def parse():
     ap.add_argument("--prompt", type=int, default=PROMPT)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--path", choices=["persistent", "per_stage"], default="persistent",
+    ap.add_argument("--path", choices=["persistent", "per_stage"], default="per_stage",
                     help="decode step as one persistent kernel, or as a graph of per-stage kernels")
     ap.add_argument("--clock-sampler", choices=["nvml", "smi", "none"], default="nvml")
     ap.add_argument("--sweep", choices=["gemv", "attn"], default=None,
                     help="kernel sweeps (one JSON line per case): config-2 GEMV, config-3 flash-decode")
-    ap.add_argument("--case", default=None, help="--sweep gemv: only quant:N:K:M (e.g. int4:14336:4096:1)")
+    ap.add_argument("--case", default=None, help="--sweep gemv: one cell quant:N:K:M, quant int4 / int8 / f16 (e.g. int4:14336:4096:1)")
     ap.add_argument("--reps", type=int, default=0, help="--sweep: timed launches per case (0 = auto)")
     ap.add_argument("--layers", type=int, default=0,
                     help="profiling only: keep the first N decoder layers (smaller device footprint)")
@@ -257,7 +257,7 @@ def run_ours(args):
     need = args.prompt + args.warmup + 2 * args.steps + 4
     m = LlamaForCausalLM(cfg, LLMQuant.INT4, max_context_length=max(CAPACITY, need), max_batch=B, seed=0,
                          device=local, tp_rank=rank, tp_size=world,
-                         flags=_lib.FLAG_NO_PERSISTENT if args.path == "per_stage" else 0)
+                         flags=_lib.FLAG_PERSISTENT if args.path == "persistent" else 0)
     if world > 1:
         uid = [None]
         if rank == 0:
@@ -438,15 +438,15 @@ def run_sweep_gemv(args):
     if args.case:   # "int4:14336:4096:1" -> one sweep cell (profiling)
         q_, n_, k_, m_ = args.case.split(":")
         only = (q_, int(n_), int(k_), int(m_))
-    for quant in ("int4", "int8"):
-        for (N, K) in [(4096, 4096), (14336, 4096), (4096, 14336)]:
-            if only and (quant, N, K) != only[:3]:
-                continue
-            wbytes = N * K // 2 if quant == "int4" else N * K
-            sbytes = N * (K // 128) * 2 if quant == "int4" else N * 2
+    quants = (only[0],) if only else ("int4", "int8")
+    shapes = [only[1:3]] if only else [(4096, 4096), (14336, 4096), (4096, 14336)]
+    for quant in quants:
+        for (N, K) in shapes:
+            wbytes = N * K // 2 if quant == "int4" else N * K * (2 if quant == "f16" else 1)
+            sbytes = N * (K // 128) * 2 if quant == "int4" else (N * 2 if quant == "int8" else 0)
             copies = max(2, int(np.ceil(1.1e9 / (wbytes + sbytes))))
             W = torch.randint(0, 256, (copies, wbytes), dtype=torch.uint8, device="cuda", generator=g)
-            Sc = (torch.rand((copies, sbytes // 2), device="cuda", generator=g) * 1e-3).half()
+            Sc = (torch.rand((copies, max(sbytes, 2) // 2), device="cuda", generator=g) * 1e-3).half()
             for M in (1, 4, 16, 64, 512):
                 if only and M != only[3]:
                     continue
@@ -456,6 +456,9 @@ def run_sweep_gemv(args):
                     f = lambda i: _lib.call("du_gemv_q4", C.c_void_p(y.data_ptr()), C.c_void_p(x.data_ptr()),
                                             _lib.DTYPE_BF16, C.c_void_p(W[i % copies].data_ptr()),
                                             C.c_void_p(Sc[i % copies].data_ptr()), 128, M, N, K, None)
+                elif quant == "f16":
+                    f = lambda i: _lib.call("du_gemv_f16", C.c_void_p(y.data_ptr()), C.c_void_p(x.data_ptr()),
+                                            _lib.DTYPE_BF16, C.c_void_p(W[i % copies].data_ptr()), M, N, K, None)
                 else:
                     f = lambda i: _lib.call("du_gemv_q8", C.c_void_p(y.data_ptr()), C.c_void_p(x.data_ptr()),
                                             _lib.DTYPE_BF16, C.c_void_p(W[i % copies].data_ptr()),
@@ -465,7 +468,7 @@ def run_sweep_gemv(args):
                 ms = _events_ms(f, reps)
                 byts = wbytes + sbytes + M * K * 2 + M * N * 4
                 gbs = byts / (ms / 1e3) / 1e9
-                print(json.dumps({"sweep": "gemv", "quant": quant + ("-g128" if quant == "int4" else "-row"),
+                print(json.dumps({"sweep": "gemv", "quant": quant + {"int4": "-g128", "int8": "-row"}.get(quant, ""),
                                   "N": N, "K": K, "M": M, "us": round(ms * 1e3, 2), "GB_s": round(gbs, 1),
                                   "frac_hbm": round(gbs / peak, 4), "TFLOP_s": round(2 * M * N * K / (ms / 1e3) / 1e12, 2),
                                   "peak_kind": kind, "copies": copies}), flush=True)

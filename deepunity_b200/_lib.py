@@ -16,6 +16,7 @@ DU_OK, DU_EINVAL, DU_ECUDA, DU_ENOMEM, DU_EBUSY, DU_ENCCL, DU_ENOTFOUND, DU_ESTA
 QUANT_FP16, QUANT_INT8, QUANT_INT4 = 0, 1, 2
 DTYPE_F32, DTYPE_F16, DTYPE_BF16 = 0, 1, 2
 FLAG_NO_PERSISTENT = 1
+FLAG_PERSISTENT = 2
 
 
 class DUError(RuntimeError):

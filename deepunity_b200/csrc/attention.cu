@@ -18,25 +18,41 @@
 // kv_len is read from device memory, so one captured CUDA graph serves every
 // decode step.  The unit itself lives in attn_impl.cuh (shared with the
 // persistent decode-step kernel).
+//
+// flash_decode_cluster_kernel (the model's decode and prefill path): the C
+// splits of one (row, kv head) form one thread-block cluster.  Each CTA leaves
+// its split's (m, l, acc) in its own shared memory; after a cluster barrier CTA
+// r merges output elements [r * G*HD/C, (r + 1) * G*HD/C): C consecutive lanes
+// per output each read one split's state through distributed shared memory and
+// combine with shuffle butterflies (fixed order), so there are no global
+// partials, atomics or second read round trip.
+#include <cooperative_groups.h>
+
 #include "attn_impl.cuh"
 #include "internal.h"
 
 namespace du {
 
 constexpr int FD_THREADS = 128;
+constexpr int FDC_THREADS = 256;     // cluster kernel: fewer positions per CTA, more threads per tile
 
+// new_rows >= 0: each query row's last new_rows K/V rows come from the previous
+// kernel (decode: 1); the unit's older rows of its first tile are loaded before
+// griddepcontrol.wait, overlapping the QKV kernel's tail.  kv_len itself was
+// written by kernels that completed before the QKV kernel passed its own wait.
 template <int HD>
-__global__ void __launch_bounds__(FD_THREADS) flash_decode_kernel(const FdParams p, int G)
+__global__ void __launch_bounds__(FD_THREADS) flash_decode_kernel(const FdParams p, int G, int new_rows)
 {
     extern __shared__ __align__(16) unsigned char fd_smem[];
     __shared__ FdShared<HD> sh;
-    pdl_wait();      // q (and this step's K/V row) come from the previous kernel
+    if (new_rows >= 0) fd_prefetch<HD, FD_THREADS>(p, blockIdx.z, blockIdx.y, blockIdx.x, gridDim.x, new_rows, fd_smem);
+    pdl_wait();      // q (and this step's K/V rows) come from the previous kernel
     pdl_trigger();
-    fd_unit<HD, FD_THREADS>(p, G, blockIdx.z, blockIdx.y, blockIdx.x, gridDim.x, fd_smem, sh);
+    fd_unit<HD, FD_THREADS>(p, G, blockIdx.z, blockIdx.y, blockIdx.x, gridDim.x, fd_smem, sh, new_rows);
 }
 
 template <int HD>
-static int fd_launch(const FdParams &p, int G, int nsplit, int nq, cudaStream_t st)
+static int fd_launch(const FdParams &p, int G, int nsplit, int nq, cudaStream_t st, int new_rows)
 {
     dim3 grid(nsplit, p.hkv, nq);
     const size_t smem = 4 * FD_TILE * (HD + 8) * sizeof(__half);
@@ -58,8 +74,129 @@ static int fd_launch(const FdParams &p, int G, int nsplit, int nq, cudaStream_t 
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl_enabled() ? 1 : 0;
-    DU_CUDA_TRY(cudaLaunchKernelEx(&cfg, flash_decode_kernel<HD>, p, G));
+    DU_CUDA_TRY(cudaLaunchKernelEx(&cfg, flash_decode_kernel<HD>, p, G, new_rows));
     return DU_OK;
+}
+
+namespace cg = cooperative_groups;
+
+template <int HD, int C>
+__global__ void __launch_bounds__(FDC_THREADS) flash_decode_cluster_kernel(const FdParams p, int G, int new_rows)
+{
+    extern __shared__ __align__(16) unsigned char fd_smem[];
+    __shared__ FdShared<HD> sh;
+    cg::cluster_group cluster = cg::this_cluster();
+    const int split = blockIdx.x, kvh = blockIdx.y, row = blockIdx.z;     // gridDim.x == C == cluster size
+    if (new_rows >= 0) fd_prefetch<HD, FDC_THREADS, true>(p, row, kvh, split, C, new_rows, fd_smem);
+    pdl_wait();      // q (and this step's K/V rows) come from the previous kernel
+    pdl_trigger();
+    fd_unit<HD, FDC_THREADS, true>(p, G, row, kvh, split, C, fd_smem, sh, new_rows);
+    cluster.sync();  // every split's state is in its CTA's shared memory
+    // CTA `split` merges outputs [split * per, (split + 1) * per): C consecutive lanes
+    // per output, lane r reading split r's state; butterflies over the C lanes
+    const int n_out = G * HD, per = (n_out + C - 1) / C;
+    const int r = threadIdx.x % C;
+    const float *rm = cluster.map_shared_rank(sh.m, r);
+    const float *rl = cluster.map_shared_rank(sh.l, r);
+    const float *ro = cluster.map_shared_rank(reinterpret_cast<float *>(fd_smem), r);
+    for (int i0 = 0; i0 < per; i0 += FDC_THREADS / C) {
+        const int i = i0 + threadIdx.x / C;
+        const int o = split * per + i;
+        const bool live = i < per && o < n_out;
+        const int g = live ? o / HD : 0;
+        const float m_r = live ? rm[g] : FD_NEG;
+        const float l_r = live ? rl[g] : 0.0f;
+        const float o_r = live ? ro[o] : 0.0f;
+        float M = m_r;
+#pragma unroll
+        for (int s = C / 2; s > 0; s >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, s));
+        const float w = expf(m_r - M);
+        float L = l_r * w, O = o_r * w;
+#pragma unroll
+        for (int s = C / 2; s > 0; s >>= 1) {
+            L += __shfl_xor_sync(0xffffffffu, L, s);
+            O += __shfl_xor_sync(0xffffffffu, O, s);
+        }
+        if (live && r == 0) p.out[((size_t)row * p.hq + kvh * G) * HD + o] = O * (1.0f / fmaxf(L, 1e-12f));
+    }
+    cluster.sync();  // peers read this CTA's shared memory until here
+}
+
+template <int HD, int C>
+static int fdc_launch(const FdParams &p, int G, int nq, cudaStream_t st, int new_rows, bool probe, int *fits)
+{
+    auto kern = flash_decode_cluster_kernel<HD, C>;
+    const size_t smem = 4 * FD_TILE * (HD + 8) * sizeof(__half) + fd_mma_extra_bytes<HD>();
+    static bool attr_set[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (!attr_set[dev & 63]) {
+        DU_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+        if (C > 8) DU_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
+        attr_set[dev & 63] = true;
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(C, p.hkv, nq);
+    cfg.blockDim = dim3(FDC_THREADS);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = C;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl_enabled() ? 2 : 1;
+    if (probe) {
+        int n = 0;
+        DU_CUDA_TRY(cudaOccupancyMaxActiveClusters(&n, kern, &cfg));
+        *fits = n;
+        return DU_OK;
+    }
+    DU_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, p, G, new_rows));
+    return DU_OK;
+}
+
+// Cluster size per device: 16 splits when such clusters can be resident, else 8.
+template <int HD>
+static int fdc_cluster_size(const FdParams &p, int G, cudaStream_t st)
+{
+    static int chosen[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (chosen[dev & 63] == 0) {
+        int n16 = 0;
+        const int rc = fdc_launch<HD, 16>(p, G, 1, st, -1, true, &n16);
+        cudaGetLastError();
+        chosen[dev & 63] = (rc == DU_OK && n16 > 0) ? 16 : 8;
+    }
+    return chosen[dev & 63];
+}
+
+int launch_flash_decode_cluster(const float *q, const __half *kc, const __half *vc, const int *seq_of,
+                                const int *kv_len, int kv_len_add, int nq, int hq, int hkv, int hd, int cap,
+                                float scale, float *out, cudaStream_t st, int new_rows)
+{
+    if (nq <= 0) return DU_OK;
+    if (hkv <= 0 || hq % hkv != 0) return fail(DU_EINVAL, "flash_decode: hq must be a multiple of hkv");
+    const int G = hq / hkv;
+    if (G < 1 || G > FD_MAXG) return fail(DU_EINVAL, "flash_decode: GQA group must be 1..8");
+    FdParams p = {};
+    p.q = q; p.k_cache = kc; p.v_cache = vc; p.seq_of = seq_of; p.kv_len = kv_len;
+    p.kv_len_add = kv_len_add;
+    p.hq = hq; p.hkv = hkv; p.cap = cap; p.scale = scale; p.out = out;
+    int dummy = 0;
+    if (hd == 128) {
+        return fdc_cluster_size<128>(p, G, st) == 16 ? fdc_launch<128, 16>(p, G, nq, st, new_rows, false, &dummy)
+                                                     : fdc_launch<128, 8>(p, G, nq, st, new_rows, false, &dummy);
+    }
+    if (hd == 64) {
+        return fdc_cluster_size<64>(p, G, st) == 16 ? fdc_launch<64, 16>(p, G, nq, st, new_rows, false, &dummy)
+                                                    : fdc_launch<64, 8>(p, G, nq, st, new_rows, false, &dummy);
+    }
+    return fail(DU_EINVAL, "flash_decode: supported head_dim 64/128");
 }
 
 int fd_choose_splits(int nq, int hkv, int max_kv)
@@ -81,7 +218,7 @@ size_t fd_scratch_floats(int nq, int hkv, int G, int hd, int nsplit)
 int launch_flash_decode(const float *q, const __half *kc, const __half *vc, const int *seq_of,
                         const int *kv_len, int kv_len_add, int nq, int hq, int hkv, int hd, int cap,
                         float scale, float *out, float *scratch, unsigned *counters, int nsplit,
-                        cudaStream_t st)
+                        cudaStream_t st, int new_rows)
 {
     if (nq <= 0) return DU_OK;
     if (hkv <= 0 || hq % hkv != 0) return fail(DU_EINVAL, "flash_decode: hq must be a multiple of hkv");
@@ -95,8 +232,8 @@ int launch_flash_decode(const float *q, const __half *kc, const __half *vc, cons
     p.counters = counters;
     if (G < 1 || G > FD_MAXG) return fail(DU_EINVAL, "flash_decode: GQA group must be 1..8");
     if (nsplit < 1 || nsplit > FD_MAXSPLIT) return fail(DU_EINVAL, "flash_decode: split count out of range");
-    if (hd == 128) return fd_launch<128>(p, G, nsplit, nq, st);
-    if (hd == 64) return fd_launch<64>(p, G, nsplit, nq, st);
+    if (hd == 128) return fd_launch<128>(p, G, nsplit, nq, st, new_rows);
+    if (hd == 64) return fd_launch<64>(p, G, nsplit, nq, st, new_rows);
     return fail(DU_EINVAL, "flash_decode: supported head_dim 64/128");
 }
 

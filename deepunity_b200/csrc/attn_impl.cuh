@@ -48,24 +48,74 @@ __device__ __forceinline__ void fd_cp_commit() { asm volatile("cp.async.commit_g
 template <int N>
 __device__ __forceinline__ void fd_cp_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 
+// warp-wide 8x8 b16 matrix loads (rows 16-byte aligned) and the f16 tensor-core MMA
+__device__ __forceinline__ void fd_ldsm_x4(uint32_t (&r)[4], const void *p)
+{
+    const unsigned a = (unsigned)__cvta_generic_to_shared(p);
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]) : "r"(a));
+}
+__device__ __forceinline__ void fd_ldsm_x2(uint32_t &r0, uint32_t &r1, const void *p)
+{
+    const unsigned a = (unsigned)__cvta_generic_to_shared(p);
+    asm volatile("ldmatrix.sync.aligned.m8n8.x2.shared.b16 {%0,%1}, [%2];" : "=r"(r0), "=r"(r1) : "r"(a));
+}
+__device__ __forceinline__ void fd_ldsm_x4_t(uint32_t (&r)[4], const void *p)
+{
+    const unsigned a = (unsigned)__cvta_generic_to_shared(p);
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]) : "r"(a));
+}
+__device__ __forceinline__ void fd_ldsm_x2_t(uint32_t &r0, uint32_t &r1, const void *p)
+{
+    const unsigned a = (unsigned)__cvta_generic_to_shared(p);
+    asm volatile("ldmatrix.sync.aligned.m8n8.x2.trans.shared.b16 {%0,%1}, [%2];" : "=r"(r0), "=r"(r1) : "r"(a));
+}
+// c += a (16x16, row) * b (16x8, col), f16 inputs, f32 accumulators
+__device__ __forceinline__ void fd_mma(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1)
+{
+    asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+                 : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+                 : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// Bytes after the K/V tiles that the tensor-core unit (TO_SMEM, 256 threads) also
+// uses: q and P as fp16 hi + lo parts, [2][16][HD + 8] and [2][16][FD_TILE + 8].
+template <int HD>
+__host__ __device__ constexpr size_t fd_mma_extra_bytes()
+{
+    return (size_t)2 * 16 * (HD + 8) * 2 + (size_t)2 * 16 * (FD_TILE + 8) * 2;
+}
+
 // Positions of unit (row, kv head, split).
 struct FdGeom {
     int kv_len, ns_act, start, end, ntiles;
     const __half *kbase, *vbase;
 };
 
-template <int HD>
+// EVEN: the kv_len's tiles are dealt evenly over the nsplit splits (cluster
+// combine); otherwise each active split takes the same whole number of tiles and
+// the active splits are counted in ns_act (global combine).
+template <int HD, bool EVEN = false>
 __device__ __forceinline__ FdGeom fd_geom(const FdParams &p, int row, int kvh, int split, int nsplit)
 {
     FdGeom g;
     const int seq = p.seq_of ? p.seq_of[row] : row;
     g.kv_len = p.kv_len[row] + p.kv_len_add;
-    // splits actually used for this length: at least one tile each
-    g.ns_act = max(1, min(nsplit, (g.kv_len + FD_TILE - 1) / FD_TILE));
-    int chunk = (g.kv_len + g.ns_act - 1) / g.ns_act;
-    chunk = (chunk + FD_TILE - 1) & ~(FD_TILE - 1);
-    g.start = split * chunk;
-    g.end = split < g.ns_act ? min(g.start + chunk, g.kv_len) : g.start;
+    const int T = (g.kv_len + FD_TILE - 1) / FD_TILE;
+    if (EVEN) {
+        g.ns_act = nsplit;
+        g.start = (int)(((int64_t)split * T) / nsplit) * FD_TILE;
+        g.end = min((int)(((int64_t)(split + 1) * T) / nsplit) * FD_TILE, g.kv_len);
+        if (g.end < g.start) g.end = g.start;
+    } else {
+        // splits actually used for this length: at least one tile each
+        g.ns_act = max(1, min(nsplit, T));
+        int chunk = (g.kv_len + g.ns_act - 1) / g.ns_act;
+        chunk = (chunk + FD_TILE - 1) & ~(FD_TILE - 1);
+        g.start = split * chunk;
+        g.end = split < g.ns_act ? min(g.start + chunk, g.kv_len) : g.start;
+    }
     g.ntiles = g.end > g.start ? (g.end - g.start + FD_TILE - 1) / FD_TILE : 0;
     g.kbase = p.k_cache + ((size_t)seq * p.cap * p.hkv + kvh) * HD;
     g.vbase = p.v_cache + ((size_t)seq * p.cap * p.hkv + kvh) * HD;
@@ -100,11 +150,11 @@ __device__ __forceinline__ void fd_load_rows(const FdParams &p, const FdGeom &g,
 // Loads, ahead of the producer of this step's K/V rows, the rows of tile 0 that
 // earlier steps wrote (positions below kv_len - new_rows).  The unit is then
 // run with pre_new = new_rows.
-template <int HD, int NT>
+template <int HD, int NT, bool EVEN = false>
 __device__ __forceinline__ void fd_prefetch(const FdParams &p, int row, int kvh, int split, int nsplit, int new_rows,
                                             unsigned char *tiles)
 {
-    const FdGeom g = fd_geom<HD>(p, row, kvh, split, nsplit);
+    const FdGeom g = fd_geom<HD, EVEN>(p, row, kvh, split, nsplit);
     if (g.ntiles > 0) fd_load_rows<HD, NT>(p, g, 0, 0, g.start, g.kv_len - new_rows, tiles);
 }
 
@@ -113,41 +163,72 @@ __device__ __forceinline__ void fd_prefetch(const FdParams &p, int row, int kvh,
 // merges all splits into p.out.  All NT threads must call it.  pre_new < 0:
 // nothing was prefetched; else fd_prefetch(..., new_rows = pre_new) ran and
 // only tile 0's rows from kv_len - pre_new on are loaded here.
-template <int HD, int NT>
-__device__ void fd_unit(const FdParams &p, int G, int row, int kvh, int split, int nsplit, unsigned char *tiles,
+//
+// TO_SMEM: instead of publishing to p.part_o / p.part_ml and combining through
+// global memory, leave this split's unnormalised state in shared memory --
+// acc as float [G][HD] at `tiles`, (m, l) in sh.m / sh.l -- for a cluster
+// combine (flash_decode_cluster_kernel).
+//
+// With TO_SMEM and 256 threads the tile math runs on tensor cores
+// (mma.sync m16n8k16, fp32 accumulators): q and the probabilities are split
+// into fp16 hi + lo parts (x = hi + lo to ~22 bits) and multiplied against the
+// exact fp16 K / V, one MMA per part; rows g >= G of the 16-row A operands are
+// zero.  Needs fd_mma_extra_bytes<HD>() of shared memory after the tiles.
+template <int HD, int NT, bool TO_SMEM = false>
+__device__ __forceinline__ void fd_unit(const FdParams &p, int G, int row, int kvh, int split, int nsplit, unsigned char *tiles,
                         FdShared<HD> &sh, int pre_new = -1)
 {
     constexpr int LDS = HD + 8;               // padded row (halves): conflict-free 16 B reads
     constexpr int NW = NT / 32;
     constexpr size_t TILE_BYTES = 4 * FD_TILE * LDS * 2;
+    constexpr bool MMA = TO_SMEM && NT == 256;
+    constexpr int QLD = HD + 8, PLD = FD_TILE + 8;
+    auto qh = reinterpret_cast<__half (*)[16][QLD]>(tiles + TILE_BYTES);                     // [2][16][QLD]
+    auto ph = reinterpret_cast<__half (*)[16][PLD]>(tiles + TILE_BYTES + (size_t)2 * 16 * QLD * 2);   // [2][16][PLD]
     auto Ks = reinterpret_cast<__half (*)[FD_TILE][LDS]>(tiles);
     auto Vs = reinterpret_cast<__half (*)[FD_TILE][LDS]>(tiles + 2 * FD_TILE * LDS * 2);
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
 
-    const FdGeom geo = fd_geom<HD>(p, row, kvh, split, nsplit);
+    const FdGeom geo = fd_geom<HD, TO_SMEM>(p, row, kvh, split, nsplit);
     const int ns_act = geo.ns_act, start = geo.start, end = geo.end, ntiles = geo.ntiles;
 
     if (ntiles > 0)
         fd_load_rows<HD, NT>(p, geo, 0, 0, pre_new < 0 ? start : geo.kv_len - pre_new, 0x7fffffff, tiles);
-    for (int i = tid; i < G * HD; i += NT) {
-        const int g = i / HD, d = i - g * HD;
-        sh.qs[g][d] = p.q[((size_t)row * p.hq + kvh * G + g) * HD + d] * p.scale;
+    if (MMA) {
+        for (int i = tid; i < 16 * HD; i += NT) {
+            const int g = i / HD, d = i - g * HD;
+            const float q = g < G ? p.q[((size_t)row * p.hq + kvh * G + g) * HD + d] * p.scale : 0.0f;
+            const __half h = __float2half_rn(q);
+            qh[0][g][d] = h;
+            qh[1][g][d] = __float2half_rn(q - __half2float(h));
+        }
+        for (int i = tid; i < 2 * 16 * PLD; i += NT) (&ph[0][0][0])[i] = __float2half_rn(0.0f);
+    } else {
+        for (int i = tid; i < G * HD; i += NT) {
+            const int g = i / HD, d = i - g * HD;
+            sh.qs[g][d] = p.q[((size_t)row * p.hq + kvh * G + g) * HD + d] * p.scale;
+        }
     }
     if (tid < G) { sh.m[tid] = FD_NEG; sh.l[tid] = 0.0f; }
 
-    // PV ownership: dim pair dp, heads g = hb, hb + HSTEP, ...
+    // QK ownership: position qj, dim slice qsl (16-byte chunks qsl, qsl + DQ, ...),
+    // every head; the DQ slices of a position sit on consecutive lanes.
+    constexpr int DQ = NT / FD_TILE;
+    constexpr int CH = HD / 8;                 // 16-byte chunks per K row
+    const int qj = tid / DQ, qsl = tid % DQ;
+    // PV ownership: dim pair dp, every head, positions pq, pq + PQ, ...; the PQ
+    // partial sums are added once after the last tile.
     constexpr int NDP = HD / 2;
-    constexpr int HSTEP = NT / NDP;
-    constexpr int HPT = (FD_MAXG + HSTEP - 1) / HSTEP;
-    const int dp = tid % NDP, hb = tid / NDP;
-    float acc[HPT][2];
+    constexpr int PQ = NT / NDP;
+    const int dp = tid % NDP, pq = tid / NDP;
+    float acc[FD_MAXG][2];
 #pragma unroll
-    for (int i = 0; i < HPT; i++) acc[i][0] = acc[i][1] = 0.0f;
-
-    // QK ownership: position j = tid % 64, heads g = qb, qb + QSTEP, ...
-    constexpr int QSTEP = NT / FD_TILE;
-    constexpr int QHPT = (FD_MAXG + QSTEP - 1) / QSTEP;
-    const int qj = tid % FD_TILE, qb = tid / FD_TILE;
+    for (int g = 0; g < FD_MAXG; g++) acc[g][0] = acc[g][1] = 0.0f;
+    // MMA ownership: scores, positions [8 warp, 8 warp + 8); P.V, dims [warp HD/8, (warp + 1) HD/8)
+    constexpr int NTL = HD / 64;               // 8-dim n-tiles per warp in P.V
+    float oc[NTL][4];
+#pragma unroll
+    for (int n = 0; n < NTL; n++) oc[n][0] = oc[n][1] = oc[n][2] = oc[n][3] = 0.0f;
     __syncthreads();
 
     for (int t = 0; t < ntiles; t++) {
@@ -156,38 +237,62 @@ __device__ void fd_unit(const FdParams &p, int G, int row, int kvh, int split, i
         else { fd_cp_wait<0>(); }
         __syncthreads();
 
-        // ---- scores
-        {
-            float s[QHPT];
+        // ---- scores: each K chunk is read once and used for every head
+        if (MMA) {
+            const int n0 = warp * 8;
+            float c[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
-            for (int i = 0; i < QHPT; i++) s[i] = 0.0f;
+            for (int ks = 0; ks < HD / 16; ks++) {
+                uint32_t b0, b1;
+                fd_ldsm_x2(b0, b1, &Ks[buf][n0 + (lane & 7)][ks * 16 + ((lane >> 3) & 1) * 8]);
+#pragma unroll
+                for (int hl = 0; hl < 2; hl++) {
+                    uint32_t a[4];
+                    fd_ldsm_x4(a, &qh[hl][lane & 15][ks * 16 + (lane >> 4) * 8]);
+                    fd_mma(c, a, b0, b1);
+                }
+            }
+            const int g = lane >> 2, j = n0 + (lane & 3) * 2;
+            if (g < G) {
+                const int pos = start + t * FD_TILE + j;
+                sh.ps[j][g] = pos < end ? c[0] : FD_NEG;
+                sh.ps[j + 1][g] = pos + 1 < end ? c[1] : FD_NEG;
+            }
+        } else {
+            float s[FD_MAXG];
+#pragma unroll
+            for (int g = 0; g < FD_MAXG; g++) s[g] = 0.0f;
             const __half *kr = &Ks[buf][qj][0];
-#pragma unroll 4
-            for (int d = 0; d < HD; d += 8) {
-                const uint4 raw = *reinterpret_cast<const uint4 *>(kr + d);
+#pragma unroll
+            for (int c = qsl; c < CH; c += DQ) {
+                const uint4 raw = *reinterpret_cast<const uint4 *>(kr + c * 8);
                 const __half2 *h = reinterpret_cast<const __half2 *>(&raw);
                 const float2 k0 = __half22float2(h[0]), k1 = __half22float2(h[1]);
                 const float2 k2 = __half22float2(h[2]), k3 = __half22float2(h[3]);
 #pragma unroll
-                for (int i = 0; i < QHPT; i++) {
-                    const int g = qb + QSTEP * i;
+                for (int g = 0; g < FD_MAXG; g++) {
                     if (g < G) {
-                        const float4 qa = *reinterpret_cast<const float4 *>(&sh.qs[g][d]);
-                        const float4 qc = *reinterpret_cast<const float4 *>(&sh.qs[g][d + 4]);
-                        float a = s[i];
+                        const float4 qa = *reinterpret_cast<const float4 *>(&sh.qs[g][c * 8]);
+                        const float4 qc = *reinterpret_cast<const float4 *>(&sh.qs[g][c * 8 + 4]);
+                        float a = s[g];
                         a = fmaf(qa.x, k0.x, a); a = fmaf(qa.y, k0.y, a);
                         a = fmaf(qa.z, k1.x, a); a = fmaf(qa.w, k1.y, a);
                         a = fmaf(qc.x, k2.x, a); a = fmaf(qc.y, k2.y, a);
                         a = fmaf(qc.z, k3.x, a); a = fmaf(qc.w, k3.y, a);
-                        s[i] = a;
+                        s[g] = a;
                     }
                 }
             }
-            const bool valid = start + t * FD_TILE + qj < end;
 #pragma unroll
-            for (int i = 0; i < QHPT; i++) {
-                const int g = qb + QSTEP * i;
-                if (g < G) sh.ps[qj][g] = valid ? s[i] : FD_NEG;
+            for (int o = 1; o < DQ; o <<= 1)
+#pragma unroll
+                for (int g = 0; g < FD_MAXG; g++)
+                    if (g < G) s[g] += __shfl_xor_sync(0xffffffffu, s[g], o);
+            if (qsl == 0) {
+                const bool valid = start + t * FD_TILE + qj < end;
+#pragma unroll
+                for (int g = 0; g < FD_MAXG; g++)
+                    if (g < G) sh.ps[qj][g] = valid ? s[g] : FD_NEG;
             }
         }
         __syncthreads();
@@ -201,6 +306,13 @@ __device__ void fd_unit(const FdParams &p, int G, int row, int kvh, int split, i
             const float pa = expf(a - m_new), pb = expf(b - m_new);
             sh.ps[2 * lane][g] = pa;
             sh.ps[2 * lane + 1][g] = pb;
+            if (MMA) {
+                const __half ha = __float2half_rn(pa), hb = __float2half_rn(pb);
+                ph[0][g][2 * lane] = ha;
+                ph[0][g][2 * lane + 1] = hb;
+                ph[1][g][2 * lane] = __float2half_rn(pa - __half2float(ha));
+                ph[1][g][2 * lane + 1] = __float2half_rn(pb - __half2float(hb));
+            }
             const float ts = warp_sum(pa + pb);
             if (lane == 0) {
                 const float alpha = expf(m_old - m_new);
@@ -211,43 +323,91 @@ __device__ void fd_unit(const FdParams &p, int G, int row, int kvh, int split, i
         }
         __syncthreads();
 
-        // ---- P.V
+        // ---- P.V over this thread's positions, every head
+        if (MMA) {
+            const int g = lane >> 2;
+            const float al = g < G ? sh.alpha[g] : 1.0f;
 #pragma unroll
-        for (int i = 0; i < HPT; i++) {
-            const int g = hb + i * HSTEP;
+            for (int n = 0; n < NTL; n++) { oc[n][0] *= al; oc[n][1] *= al; }
+            const int d0 = warp * (HD / 8);
+#pragma unroll
+            for (int ks = 0; ks < FD_TILE / 16; ks++) {
+                const int pos = ks * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
+                uint32_t b[4];
+                if (NTL == 2) fd_ldsm_x4_t(b, &Vs[buf][pos][d0 + (lane >> 4) * 8]);
+                else fd_ldsm_x2_t(b[0], b[1], &Vs[buf][pos][d0]);
+#pragma unroll
+                for (int hl = 0; hl < 2; hl++) {
+                    uint32_t a[4];
+                    fd_ldsm_x4(a, &ph[hl][lane & 15][ks * 16 + (lane >> 4) * 8]);
+#pragma unroll
+                    for (int n = 0; n < NTL; n++) fd_mma(oc[n], a, b[2 * n], b[2 * n + 1]);
+                }
+            }
+            __syncthreads();   // ps / buffers are rewritten next tile
+            continue;
+        }
+#pragma unroll
+        for (int g = 0; g < FD_MAXG; g++) {
             if (g < G) {
                 const float al = sh.alpha[g];
-                acc[i][0] *= al;
-                acc[i][1] *= al;
+                acc[g][0] *= al;
+                acc[g][1] *= al;
             }
         }
-#pragma unroll 8
-        for (int j = 0; j < FD_TILE; j++) {
+#pragma unroll 4
+        for (int j = pq; j < FD_TILE; j += PQ) {
             const float2 v = __half22float2(*reinterpret_cast<const __half2 *>(&Vs[buf][j][2 * dp]));
+            const float4 p0 = *reinterpret_cast<const float4 *>(&sh.ps[j][0]);
+            const float4 p1 = *reinterpret_cast<const float4 *>(&sh.ps[j][4]);
+            const float pj[8] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
 #pragma unroll
-            for (int i = 0; i < HPT; i++) {
-                const int g = hb + i * HSTEP;
+            for (int g = 0; g < FD_MAXG; g++) {
                 if (g < G) {
-                    const float pj = sh.ps[j][g];
-                    acc[i][0] = fmaf(pj, v.x, acc[i][0]);
-                    acc[i][1] = fmaf(pj, v.y, acc[i][1]);
+                    acc[g][0] = fmaf(pj[g], v.x, acc[g][0]);
+                    acc[g][1] = fmaf(pj[g], v.y, acc[g][1]);
                 }
             }
         }
         __syncthreads();   // ps / buffers are rewritten next tile
     }
 
-    // ---- this split's partial state
-    const size_t rk = (size_t)row * p.hkv + kvh;
-    float *po = p.part_o + (rk * nsplit + split) * G * HD;
+    // ---- this split's partial state: add the PQ position groups (fixed order)
+    float *so = reinterpret_cast<float *>(tiles);           // [G][HD]; the tiles are free now
+    if (MMA) {
+        const int g = lane >> 2, d0 = warp * (HD / 8);
+        if (g < G)
 #pragma unroll
-    for (int i = 0; i < HPT; i++) {
-        const int g = hb + i * HSTEP;
+            for (int n = 0; n < NTL; n++) {
+                so[g * HD + d0 + n * 8 + (lane & 3) * 2] = oc[n][0];
+                so[g * HD + d0 + n * 8 + (lane & 3) * 2 + 1] = oc[n][1];
+            }
+        __syncthreads();
+        return;
+    }
+    float *sred = so + FD_MAXG * HD;                         // [PQ][G][HD]
+#pragma unroll
+    for (int g = 0; g < FD_MAXG; g++) {
         if (g < G) {
-            po[g * HD + 2 * dp] = acc[i][0];
-            po[g * HD + 2 * dp + 1] = acc[i][1];
+            sred[(pq * G + g) * HD + 2 * dp] = acc[g][0];
+            sred[(pq * G + g) * HD + 2 * dp + 1] = acc[g][1];
         }
     }
+    __syncthreads();
+    for (int i = tid; i < G * HD; i += NT) {
+        float v = 0.0f;
+#pragma unroll
+        for (int q = 0; q < PQ; q++) v += sred[q * G * HD + i];
+        so[i] = v;
+    }
+    if (TO_SMEM) {
+        __syncthreads();
+        return;
+    }
+    const size_t rk = (size_t)row * p.hkv + kvh;
+    float *po = p.part_o + (rk * nsplit + split) * G * HD;
+    __syncthreads();
+    for (int i = tid; i < G * HD; i += NT) po[i] = so[i];
     if (tid < G) {
         float *pm = p.part_ml + ((rk * nsplit + split) * G + tid) * 2;
         pm[0] = sh.m[tid];

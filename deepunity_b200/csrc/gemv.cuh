@@ -154,6 +154,30 @@ __device__ __forceinline__ void gv_dot_f16(uint32_t w, float a, float b, float2 
     ffma2(acc, f.x, f.y, a, b);
 }
 
+// L2 policy for data read once per step (weights): evicted first, so the
+// streamed gigabytes do not push kernel code, activations and the KV rows
+// written this step out of L2.
+__device__ __forceinline__ uint64_t l2_evict_first_policy()
+{
+    uint64_t pol;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+    return pol;
+}
+__device__ __forceinline__ void cp_async16_cg_ef(void *smem, const void *gmem, bool valid, uint64_t pol)
+{
+    const unsigned s = (unsigned)__cvta_generic_to_shared(smem);
+    const int n = valid ? 16 : 0;
+    asm volatile("cp.async.cg.shared.global.L2::cache_hint [%0], [%1], 16, %2, %3;" ::"r"(s), "l"(gmem), "r"(n), "l"(pol)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_async4_ca_ef(void *smem, const void *gmem, bool valid, uint64_t pol)
+{
+    const unsigned s = (unsigned)__cvta_generic_to_shared(smem);
+    const int n = valid ? 4 : 0;
+    asm volatile("cp.async.ca.shared.global.L2::cache_hint [%0], [%1], 4, %2, %3;" ::"r"(s), "l"(gmem), "r"(n), "l"(pol)
+                 : "memory");
+}
+
 __device__ __forceinline__ void cp_async16_cg(void *smem, const void *gmem, bool valid)
 {
     const unsigned s = (unsigned)__cvta_generic_to_shared(smem);

@@ -44,7 +44,7 @@ struct __align__(16) GemvShared {
 //  INT8: per-token power-of-two scale over the normalised x; xscale = 2^-s
 //  FP16: x * (1 + gamma') in fp32, swizzled; xscale = 1 / rms (or 1)
 template <int QT, int MT, int NW>
-__device__ void gv_stage_x(const GemvParams &p, uint4 *xq, GemvShared<MT, NW> &sh, int nchunk)
+__device__ __forceinline__ void gv_stage_x(const GemvParams &p, uint4 *xq, GemvShared<MT, NW> &sh, int nchunk)
 {
     constexpr int NT = NW * 32;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -288,6 +288,7 @@ struct GemvStream {
     // and the physical rows of that group (-1 past the last row)
     int is_g, is_s, is_stage, is_left;
     int ipr[RW];
+    uint64_t pol;         // L2 evict-first policy of the weight stream
 
     __device__ __forceinline__ int unit_lo(int w) const { return (int)(((int64_t)w * U) / NW); }
 
@@ -310,9 +311,11 @@ struct GemvStream {
 #pragma unroll
             for (int j = 0; j < RW; j++) {
                 const int64_t r = ipr[j] < 0 ? 0 : ipr[j];
-                cp_async16_cg(ring + (is_stage * RW + j) * 32, wbase + r * row_bytes + is_s * 512, cv && ipr[j] >= 0);
+                cp_async16_cg_ef(ring + (is_stage * RW + j) * 32, wbase + r * row_bytes + is_s * 512, cv && ipr[j] >= 0,
+                                 pol);
                 if (QT == Q_I4)
-                    cp_async4_ca(sring + (is_stage * RW + j) * 32, sbase + r * srow_bytes + sw_off, cv && ipr[j] >= 0);
+                    cp_async4_ca_ef(sring + (is_stage * RW + j) * 32, sbase + r * srow_bytes + sw_off,
+                                    cv && ipr[j] >= 0, pol);
             }
             is_left--;
             if (++is_stage == D) is_stage = 0;
@@ -340,6 +343,7 @@ struct GemvStream {
         srow_bytes = QT == Q_I4 ? (p.K >> gshift) * 2 : 0;
         wbase = p.w + lane * 16;
         sbase = reinterpret_cast<const uint8_t *>(p.scales);
+        pol = l2_evict_first_policy();
         const int NG = (p.N + RW - 1) / RW;
         g_begin = (int)(((int64_t)cta * NG) / ncta);
         const int g_end = (int)(((int64_t)(cta + 1) * NG) / ncta);

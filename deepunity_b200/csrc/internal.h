@@ -24,7 +24,11 @@ size_t fd_scratch_floats(int nq, int hkv, int G, int hd, int nsplit);
 int launch_flash_decode(const float *q, const __half *kc, const __half *vc, const int *seq_of,
                         const int *kv_len, int kv_len_add, int nq, int hq, int hkv, int hd, int cap,
                         float scale, float *out, float *scratch, unsigned *counters, int nsplit,
-                        cudaStream_t st);
+                        cudaStream_t st, int new_rows = -1);
+// The model's path: splits of a (row, kv head) combined inside a thread-block cluster.
+int launch_flash_decode_cluster(const float *q, const __half *kc, const __half *vc, const int *seq_of,
+                                const int *kv_len, int kv_len_add, int nq, int hq, int hkv, int hd, int cap,
+                                float scale, float *out, cudaStream_t st, int new_rows = -1);
 
 // elementwise.cu
 int launch_embed(const int *ids, const __half *embed, float scale, int M, int H, float *out, cudaStream_t st);

@@ -525,6 +525,7 @@ struct StepIO {
     const int *seq_of;     // [M] or nullptr
     const int *kv_len;     // [M] kv length before kv_len_add
     int kv_len_add;
+    int kv_new = -1;       // K/V rows per token row written by this pass's QKV stage (-1: not uniform)
     int fd_nsplit;
     int logits_rows;       // rows whose logits are produced (last token per sequence, or all)
     const int *logit_tok;  // tokens -> which rows of x_res feed the lm_head: nullptr = all M
@@ -615,9 +616,8 @@ static int enqueue_stage(du_model *m, const StepIO &io, int l, int stage, bool c
     if (stage == ST_ATTN) {
         __half *kc = m->k_cache + (size_t)l * m->kv_layer_elems;
         __half *vc = m->v_cache + (size_t)l * m->kv_layer_elems;
-        return launch_flash_decode(m->q, kc, vc, io.seq_of, io.kv_len, io.kv_len_add, M, m->hq_l, m->hkv_l, hd,
-                                   m->cap, powf((float)hd, -0.5f), m->att, m->fd_scratch, m->fd_counters,
-                                   io.fd_nsplit, st);
+        return launch_flash_decode_cluster(m->q, kc, vc, io.seq_of, io.kv_len, io.kv_len_add, M, m->hq_l, m->hkv_l,
+                                           hd, m->cap, powf((float)hd, -0.5f), m->att, st, io.kv_new);
     }
     if (stage < ST_QKV || stage > ST_DOWN) return fail(DU_EINVAL, "unknown stage");
     if ((rc = run_gemv(m, qt, stage_gemv_params(m, io, l, stage), M))) return rc;
@@ -740,6 +740,7 @@ static StepIO decode_io(du_model *m, int batch)
     io.seq_of = nullptr;
     io.kv_len = m->d_cache_len;
     io.kv_len_add = 1;
+    io.kv_new = 1;
     io.fd_nsplit = fd_choose_splits(batch, m->hkv_l, m->cap);
     io.logits_rows = batch;
     io.logit_stride = 1;
@@ -752,13 +753,14 @@ static StepIO decode_io(du_model *m, int batch)
 
 // Stage list of the persistent decode-step kernel for the decode rows of `io`.
 // Fails (and the caller falls back to per-stage kernels) when the model asks for
-// that (DU_FLAG_NO_PERSISTENT), runs tensor-parallel, or the batch does not fit
+// that (no DU_FLAG_PERSISTENT, or DU_FLAG_NO_PERSISTENT), runs tensor-parallel, or the batch does not fit
 // one token tile / the shared-memory budget.
 static int build_step_plan(du_model *m, const StepIO &io, StepPlan *plan, int *qt_out, int *mt_out, size_t *smem_out,
                            StepStage **d_stages)
 {
     *d_stages = nullptr;
-    if ((m->cfg.flags & DU_FLAG_NO_PERSISTENT) || m->tp > 1 || io.M > 8) return DU_ESTATE;
+    if (!(m->cfg.flags & DU_FLAG_PERSISTENT) || (m->cfg.flags & DU_FLAG_NO_PERSISTENT) || m->tp > 1 || io.M > 8)
+        return DU_ESTATE;
     const int qt = qt_of(m->quant);
     const int mt = io.M <= 1 ? 1 : io.M <= 2 ? 2 : io.M <= 4 ? 4 : 8;
     std::vector<StepStage> st;

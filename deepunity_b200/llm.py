@@ -98,7 +98,7 @@ class LlamaForCausalLM(LLM):
         cfg.quant, cfg.group_size = int(self.quant), config.group_size
         cfg.kv_capacity, cfg.max_batch = max_context_length, max_batch
         cfg.tp_rank, cfg.tp_size, cfg.tie_embedding = tp_rank, tp_size, int(config.tie_embedding)
-        cfg.flags = flags     # FLAG_NO_PERSISTENT: per-stage kernels instead of the persistent step kernel
+        cfg.flags = flags     # FLAG_PERSISTENT: decode steps as one persistent kernel (default: per-stage graph)
         h = C.c_void_p()
         _lib.call("du_model_create", C.byref(cfg), C.byref(h))
         self._h = h

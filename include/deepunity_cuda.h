@@ -72,8 +72,9 @@ typedef struct du_model_config {
 
 /* du_model_config.flags */
 enum {
-    DU_FLAG_NO_PERSISTENT = 1   /* decode steps as a graph of per-stage kernels instead of the
-                                   persistent decode-step kernel */
+    DU_FLAG_NO_PERSISTENT = 1,  /* decode steps as a graph of per-stage kernels (the default) */
+    DU_FLAG_PERSISTENT = 2      /* decode steps as one persistent decode-step kernel (single GPU,
+                                   batch <= 8, when its shared-memory plan fits; else per-stage) */
 };
 
 typedef struct du_model du_model;

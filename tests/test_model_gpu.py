@@ -37,7 +37,7 @@ def build(cfg: TestConfig, seed=0, cap=128, max_batch=1, flags=0):
 
 
 # decode steps: the persistent decode-step kernel (default) and the graph of per-stage kernels
-PATHS = {"persistent": 0, "per_stage": _lib.FLAG_NO_PERSISTENT}
+PATHS = {"persistent": _lib.FLAG_PERSISTENT, "per_stage": 0}
 
 
 VARIANTS = [SMALL, MID,
