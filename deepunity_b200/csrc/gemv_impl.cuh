@@ -35,7 +35,7 @@ struct __align__(16) GemvShared {
     float xscale[MT];          // per-token factor of the folded dot product
     float amv[NW][MT];
     int ami[NW][MT];
-    float pbuf[NW][2][(MT == 1 ? 4 : 2) * MT];   // partial row groups split between warps (first / last)
+    float pbuf[NW][2][16];     // partial row groups split between warps (first / last); rows x tokens <= 16
 };
 
 // Stages the activations of the MT tokens in shared memory.
@@ -267,6 +267,49 @@ __host__ __device__ constexpr size_t gemv_ring_bytes()
     return (size_t)NW * D * RW * 32 * 16 + (QT == Q_I4 ? (size_t)NW * D * RW * 32 * 4 : 0);
 }
 
+// Epilogue of the finished row group starting at logical row lr0 (v: every lane
+// holds every value); lane j * MT + m owns output (row j, token m).
+template <int QT, int MT, int RW>
+__device__ __forceinline__ void gv_epilogue(const GemvParams &p, int lr0, const float (&v)[RW][MT], float *am_v,
+                                        int *am_i, int lane)
+{
+    if (p.epi == EPI_QKV || p.epi == EPI_GATEUP) {
+#pragma unroll
+        for (int jp = 0; jp < RW; jp += 2)
+#pragma unroll
+            for (int m = 0; m < MT; m++)
+                if (lane == (jp / 2) * MT + m && m < p.M && lr0 + jp + 1 < p.N) {
+                    float x1 = v[jp][m], x2 = v[jp + 1][m];
+                    if (QT == Q_I8) {
+                        x1 *= gv_row_scale<QT>(p, lr0 + jp);
+                        x2 *= gv_row_scale<QT>(p, lr0 + jp + 1);
+                    }
+                    gv_epi_pair(p, lr0 + jp, m, x1, x2);
+                }
+    } else {
+#pragma unroll
+        for (int j = 0; j < RW; j++)
+#pragma unroll
+            for (int m = 0; m < MT; m++) {
+                const int lr = lr0 + j;
+                if (m < p.M && lr < p.N) {
+                    if (p.epi == EPI_LOGITS) {
+                        const float f = v[j][m];
+                        const int ix = p.vocab_off + lr;    // global index; the shard write is local
+                        if (f > am_v[m] || (f == am_v[m] && ix < am_i[m])) { am_v[m] = f; am_i[m] = ix; }
+                        if (lane == j * MT + m && p.logits) p.logits[(size_t)m * p.ldl + lr] = f;
+                    } else if (lane == j * MT + m) {
+                        float f = v[j][m];
+                        if (QT == Q_I8) f *= gv_row_scale<QT>(p, lr);
+                        if (p.epi == EPI_STORE) p.y[(size_t)m * p.ldy + lr] = f;
+                        else p.y[(size_t)m * p.ldy + lr] += f;      // EPI_RESID
+                    }
+                }
+            }
+    }
+}
+
+
 // Work split: a CTA owns a contiguous range of row groups; their (group,
 // 512-byte segment) units, group-major, are cut into NW contiguous, equal
 // ranges, one per warp (split-K inside the CTA).  A group whose units fall to
@@ -359,44 +402,10 @@ struct GemvStream {
         for (int j = 0; j < D - 1; j++) issue(p);
     }
 
-    // Epilogue of the finished row group starting at logical row lr0 (v: every lane holds every value).
     __device__ __forceinline__ void epilogue(const GemvParams &p, int lr0, const float (&v)[RW][MT], float *am_v,
                                              int *am_i) const
     {
-        if (p.epi == EPI_QKV || p.epi == EPI_GATEUP) {
-#pragma unroll
-            for (int jp = 0; jp < RW; jp += 2)
-#pragma unroll
-                for (int m = 0; m < MT; m++)
-                    if (lane == (jp / 2) * MT + m && m < p.M && lr0 + jp + 1 < p.N) {
-                        float x1 = v[jp][m], x2 = v[jp + 1][m];
-                        if (QT == Q_I8) {
-                            x1 *= gv_row_scale<QT>(p, lr0 + jp);
-                            x2 *= gv_row_scale<QT>(p, lr0 + jp + 1);
-                        }
-                        gv_epi_pair(p, lr0 + jp, m, x1, x2);
-                    }
-        } else {
-#pragma unroll
-            for (int j = 0; j < RW; j++)
-#pragma unroll
-                for (int m = 0; m < MT; m++) {
-                    const int lr = lr0 + j;
-                    if (m < p.M && lr < p.N) {
-                        if (p.epi == EPI_LOGITS) {
-                            const float f = v[j][m];
-                            const int ix = p.vocab_off + lr;    // global index; the shard write is local
-                            if (f > am_v[m] || (f == am_v[m] && ix < am_i[m])) { am_v[m] = f; am_i[m] = ix; }
-                            if (lane == j * MT + m && p.logits) p.logits[(size_t)m * p.ldl + lr] = f;
-                        } else if (lane == j * MT + m) {
-                            float f = v[j][m];
-                            if (QT == Q_I8) f *= gv_row_scale<QT>(p, lr);
-                            if (p.epi == EPI_STORE) p.y[(size_t)m * p.ldy + lr] = f;
-                            else p.y[(size_t)m * p.ldy + lr] += f;      // EPI_RESID
-                        }
-                    }
-                }
-        }
+        gv_epilogue<QT, MT, RW>(p, lr0, v, am_v, am_i, lane);
     }
 
     // Phase 2: activations -> smem, stream, epilogue.  All threads of the CTA call it.
