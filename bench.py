@@ -295,9 +295,11 @@ def run_ours(args):
     with (sampler(local) if sampler else contextlib.nullcontext()) as clk:
         barrier()
         torch.cuda.synchronize()
+        torch.cuda.nvtx.range_push("decode_timed")      # ncu --nvtx-include decode_timed/ selects these launches
         ev0.record(stream)
         toks = m.decode_loop(ids, args.steps)
         ev1.record(stream)
+        torch.cuda.nvtx.range_pop()
         torch.cuda.synchronize()
         barrier()
     ms = max_over_ranks(ev0.elapsed_time(ev1))
@@ -358,11 +360,16 @@ def run_ours(args):
     # DRAM bytes per launch of decode_step_kernel from ncu captures at two layer counts
     # (traffic = fixed + per_layer * layers), scaled to this run's layer count
     traffic = None
-    prof = os.path.join(ROOT, "profiles", "decode_step_traffic.json")
-    if stage_us is not None and os.path.exists(prof):
+    if stage_us is not None:
+        prof = os.path.join(ROOT, "profiles", "decode_step_traffic.json")
+        key = None
+    else:       # per-stage graph: DRAM bytes per launch of the gate|up GEMV (ncu, layer-independent)
+        prof = os.path.join(ROOT, "profiles", "gateup_gemv_traffic.json")
+    if os.path.exists(prof):
         try:
             tj = json.load(open(prof))
-            traffic = int(tj["fixed_bytes"] + tj["per_layer_bytes"] * cfg.num_layers)
+            traffic = int(tj["fixed_bytes"] + tj["per_layer_bytes"] * cfg.num_layers) if stage_us is not None \
+                else int(tj["bytes_per_launch"])
         except Exception:
             traffic = None
     stage_roof = None
