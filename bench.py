@@ -50,6 +50,7 @@ def parse():
     ap.add_argument("--path", choices=["persistent", "per_stage"], default="per_stage",
                     help="decode step as one persistent kernel, or as a graph of per-stage kernels")
     ap.add_argument("--clock-sampler", choices=["nvml", "smi", "none"], default="nvml")
+    ap.add_argument("--nccl-only", action="store_true", help="TP: decode reductions with ncclAllReduce only")
     ap.add_argument("--sweep", choices=["gemv", "attn"], default=None,
                     help="kernel sweeps (one JSON line per case): config-2 GEMV, config-3 flash-decode")
     ap.add_argument("--case", default=None, help="--sweep gemv: one cell quant:N:K:M, quant int4 / int8 / f16 (e.g. int4:14336:4096:1)")
@@ -266,6 +267,10 @@ def run_ours(args):
             uid[0] = buf.raw
         dist.broadcast_object_list(uid, src=0)
         m.init_tp(uid[0], timeout_ms=120000)
+        if not args.nccl_only:      # decode reductions over NVLink peer memory
+            hs = [None] * world
+            dist.all_gather_object(hs, m.p2p_handle())
+            m.init_p2p(hs)
 
     prompt = np.random.default_rng(0).integers(0, cfg.vocab_size, (B, args.prompt)).astype(np.int32)
     _, nxt = m.forward(prompt, want_logits=False)

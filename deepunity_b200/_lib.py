@@ -47,6 +47,8 @@ SIGNATURES = {
     "du_model_init_random": (I, [P, U64, F]),
     "du_nccl_unique_id": (I, [P]),
     "du_tp_init": (I, [P, P, I]),
+    "du_tp_comm_handle": (I, [P, P]),
+    "du_tp_comm_open": (I, [P, P, I]),
     "du_tp_shard_window": (I, [C.POINTER(ModelConfig), C.c_char_p, C.POINTER(C.c_int64)]),
     "du_forward": (I, [P, P, I, I, I, I, P, P]),
     "du_decode_step": (I, [P, P, I, P]),

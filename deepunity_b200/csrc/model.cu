@@ -27,6 +27,7 @@
 #include "internal.h"
 #include "nccl_shim.h"
 #include "step_plan.h"
+#include "tp_comm.h"
 
 namespace du {
 
@@ -94,6 +95,7 @@ struct du_model {
     // TP
     ncclComm_t comm = nullptr;
     bool tp_ready = false;
+    du::TpComm tpc;                         // peer-memory allreduce of decode-sized reductions
     int nccl_timeout_ms = 60000;
     uint64_t weight_bytes = 0;
 };
@@ -282,6 +284,7 @@ static void model_free(du_model *m)
     if (m->h_pin_err) cudaFreeHost(m->h_pin_err);
     m->h_pin_err = nullptr;
     m->graphs.clear();
+    tp_comm_free(&m->tpc);
     if (m->comm) {
         const NcclApi *n = nccl_api();
         if (n) n->CommDestroy(m->comm);
@@ -526,6 +529,7 @@ struct StepIO {
     const int *kv_len;     // [M] kv length before kv_len_add
     int kv_len_add;
     int kv_new = -1;       // K/V rows per token row written by this pass's QKV stage (-1: not uniform)
+    bool p2p = false;      // TP reductions may take the peer-memory allreduce (decode graphs)
     int fd_nsplit;
     int logits_rows;       // rows whose logits are produced (last token per sequence, or all)
     const int *logit_tok;  // tokens -> which rows of x_res feed the lm_head: nullptr = all M
@@ -622,6 +626,8 @@ static int enqueue_stage(du_model *m, const StepIO &io, int l, int stage, bool c
     if (stage < ST_QKV || stage > ST_DOWN) return fail(DU_EINVAL, "unknown stage");
     if ((rc = run_gemv(m, qt, stage_gemv_params(m, io, l, stage), M))) return rc;
     if ((stage == ST_O || stage == ST_DOWN) && m->tp > 1 && collective) {
+        if (io.p2p && m->tpc.ready && (size_t)M * H <= m->tpc.maxn)
+            return launch_tp_allreduce(&m->tpc, m->part, m->x_res, (size_t)M * H, m->d_err, st);
         if ((rc = allreduce_sum(m, m->part, (size_t)M * H))) return rc;
         if ((rc = launch_add_inplace(m->x_res, m->part, (size_t)M * H, st))) return rc;
     }
@@ -741,6 +747,7 @@ static StepIO decode_io(du_model *m, int batch)
     io.kv_len = m->d_cache_len;
     io.kv_len_add = 1;
     io.kv_new = 1;
+    io.p2p = true;
     io.fd_nsplit = fd_choose_splits(batch, m->hkv_l, m->cap);
     io.logits_rows = batch;
     io.logit_stride = 1;
@@ -849,7 +856,7 @@ static int check_step_error(du_model *m)
     if (*m->h_pin_err == 0) return DU_OK;
     *m->h_pin_err = 0;
     cudaMemset(m->d_err, 0, sizeof(int));
-    return fail(DU_ECUDA, "decode step: grid barrier timed out (kernel aborted)");
+    return fail(DU_ECUDA, "decode step: a device wait timed out (grid barrier or tensor-parallel peer); step aborted");
 }
 
 static int get_graph(du_model *m, int batch, cudaGraphExec_t *out, Graph **gout = nullptr)
@@ -1044,7 +1051,24 @@ DU_API int du_tp_init(du_model *m, const void *nccl_unique_id, int timeout_ms)
     int rc = nccl_check(m, ncclInProgress, "ncclCommInitRankConfig");
     if (rc) return rc;
     m->tp_ready = true;
-    return DU_OK;
+    return tp_comm_alloc(&m->tpc, ((size_t)m->maxb * m->H + 3) & ~(size_t)3);
+}
+
+DU_API int du_tp_comm_handle(du_model *m, void *handle_out64)
+{
+    DU_GUARD(m);
+    DU_CHECK_ARG(handle_out64 != nullptr, "du_tp_comm_handle: null output");
+    if (m->tp == 1 || !m->tp_ready) return fail(DU_ESTATE, "du_tp_comm_handle: call du_tp_init first");
+    return tp_comm_handle(&m->tpc, handle_out64);
+}
+
+DU_API int du_tp_comm_open(du_model *m, const void *handles, int nranks)
+{
+    DU_GUARD(m);
+    DU_CHECK_ARG(handles != nullptr && nranks == m->tp, "du_tp_comm_open: need one 64-byte handle per rank");
+    if (m->tp == 1 || !m->tp_ready) return fail(DU_ESTATE, "du_tp_comm_open: call du_tp_init first");
+    if (!m->graphs.empty()) return fail(DU_ESTATE, "du_tp_comm_open: open before the first decode step");
+    return tp_comm_open(&m->tpc, handles, nranks, m->rank);
 }
 
 DU_API int du_forward(du_model *m, const int32_t *ids, int batch, int seq_len, int use_cache, int last_pos_only,

@@ -131,6 +131,19 @@ class LlamaForCausalLM(LLM):
         buf = C.create_string_buffer(bytes(unique_id), 128)
         _lib.call("du_tp_init", self._h, buf, timeout_ms)
 
+    def p2p_handle(self) -> bytes:
+        """This rank's 64-byte IPC handle for the peer-memory allreduce (after init_tp)."""
+        buf = C.create_string_buffer(64)
+        _lib.call("du_tp_comm_handle", self._h, buf)
+        return buf.raw
+
+    def init_p2p(self, handles):
+        """Maps every rank's communication buffer (handles in rank order); decode then reduces
+        over NVLink peer memory instead of NCCL.  Every rank must call it before its first decode step."""
+        blob = b"".join(bytes(h) for h in handles)
+        buf = C.create_string_buffer(blob, len(blob))
+        _lib.call("du_tp_comm_open", self._h, buf, len(handles))
+
     def forward(self, ids, use_cache: bool = True, last_pos_only: bool = True, want_logits: bool = True):
         """MiniCPM5Model.Forward: ids [batch, seq] -> (logits, greedy next ids)."""
         ids = np.ascontiguousarray(np.atleast_2d(np.asarray(ids, dtype=np.int32)))

@@ -119,6 +119,15 @@ DU_API int du_nccl_unique_id(void *out128);
  * counterpart: the reference is single-GPU).  Non-blocking communicator
  * polled against timeout_ms. */
 DU_API int du_tp_init(du_model *m, const void *nccl_unique_id, int timeout_ms);
+/* Optional, after du_tp_init and before the first decode step (no reference
+ * counterpart).  du_tp_comm_handle writes this rank's 64-byte CUDA IPC handle of
+ * its peer-communication buffer; once every rank has every handle,
+ * du_tp_comm_open(m, handles, tp_size) -- handles in rank order -- maps the
+ * peers' buffers, and the decode graphs then reduce o_proj / down_proj partial
+ * sums with a one-shot NVLink peer-memory allreduce instead of ncclAllReduce
+ * (prefill keeps NCCL).  All ranks must open, or none. */
+DU_API int du_tp_comm_handle(du_model *m, void *handle_out64);
+DU_API int du_tp_comm_open(du_model *m, const void *handles, int nranks);
 
 /* Host-only (no device work): the slice of a global tensor that rank
  * cfg->tp_rank keeps.  tensor is a stem of IMP's file names

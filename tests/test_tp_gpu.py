@@ -1,8 +1,9 @@
 """Tensor parallelism on 2 GPUs (one process per GPU, NCCL inside the library):
 a TP=2 model loaded from the same IMP-format export must produce the oracle's
 greedy tokens and logits (within 1e-3 relative) for prefill + 24 decode steps,
-through both du_decode_step and the device-resident du_decode_loop.  Skipped
-with fewer than 2 GPUs."""
+through both du_decode_step and the device-resident du_decode_loop, with the
+decode reductions on NCCL and on the NVLink peer-memory allreduce
+(du_tp_comm_open).  Skipped with fewer than 2 GPUs."""
 import ctypes as C
 import os
 
@@ -16,7 +17,7 @@ pytestmark = pytest.mark.gpu
 CFG = dict(hidden=512, inter=1024, layers=2, hq=8, hkv=4, hd=64, vocab=2048)
 
 
-def _rank(rank, world, q_in, q_out):
+def _rank(rank, world, q_in, q_out, q_h, p2p):
     try:
         torch.cuda.set_device(rank)
         from deepunity_b200 import _lib, LlamaForCausalLM, LLMQuant
@@ -35,6 +36,19 @@ def _rank(rank, world, q_in, q_out):
         else:
             uid = q_in.get(timeout=120)
         m.init_tp(uid, timeout_ms=60000)
+        if p2p:     # rank 0 gathers the IPC handles and hands every rank the full list
+            if rank == 0:
+                hs = {0: m.p2p_handle()}
+                for _ in range(world - 1):
+                    r_, h_ = q_h.get(timeout=120)
+                    hs[r_] = h_
+                allh = [hs[r_] for r_ in range(world)]
+                for _ in range(world - 1):
+                    q_in.put(allh)
+            else:
+                q_h.put((rank, m.p2p_handle()))
+                allh = q_in.get(timeout=120)
+            m.init_p2p(allh)
         prompt = np.random.default_rng(5).integers(0, cfg.vocab, 12).astype(np.int32)
         logits, nxt = m.forward(prompt[None, :])
         toks = [int(nxt[0])]
@@ -48,13 +62,14 @@ def _rank(rank, world, q_in, q_out):
         q_out.put((rank, None, None, repr(e)))
 
 
-def test_tp2_matches_oracle():
+@pytest.mark.parametrize("p2p", [False, True], ids=["nccl", "p2p"])
+def test_tp2_matches_oracle(p2p):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
     os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
     ctx = mp.get_context("spawn")
-    q_in, q_out = ctx.Queue(), ctx.Queue()
-    procs = [ctx.Process(target=_rank, args=(r, 2, q_in, q_out)) for r in range(2)]
+    q_in, q_out, q_h = ctx.Queue(), ctx.Queue(), ctx.Queue()
+    procs = [ctx.Process(target=_rank, args=(r, 2, q_in, q_out, q_h, p2p)) for r in range(2)]
     for p in procs:
         p.start()
     res = {}
