@@ -21,11 +21,12 @@
 //
 // flash_decode_cluster_kernel (the model's decode and prefill path): the C
 // splits of one (row, kv head) form one thread-block cluster.  Each CTA leaves
-// its split's (m, l, acc) in its own shared memory; after a cluster barrier CTA
-// r merges output elements [r * G*HD/C, (r + 1) * G*HD/C): C consecutive lanes
-// per output each read one split's state through distributed shared memory and
-// combine with shuffle butterflies (fixed order), so there are no global
-// partials, atomics or second read round trip.
+// its split's (m, l, acc) in shared memory and pushes each output element's
+// value, and every head's (m, l), into the shared memory of the CTA that merges
+// it (distributed shared-memory stores): CTA r merges output elements
+// [r * G*HD/C, (r + 1) * G*HD/C).  One cluster barrier later every CTA reads
+// only its own shared memory and merges in split order, so there are no global
+// partials, atomics or remote-read round trips.
 #include <cooperative_groups.h>
 
 #include "attn_impl.cuh"
@@ -80,53 +81,73 @@ static int fd_launch(const FdParams &p, int G, int nsplit, int nq, cudaStream_t 
 
 namespace cg = cooperative_groups;
 
+// Shared memory of the cluster kernel after the tiles and the tensor-core
+// operands: where the other splits push their state for this CTA's outputs.
+template <int HD, int C>
+__host__ __device__ constexpr size_t fdc_recv_bytes()
+{
+    return sizeof(float) * ((size_t)C * (FD_MAXG * HD / C) + (size_t)C * FD_MAXG * 2);
+}
+
 template <int HD, int C>
 __global__ void __launch_bounds__(FDC_THREADS) flash_decode_cluster_kernel(const FdParams p, int G, int new_rows)
 {
+    constexpr int PER_MAX = FD_MAXG * HD / C;        // outputs merged per CTA, at most
     extern __shared__ __align__(16) unsigned char fd_smem[];
     __shared__ FdShared<HD> sh;
     cg::cluster_group cluster = cg::this_cluster();
     const int split = blockIdx.x, kvh = blockIdx.y, row = blockIdx.z;     // gridDim.x == C == cluster size
+    float *rcv_o = reinterpret_cast<float *>(fd_smem + 4 * FD_TILE * (HD + 8) * sizeof(__half) + fd_mma_extra_bytes<HD>());
+    float *rcv_ml = rcv_o + C * PER_MAX;             // [C][FD_MAXG][2]
+    // first phase of the cluster barrier: every CTA of the cluster has started before
+    // any CTA stores into a peer's shared memory (waited on just before the push)
+    asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
     if (new_rows >= 0) fd_prefetch<HD, FDC_THREADS, true>(p, row, kvh, split, C, new_rows, fd_smem);
     pdl_wait();      // q (and this step's K/V rows) come from the previous kernel
     pdl_trigger();
     fd_unit<HD, FDC_THREADS, true>(p, G, row, kvh, split, C, fd_smem, sh, new_rows);
-    cluster.sync();  // every split's state is in its CTA's shared memory
-    // CTA `split` merges outputs [split * per, (split + 1) * per): C consecutive lanes
-    // per output, lane r reading split r's state; butterflies over the C lanes
+    asm volatile("barrier.cluster.wait.aligned;" ::: "memory");
+
+    // push: output o of this split's acc goes to CTA o / per, slot [split][o % per];
+    // (m, l) of every head to every CTA
     const int n_out = G * HD, per = (n_out + C - 1) / C;
-    const int r = threadIdx.x % C;
-    const float *rm = cluster.map_shared_rank(sh.m, r);
-    const float *rl = cluster.map_shared_rank(sh.l, r);
-    const float *ro = cluster.map_shared_rank(reinterpret_cast<float *>(fd_smem), r);
-    for (int i0 = 0; i0 < per; i0 += FDC_THREADS / C) {
-        const int i = i0 + threadIdx.x / C;
-        const int o = split * per + i;
-        const bool live = i < per && o < n_out;
-        const int g = live ? o / HD : 0;
-        const float m_r = live ? rm[g] : FD_NEG;
-        const float l_r = live ? rl[g] : 0.0f;
-        const float o_r = live ? ro[o] : 0.0f;
-        float M = m_r;
-#pragma unroll
-        for (int s = C / 2; s > 0; s >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, s));
-        const float w = expf(m_r - M);
-        float L = l_r * w, O = o_r * w;
-#pragma unroll
-        for (int s = C / 2; s > 0; s >>= 1) {
-            L += __shfl_xor_sync(0xffffffffu, L, s);
-            O += __shfl_xor_sync(0xffffffffu, O, s);
-        }
-        if (live && r == 0) p.out[((size_t)row * p.hq + kvh * G) * HD + o] = O * (1.0f / fmaxf(L, 1e-12f));
+    const float *so = reinterpret_cast<const float *>(fd_smem);
+    for (int o = threadIdx.x; o < n_out; o += FDC_THREADS) {
+        const int j = o / per;
+        cluster.map_shared_rank(rcv_o, j)[split * PER_MAX + (o - j * per)] = so[o];
     }
-    cluster.sync();  // peers read this CTA's shared memory until here
+    if (threadIdx.x < C * G) {
+        const int j = threadIdx.x / G, g = threadIdx.x - j * G;
+        float *d = cluster.map_shared_rank(rcv_ml, j) + (split * FD_MAXG + g) * 2;
+        d[0] = sh.m[g];
+        d[1] = sh.l[g];
+    }
+    cluster.sync();  // every split's state for this CTA's outputs is in its own shared memory
+
+    // merge outputs [split * per, (split + 1) * per) in split order
+    for (int i = threadIdx.x; i < per; i += FDC_THREADS) {
+        const int o = split * per + i;
+        if (o >= n_out) break;
+        const int g = o / HD;
+        float M = FD_NEG;
+#pragma unroll
+        for (int r = 0; r < C; r++) M = fmaxf(M, rcv_ml[(r * FD_MAXG + g) * 2]);
+        float L = 0.0f, O = 0.0f;
+#pragma unroll
+        for (int r = 0; r < C; r++) {
+            const float w = expf(rcv_ml[(r * FD_MAXG + g) * 2] - M);
+            L = fmaf(rcv_ml[(r * FD_MAXG + g) * 2 + 1], w, L);
+            O = fmaf(rcv_o[r * PER_MAX + i], w, O);
+        }
+        p.out[((size_t)row * p.hq + kvh * G) * HD + o] = O * (1.0f / fmaxf(L, 1e-12f));
+    }
 }
 
 template <int HD, int C>
 static int fdc_launch(const FdParams &p, int G, int nq, cudaStream_t st, int new_rows, bool probe, int *fits)
 {
     auto kern = flash_decode_cluster_kernel<HD, C>;
-    const size_t smem = 4 * FD_TILE * (HD + 8) * sizeof(__half) + fd_mma_extra_bytes<HD>();
+    const size_t smem = 4 * FD_TILE * (HD + 8) * sizeof(__half) + fd_mma_extra_bytes<HD>() + fdc_recv_bytes<HD, C>();
     static bool attr_set[64] = {};
     int dev = 0;
     cudaGetDevice(&dev);

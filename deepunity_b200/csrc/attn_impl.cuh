@@ -195,14 +195,29 @@ __device__ __forceinline__ void fd_unit(const FdParams &p, int G, int row, int k
     if (ntiles > 0)
         fd_load_rows<HD, NT>(p, geo, 0, 0, pre_new < 0 ? start : geo.kv_len - pre_new, 0x7fffffff, tiles);
     if (MMA) {
-        for (int i = tid; i < 16 * HD; i += NT) {
-            const int g = i / HD, d = i - g * HD;
-            const float q = g < G ? p.q[((size_t)row * p.hq + kvh * G + g) * HD + d] * p.scale : 0.0f;
-            const __half h = __float2half_rn(q);
-            qh[0][g][d] = h;
-            qh[1][g][d] = __float2half_rn(q - __half2float(h));
+        // q rows g < G as hi + lo halves (rows G..15 zero); all loads issued before the stores
+        constexpr int QV = (16 * HD / 4 + NT - 1) / NT;     // float4 per thread
+        float4 qv[QV];
+#pragma unroll
+        for (int k = 0; k < QV; k++) {
+            const int i4 = tid + k * NT, g = i4 * 4 / HD, d = i4 * 4 - g * HD;
+            qv[k] = g < G && i4 < 16 * HD / 4
+                        ? *reinterpret_cast<const float4 *>(p.q + ((size_t)row * p.hq + kvh * G + g) * HD + d)
+                        : make_float4(0.f, 0.f, 0.f, 0.f);
         }
-        for (int i = tid; i < 2 * 16 * PLD; i += NT) (&ph[0][0][0])[i] = __float2half_rn(0.0f);
+#pragma unroll
+        for (int k = 0; k < QV; k++) {
+            const int i4 = tid + k * NT, g = i4 * 4 / HD, d = i4 * 4 - g * HD;
+            if (i4 >= 16 * HD / 4) break;
+            const float q[4] = {qv[k].x * p.scale, qv[k].y * p.scale, qv[k].z * p.scale, qv[k].w * p.scale};
+#pragma unroll
+            for (int e = 0; e < 4; e++) {
+                const __half h = __float2half_rn(q[e]);
+                qh[0][g][d + e] = h;
+                qh[1][g][d + e] = __float2half_rn(q[e] - __half2float(h));
+            }
+        }
+        for (int i = tid; i < 2 * 16 * PLD / 8; i += NT) reinterpret_cast<uint4 *>(&ph[0][0][0])[i] = make_uint4(0u, 0u, 0u, 0u);
     } else {
         for (int i = tid; i < G * HD; i += NT) {
             const int g = i / HD, d = i - g * HD;
