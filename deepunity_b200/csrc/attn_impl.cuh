@@ -80,11 +80,12 @@ __device__ __forceinline__ void fd_mma(float (&c)[4], const uint32_t (&a)[4], ui
 }
 
 // Bytes after the K/V tiles that the tensor-core unit (TO_SMEM, 256 threads) also
-// uses: q and P as fp16 hi + lo parts, [2][16][HD + 8] and [2][16][FD_TILE + 8].
+// uses: q and P as fp16 hi + lo parts, [2][16][HD + 8] and [2][16][FD_TILE + 8],
+// and the scores head-major, [FD_MAXG][FD_TILE + 4] fp32.
 template <int HD>
 __host__ __device__ constexpr size_t fd_mma_extra_bytes()
 {
-    return (size_t)2 * 16 * (HD + 8) * 2 + (size_t)2 * 16 * (FD_TILE + 8) * 2;
+    return (size_t)2 * 16 * (HD + 8) * 2 + (size_t)2 * 16 * (FD_TILE + 8) * 2 + (size_t)FD_MAXG * (FD_TILE + 4) * 4;
 }
 
 // Positions of unit (row, kv head, split).
@@ -147,22 +148,23 @@ __device__ __forceinline__ void fd_load_rows(const FdParams &p, const FdGeom &g,
     fd_cp_commit();
 }
 
-// Loads, ahead of the producer of this step's K/V rows, the rows of tile 0 that
-// earlier steps wrote (positions below kv_len - new_rows).  The unit is then
-// run with pre_new = new_rows.
+// Loads, ahead of the producer of this step's K/V rows, the rows of tiles 0 and
+// 1 (the two tile buffers) that earlier steps wrote: positions below kv_len -
+// new_rows; two commit groups.  The unit is then run with pre_new = new_rows.
 template <int HD, int NT, bool EVEN = false>
 __device__ __forceinline__ void fd_prefetch(const FdParams &p, int row, int kvh, int split, int nsplit, int new_rows,
                                             unsigned char *tiles)
 {
     const FdGeom g = fd_geom<HD, EVEN>(p, row, kvh, split, nsplit);
     if (g.ntiles > 0) fd_load_rows<HD, NT>(p, g, 0, 0, g.start, g.kv_len - new_rows, tiles);
+    if (g.ntiles > 1) fd_load_rows<HD, NT>(p, g, 1, 1, g.start, g.kv_len - new_rows, tiles);
 }
 
 // Processes unit (row, kvh, split) of a launch with `nsplit` splits per
 // (row, kv head).  The CTA that finishes the last split of a (row, kv head)
 // merges all splits into p.out.  All NT threads must call it.  pre_new < 0:
 // nothing was prefetched; else fd_prefetch(..., new_rows = pre_new) ran and
-// only tile 0's rows from kv_len - pre_new on are loaded here.
+// only the rows of tiles 0 and 1 from kv_len - pre_new on are loaded here.
 //
 // TO_SMEM: instead of publishing to p.part_o / p.part_ml and combining through
 // global memory, leave this split's unnormalised state in shared memory --
@@ -185,6 +187,8 @@ __device__ __forceinline__ void fd_unit(const FdParams &p, int G, int row, int k
     constexpr int QLD = HD + 8, PLD = FD_TILE + 8;
     auto qh = reinterpret_cast<__half (*)[16][QLD]>(tiles + TILE_BYTES);                     // [2][16][QLD]
     auto ph = reinterpret_cast<__half (*)[16][PLD]>(tiles + TILE_BYTES + (size_t)2 * 16 * QLD * 2);   // [2][16][PLD]
+    auto pst = reinterpret_cast<float (*)[FD_TILE + 4]>(tiles + TILE_BYTES + (size_t)2 * 16 * QLD * 2 +
+                                                        (size_t)2 * 16 * PLD * 2);              // [FD_MAXG][FD_TILE + 4]
     auto Ks = reinterpret_cast<__half (*)[FD_TILE][LDS]>(tiles);
     auto Vs = reinterpret_cast<__half (*)[FD_TILE][LDS]>(tiles + 2 * FD_TILE * LDS * 2);
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -248,8 +252,14 @@ __device__ __forceinline__ void fd_unit(const FdParams &p, int G, int row, int k
 
     for (int t = 0; t < ntiles; t++) {
         const int buf = t & 1;
-        if (t + 1 < ntiles) { fd_load_rows<HD, NT>(p, geo, t + 1, buf ^ 1, 0, 0x7fffffff, tiles); fd_cp_wait<1>(); }
-        else { fd_cp_wait<0>(); }
+        if (t + 1 < ntiles) {
+            // tile 1's older rows came with the prefetch
+            fd_load_rows<HD, NT>(p, geo, t + 1, buf ^ 1, (t == 0 && pre_new >= 0) ? geo.kv_len - pre_new : 0, 0x7fffffff,
+                                 tiles);
+            fd_cp_wait<1>();
+        } else {
+            fd_cp_wait<0>();
+        }
         __syncthreads();
 
         // ---- scores: each K chunk is read once and used for every head
@@ -270,8 +280,7 @@ __device__ __forceinline__ void fd_unit(const FdParams &p, int G, int row, int k
             const int g = lane >> 2, j = n0 + (lane & 3) * 2;
             if (g < G) {
                 const int pos = start + t * FD_TILE + j;
-                sh.ps[j][g] = pos < end ? c[0] : FD_NEG;
-                sh.ps[j + 1][g] = pos + 1 < end ? c[1] : FD_NEG;
+                *reinterpret_cast<float2 *>(&pst[g][j]) = make_float2(pos < end ? c[0] : FD_NEG, pos + 1 < end ? c[1] : FD_NEG);
             }
         } else {
             float s[FD_MAXG];
@@ -314,19 +323,27 @@ __device__ __forceinline__ void fd_unit(const FdParams &p, int G, int row, int k
 
         // ---- online softmax, one warp per head
         for (int g = warp; g < G; g += NW) {
-            const float a = sh.ps[2 * lane][g], b = sh.ps[2 * lane + 1][g];
+            float a, b;
+            if (MMA) {              // head-major scores: one conflict-free 8-byte read per lane
+                const float2 ab = *reinterpret_cast<const float2 *>(&pst[g][2 * lane]);
+                a = ab.x;
+                b = ab.y;
+            } else {
+                a = sh.ps[2 * lane][g];
+                b = sh.ps[2 * lane + 1][g];
+            }
             const float mt = warp_max(fmaxf(a, b));
             const float m_old = sh.m[g];
             const float m_new = fmaxf(m_old, mt);
             const float pa = expf(a - m_new), pb = expf(b - m_new);
-            sh.ps[2 * lane][g] = pa;
-            sh.ps[2 * lane + 1][g] = pb;
             if (MMA) {
                 const __half ha = __float2half_rn(pa), hb = __float2half_rn(pb);
-                ph[0][g][2 * lane] = ha;
-                ph[0][g][2 * lane + 1] = hb;
-                ph[1][g][2 * lane] = __float2half_rn(pa - __half2float(ha));
-                ph[1][g][2 * lane + 1] = __float2half_rn(pb - __half2float(hb));
+                *reinterpret_cast<__half2 *>(&ph[0][g][2 * lane]) = __halves2half2(ha, hb);
+                *reinterpret_cast<__half2 *>(&ph[1][g][2 * lane]) =
+                    __halves2half2(__float2half_rn(pa - __half2float(ha)), __float2half_rn(pb - __half2float(hb)));
+            } else {
+                sh.ps[2 * lane][g] = pa;
+                sh.ps[2 * lane + 1][g] = pb;
             }
             const float ts = warp_sum(pa + pb);
             if (lane == 0) {
