@@ -27,6 +27,19 @@ int cuda_fail(cudaError_t e, const char *what);
 
 enum QuantKind { Q_F16 = 0, Q_I8 = 1, Q_I4 = 2 };
 
+constexpr int TP_MAX_RANKS = 8;
+
+// Device-side handles of the peer-memory tensor-parallel reduction (device
+// memory, written when the peers are opened; device code in tp_fuse.cuh).
+struct TpFuse {
+    uint2 *peer_recv[TP_MAX_RANKS];  // rank r's receive words [2 parities][TP_MAX_RANKS][maxn]
+    unsigned *seq;                   // this rank's last completed sequence number
+    unsigned *done;                  // CTAs finished in the current launch (the last one resets it)
+    int *err;                        // set on a timed-out wait
+    size_t maxn;                     // elements per slot
+    int rank, nranks;
+};
+
 // 16-byte streaming load: weights are read exactly once per launch, so they
 // bypass L1 (no_allocate) and come through the read-only path.
 __device__ __forceinline__ uint4 ldg_stream(const void *p)

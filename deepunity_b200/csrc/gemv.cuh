@@ -43,9 +43,12 @@ namespace du {
 
 constexpr int GV_THREADS = 256;
 constexpr int GV_WARPS = GV_THREADS / 32;
+constexpr int GV_WARPS_WIDE = 16;   // one CTA per SM (decode token tile 1, large K)
 
 enum GemvMap { MAP_IDENT = 0, MAP_ROPE_PAIR = 1, MAP_GATEUP = 2 };
-enum GemvEpi { EPI_STORE = 0, EPI_RESID = 1, EPI_QKV = 2, EPI_GATEUP = 3, EPI_LOGITS = 4 };
+// EPI_TP_RESID: resid += the sum over the tensor-parallel ranks' outputs, through
+// peer memory (tp_fuse.cuh); y is not written.  The launch must fit in one wave.
+enum GemvEpi { EPI_STORE = 0, EPI_RESID = 1, EPI_QKV = 2, EPI_GATEUP = 3, EPI_LOGITS = 4, EPI_TP_RESID = 5 };
 
 struct GemvParams {
     // activations in: x fp32 [M][ldx]; optional RMSNorm with gamma' = gamma - 1 (fp16)
@@ -80,6 +83,9 @@ struct GemvParams {
     float *am_val;          // [M][gridDim.x]
     int *am_idx;
     int vocab_off;
+    // EPI_TP_RESID: peer handles (device memory) and the residual
+    const TpFuse *tp;
+    float *resid;
 };
 
 // COLS: weight columns per 16-byte chunk; XU4: uint4s of staged activations per chunk

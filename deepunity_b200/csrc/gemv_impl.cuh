@@ -11,6 +11,7 @@
 #pragma once
 
 #include "gemv.cuh"
+#include "tp_fuse.cuh"
 
 namespace du {
 
@@ -269,10 +270,26 @@ __host__ __device__ constexpr size_t gemv_ring_bytes()
 
 // Epilogue of the finished row group starting at logical row lr0 (v: every lane
 // holds every value); lane j * MT + m owns output (row j, token m).
-template <int QT, int MT, int RW>
+// TPR: the EPI_TP_RESID kernels (a separate instantiation, so that the other
+// epilogues compile exactly as without it): each output goes to every rank.
+template <int QT, int MT, int RW, bool TPR = false>
 __device__ __forceinline__ void gv_epilogue(const GemvParams &p, int lr0, const float (&v)[RW][MT], float *am_v,
-                                        int *am_i, int lane)
+                                        int *am_i, int lane, unsigned tp_s = 0u)
 {
+    if constexpr (TPR) {
+#pragma unroll
+        for (int j = 0; j < RW; j++)
+#pragma unroll
+            for (int m = 0; m < MT; m++) {
+                const int lr = lr0 + j;
+                if (lane == j * MT + m && m < p.M && lr < p.N) {
+                    float f = v[j][m];
+                    if (QT == Q_I8) f *= gv_row_scale<QT>(p, lr);
+                    tp_push(*p.tp, tp_s, (size_t)m * p.N + lr, f);
+                }
+            }
+        return;
+    }
     if (p.epi == EPI_QKV || p.epi == EPI_GATEUP) {
 #pragma unroll
         for (int jp = 0; jp < RW; jp += 2)
@@ -316,7 +333,7 @@ __device__ __forceinline__ void gv_epilogue(const GemvParams &p, int lr0, const 
 // several warps leaves per-warp partial sums in shared memory; the warp that
 // holds its last unit adds them in warp order (deterministic) and runs the
 // epilogue.
-template <int QT, int MT, int RW, int D, int NW = GV_WARPS>
+template <int QT, int MT, int RW, int D, int NW = GV_WARPS, bool TPR = false>
 struct GemvStream {
     using T = GvTraits<QT>;
     int lane, warp, nchunk, S, gshift;
@@ -332,6 +349,7 @@ struct GemvStream {
     int is_g, is_s, is_stage, is_left;
     int ipr[RW];
     uint64_t pol;         // L2 evict-first policy of the weight stream
+    unsigned tp_s;        // TPR: sequence number of this launch's reduction
 
     __device__ __forceinline__ int unit_lo(int w) const { return (int)(((int64_t)w * U) / NW); }
 
@@ -405,7 +423,7 @@ struct GemvStream {
     __device__ __forceinline__ void epilogue(const GemvParams &p, int lr0, const float (&v)[RW][MT], float *am_v,
                                              int *am_i) const
     {
-        gv_epilogue<QT, MT, RW>(p, lr0, v, am_v, am_i, lane);
+        gv_epilogue<QT, MT, RW, TPR>(p, lr0, v, am_v, am_i, lane, tp_s);
     }
 
     // Phase 2: activations -> smem, stream, epilogue.  All threads of the CTA call it.
@@ -417,6 +435,7 @@ struct GemvStream {
         uint4 *xq = reinterpret_cast<uint4 *>(x_smem);
         gv_stage_x<QT, MT, NW>(p, xq, sh, nchunk);
         after_stage();
+        if constexpr (TPR) tp_s = tp_next_seq(*p.tp);
 
         // accumulators: INT8 exact int32 plane sums; INT4 / FP16 fp32
         int s8[RW][MT][3];
@@ -582,6 +601,20 @@ struct GemvStream {
                     for (int m = 0; m < MT; m++) v[j][m] += pb[j * MT + m];
             }
             epilogue(p, (g_begin + gl) * RW, v, am_v, am_i);
+        }
+
+        if constexpr (TPR) {
+            // every rank's values of this CTA's rows (the same rows on every rank),
+            // added to the residual in rank order
+            const TpFuse &t = *p.tp;
+            const int r0 = g_begin * RW, r1 = min((g_begin + U / S) * RW, p.N), nr = r1 - r0;
+            for (int e = threadIdx.x; e < nr * p.M; e += NW * 32) {
+                const int m = e / nr, lr = r0 + (e - m * nr);
+                float sum;
+                if (!tp_wait_sum(t, tp_s, (size_t)m * p.N + lr, sum)) break;
+                p.resid[(size_t)m * p.ldy + lr] += sum;
+            }
+            tp_launch_done(t, tp_s);
         }
 
         if (p.epi == EPI_LOGITS) {

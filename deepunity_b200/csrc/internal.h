@@ -13,6 +13,7 @@ int num_sms();
 // gemv.cu
 int launch_gemv(int qt, GemvParams p, cudaStream_t st);
 size_t gemv_smem_bytes(int qt, int mt, int64_t row_bytes);
+int gemv_ctas_per_sm(int qt, int mt, int64_t row_bytes);   // CTAs per SM of the launcher's layout
 size_t gemv_x_bytes(int qt, int mt, int64_t row_bytes);     // activation stage of one CTA
 int gemv_grid_for(int N, int M, int want);
 void gemv_set_pdl(bool on);

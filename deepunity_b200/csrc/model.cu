@@ -15,6 +15,7 @@
 #include <atomic>
 #include <cmath>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <map>
 #include <string>
@@ -542,6 +543,23 @@ struct StepIO {
 
 enum Stage { ST_QKV = 0, ST_ATTN = 1, ST_O = 2, ST_GATEUP = 3, ST_DOWN = 4 };
 
+// Decode reductions of a tensor-parallel model may use the peer-memory path.
+static bool tp_peer_ok(const du_model *m, const StepIO &io)
+{
+    return m->tp > 1 && io.p2p && m->tpc.ready && (size_t)io.M * m->H <= m->tpc.maxn;
+}
+
+// The peer-memory reduction runs in the O / down GEMV's epilogue; DU_TP_FUSE=0
+// in the environment runs it as a separate kernel after the GEMV instead.
+static bool tp_fuse_enabled()
+{
+    static const bool on = [] {
+        const char *e = getenv("DU_TP_FUSE");
+        return e == nullptr || atoi(e) != 0;
+    }();
+    return on;
+}
+
 // One stage of layer l for the token rows of `io`.  With tensor parallelism
 // the O and down stages end in an allreduce of the partial sums plus the
 // residual add (collective = false leaves both out, for kernel timing).
@@ -575,7 +593,10 @@ static GemvParams stage_gemv_params(du_model *m, const StepIO &io, int l, int st
         }
         p.N = H; p.map = MAP_IDENT;
         if (m->tp == 1) { p.epi = EPI_RESID; p.y = m->x_res; p.ldy = H; }
-        else { p.epi = EPI_STORE; p.y = m->part; p.ldy = H; }
+        else if (tp_peer_ok(m, io) && tp_fuse_enabled()) {
+            // decode: the allreduce over peer memory runs in the GEMV's epilogue
+            p.epi = EPI_TP_RESID; p.y = m->part; p.ldy = H; p.tp = m->tpc.dev; p.resid = m->x_res;
+        } else { p.epi = EPI_STORE; p.y = m->part; p.ldy = H; }
         break;
     default:       // ST_GATEUP: RMSNorm(ln2) -> gate|up GEMV -> SiLU(g) * u
         p = gp_base(m, ly.w_gu, ly.s_gu, H);
@@ -624,10 +645,11 @@ static int enqueue_stage(du_model *m, const StepIO &io, int l, int stage, bool c
                                            hd, m->cap, powf((float)hd, -0.5f), m->att, st, io.kv_new);
     }
     if (stage < ST_QKV || stage > ST_DOWN) return fail(DU_EINVAL, "unknown stage");
-    if ((rc = run_gemv(m, qt, stage_gemv_params(m, io, l, stage), M))) return rc;
-    if ((stage == ST_O || stage == ST_DOWN) && m->tp > 1 && collective) {
-        if (io.p2p && m->tpc.ready && (size_t)M * H <= m->tpc.maxn)
-            return launch_tp_allreduce(&m->tpc, m->part, m->x_res, (size_t)M * H, m->d_err, st);
+    GemvParams gp = stage_gemv_params(m, io, l, stage);
+    if (gp.epi == EPI_TP_RESID && !collective) gp.epi = EPI_STORE;     // partial sums into m->part only
+    if ((rc = run_gemv(m, qt, gp, M))) return rc;
+    if ((stage == ST_O || stage == ST_DOWN) && m->tp > 1 && collective && gp.epi != EPI_TP_RESID) {
+        if (tp_peer_ok(m, io)) return launch_tp_allreduce(&m->tpc, m->part, m->x_res, (size_t)M * H, st);
         if ((rc = allreduce_sum(m, m->part, (size_t)M * H))) return rc;
         if ((rc = launch_add_inplace(m->x_res, m->part, (size_t)M * H, st))) return rc;
     }
@@ -672,7 +694,10 @@ static int enqueue_head(du_model *m, const StepIO &io)
     int rc = DU_OK;
     const int R = io.logits_rows;
     GemvParams p = head_gemv_params(m, io);
-    const int nparts = gemv_grid_for(p.N, 1, m->am_parts);   // same CTA count for every token tile
+    // one CTA count for every token tile (the argmax reads nparts partials per row); a
+    // single row uses the token-tile-1 layout's count, so that it runs in one wave
+    const int nparts = gemv_grid_for(
+        p.N, 1, R == 1 ? gemv_ctas_per_sm(Q_F16, 1, p.row_bytes) * num_sms() : m->am_parts);
     p.grid = nparts;
     const int mt = gemv_max_tokens(Q_F16, p.row_bytes);
     for (int t0 = 0; t0 < R; t0 += mt) {
@@ -1068,7 +1093,7 @@ DU_API int du_tp_comm_open(du_model *m, const void *handles, int nranks)
     DU_CHECK_ARG(handles != nullptr && nranks == m->tp, "du_tp_comm_open: need one 64-byte handle per rank");
     if (m->tp == 1 || !m->tp_ready) return fail(DU_ESTATE, "du_tp_comm_open: call du_tp_init first");
     if (!m->graphs.empty()) return fail(DU_ESTATE, "du_tp_comm_open: open before the first decode step");
-    return tp_comm_open(&m->tpc, handles, nranks, m->rank);
+    return tp_comm_open(&m->tpc, handles, nranks, m->rank, m->d_err);
 }
 
 DU_API int du_forward(du_model *m, const int32_t *ids, int batch, int seq_len, int use_cache, int last_pos_only,

@@ -5,91 +5,34 @@
 // carry tokens x hidden fp32 values: 16 KB at batch 1.  At that size
 // ncclAllReduce costs a fixed ~10 us per call.  With 64 calls per step that is
 // more than the GEMV time TP saves.  Each rank maps every peer's communication
-// buffer (CUDA IPC) and one kernel does, per element i of its slice:
-//   1. push: one 64-bit store of (sequence number << 32 | value) into slot
-//      [parity][my rank][i] of every rank's receive buffer (NVLink stores; the
-//      own slot is a local store).  A naturally aligned 64-bit scalar access is
-//      single-copy atomic, so the sequence number in the same word flags the
-//      value: no fence and no separate flag are needed;
-//   2. wait + reduce: poll slot [parity][r][i] of the own buffer for every
-//      rank r until it carries this sequence number (bounded; sets the error
-//      word on timeout), and add the values in rank order, so every rank
-//      computes bit-identical residuals: dst[i] += sum.
+// buffer (CUDA IPC).  The decode graph fuses the reduction into the O / down
+// GEMV epilogue (gemv_impl.cuh); this file holds the buffers, the handle
+// exchange and a standalone kernel for the same protocol (tp_fuse.cuh), which
+// does, per element i of its slice:
+//   1. push this rank's value to every rank's receive buffer;
+//   2. wait for every rank's value and add them in rank order: dst[i] += sum;
 //   3. the last CTA to finish advances the rank's sequence counter.
-// Receive slots alternate by the sequence parity: a rank can run at most one
-// allreduce ahead of a peer (it cannot finish allreduce k + 1 before the peer
-// has contributed to it, which the peer does only after it finished k), so the
-// slot a fast rank writes is never the one a slow rank is still reading.
-// Sequence numbers only grow, so slots never need resetting.  Every rank runs
-// the same sequence of allreduces (the same graphs and prefill chunks).
+// Every rank runs the same sequence of reductions (the same graphs and prefill
+// chunks).
 #include <cstring>
 
 #include "internal.h"
 #include "tp_comm.h"
+#include "tp_fuse.cuh"
 
 namespace du {
 
-constexpr unsigned TP_SPIN_LIMIT = 1u << 24;
-
-struct TpArgs {
-    uint2 *peer_recv[TP_MAX_RANKS];      // rank r's receive region ([2][TP_MAX_RANKS][maxn] (value, seq) words)
-    const uint2 *my_recv;
-    unsigned *seq;                       // this rank's last completed sequence number
-    unsigned *done;                      // CTAs finished in this launch (last one resets it)
-    int *err;
-    const float *src;                    // this rank's partial sums [n]
-    float *dst;                          // residual [n] (+= the sum)
-    int n, rank, nranks;
-    size_t maxn;
-};
-
-__global__ void __launch_bounds__(256) tp_allreduce_kernel(const TpArgs a)
+__global__ void __launch_bounds__(256) tp_allreduce_kernel(const TpFuse t, const float *src, float *dst, int n)
 {
     const int tid = blockIdx.x * blockDim.x + threadIdx.x, nthr = gridDim.x * blockDim.x;
-    const unsigned s = *(volatile unsigned *)a.seq + 1u;
-    const size_t par = s & 1u;
-    // 1. push (value, seq) words
-    for (int i = tid; i < a.n; i += nthr) {
-        const unsigned v = __float_as_uint(a.src[i]);
-        for (int r = 0; r < a.nranks; r++) {
-            uint2 *d = a.peer_recv[r] + (par * TP_MAX_RANKS + a.rank) * a.maxn + i;
-            const unsigned long long word = ((unsigned long long)s << 32) | v;      // one 64-bit access: seen whole
-            asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(d), "l"(word) : "memory");
-        }
+    const unsigned s = tp_next_seq(t);
+    for (int i = tid; i < n; i += nthr) tp_push(t, s, i, src[i]);
+    for (int i = tid; i < n; i += nthr) {
+        float sum;
+        if (!tp_wait_sum(t, s, i, sum)) break;
+        dst[i] += sum;
     }
-    // 2. wait for every rank's word and reduce in rank order
-    bool ok = true;
-    for (int i = tid; i < a.n; i += nthr) {
-        float sum = 0.0f;
-        for (int r = 0; r < a.nranks; r++) {
-            const uint2 *w = a.my_recv + (par * TP_MAX_RANKS + r) * a.maxn + i;
-            unsigned v = 0, n = 0;
-            for (;;) {
-                unsigned long long word;
-                asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(word) : "l"(w) : "memory");
-                v = (unsigned)word;
-                if ((unsigned)(word >> 32) == s) break;
-                if (++n > TP_SPIN_LIMIT || (n & 1023) == 0 && *(volatile int *)a.err) {
-                    atomicExch(a.err, 1);
-                    ok = false;
-                    break;
-                }
-            }
-            if (!ok) break;
-            sum += __uint_as_float(v);
-        }
-        if (!ok) break;
-        a.dst[i] += sum;
-    }
-    // 3. the last CTA advances the sequence
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        __threadfence();
-        if (atomicAdd(a.done, 1u) == gridDim.x - 1u) {
-            *a.done = 0u;
-            *(volatile unsigned *)a.seq = s;
-        }
-    }
+    tp_launch_done(t, s);
 }
 
 size_t tp_comm_bytes(size_t maxn)
@@ -105,6 +48,7 @@ int tp_comm_alloc(TpComm *c, size_t maxn)
     DU_CUDA_TRY(cudaMemset(c->buf, 0, bytes));
     DU_CUDA_TRY(cudaMalloc(&c->ctl, sizeof(unsigned) * 2));
     DU_CUDA_TRY(cudaMemset(c->ctl, 0, sizeof(unsigned) * 2));
+    DU_CUDA_TRY(cudaMalloc(&c->dev, sizeof(TpFuse)));
     return DU_OK;
 }
 
@@ -118,10 +62,11 @@ int tp_comm_handle(TpComm *c, void *out64)
     return DU_OK;
 }
 
-int tp_comm_open(TpComm *c, const void *handles, int nranks, int rank)
+int tp_comm_open(TpComm *c, const void *handles, int nranks, int rank, int *err)
 {
     if (nranks < 2 || nranks > TP_MAX_RANKS || rank < 0 || rank >= nranks)
         return fail(DU_EINVAL, "tp comm: 2..8 ranks");
+    if (!c->buf || !c->dev || !err) return fail(DU_ESTATE, "tp comm: buffer not allocated");
     for (int r = 0; r < nranks; r++) {
         if (r == rank) {
             c->peer[r] = c->buf;
@@ -140,6 +85,20 @@ int tp_comm_open(TpComm *c, const void *handles, int nranks, int rank)
     }
     c->nranks = nranks;
     c->rank = rank;
+    TpFuse h = {};
+    for (int r = 0; r < nranks; r++) h.peer_recv[r] = static_cast<uint2 *>(c->peer[r]);
+    h.seq = c->ctl;
+    h.done = c->ctl + 1;
+    h.err = err;
+    h.maxn = c->maxn;
+    h.rank = rank;
+    h.nranks = nranks;
+    cudaError_t e = cudaMemcpy(c->dev, &h, sizeof(h), cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) {
+        tp_comm_close(c);
+        return cuda_fail(e, "tp comm: handle upload");
+    }
+    c->host = h;
     c->ready = true;
     return DU_OK;
 }
@@ -159,29 +118,19 @@ void tp_comm_free(TpComm *c)
     tp_comm_close(c);
     if (c->buf) cudaFree(c->buf);
     if (c->ctl) cudaFree(c->ctl);
+    if (c->dev) cudaFree(c->dev);
     c->buf = nullptr;
     c->ctl = nullptr;
+    c->dev = nullptr;
 }
 
-int launch_tp_allreduce(TpComm *c, const float *src, float *dst, size_t n, int *err, cudaStream_t st)
+int launch_tp_allreduce(TpComm *c, const float *src, float *dst, size_t n, cudaStream_t st)
 {
     if (!c->ready || n > c->maxn) return fail(DU_ESTATE, "tp allreduce: peer buffers not open or too small");
-    TpArgs a = {};
-    for (int r = 0; r < c->nranks; r++) a.peer_recv[r] = static_cast<uint2 *>(c->peer[r]);
-    a.my_recv = a.peer_recv[c->rank];
-    a.seq = c->ctl;
-    a.done = c->ctl + 1;
-    a.err = err;
-    a.src = src;
-    a.dst = dst;
-    a.n = (int)n;
-    a.rank = c->rank;
-    a.nranks = c->nranks;
-    a.maxn = c->maxn;
     int ncta = (int)((n + 255) / 256);
     if (ncta > 64) ncta = 64;
     if (ncta < 1) ncta = 1;
-    tp_allreduce_kernel<<<ncta, 256, 0, st>>>(a);
+    tp_allreduce_kernel<<<ncta, 256, 0, st>>>(c->host, src, dst, (int)n);
     DU_CUDA_TRY(cudaGetLastError());
     return DU_OK;
 }
