@@ -44,10 +44,8 @@ struct __align__(16) GemvShared {
 //        (8 * sum x_int, 2^-s) in the pad words 24, 25; xscale = 1 / rms (or 1)
 //  INT8: per-token power-of-two scale over the normalised x; xscale = 2^-s
 //  FP16: x * (1 + gamma') in fp32, swizzled; xscale = 1 / rms (or 1)
-// xs[m] receives the per-token factor (xscale) in every thread.
 template <int QT, int MT, int NW>
-__device__ __forceinline__ void gv_stage_x(const GemvParams &p, uint4 *xq, GemvShared<MT, NW> &sh, int nchunk,
-                                           float (&xs)[MT])
+__device__ __forceinline__ void gv_stage_x(const GemvParams &p, uint4 *xq, GemvShared<MT, NW> &sh, int nchunk)
 {
     constexpr int NT = NW * 32;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -104,8 +102,6 @@ __device__ __forceinline__ void gv_stage_x(const GemvParams &p, uint4 *xq, GemvS
             }
         }
         __syncthreads();
-#pragma unroll
-        for (int m = 0; m < MT; m++) xs[m] = sh.xscale[m];
         return;
     }
 
@@ -215,14 +211,13 @@ __device__ __forceinline__ void gv_stage_x(const GemvParams &p, uint4 *xq, GemvS
         if (lane == 0) sh.ssq[warp][m] = w;
     }
     __syncthreads();
-    // every thread derives the factors itself (same summation order in every thread)
-#pragma unroll
-    for (int m = 0; m < MT; m++) {
+    if (tid < MT) {
         float t = 0.0f;
 #pragma unroll
-        for (int i = 0; i < NW; i++) t += sh.ssq[i][m];
-        xs[m] = p.gamma != nullptr ? 1.0f / sqrtf(t / (float)p.K + p.eps) : 1.0f;
+        for (int i = 0; i < NW; i++) t += sh.ssq[i][tid];
+        sh.xscale[tid] = p.gamma != nullptr ? 1.0f / sqrtf(t / (float)p.K + p.eps) : 1.0f;
     }
+    __syncthreads();
 }
 
 __device__ __forceinline__ void gv_epi_pair(const GemvParams &p, int lr0, int m, float x1, float x2)
@@ -438,8 +433,7 @@ struct GemvStream {
                                         int ncta, AfterStage after_stage)
     {
         uint4 *xq = reinterpret_cast<uint4 *>(x_smem);
-        float xs[MT];
-        gv_stage_x<QT, MT, NW>(p, xq, sh, nchunk, xs);
+        gv_stage_x<QT, MT, NW>(p, xq, sh, nchunk);
         after_stage();
         if constexpr (TPR) tp_s = tp_next_seq(*p.tp);
 
@@ -563,10 +557,10 @@ struct GemvStream {
                                 t2 += __shfl_xor_sync(0xffffffffu, t2, o);
                             }
                             const long long tot = t0 + (t1 << 8) + (t2 << 16);   // exact sum q * x_int
-                            v[j][m] = (float)tot * xs[m];
+                            v[j][m] = (float)tot * sh.xscale[m];
                             s8[j][m][0] = s8[j][m][1] = s8[j][m][2] = 0;
                         } else {
-                            v[j][m] = warp_sum(acc[j][m]) * xs[m];
+                            v[j][m] = warp_sum(acc[j][m]) * sh.xscale[m];
                             acc[j][m] = 0.0f;
                         }
                     }
