@@ -549,15 +549,17 @@ static bool tp_peer_ok(const du_model *m, const StepIO &io)
     return m->tp > 1 && io.p2p && m->tpc.ready && (size_t)io.M * m->H <= m->tpc.maxn;
 }
 
-// The peer-memory reduction runs in the O / down GEMV's epilogue; DU_TP_FUSE=0
-// in the environment runs it as a separate kernel after the GEMV instead.
-static bool tp_fuse_enabled()
+// The peer-memory reduction runs in the O / down GEMV's epilogue up to 4 ranks, and
+// as a separate kernel after the GEMV at more (8B INT4, batch 1: TP2 633 vs 581 tok/s
+// fused vs separate, TP8 730 vs 761).  DU_TP_FUSE=1 / 0 in the environment forces
+// either.
+static bool tp_fuse_enabled(const du_model *m)
 {
-    static const bool on = [] {
+    static const int force = [] {
         const char *e = getenv("DU_TP_FUSE");
-        return e == nullptr || atoi(e) != 0;
+        return e == nullptr ? -1 : (atoi(e) != 0 ? 1 : 0);
     }();
-    return on;
+    return force < 0 ? m->tp <= 4 : force == 1;
 }
 
 // One stage of layer l for the token rows of `io`.  With tensor parallelism
@@ -593,7 +595,7 @@ static GemvParams stage_gemv_params(du_model *m, const StepIO &io, int l, int st
         }
         p.N = H; p.map = MAP_IDENT;
         if (m->tp == 1) { p.epi = EPI_RESID; p.y = m->x_res; p.ldy = H; }
-        else if (tp_peer_ok(m, io) && tp_fuse_enabled()) {
+        else if (tp_peer_ok(m, io) && tp_fuse_enabled(m)) {
             // decode: the allreduce over peer memory runs in the GEMV's epilogue
             p.epi = EPI_TP_RESID; p.y = m->part; p.ldy = H; p.tp = m->tpc.dev; p.resid = m->x_res;
         } else { p.epi = EPI_STORE; p.y = m->part; p.ldy = H; }
