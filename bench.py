@@ -55,9 +55,20 @@ def parse():
                     help="kernel sweeps (one JSON line per case): config-2 GEMV, config-3 flash-decode")
     ap.add_argument("--case", default=None, help="--sweep gemv: one cell quant:N:K:M, quant int4 / int8 / f16 (e.g. int4:14336:4096:1)")
     ap.add_argument("--reps", type=int, default=0, help="--sweep: timed launches per case (0 = auto)")
+    ap.add_argument("--model", choices=["llama-8b", "llama-1.1b"], default="llama-8b",
+                    help="llama-8b: BASELINE config 5 (INT4 g128); llama-1.1b: config 4 (INT8 per row)")
     ap.add_argument("--layers", type=int, default=0,
                     help="profiling only: keep the first N decoder layers (smaller device footprint)")
     return ap.parse_args()
+
+
+def tensor_peak():
+    """Measured dense bf16 TFLOP/s (burst) of MEASURED_PEAKS.json, else the fallback."""
+    try:
+        with open(PEAKS) as f:
+            return float(json.load(f)["bf16_tflops"])
+    except Exception:
+        return 1590.0
 
 
 def peaks():
@@ -216,14 +227,15 @@ def run_reference(args):
     if rank != 0:
         return 0
     from deepunity_b200.llm import CONFIGS
-    cfg = CONFIGS[CONFIG]
+    cfg = CONFIGS[args.model]
     tok_s, sample, cores, times = cpu_reference_sample(cfg, args.batch, args.prompt, args.steps, args.warmup)
-    line = {"metric": "decode tok/s (INT4 8B-class, bs1)", "value": round(tok_s, 4), "unit": "tok/s",
+    mclass = "INT4 8B-class" if args.model == "llama-8b" else "INT8 1.1B-class"
+    line = {"metric": f"decode tok/s ({mclass}, bs{args.batch})", "value": round(tok_s, 4), "unit": "tok/s",
             "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": round(1000.0 / tok_s, 3) if tok_s else None, "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": "llama-8b decode step, batch 1, kv 1024 (CPU sample)", "model": CONFIG,
-                       "global_batch": 1, "seq_len": args.prompt},
+            "config": {"workload": f"{args.model} decode step, batch {args.batch}, kv {args.prompt} (CPU sample)",
+                       "model": args.model, "global_batch": args.batch, "seq_len": args.prompt},
             "impl": "reference",
             "cpu_baseline": {"value": round(tok_s, 4), "unit": "tok/s", "cores": cores, "kind": "port",
                              "sample": sample},
@@ -250,13 +262,15 @@ def run_ours(args):
     torch.cuda.set_device(local)
     if world > 1:
         dist.init_process_group("gloo", timeout=timedelta(seconds=600))
-    cfg = CONFIGS[CONFIG]
+    cfg = CONFIGS[args.model]
+    quant = LLMQuant.INT4 if args.model == "llama-8b" else LLMQuant.INT8
     if args.layers:
         import dataclasses
         cfg = dataclasses.replace(cfg, num_layers=args.layers)
     B = args.batch
     need = args.prompt + args.warmup + 2 * args.steps + 4
-    m = LlamaForCausalLM(cfg, LLMQuant.INT4, max_context_length=max(CAPACITY, need), max_batch=B, seed=0,
+    cap = max(CAPACITY if args.model == "llama-8b" else 0, need)
+    m = LlamaForCausalLM(cfg, quant, max_context_length=cap, max_batch=B, seed=0,
                          device=local, tp_rank=rank, tp_size=world,
                          flags=_lib.FLAG_PERSISTENT if args.path == "persistent" else 0)
     if world > 1:
@@ -349,11 +363,25 @@ def run_ours(args):
     peak, peak_kind = peaks()
     I_l, H = cfg.intermediate_size // world, cfg.hidden_size
     g = cfg.group_size
-    gu_bytes = 2 * I_l * H // 2 + 2 * I_l * (H // g) * 2 + B * H * 4 + B * I_l * 4
-    kv_read = 2 * cfg.num_layers * B * (args.prompt + args.warmup + args.steps) * \
-        (cfg.num_heads_kv // world) * cfg.head_dim * 2        # K and V rows read per step (mean length)
+
+    def wbytes(n, k):      # algorithmic bytes of one linear's weights and scales
+        return n * k // 2 + n * (k // g) * 2 if quant == LLMQuant.INT4 else n * k + 2 * n
+
+    hq_l, hkv_l, hd = cfg.num_heads_q // world, cfg.num_heads_kv // world, cfg.head_dim
+    gu_bytes = wbytes(2 * I_l, H) + B * H * 4 + B * I_l * 4
+    # K and V rows read per step at the mean cache length of the timed steps
+    kv_mean = args.prompt + args.warmup + args.steps // 2 + 1
+    kv_layer = 2 * B * kv_mean * hkv_l * hd * 2
+    kv_read = cfg.num_layers * kv_layer
     step_bytes = m.weight_bytes() + kv_read
     step_ms = ms / args.steps
+    # per-kernel algorithmic bytes (weights + the activations each reads and writes)
+    stage_bytes = {"qkv": wbytes((hq_l + 2 * hkv_l) * hd, H) + B * H * 4 + B * hq_l * hd * 4,
+                   "attn": kv_layer + 2 * B * hq_l * hd * 4,
+                   "o_proj": wbytes(H, hq_l * hd) + B * hq_l * hd * 4 + 2 * B * H * 4,
+                   "gate_up": gu_bytes,
+                   "down": wbytes(H, I_l) + B * I_l * 4 + 2 * B * H * 4,
+                   "lm_head": (cfg.vocab_size // world) * H * 2 + B * H * 4}
     if stage_us is not None:
         # one launch per step: the roofline is the whole persistent kernel
         roof_kernel = "decode_step_kernel (persistent; one launch = one decode step)"
@@ -370,7 +398,7 @@ def run_ours(args):
         key = None
     else:       # per-stage graph: DRAM bytes per launch of the gate|up GEMV (ncu, layer-independent)
         prof = os.path.join(ROOT, "profiles", "gateup_gemv_traffic.json")
-    if os.path.exists(prof):
+    if os.path.exists(prof) and args.model == "llama-8b" and B == 1 and world == 1:
         try:
             tj = json.load(open(prof))
             traffic = int(tj["fixed_bytes"] + tj["per_layer_bytes"] * cfg.num_layers) if stage_us is not None \
@@ -389,17 +417,21 @@ def run_ours(args):
         cpu = {"value": round(v, 4), "unit": "tok/s", "cores": cores, "kind": "port", "sample": sample}
 
     if rank == 0:
+        mclass = "INT4 8B-class" if args.model == "llama-8b" else "INT8 1.1B-class"
         line = {
-            "metric": "decode tok/s (INT4 8B-class, bs1)" if B == 1 else f"decode tok/s (INT4 8B-class, bs{B})",
+            "metric": f"decode tok/s ({mclass}, bs{B})",
             "value": round(value, 2), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 4), "higher_is_better": True,
-            "scaling": "strong", "vs_baseline": None, "dtype": "int4 weights x fp32 activations (fp16 KV)",
+            "scaling": "strong", "vs_baseline": None,
+            "dtype": ("int4" if quant == LLMQuant.INT4 else "int8") + " weights x fp32 activations (fp16 KV)",
             "data": "synthetic (seeded random-init weights, random prompt ids)",
-            "config": {"workload": f"llama-8b INT4-g128 decode, batch {B}, prompt {args.prompt}, "
+            "config": {"workload": f"{args.model} {'INT4-g128' if quant == LLMQuant.INT4 else 'INT8-row'} decode, "
+                                   f"batch {B}, prompt {args.prompt}, "
                                    f"kv {args.prompt}..{args.prompt + args.warmup + args.steps}",
-                       "model": CONFIG if not args.layers else f"{CONFIG} (first {args.layers} layers, profiling)",
+                       "model": args.model if not args.layers else f"{args.model} (first {args.layers} layers, profiling)",
                        "global_batch": B, "seq_len": args.prompt,
-                       "parallelism": f"tp{world}", "l2": "no flush: ~4.8 GB streamed per step >> 126 MB L2"},
+                       "parallelism": f"tp{world}",
+                       "l2": f"no flush: {step_bytes / 1e9:.2f} GB streamed per step >> 126 MB L2"},
             "decode_path": "persistent decode-step kernel" if stage_us else "graph of per-stage kernels",
             "stage_us": stage_us,
             "roofline": {"bound": "hbm", "kernel": roof_kernel,
@@ -407,8 +439,19 @@ def run_ours(args):
                          "frac": round(achieved / peak, 4), "peak_kind": peak_kind, "traffic": traffic,
                          "algorithmic_bytes_per_launch": roof_bytes, "launch_ms": round(roof_ms, 5)},
             "stage_roofline": stage_roof,
+            "step_roofline": {"bound": "hbm", "what": "whole decode step: weights + K/V rows read per step "
+                                                     "over the device-timed step",
+                              "bytes_per_step": int(step_bytes), "ms_per_step": round(step_ms, 4),
+                              "achieved": round(step_bytes / (step_ms / 1000.0) / 1e9, 1), "peak": peak,
+                              "unit": "GB/s", "frac": round(step_bytes / (step_ms / 1000.0) / 1e9 / peak, 4),
+                              "peak_kind": peak_kind},
             "kernel_ms": dict(zip(["qkv", "attn", "o_proj", "gate_up", "down", "lm_head"],
                                   [round(v, 5) for v in kt])),
+            "kernel_frac_hbm": {k: round(stage_bytes[k] / (v / 1000.0) / 1e9 / peak, 4)
+                                for k, v in zip(["qkv", "attn", "o_proj", "gate_up", "down", "lm_head"], kt)
+                                if v > 0},
+            "kernel_ms_note": "each stage kernel replayed back to back outside the decode graph (CUDA events, "
+                              "all layers), averaged per launch; fractions are algorithmic bytes / time / peak",
             "e2e": {"value": round(e2e, 2), "unit": "tok/s", "h2d_bytes_per_step": 4 * B,
                     "d2h_bytes_per_step": 4 * B},
             "gpu_launches": int(kn.value) * args.steps,
@@ -435,6 +478,33 @@ def _events_ms(fn, reps: int, stream=None):
     return s.elapsed_time(e) / reps
 
 
+def _graph_ms(fn, reps: int):
+    """Device time per call of fn(i, stream) with `reps` calls captured in one CUDA graph
+    (launch gaps of the host loop removed); CUDA events on the capturing stream."""
+    import torch
+    s = torch.cuda.Stream()
+    torch.cuda.synchronize()
+    with torch.cuda.stream(s):
+        for i in range(2):          # first calls outside capture: attributes, grow-only scratch
+            fn(i, s.cuda_stream)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=s):
+        for i in range(reps):
+            fn(i, s.cuda_stream)
+    with torch.cuda.stream(s):
+        g.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(s)
+        g.replay()
+        e1.record(s)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / reps
+    del g
+    return ms
+
+
 def run_sweep_gemv(args):
     """quant-GEMV HBM GB/s vs peak through du_gemv_q4 / du_gemv_q8.
     Distinct weight copies (>= 1 GB in total) rotate between launches so no launch
@@ -445,6 +515,7 @@ def run_sweep_gemv(args):
     torch.cuda.set_device(0)
     _lib.call("du_init", 0)
     peak, kind = peaks()
+    tpeak = tensor_peak()
     g = torch.Generator(device="cuda").manual_seed(0)
     only = None
     if args.case:   # "int4:14336:4096:1" -> one sweep cell (profiling)
@@ -465,25 +536,30 @@ def run_sweep_gemv(args):
                 x = torch.randn((M, K), device="cuda", generator=g).bfloat16()
                 y = torch.empty((M, N), device="cuda")
                 if quant == "int4":
-                    f = lambda i: _lib.call("du_gemv_q4", C.c_void_p(y.data_ptr()), C.c_void_p(x.data_ptr()),
-                                            _lib.DTYPE_BF16, C.c_void_p(W[i % copies].data_ptr()),
-                                            C.c_void_p(Sc[i % copies].data_ptr()), 128, M, N, K, None)
+                    f = lambda i, st: _lib.call("du_gemv_q4", C.c_void_p(y.data_ptr()), C.c_void_p(x.data_ptr()),
+                                                _lib.DTYPE_BF16, C.c_void_p(W[i % copies].data_ptr()),
+                                                C.c_void_p(Sc[i % copies].data_ptr()), 128, M, N, K, C.c_void_p(st))
                 elif quant == "f16":
-                    f = lambda i: _lib.call("du_gemv_f16", C.c_void_p(y.data_ptr()), C.c_void_p(x.data_ptr()),
-                                            _lib.DTYPE_BF16, C.c_void_p(W[i % copies].data_ptr()), M, N, K, None)
+                    f = lambda i, st: _lib.call("du_gemv_f16", C.c_void_p(y.data_ptr()), C.c_void_p(x.data_ptr()),
+                                                _lib.DTYPE_BF16, C.c_void_p(W[i % copies].data_ptr()), M, N, K,
+                                                C.c_void_p(st))
                 else:
-                    f = lambda i: _lib.call("du_gemv_q8", C.c_void_p(y.data_ptr()), C.c_void_p(x.data_ptr()),
-                                            _lib.DTYPE_BF16, C.c_void_p(W[i % copies].data_ptr()),
-                                            C.c_void_p(Sc[i % copies].data_ptr()), _lib.DTYPE_F16, M, N, K, None)
-                reps = args.reps or max(4, min(200, int(2e9 / ((wbytes + sbytes) * max(1, M // 8)))))
-                _events_ms(f, 3)
-                ms = _events_ms(f, reps)
+                    f = lambda i, st: _lib.call("du_gemv_q8", C.c_void_p(y.data_ptr()), C.c_void_p(x.data_ptr()),
+                                                _lib.DTYPE_BF16, C.c_void_p(W[i % copies].data_ptr()),
+                                                C.c_void_p(Sc[i % copies].data_ptr()), _lib.DTYPE_F16, M, N, K,
+                                                C.c_void_p(st))
+                reps = args.reps or max(8, min(64, int(2e9 / (wbytes + sbytes))))
+                ms = _graph_ms(f, reps)
                 byts = wbytes + sbytes + M * K * 2 + M * N * 4
                 gbs = byts / (ms / 1e3) / 1e9
+                tflops = 2 * M * N * K / (ms / 1e3) / 1e12
+                path = "tcgen05 GEMM" if M >= 16 and K % 64 == 0 else "GEMV"
                 print(json.dumps({"sweep": "gemv", "quant": quant + {"int4": "-g128", "int8": "-row"}.get(quant, ""),
-                                  "N": N, "K": K, "M": M, "us": round(ms * 1e3, 2), "GB_s": round(gbs, 1),
-                                  "frac_hbm": round(gbs / peak, 4), "TFLOP_s": round(2 * M * N * K / (ms / 1e3) / 1e12, 2),
-                                  "peak_kind": kind, "copies": copies}), flush=True)
+                                  "N": N, "K": K, "M": M, "path": path, "us": round(ms * 1e3, 2),
+                                  "GB_s": round(gbs, 1), "frac_hbm": round(gbs / peak, 4),
+                                  "TFLOP_s": round(tflops, 2), "frac_tensor_bf16": round(tflops * 1e3 / tpeak, 4),
+                                  "peak_kind": kind, "copies": copies,
+                                  "timing": "CUDA graph of the launches, weights rotated over >= 1.1 GB"}), flush=True)
             del W, Sc
 
 
@@ -508,15 +584,16 @@ def run_sweep_attn(args):
             q = torch.randn((B, hq, hd), device="cuda", generator=g)
             out = torch.empty((B, hq, hd), device="cuda")
             lens = torch.full((B,), ctx, dtype=torch.int32, device="cuda")
-            f = lambda i: _lib.call("du_flash_decode", C.c_void_p(out.data_ptr()), C.c_void_p(q.data_ptr()),
-                                    C.c_void_p(kc[i % copies].data_ptr()), C.c_void_p(vc[i % copies].data_ptr()),
-                                    C.c_void_p(lens.data_ptr()), B, hq, hkv, hd, ctx, C.c_float(hd ** -0.5), None)
-            _events_ms(f, 3)
-            ms = _events_ms(f, 20)
+            f = lambda i, st: _lib.call("du_flash_decode", C.c_void_p(out.data_ptr()), C.c_void_p(q.data_ptr()),
+                                        C.c_void_p(kc[i % copies].data_ptr()), C.c_void_p(vc[i % copies].data_ptr()),
+                                        C.c_void_p(lens.data_ptr()), B, hq, hkv, hd, ctx, C.c_float(hd ** -0.5),
+                                        C.c_void_p(st))
+            ms = _graph_ms(f, max(8, min(64, int(2e9 / kv_bytes))))
             gbs = kv_bytes / (ms / 1e3) / 1e9
             print(json.dumps({"sweep": "flash_decode", "ctx": ctx, "batch": B, "us": round(ms * 1e3, 2),
                               "GB_s": round(gbs, 1), "frac_hbm": round(gbs / peak, 4), "peak_kind": kind,
-                              "copies": copies}), flush=True)
+                              "copies": copies, "kernel": "flash_decode_cluster_kernel (du_flash_decode)",
+                              "timing": "CUDA graph of the launches, caches rotated over >= 0.6 GB"}), flush=True)
             del kc, vc
 
 

@@ -70,6 +70,8 @@ SIGNATURES = {
     "du_quantize_int8": (I, [P, I64, I64, P, P, P]),
     "du_quantize_int4": (I, [P, I64, I64, I, P, P, P]),
     "du_rmsnorm": (I, [P, P, P, I, I, F, P]),
+    "du_tp_wait_selftest": (I, [C.c_uint, C.POINTER(C.c_int)]),
+    "du_dequant": (I, [P, P, P, I, I, I, I64, I, I, P]),
 }
 
 _lib = None

@@ -29,6 +29,8 @@
 // partials, atomics or remote-read round trips.
 #include <cooperative_groups.h>
 
+#include <mutex>
+
 #include "attn_impl.cuh"
 #include "internal.h"
 
@@ -57,14 +59,8 @@ static int fd_launch(const FdParams &p, int G, int nsplit, int nq, cudaStream_t 
 {
     dim3 grid(nsplit, p.hkv, nq);
     const size_t smem = 4 * FD_TILE * (HD + 8) * sizeof(__half);
-    static bool attr_set[64] = {};
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (!attr_set[dev & 63]) {
-        DU_CUDA_TRY(cudaFuncSetAttribute(flash_decode_kernel<HD>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-        attr_set[dev & 63] = true;
-    }
+    int rc = ensure_func_attrs((const void *)flash_decode_kernel<HD>, (int)smem);
+    if (rc) return rc;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = grid;
     cfg.blockDim = dim3(FD_THREADS);
@@ -148,14 +144,8 @@ static int fdc_launch(const FdParams &p, int G, int nq, cudaStream_t st, int new
 {
     auto kern = flash_decode_cluster_kernel<HD, C>;
     const size_t smem = 4 * FD_TILE * (HD + 8) * sizeof(__half) + fd_mma_extra_bytes<HD>() + fdc_recv_bytes<HD, C>();
-    static bool attr_set[64] = {};
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (!attr_set[dev & 63]) {
-        DU_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-        if (C > 8) DU_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
-        attr_set[dev & 63] = true;
-    }
+    int rc = ensure_func_attrs((const void *)kern, (int)smem, C > 8);
+    if (rc) return rc;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(C, p.hkv, nq);
     cfg.blockDim = dim3(FDC_THREADS);
@@ -184,13 +174,15 @@ static int fdc_launch(const FdParams &p, int G, int nq, cudaStream_t st, int new
 template <int HD>
 static int fdc_cluster_size(const FdParams &p, int G, cudaStream_t st)
 {
+    static std::mutex mu;
     static int chosen[64] = {};
     int dev = 0;
     cudaGetDevice(&dev);
+    std::lock_guard<std::mutex> lk(mu);
     if (chosen[dev & 63] == 0) {
         int n16 = 0;
         const int rc = fdc_launch<HD, 16>(p, G, 1, st, -1, true, &n16);
-        cudaGetLastError();
+        if (rc != DU_OK) cudaGetLastError();    // the probe's own failure: 16-CTA clusters unavailable
         chosen[dev & 63] = (rc == DU_OK && n16 > 0) ? 16 : 8;
     }
     return chosen[dev & 63];

@@ -2,7 +2,11 @@
 // C entry points of libdeepunity_cuda.
 #include <dlfcn.h>
 
+#include <atomic>
+
+#include <map>
 #include <mutex>
+#include <utility>
 #include <string>
 #include <vector>
 
@@ -30,15 +34,35 @@ int cuda_fail(cudaError_t e, const char *what)
 
 int num_sms()
 {
-    static int cache[64] = {};
+    static std::atomic<int> cache[64] = {};
     int dev = 0;
     cudaGetDevice(&dev);
-    if (cache[dev & 63] == 0) {
-        int n = 0;
+    int n = cache[dev & 63].load(std::memory_order_relaxed);
+    if (n == 0) {
         cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
-        cache[dev & 63] = n > 0 ? n : 148;
+        if (n <= 0) n = 148;
+        cache[dev & 63].store(n, std::memory_order_relaxed);   // every thread computes the same value
     }
-    return cache[dev & 63];
+    return n;
+}
+
+// Raises a kernel's dynamic shared-memory limit (and optionally allows
+// non-portable cluster sizes) once per (kernel, device).  Launchers may run on
+// several host threads at once, so the record is guarded.
+int ensure_func_attrs(const void *kern, int smem_bytes, bool nonportable_cluster)
+{
+    static std::mutex mu;
+    static std::map<std::pair<const void *, int>, int> done;
+    int dev = 0;
+    DU_CUDA_TRY(cudaGetDevice(&dev));
+    std::lock_guard<std::mutex> lk(mu);
+    const auto key = std::make_pair(kern, dev);
+    const auto it = done.find(key);
+    if (it != done.end() && it->second >= smem_bytes) return DU_OK;
+    DU_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes));
+    if (nonportable_cluster) DU_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
+    done[key] = smem_bytes;
+    return DU_OK;
 }
 
 // Grow-only per-device scratch for the kernel-level entry points.  Slot 0/1
@@ -125,6 +149,31 @@ static int gemv_entry(int qt, float *y, const void *x, int x_dtype, const void *
     int rc = x_to_f32(x, x_dtype, (size_t)M * K, &xf, st);
     if (rc) return rc;
     const int64_t row_bytes = qt == Q_I4 ? K / 2 : qt == Q_I8 ? K : 2 * (int64_t)K;
+    if (M >= gemm_min_tokens()) {
+        // tensor-core GEMM: weights streamed once for all M rows
+        GemvParams p = {};
+        p.x = xf; p.ldx = K;
+        p.w = static_cast<const uint8_t *>(w);
+        p.scales = scales;
+        p.scale_f32 = scale_f32;
+        p.row_bytes = row_bytes;
+        p.K = K; p.N = N; p.M = M; p.group = group;
+        p.map = MAP_IDENT;
+        p.epi = EPI_STORE;
+        p.y = y;
+        p.ldy = N;
+        if (gemm_supported(qt, p)) {
+            GemmScratch g;
+            g.elems = (size_t)M * K;
+            g.rows = (size_t)M;
+            char *buf = static_cast<char *>(device_scratch(4 * g.elems + 4 * g.rows + 16, 3));
+            if (!buf) return fail(DU_ENOMEM, "gemm: scratch allocation failed");
+            g.xh = reinterpret_cast<__half *>(buf);
+            g.xl = g.xh + g.elems;
+            g.xscale = reinterpret_cast<float *>(buf + 4 * g.elems);
+            return launch_gemm(qt, p, g, st);
+        }
+    }
     int mt = 8;
     while (mt > 1 && gemv_smem_bytes(qt, mt, row_bytes) > 220 * 1024) mt >>= 1;
     if (gemv_smem_bytes(qt, mt, row_bytes) > 220 * 1024) return fail(DU_EINVAL, "gemv: K too large");
@@ -195,15 +244,26 @@ DU_API int du_flash_decode(float *out, const float *q, const uint16_t *k_cache, 
     DU_CHECK_ARG(out && q && k_cache && v_cache && kv_len, "du_flash_decode: null pointer");
     DU_CHECK_ARG(batch >= 0 && hq > 0 && hkv > 0 && capacity > 0, "du_flash_decode: bad sizes");
     DU_CHECK_ARG(hq % hkv == 0, "du_flash_decode: hq must be a multiple of hkv");
-    cudaStream_t st = static_cast<cudaStream_t>(stream);
-    const int ns = fd_choose_splits(batch, hkv, capacity);
-    const size_t fl = fd_scratch_floats(batch, hkv, hq / hkv, hd, ns);
-    float *scratch = static_cast<float *>(device_scratch(fl * sizeof(float), 0));
-    unsigned *counters = static_cast<unsigned *>(device_scratch((size_t)batch * hkv * sizeof(unsigned), 2));
-    if (!scratch || !counters) return fail(DU_ENOMEM, "du_flash_decode: scratch allocation failed");
-    return launch_flash_decode(q, reinterpret_cast<const __half *>(k_cache), reinterpret_cast<const __half *>(v_cache),
-                               nullptr, kv_len, 0, batch, hq, hkv, hd, capacity, scale, out, scratch, counters, ns,
-                               st);
+    // the model's kernel: the splits of a (sequence, kv head) combine inside a
+    // thread-block cluster, so no global scratch is needed
+    return launch_flash_decode_cluster(q, reinterpret_cast<const __half *>(k_cache),
+                                       reinterpret_cast<const __half *>(v_cache), nullptr, kv_len, 0, batch, hq, hkv,
+                                       hd, capacity, scale, out, static_cast<cudaStream_t>(stream));
+}
+
+DU_API int du_dequant(float *out, const void *w, const void *scales, int quant, int scale_dtype, int group,
+                      int64_t row0, int nrows, int K, void *stream)
+{
+    DU_CHECK_ARG(out && w && nrows >= 0 && row0 >= 0 && K > 0 && K % 8 == 0, "du_dequant: bad arguments");
+    DU_CHECK_ARG(quant == DU_QUANT_FP16 || quant == DU_QUANT_INT8 || quant == DU_QUANT_INT4, "du_dequant: quant");
+    if (quant != DU_QUANT_FP16) DU_CHECK_ARG(scales != nullptr, "du_dequant: scales required");
+    if (quant == DU_QUANT_INT4)
+        DU_CHECK_ARG(group >= 8 && group % 8 == 0 && K % group == 0, "du_dequant: group must be a multiple of 8 dividing K");
+    if (quant == DU_QUANT_INT8)
+        DU_CHECK_ARG(scale_dtype == DU_DTYPE_F16 || scale_dtype == DU_DTYPE_F32, "du_dequant: scale_dtype F16 or F32");
+    const int qt = quant == DU_QUANT_INT4 ? Q_I4 : quant == DU_QUANT_INT8 ? Q_I8 : Q_F16;
+    return launch_dequant_rows(qt, w, scales, scale_dtype == DU_DTYPE_F32, group, row0, nrows, K, out,
+                               static_cast<cudaStream_t>(stream));
 }
 
 DU_API int du_quantize_int8(const float *w, int64_t rows, int64_t cols, int8_t *q, uint16_t *scales_f16,

@@ -38,6 +38,7 @@ struct TpFuse {
     int *err;                        // set on a timed-out wait
     size_t maxn;                     // elements per slot
     int rank, nranks;
+    unsigned spin_limit;             // polls of one peer word before a wait gives up
 };
 
 // 16-byte streaming load: weights are read exactly once per launch, so they
@@ -71,5 +72,23 @@ __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;"
 __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;"); }
 
 __device__ __forceinline__ float silu(float x) { return x / (1.0f + __expf(-x)); }
+
+// Greedy tie-break of the reference's ArgMax (Gemma3CS.compute:911-928): 256
+// threads stride the vocabulary keeping their first strict maximum (lowest
+// index of the thread's stride set), then a tree over threads where slot t
+// absorbs slot t + s (s = 128, 64, .., 1) only on a strictly larger value.  Among
+// tied maxima the winner is therefore the thread whose id, read from bit 0
+// upwards, is smallest (the bit-reversed thread id), then the lowest index of
+// that thread.  am_rank orders vocabulary indices by that rule.
+__device__ __forceinline__ unsigned am_rank(int i)
+{
+    return (__brev((unsigned)i & 255u) & 0xFF000000u) | ((unsigned)i >> 8);
+}
+
+// (v, i) beats (bv, bi): larger value, or an equal value with the reference's tie-break.
+__device__ __forceinline__ bool am_better(float v, int i, float bv, int bi)
+{
+    return v > bv || (v == bv && am_rank(i) < am_rank(bi));
+}
 
 }  // namespace du

@@ -129,19 +129,19 @@ __global__ void __launch_bounds__(DS_THREADS, 1) decode_step_kernel(const StepPl
                     for (int i = tid; i < plan.nparts; i += DS_THREADS) {
                         const float v = plan.am_val[(size_t)m * plan.nparts + i];
                         const int ix = plan.am_idx[(size_t)m * plan.nparts + i];
-                        if (v > bv || (v == bv && ix < bi)) { bv = v; bi = ix; }
+                        if (am_better(v, ix, bv, bi)) { bv = v; bi = ix; }
                     }
                     for (int o = 16; o > 0; o >>= 1) {
                         const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
                         const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-                        if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+                        if (am_better(ov, oi, bv, bi)) { bv = ov; bi = oi; }
                     }
                     if ((tid & 31) == 0) { gsh.amv[tid >> 5][0] = bv; gsh.ami[tid >> 5][0] = bi; }
                     __syncthreads();
                     if (tid == 0) {
                         bv = gsh.amv[0][0]; bi = gsh.ami[0][0];
                         for (int w = 1; w < DS_WARPS; w++)
-                            if (gsh.amv[w][0] > bv || (gsh.amv[w][0] == bv && gsh.ami[w][0] < bi)) {
+                            if (am_better(gsh.amv[w][0], gsh.ami[w][0], bv, bi)) {
                                 bv = gsh.amv[w][0]; bi = gsh.ami[w][0];
                             }
                         plan.next_out[m] = bi;
@@ -187,13 +187,8 @@ template <int QT, int MT, int HD>
 static int ds_launch(const StepPlan &plan, size_t smem, cudaStream_t st)
 {
     auto kern = decode_step_kernel<QT, MT, HD>;
-    static size_t attr_set[64] = {};        // dynamic smem already allowed, per device
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (attr_set[dev & 63] < smem) {
-        DU_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-        attr_set[dev & 63] = smem;
-    }
+    int rc = ensure_func_attrs((const void *)kern, (int)smem);
+    if (rc) return rc;
     int per_sm = 0;
     DU_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, DS_THREADS, smem));
     if (per_sm < 1) return fail(DU_EINVAL, "decode step kernel does not fit on an SM");

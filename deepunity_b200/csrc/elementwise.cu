@@ -49,14 +49,10 @@ int launch_rmsnorm(const float *x, const __half *g, int rows, int H, float eps, 
 }
 
 // Final greedy pick from the per-CTA (max, argmax) partials of the lm_head
-// GEMV: the largest value wins, the lowest vocab index breaks a tie.
-// Writes the id (and optionally the next step's input id, for the
-// device-resident loop) or, with `pairs`, the (value, index-bits) pair that
-// tensor-parallel ranks exchange.
-__device__ __forceinline__ bool am_better(float v, int i, float bv, int bi)
-{
-    return v > bv || (v == bv && i < bi);
-}
+// GEMV: the largest value wins, ties follow the reference's ArgMax tree
+// (am_better, common.cuh).  Writes the id (and optionally the next step's input
+// id, for the device-resident loop) or, with `pairs`, the (value, index-bits)
+// pair that tensor-parallel ranks exchange.
 
 __global__ void argmax_final_kernel(const float *am_val, const int *am_idx, int nparts, int *out_ids,
                                     int *feed_ids, float *pairs, TokHist hist)

@@ -52,15 +52,13 @@ struct GvCfg {
     int nw, d, cps;
 };
 
-static int g_wide = -1;     // -1: not read yet
-
 static bool wide_enabled()
 {
-    if (g_wide < 0) {
+    static const bool on = [] {     // read once (thread-safe static initialisation)
         const char *e = getenv("DU_GEMV_WIDE");
-        g_wide = e ? (atoi(e) != 0) : 1;
-    }
-    return g_wide != 0;
+        return e ? atoi(e) != 0 : true;
+    }();
+    return on;
 }
 
 static GvCfg choose_cfg(int qt, int mt, int64_t row_bytes)
@@ -94,13 +92,8 @@ template <int QT, int MT, int D, int NW, bool TPR>
 static int launch_kernel(const GemvParams &p, int grid, size_t smem, cudaStream_t st)
 {
     auto kern = qgemv_kernel<QT, MT, rw_of(MT), D, NW, TPR>;
-    static bool attr_set[64] = {};
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (!attr_set[dev & 63]) {
-        DU_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)GV_SMEM_MAX));
-        attr_set[dev & 63] = true;
-    }
+    int rc = ensure_func_attrs((const void *)kern, (int)GV_SMEM_MAX);
+    if (rc) return rc;
     if (TPR) {
         // each CTA waits for the other ranks' values of its rows: all CTAs must be
         // resident at once, so the grid is capped at one wave

@@ -73,7 +73,8 @@ struct GemvParams {
     float *q_out;           // [M][hq*hd]
     __half *k_cache, *v_cache;   // [seq][cap][hkv][hd]
     const int *pos;         // [M] cache slot / RoPE position per token
-    const int *seq_of;      // [M] sequence per token (nullptr: token m -> sequence m)
+    const int *seq_of;      // [M] sequence per token (nullptr: token m -> sequence seq_off + m)
+    int seq_off;
     int hq, hkv, hd, cap;
     const __half *rope_cos, *rope_sin;  // [cap][hd/2]
     // EPI_LOGITS: logits[m][row] of this rank's vocab shard (optional) + per-CTA

@@ -229,7 +229,7 @@ __device__ __forceinline__ void gv_epi_pair(const GemvParams &p, int lr0, int m,
     // EPI_QKV: rows (lr0, lr0 + 1) are the RoPE pair (i, i + hd/2) of one head
     const int hd = p.hd, head = lr0 / hd, i = (lr0 - head * hd) >> 1;
     const int pos = p.pos[m];
-    const int seq = p.seq_of ? p.seq_of[m] : m;
+    const int seq = p.seq_of ? p.seq_of[m] : p.seq_off + m;
     if (head < p.hq + p.hkv) {
         const float c = __half2float(p.rope_cos[(size_t)pos * (hd >> 1) + i]);
         const float s = __half2float(p.rope_sin[(size_t)pos * (hd >> 1) + i]);
@@ -313,7 +313,7 @@ __device__ __forceinline__ void gv_epilogue(const GemvParams &p, int lr0, const 
                     if (p.epi == EPI_LOGITS) {
                         const float f = v[j][m];
                         const int ix = p.vocab_off + lr;    // global index; the shard write is local
-                        if (f > am_v[m] || (f == am_v[m] && ix < am_i[m])) { am_v[m] = f; am_i[m] = ix; }
+                        if (am_better(f, ix, am_v[m], am_i[m])) { am_v[m] = f; am_i[m] = ix; }
                         if (lane == j * MT + m && p.logits) p.logits[(size_t)m * p.ldl + lr] = f;
                     } else if (lane == j * MT + m) {
                         float f = v[j][m];
@@ -618,7 +618,7 @@ struct GemvStream {
         }
 
         if (p.epi == EPI_LOGITS) {
-            // per-CTA (max, argmax); ties keep the lowest index
+            // per-CTA (max, argmax); ties follow the reference's ArgMax tree (am_better)
             if (lane == 0)
 #pragma unroll
                 for (int m = 0; m < MT; m++) { sh.amv[warp][m] = am_v[m]; sh.ami[warp][m] = am_i[m]; }
@@ -630,7 +630,7 @@ struct GemvStream {
                 for (int w = 0; w < NW; w++) {
                     const float vv = sh.amv[w][tid];
                     const int ix = sh.ami[w][tid];
-                    if (vv > bv || (vv == bv && ix < bi)) { bv = vv; bi = ix; }
+                    if (am_better(vv, ix, bv, bi)) { bv = vv; bi = ix; }
                 }
                 p.am_val[(size_t)tid * ncta + cta] = bv;
                 p.am_idx[(size_t)tid * ncta + cta] = bi;

@@ -9,6 +9,8 @@ namespace du {
 struct GemvParams;
 
 int num_sms();
+// cudaFuncSetAttribute(MaxDynamicSharedMemorySize) once per (kernel, device), thread-safe
+int ensure_func_attrs(const void *kern, int smem_bytes, bool nonportable_cluster = false);
 
 // gemv.cu
 int launch_gemv(int qt, GemvParams p, cudaStream_t st);
@@ -18,6 +20,19 @@ size_t gemv_x_bytes(int qt, int mt, int64_t row_bytes);     // activation stage 
 int gemv_grid_for(int N, int M, int want);
 void gemv_set_pdl(bool on);
 bool pdl_enabled();
+
+// gemm.cu: tensor-core dequant GEMM for M > 8 token rows (prefill chunks, large decode batches)
+struct GemmScratch {
+    __half *xh = nullptr, *xl = nullptr;   // [rows][K] staged activations (exact fp16 pairs)
+    float *xscale = nullptr;               // [rows]
+    size_t elems = 0, rows = 0;            // capacity: rows * K elements, rows
+    int *err = nullptr;                    // device error word of the bounded waits (may be null)
+};
+bool gemm_supported(int qt, const GemvParams &p);
+int gemm_min_tokens();                      // smallest M routed to the GEMM (DU_GEMM_MIN_M, default 16)
+int launch_gemm(int qt, const GemvParams &p, const GemmScratch &scr, cudaStream_t st);
+int launch_dequant_rows(int qt, const void *w, const void *scales, int scale_f32, int group, int64_t row0, int nrows,
+                        int K, float *out, cudaStream_t st);
 
 // attention.cu
 int fd_choose_splits(int nq, int hkv, int max_kv);

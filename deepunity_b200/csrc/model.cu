@@ -80,6 +80,7 @@ struct du_model {
     float *best_val = nullptr; int *best_idx = nullptr;  // TP: [maxb] local, [tp][maxb] gathered
     float *gbest_val = nullptr; int *gbest_idx = nullptr;
     int am_parts = 0;
+    du::GemmScratch gm;                     // staged activations of the tensor-core GEMM (M >= 16 rows)
     float *fd_scratch = nullptr; unsigned *fd_counters = nullptr;
     int fd_nsplit_decode = 1;
     size_t fd_scratch_fl = 0;
@@ -250,6 +251,16 @@ static int model_alloc(du_model *m)
     m->fd_counters = (unsigned *)dalloc(m, sizeof(unsigned) * (size_t)T * m->hkv_l, &rc);
     m->d_barrier = (unsigned *)dalloc(m, sizeof(unsigned), &rc);
     m->d_err = (int *)dalloc(m, sizeof(int), &rc);
+    {   // GEMM activation stage: every K a chunk's GEMM can see (H, I_l, hq_l * hd)
+        int64_t kmax = H > m->I_l ? H : m->I_l;
+        if ((int64_t)m->hq_l * hd > kmax) kmax = (int64_t)m->hq_l * hd;
+        m->gm.rows = (size_t)T;
+        m->gm.elems = (size_t)T * kmax;
+        m->gm.xh = (__half *)dalloc(m, 2 * m->gm.elems, &rc);
+        m->gm.xl = (__half *)dalloc(m, 2 * m->gm.elems, &rc);
+        m->gm.xscale = (float *)dalloc(m, sizeof(float) * T, &rc);
+        m->gm.err = m->d_err;
+    }
     m->d_stamps = (unsigned long long *)dalloc(m, sizeof(unsigned long long) * (5 * (size_t)m->L + 8), &rc);
     if (rc) return rc;
     DU_CUDA_TRY(cudaMallocHost(&m->h_pin_err, sizeof(int)));
@@ -476,6 +487,11 @@ static int gemv_max_tokens(int qt, int64_t row_bytes)
 // Token-indexed pointers of `p` are advanced per chunk.
 static int run_gemv(du_model *m, int qt, GemvParams p, int M)
 {
+    if (M >= gemm_min_tokens()) {     // tensor-core GEMM: every weight streamed once for all M rows
+        GemvParams g = p;
+        g.M = M;
+        if (gemm_supported(qt, g)) return launch_gemm(qt, g, m->gm, m->stream);
+    }
     const int mt = gemv_max_tokens(qt, p.row_bytes);
     for (int t0 = 0; t0 < M; t0 += mt) {
         GemvParams c = p;
@@ -485,6 +501,7 @@ static int run_gemv(du_model *m, int qt, GemvParams p, int M)
         if (p.q_out) c.q_out = p.q_out + (size_t)t0 * p.hq * p.hd;
         if (p.pos) c.pos = p.pos + t0;
         if (p.seq_of) c.seq_of = p.seq_of + t0;
+        else c.seq_off = p.seq_off + t0;      // token t0 + m belongs to sequence t0 + m
         if (p.logits) c.logits = p.logits + (size_t)t0 * p.ldl;
         int rc = launch_gemv(qt, c, m->stream);
         if (rc) return rc;
@@ -883,7 +900,8 @@ static int check_step_error(du_model *m)
     if (*m->h_pin_err == 0) return DU_OK;
     *m->h_pin_err = 0;
     cudaMemset(m->d_err, 0, sizeof(int));
-    return fail(DU_ECUDA, "decode step: a device wait timed out (grid barrier or tensor-parallel peer); step aborted");
+    return fail(DU_ECUDA, "a device wait timed out (grid barrier, tensor-parallel peer or GEMM pipeline); "
+                          "the call was aborted");
 }
 
 static int get_graph(du_model *m, int batch, cudaGraphExec_t *out, Graph **gout = nullptr)
@@ -1198,7 +1216,9 @@ DU_API int du_forward(du_model *m, const int32_t *ids, int batch, int seq_len, i
     if (next_ids_out) {
         DU_CUDA_TRY(cudaMemcpyAsync(m->h_pin_next, m->d_next, sizeof(int) * batch, cudaMemcpyDeviceToHost, st));
     }
+    DU_CUDA_TRY(cudaMemcpyAsync(m->h_pin_err, m->d_err, sizeof(int), cudaMemcpyDeviceToHost, st));
     DU_CUDA_TRY(cudaStreamSynchronize(st));
+    if ((rc = check_step_error(m))) return rc;
     if (next_ids_out) memcpy(next_ids_out, m->h_pin_next, sizeof(int) * batch);
     if (last_pos_only && logits_out) {
         m->busy.store(0);

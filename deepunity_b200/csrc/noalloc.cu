@@ -15,6 +15,7 @@
 // always written before they are read.
 #include <mutex>
 
+#include "attn_impl.cuh"
 #include "internal.h"
 
 namespace du {
@@ -33,7 +34,10 @@ struct NoallocPtrs {
 };
 
 // Resolves the device addresses of the scratch arrays once per device (the
-// calling thread's current device).
+// calling thread's current device).  The cached addresses belong to the
+// device's primary context: after cudaDeviceReset in this process they are
+// stale, so a host that resets a device must not call this entry point on it
+// again.
 static int noalloc_ptrs(NoallocPtrs *out)
 {
     static std::mutex mu;
@@ -65,6 +69,8 @@ extern "C" DU_API int du_flash_decode_noalloc(float *out, const float *q, const 
     DU_CHECK_ARG(out && q && k_cache && v_cache && kv_len, "du_flash_decode_noalloc: null pointer");
     DU_CHECK_ARG(batch >= 0 && hq > 0 && hkv > 0 && capacity > 0, "du_flash_decode_noalloc: bad sizes");
     DU_CHECK_ARG(hq % hkv == 0, "du_flash_decode_noalloc: hq must be a multiple of hkv");
+    DU_CHECK_ARG(hd == 64 || hd == 128, "du_flash_decode_noalloc: head_dim must be 64 or 128");
+    DU_CHECK_ARG(hq / hkv <= FD_MAXG, "du_flash_decode_noalloc: num_heads_q / num_heads_kv must be at most 8");
     if (batch == 0) return DU_OK;
     const int G = hq / hkv;
     if ((size_t)batch * hkv > (size_t)DU_NOALLOC_MAX_COUNTERS)

@@ -14,6 +14,7 @@
 //   3. the last CTA to finish advances the rank's sequence counter.
 // Every rank runs the same sequence of reductions (the same graphs and prefill
 // chunks).
+#include <cstdlib>
 #include <cstring>
 
 #include "internal.h"
@@ -62,6 +63,13 @@ int tp_comm_handle(TpComm *c, void *out64)
     return DU_OK;
 }
 
+unsigned tp_spin_limit()
+{
+    const char *e = getenv("DU_TP_SPIN_LIMIT");
+    const long long v = e ? atoll(e) : 0;
+    return v > 0 && v < (1ll << 31) ? (unsigned)v : TP_SPIN_LIMIT;
+}
+
 int tp_comm_open(TpComm *c, const void *handles, int nranks, int rank, int *err)
 {
     if (nranks < 2 || nranks > TP_MAX_RANKS || rank < 0 || rank >= nranks)
@@ -93,6 +101,7 @@ int tp_comm_open(TpComm *c, const void *handles, int nranks, int rank, int *err)
     h.maxn = c->maxn;
     h.rank = rank;
     h.nranks = nranks;
+    h.spin_limit = tp_spin_limit();
     cudaError_t e = cudaMemcpy(c->dev, &h, sizeof(h), cudaMemcpyHostToDevice);
     if (e != cudaSuccess) {
         tp_comm_close(c);
@@ -136,3 +145,54 @@ int launch_tp_allreduce(TpComm *c, const float *src, float *dst, size_t n, cudaS
 }
 
 }  // namespace du
+
+using namespace du;
+
+// One-process check of the bounded peer wait (no reference counterpart).  A
+// two-rank communicator is built from two local buffers; this process plays
+// rank 0 and nothing ever plays rank 1, so every wait for rank 1's value must
+// give up after spin_limit polls, set the error word and let the kernel return.
+// *timed_out = the error word the host reads back (1 when the wait ran out).
+extern "C" DU_API int du_tp_wait_selftest(unsigned spin_limit, int *timed_out)
+{
+    DU_CHECK_ARG(timed_out != nullptr && spin_limit > 0, "du_tp_wait_selftest: bad arguments");
+    *timed_out = 0;
+    const size_t maxn = 256;
+    void *bufs[2] = {nullptr, nullptr};
+    unsigned *ctl = nullptr;
+    int *err = nullptr;
+    float *src = nullptr, *dst = nullptr;
+    int rc = DU_OK;
+    auto alloc = [&](void **p, size_t bytes) {
+        if (rc) return;
+        cudaError_t e = cudaMalloc(p, bytes);
+        if (e == cudaSuccess) e = cudaMemset(*p, 0, bytes);
+        if (e != cudaSuccess) rc = cuda_fail(e, "du_tp_wait_selftest: allocation");
+    };
+    alloc(&bufs[0], tp_comm_bytes(maxn));
+    alloc(&bufs[1], tp_comm_bytes(maxn));
+    alloc((void **)&ctl, 2 * sizeof(unsigned));
+    alloc((void **)&err, sizeof(int));
+    alloc((void **)&src, maxn * sizeof(float));
+    alloc((void **)&dst, maxn * sizeof(float));
+    if (!rc) {
+        TpFuse h = {};
+        h.peer_recv[0] = static_cast<uint2 *>(bufs[0]);
+        h.peer_recv[1] = static_cast<uint2 *>(bufs[1]);
+        h.seq = ctl;
+        h.done = ctl + 1;
+        h.err = err;
+        h.maxn = maxn;
+        h.rank = 0;
+        h.nranks = 2;
+        h.spin_limit = spin_limit;
+        tp_allreduce_kernel<<<1, 256>>>(h, src, dst, (int)maxn);
+        cudaError_t e = cudaGetLastError();
+        if (e == cudaSuccess) e = cudaDeviceSynchronize();
+        if (e == cudaSuccess) e = cudaMemcpy(timed_out, err, sizeof(int), cudaMemcpyDeviceToHost);
+        if (e != cudaSuccess) rc = cuda_fail(e, "du_tp_wait_selftest");
+    }
+    for (void *p : {bufs[0], bufs[1], (void *)ctl, (void *)err, (void *)src, (void *)dst})
+        if (p) cudaFree(p);
+    return rc;
+}

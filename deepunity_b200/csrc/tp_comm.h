@@ -20,6 +20,8 @@ struct TpComm {
 };
 
 size_t tp_comm_bytes(size_t maxn);
+// polls of one peer word before a wait gives up (DU_TP_SPIN_LIMIT, else TP_SPIN_LIMIT)
+unsigned tp_spin_limit();
 int tp_comm_alloc(TpComm *c, size_t maxn);
 int tp_comm_handle(TpComm *c, void *out64);
 // maps the peers' buffers; waits that time out set *err

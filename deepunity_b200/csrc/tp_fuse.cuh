@@ -17,6 +17,9 @@
 
 namespace du {
 
+// Default number of polls of one peer word before a wait gives up (several
+// seconds); DU_TP_SPIN_LIMIT in the environment overrides it when the peers are
+// opened.
 constexpr unsigned TP_SPIN_LIMIT = 1u << 24;
 
 __device__ __forceinline__ size_t tp_slot(const TpFuse &t, unsigned s, int from, size_t i)
@@ -48,7 +51,7 @@ __device__ __forceinline__ bool tp_wait_sum(const TpFuse &t, unsigned s, size_t 
                 acc += __uint_as_float((unsigned)word);
                 break;
             }
-            if (++n > TP_SPIN_LIMIT || ((n & 1023) == 0 && *(volatile int *)t.err)) {
+            if (++n > t.spin_limit || ((n & 1023) == 0 && *(volatile int *)t.err)) {
                 atomicExch(t.err, 1);
                 return false;
             }

@@ -128,6 +128,18 @@ DU_API int du_tp_init(du_model *m, const void *nccl_unique_id, int timeout_ms);
  * (prefill keeps NCCL).  All ranks must open, or none. */
 DU_API int du_tp_comm_handle(du_model *m, void *handle_out64);
 DU_API int du_tp_comm_open(du_model *m, const void *handles, int nranks);
+/* The peer-memory reduction waits for every rank's values with a bounded spin
+ * (DU_TP_SPIN_LIMIT polls per value when set in the environment before
+ * du_tp_comm_open, else about 2^24).  A wait that runs out sets the model's
+ * error word, the kernels finish without the missing values, and the decode
+ * call returns DU_ECUDA.  The ranks' residual streams and KV caches then
+ * disagree for that step: destroy the models and build the group again.
+ *
+ * du_tp_wait_selftest (no reference counterpart) checks that bound on one GPU:
+ * it runs the reduction kernel as rank 0 of a two-rank group in which no rank
+ * 1 exists, with spin_limit polls per wait; *timed_out receives the error word
+ * the host reads back (1 when the waits ran out, as they must). */
+DU_API int du_tp_wait_selftest(unsigned spin_limit, int *timed_out);
 
 /* Host-only (no device work): the slice of a global tensor that rank
  * cfg->tp_rank keeps.  tensor is a stem of IMP's file names
@@ -204,6 +216,19 @@ DU_API int du_gemv_q4(float *y, const void *x, int x_dtype, const uint8_t *w,
 /* fp16 weights [N, K] (LmHeadPredict1VecCoal, G3CS:1284-1302). */
 DU_API int du_gemv_f16(float *y, const void *x, int x_dtype, const uint16_t *w, int M, int N, int K,
                        void *stream);
+/* The three entry points above run the decode GEMV for M < 16 token rows and
+ * the tensor-core GEMM (tcgen05; the role of the *GemmCoal kernels,
+ * G3CS:1304-1439) for M >= 16 when K is a multiple of 64 (DU_GEMM_MIN_M in the
+ * environment moves the threshold).  The GEMM keeps fp32 accuracy: weights and
+ * activations enter the tensor cores as exact fp16 hi + lo pairs. */
+
+/* The weight values the tensor-core GEMM multiplies, as fp32, for rows
+ * [row0, row0 + nrows) of a weight matrix [N, K] (readQ4 / readQ8 / readH and
+ * wScale, G3CS:49-101): INT4 (n - 8) * d from the unpack's exact fp16 pair,
+ * INT8 q * row scale (scale_dtype F16 or F32), fp16 as stored.  out [nrows, K]
+ * fp32 (device).  quant: DU_QUANT_*; group: INT4 group size. */
+DU_API int du_dequant(float *out, const void *w, const void *scales, int quant, int scale_dtype, int group,
+                      int64_t row0, int nrows, int K, void *stream);
 
 /* Split-K flash-decode (FlashAttention, G3CS:643-753) for one new query per
  * sequence: q fp32 [batch, hq, hd] (already roped, unscaled); caches fp16
@@ -223,8 +248,12 @@ DU_API int du_flash_decode(float *out, const float *q, const uint16_t *k_cache,
  * (head_dim + 2) > 1048576, or batch * num_heads_kv > 8192) fail with DU_EINVAL.
  * The split count is reduced to fit the array.  The first call on a device
  * resolves the array's device address (cudaGetSymbolAddress) for that device;
- * make that first call before any stream capture.  Every call shares the array
- * and clears its counters first; calls whose kernels overlap on the GPU race. */
+ * make that first call before any stream capture.  The resolved address is
+ * cached for the life of the process and does not survive cudaDeviceReset: do
+ * not call this entry point on a device after resetting it.  Every call shares
+ * the array and clears its counters first; calls whose kernels overlap on the
+ * GPU race.  head_dim must be 64 or 128 and num_heads_q / num_heads_kv at most
+ * 8 (DU_EINVAL otherwise). */
 DU_API int du_flash_decode_noalloc(float *out, const float *q, const uint16_t *k_cache,
                                    const uint16_t *v_cache, const int32_t *kv_len, int batch, int hq,
                                    int hkv, int hd, int capacity, float scale, void *stream);

@@ -168,9 +168,18 @@ static inline float read_q4(const uint8_t *buf, uint64_t idx)
     return (float)((idx & 1) ? (b >> 4) : (b & 0xF)) - 8.0f;
 }
 
+/* readH through a table of every fp16 value's orc_f16_to_f32 (filled once when
+ * the library loads): the same values, without the per-element bit decoding. */
+static float g_f16_table[65536];
+
+__attribute__((constructor)) static void orc_fill_f16_table(void)
+{
+    for (uint32_t h = 0; h < 65536u; h++) g_f16_table[h] = orc_f16_to_f32((uint16_t)h);
+}
+
 static inline float read_h(const uint16_t *buf, uint64_t idx)
 {
-    return orc_f16_to_f32(buf[idx]);
+    return g_f16_table[buf[idx]];
 }
 
 /* A (possibly concatenated) matmul weight as the shader sees it. */

@@ -70,6 +70,72 @@ def test_device_quantize_int4_bit_exact(rows, cols, group):
     np.testing.assert_array_equal(d.cpu().numpy().view(np.uint16), d_ref)
 
 
+# ---------------------------------------------------- dequantised weights
+@pytest.mark.parametrize("quant,group", [("int4", 32), ("int4", 128), ("int8", 0), ("fp16", 0)])
+def test_dequant_bit_exact(quant, group):
+    """North-star gate: dequantised weight values bit-exact.  du_dequant writes the values
+    the tensor-core GEMM's unpack feeds the MMAs (INT4 as its exact fp16 hi + lo pair);
+    the oracle is readQ4 / readQ8 * wScale (G3CS:49-101) on the same bytes."""
+    rng = np.random.default_rng(7 + group)
+    N, K = 300, 4096
+    w = rng.standard_normal((N, K), dtype=np.float32) * 0.02
+    w[3] = 0.0                                   # quantizer floors
+    w[5, :64] *= 1e-3                            # small scales
+    w[6, 7] = 0.9                                # one large element per row / group
+    if quant == "int8":
+        wq, sc = orc.quantize_int8(w)
+    elif quant == "int4":
+        wq, sc = orc.quantize_int4(w, group)
+    else:
+        wq, sc = w.astype(np.float16).view(np.uint16), None
+    r0, nr = 17, 211
+    out = torch.empty((nr, K), dtype=torch.float32, device="cuda")
+    wd = dev(wq)
+    sd = dev(sc) if sc is not None else None
+    qid = {"fp16": _lib.QUANT_FP16, "int8": _lib.QUANT_INT8, "int4": _lib.QUANT_INT4}[quant]
+    _lib.call("du_dequant", ptr(out), ptr(wd), ptr(sd) if sd is not None else None, qid, _lib.DTYPE_F16,
+              group or 32, r0, nr, K, None)
+    torch.cuda.synchronize()
+    ref = orc.dequant(wq, sc, quant, N, K, group or 32)[r0:r0 + nr]
+    np.testing.assert_array_equal(out.cpu().numpy(), ref)
+
+
+def test_dequant_real_int8_export_bit_exact():
+    """Known-answer data: rows of the reference's shipped int8 export."""
+    import os
+    ex = np.load(os.path.join(os.path.dirname(__file__), "golden", "int8_export.npz"))
+    q, s = ex["q"], ex["s"]
+    N, K = q.shape
+    out = torch.empty((N, K), dtype=torch.float32, device="cuda")
+    qd, sd = dev(q), dev(s)
+    _lib.call("du_dequant", ptr(out), ptr(qd), ptr(sd), _lib.QUANT_INT8, _lib.DTYPE_F16, 32, 0, N, K, None)
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(out.cpu().numpy(), orc.dequant(q, s, "int8", N, K))
+
+
+# ------------------------------------------------------------------ GEMM
+@pytest.mark.parametrize("quant,group", [("int4", 32), ("int4", 128), ("int8", 0), ("fp16", 0)])
+@pytest.mark.parametrize("M,N,K", [(16, 128, 64), (17, 300, 256), (40, 256, 1024), (64, 130, 2048),
+                                   (100, 384, 512), (128, 200, 4096), (200, 128, 128)])
+def test_gemm_small_shapes(quant, group, M, N, K):
+    """The tensor-core GEMM (M >= 16) against the oracle: ragged M and N (partial
+    token and row tiles), K from one 64-column block up, every weight format."""
+    if quant == "int4" and K % group:
+        pytest.skip("K not a multiple of the group")
+    rng = np.random.default_rng(M * 7 + N + K)
+    w = rng.standard_normal((N, K), dtype=np.float32) * 0.02
+    x = rng.standard_normal((M, K)).astype(np.float32)
+    if quant == "int8":
+        wq, sc = orc.quantize_int8(w)
+    elif quant == "int4":
+        wq, sc = orc.quantize_int4(w, group)
+    else:
+        wq, sc = w.astype(np.float16).view(np.uint16), None
+    ref = orc.gemv(x, wq, sc, quant, N, group or 32)
+    y = _gemv(quant, x, wq, sc, N, K, group or 128)
+    assert relerr(y, ref) < GEMV_TOL
+
+
 # ------------------------------------------------------------------ GEMV
 def _gemv(quant, x, wq, s, N, K, group=128, scale_f32=False):
     M = x.shape[0]
@@ -138,6 +204,33 @@ def test_gemv_batch_sizes_and_fp16(M):
     assert relerr(_gemv("int4", x, wq, s, N, K), ref) < GEMV_TOL
 
 
+C2_SHAPES = [(4096, 4096), (14336, 4096), (4096, 14336)]
+
+
+@pytest.mark.parametrize("N,K", C2_SHAPES)
+@pytest.mark.parametrize("quant,group", [("int8", 0), ("int4", 128)])
+@pytest.mark.parametrize("M", [16, 64, 512])
+def test_config2_batched_tokens(N, K, quant, group, M):
+    """BASELINE config 2 at M = 16, 64, 512 with bf16 activations ~N(0,1), W ~N(0,0.02):
+    the oracle checks all M tokens on three 256-row windows (first, middle, last)."""
+    rng = np.random.default_rng(N + 3 * K + M)
+    w = (rng.standard_normal((N, K), dtype=np.float32) * 0.02)
+    xb = torch.randn((M, K), generator=torch.Generator().manual_seed(M + K)).to(torch.bfloat16)
+    x = xb.float().numpy()
+    wq, s = orc.quantize_int8(w) if quant == "int8" else orc.quantize_int4(w, group)
+    y = torch.empty((M, N), dtype=torch.float32, device="cuda")
+    xd, wd, sd = xb.cuda(), dev(wq), dev(s)
+    if quant == "int8":
+        _lib.call("du_gemv_q8", ptr(y), ptr(xd), _lib.DTYPE_BF16, ptr(wd), ptr(sd), _lib.DTYPE_F16, M, N, K, None)
+    else:
+        _lib.call("du_gemv_q4", ptr(y), ptr(xd), _lib.DTYPE_BF16, ptr(wd), ptr(sd), group, M, N, K, None)
+    torch.cuda.synchronize()
+    got = y.cpu().numpy()
+    for r0 in (0, N // 2 - 128, N - 256):
+        ref = orc.gemv(x, wq, s, quant, 256, group or 32, row_off=r0)
+        assert relerr(got[:, r0:r0 + 256], ref) < GEMV_TOL, r0
+
+
 def test_gemv_real_int8_export_rows():
     """Rows of the reference's shipped int8 export (known-answer data)."""
     import os
@@ -190,9 +283,12 @@ def test_flash_decode_matches_oracle(hq, hkv, hd):
     np.testing.assert_array_equal(out.cpu().numpy(), got)
 
 
-@pytest.mark.parametrize("ctx,B", [(512, 1), (2048, 8), (8192, 1), (32768, 1), (8192, 32)])
+@pytest.mark.parametrize("ctx,B", [(512, 1), (512, 8), (2048, 8), (2048, 32), (8192, 1), (8192, 8), (8192, 32),
+                                   (32768, 1), (32768, 8), (32768, 32)])
 def test_flash_decode_baseline_config3(ctx, B):
-    """BASELINE config 3 shapes (32 q / 8 kv heads, hd 128); the oracle checks two sequences."""
+    """BASELINE config 3 shapes (32 q / 8 kv heads, hd 128) on the model's kernel (the
+    thread-block-cluster flash-decode behind du_flash_decode); the oracle checks the first
+    and the last sequence."""
     hq, hkv, hd = 32, 8, 128
     g = torch.Generator(device="cuda").manual_seed(ctx + B)
     q = torch.randn((B, hq, hd), device="cuda", generator=g)

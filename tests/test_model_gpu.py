@@ -11,7 +11,7 @@ import torch
 
 from deepunity_b200 import DUError, LlamaForCausalLM, LLMQuant, _lib
 from oracle import oracle as orc
-from tests.modelgen import C4, MID, SMALL, ModelWeights, TestConfig
+from tests.modelgen import C4, C5_SLICE, MID, SMALL, ModelWeights, TestConfig
 
 pytestmark = pytest.mark.gpu
 LOGIT_TOL = 1e-3
@@ -140,4 +140,92 @@ def test_config4_llama_1p1b_int8_greedy_64():
     for _ in range(63):
         rt.append(orc.argmax(om.forward([rt[-1]])))
     assert toks == rt
+    m.Release()
+
+
+# ---------------------------------------------------------------- BASELINE config 5
+# The benchmarked 8B INT4-G128 architecture (hidden 4096, FFN 14336, 32 q / 8 kv
+# heads of 128, vocab 128256) on a 2-layer slice: a 128-token prompt, then 64
+# greedy ids.  The oracle run is shared by both decode paths.
+_C5 = {}
+
+
+def _c5_oracle():
+    if not _C5:
+        w = ModelWeights(C5_SLICE, seed=5)
+        om = orc.OracleModel(w, capacity=256)
+        prompt = np.random.default_rng(5).integers(0, C5_SLICE.vocab, 128).astype(np.int32)
+        ref = om.forward(prompt)
+        rt, last = [orc.argmax(ref)], None
+        for _ in range(63):
+            last = om.forward([rt[-1]])
+            rt.append(orc.argmax(last))
+        _C5.update(w=w, prompt=prompt, ref=ref, tokens=rt, last=last)
+    return _C5
+
+
+@pytest.mark.parametrize("path", list(PATHS))
+def test_config5_slice_int4_g128_greedy_64(path):
+    d = _c5_oracle()
+    m = LlamaForCausalLM(C5_SLICE.du_kwargs(), LLMQuant.INT4, max_context_length=256, seed=None,
+                         flags=PATHS[path])
+    d["w"].load_into(m)
+    logits, nxt = m.forward(d["prompt"][None, :])
+    assert relerr(logits[0], d["ref"]) < LOGIT_TOL
+    toks = [int(nxt[0])] + m.decode_loop([int(nxt[0])], 63)[:, 0].tolist()
+    assert toks == d["tokens"]
+    assert relerr(m.read_logits(1)[0], d["last"]) < LOGIT_TOL
+    m.Release()
+
+
+def test_config4_batch16_int8():
+    """BASELINE config 4 at batch 16: 16 sequences prefilled and decoded together;
+    the first, a middle and the last sequence are checked against independent
+    oracle runs (logits of the prompt and 25 greedy ids)."""
+    w, m = build(C4, seed=1, cap=64, max_batch=16)
+    prompts = np.random.default_rng(16).integers(0, C4.vocab, (16, 16)).astype(np.int32)
+    logits, nxt = m.forward(prompts)
+    toks = m.decode_loop(nxt, 24)
+    for b in (0, 7, 15):
+        om = orc.OracleModel(w, capacity=64)
+        ref = om.forward(prompts[b])
+        assert relerr(logits[b], ref) < LOGIT_TOL, b
+        rt = [orc.argmax(ref)]
+        for _ in range(24):
+            rt.append(orc.argmax(om.forward([rt[-1]])))
+        assert [int(nxt[b])] + toks[:, b].tolist() == rt, b
+    m.Release()
+
+
+def _tree_rank(i: int):
+    """Order of the reference ArgMax tree among tied maxima (G3CS:911-928):
+    bit-reversed thread id (i % 256), then the lowest index of that thread."""
+    t = i % 256
+    return (int(f"{t:08b}"[::-1], 2), i // 256)
+
+
+@pytest.mark.parametrize("path", list(PATHS))
+def test_greedy_ties_follow_the_reference_argmax_tree(path):
+    """Two lm_head rows made identical give bit-identical logits; the greedy pick must
+    be the one the reference's ArgMax tree keeps, which here is not the lower index."""
+    cfg = SMALL
+    w = ModelWeights(cfg, seed=4)
+    prompt = np.arange(3, 11, dtype=np.int32)
+    top = orc.argmax(orc.OracleModel(w, capacity=64).forward(prompt))
+    cands = [j for j in range(cfg.vocab) if j != top and (j < top) != (_tree_rank(j) < _tree_rank(top))]
+    assert cands, top
+    j = cands[0]
+    w.lm_head[j] = w.lm_head[top]
+    expect = top if _tree_rank(top) < _tree_rank(j) else j
+    ref = orc.OracleModel(w, capacity=64).forward(prompt)
+    assert ref[top] == ref[j] and orc.argmax(ref) == expect
+    q = {"int8": LLMQuant.INT8, "int4": LLMQuant.INT4, "fp16": LLMQuant.FP16}[cfg.quant]
+    m = LlamaForCausalLM(cfg.du_kwargs(), q, max_context_length=64, seed=None, flags=PATHS[path])
+    w.load_into(m)
+    logits, nxt = m.forward(prompt[None, :])
+    assert logits[0][top] == logits[0][j]
+    assert int(nxt[0]) == expect                       # prefill head + greedy pick
+    m.ResetCache()
+    m.forward(prompt[None, :-1])
+    assert int(m.decode_step([prompt[-1]])[0]) == expect   # decode graph's head + pick
     m.Release()

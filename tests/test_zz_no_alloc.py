@@ -47,9 +47,17 @@ def test_noalloc_matches_allocating_entry_point(hq, hkv, hd, batch, cap):
         a, b = out.cpu().numpy(), ref.cpu().numpy()
         assert np.isfinite(a).all()
         assert float(np.max(np.abs(a - b)) / np.max(np.abs(b))) < ATTN_TOL
+    # and directly against the CPU oracle's restatement of FlashAttention (G3CS:643-753)
+    from oracle import oracle as orc
+    qn, kn, vn = q.cpu().numpy(), kc.cpu().numpy().view(np.uint16), vc.cpu().numpy().view(np.uint16)
+    for s in sorted({0, batch - 1}):
+        o = orc.flash_attention(qn[s:s + 1], kn[s], vn[s], int(lens[s].item()), hq, hkv, hd, hd ** -0.5)[0]
+        assert float(np.max(np.abs(a[s] - o)) / np.max(np.abs(o))) < ATTN_TOL, s
 
 
 def test_noalloc_rejects_sizes_beyond_its_fixed_scratch():
+    """Sizes beyond the fixed array, and head shapes the kernel does not serve,
+    return DU_EINVAL before anything is enqueued."""
     if not torch.cuda.is_available():
         pytest.skip("no CUDA device")
     _lib.call("du_init", 0)
@@ -62,3 +70,11 @@ def test_noalloc_rejects_sizes_beyond_its_fixed_scratch():
     rc = _lib.lib().du_flash_decode_noalloc(_p(x), _p(x), _p(x), _p(x), _p(x), 300, 32, 8, 128, 64,
                                             C.c_float(0.1), None)
     assert rc == _lib.DU_EINVAL and "1048576" in _lib.last_error()
+    # head_dim the kernel does not serve (would size the scratch from a bad value)
+    rc = _lib.lib().du_flash_decode_noalloc(_p(x), _p(x), _p(x), _p(x), _p(x), 1, 32, 8, -2, 64,
+                                            C.c_float(0.1), None)
+    assert rc == _lib.DU_EINVAL and "head_dim" in _lib.last_error()
+    # GQA group above 8
+    rc = _lib.lib().du_flash_decode_noalloc(_p(x), _p(x), _p(x), _p(x), _p(x), 1, 32, 2, 128, 64,
+                                            C.c_float(0.1), None)
+    assert rc == _lib.DU_EINVAL and "at most 8" in _lib.last_error()
