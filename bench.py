@@ -553,7 +553,13 @@ def run_sweep_gemv(args):
                 byts = wbytes + sbytes + M * K * 2 + M * N * 4
                 gbs = byts / (ms / 1e3) / 1e9
                 tflops = 2 * M * N * K / (ms / 1e3) / 1e12
-                path = "tcgen05 GEMM" if M >= 16 and K % 64 == 0 else "GEMV"
+                if M >= 16 and K % 64 == 0:
+                    path = "tcgen05 GEMM (kind::f16, exact fp16 hi/lo operands)"
+                elif (M <= 2 and quant == "int4" and K % 128 == 0 and (K // 128) % 8 == 0
+                      and os.environ.get("DU_DECODE_GEMV") == "tcgen05"):
+                    path = "tcgen05 GEMV (kind::i8, nibble x byte planes)"
+                else:
+                    path = "dp4a GEMV"
                 print(json.dumps({"sweep": "gemv", "quant": quant + {"int4": "-g128", "int8": "-row"}.get(quant, ""),
                                   "N": N, "K": K, "M": M, "path": path, "us": round(ms * 1e3, 2),
                                   "GB_s": round(gbs, 1), "frac_hbm": round(gbs / peak, 4),

@@ -72,6 +72,8 @@ SIGNATURES = {
     "du_rmsnorm": (I, [P, P, P, I, I, F, P]),
     "du_tp_wait_selftest": (I, [C.c_uint, C.POINTER(C.c_int)]),
     "du_dequant": (I, [P, P, P, I, I, I, I64, I, I, P]),
+    "du_sample": (I, [P, P, I, I, I, F, I, F, F, P, P]),
+    "du_decode_step_sample": (I, [P, P, I, F, I, F, F, P, P]),
 }
 
 _lib = None

@@ -15,8 +15,8 @@ import sys
 HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(HERE, "csrc")
 LIB = os.path.join(HERE, "libdeepunity_cuda.so")
-SOURCES = ["capi.cu", "gemv.cu", "gemm.cu", "attention.cu", "elementwise.cu", "model.cu", "noalloc.cu",
-           "decode_step.cu", "tp_comm.cu"]
+SOURCES = ["capi.cu", "gemv.cu", "gemm.cu", "tgemv.cu", "attention.cu", "elementwise.cu", "model.cu", "noalloc.cu",
+           "decode_step.cu", "tp_comm.cu", "sampler.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

@@ -71,8 +71,8 @@ int ensure_func_attrs(const void *kern, int smem_bytes, bool nonportable_cluster
 void *device_scratch(size_t bytes, int slot)
 {
     static std::mutex mu;
-    static void *ptr[64][4] = {};
-    static size_t cap[64][4] = {};
+    static void *ptr[64][8] = {};
+    static size_t cap[64][8] = {};
     std::lock_guard<std::mutex> lk(mu);
     int dev = 0;
     cudaGetDevice(&dev);
@@ -149,6 +149,29 @@ static int gemv_entry(int qt, float *y, const void *x, int x_dtype, const void *
     int rc = x_to_f32(x, x_dtype, (size_t)M * K, &xf, st);
     if (rc) return rc;
     const int64_t row_bytes = qt == Q_I4 ? K / 2 : qt == Q_I8 ? K : 2 * (int64_t)K;
+    if (M <= 2 && qt == Q_I4) {
+        // tensor-core decode GEMV
+        GemvParams p = {};
+        p.x = xf; p.ldx = K;
+        p.w = static_cast<const uint8_t *>(w);
+        p.scales = scales;
+        p.row_bytes = row_bytes;
+        p.K = K; p.N = N; p.M = M; p.group = group;
+        p.map = MAP_IDENT;
+        p.epi = EPI_STORE;
+        p.y = y;
+        p.ldy = N;
+        if (tgemv_supported(qt, p)) {
+            GemmScratch g;
+            g.partial_floats = GEMM_PARTIAL_FLOATS_PER_SM * (size_t)num_sms();
+            g.counter_n = 1 << 16;
+            char *ps = static_cast<char *>(device_scratch(4 * g.partial_floats + 4 * g.counter_n, 4));
+            if (!ps) return fail(DU_ENOMEM, "gemv: scratch allocation failed");
+            g.partials = reinterpret_cast<float *>(ps);
+            g.counters = reinterpret_cast<unsigned *>(ps + 4 * g.partial_floats);
+            return launch_tgemv(qt, p, g, st);
+        }
+    }
     if (M >= gemm_min_tokens()) {
         // tensor-core GEMM: weights streamed once for all M rows
         GemvParams p = {};
@@ -171,6 +194,12 @@ static int gemv_entry(int qt, float *y, const void *x, int x_dtype, const void *
             g.xh = reinterpret_cast<__half *>(buf);
             g.xl = g.xh + g.elems;
             g.xscale = reinterpret_cast<float *>(buf + 4 * g.elems);
+            g.partial_floats = GEMM_PARTIAL_FLOATS_PER_SM * (size_t)num_sms();
+            g.counter_n = 1 << 16;
+            char *ps = static_cast<char *>(device_scratch(4 * g.partial_floats + 4 * g.counter_n, 4));
+            if (!ps) return fail(DU_ENOMEM, "gemm: scratch allocation failed");
+            g.partials = reinterpret_cast<float *>(ps);
+            g.counters = reinterpret_cast<unsigned *>(ps + 4 * g.partial_floats);
             return launch_gemm(qt, p, g, st);
         }
     }

@@ -54,6 +54,12 @@ struct GemmArgs {
     int kb_bytes;           // raw bytes of one row per K block
     int tmem_cols;
     int *err;               // device error word (bounded waits)
+    // split-K: gridDim.z CTAs share a (row tile, token tile); each leaves its partial
+    // accumulators in `partials`, the last to finish (per `counters`) sums them in
+    // split order and runs the epilogue
+    int ksplit;
+    float *partials;        // [tiles][ksplit][TN][128]
+    unsigned *counters;     // [tiles], zero between launches
 };
 
 // ------------------------------------------------------------ staging kernel
@@ -143,10 +149,16 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
     uint64_t *op_empty = a_full + S, *acc_full = op_empty + S;
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(acc_full + 1);
     volatile int *abort_f = reinterpret_cast<volatile int *>(tmem_slot + 1);
+    volatile int *last_f = reinterpret_cast<volatile int *>(tmem_slot + 2);
+    float *am_v = reinterpret_cast<float *>(tmem_slot + 4);          // [4 warps][32 tokens] (EPI_LOGITS)
+    int *am_i = reinterpret_cast<int *>(am_v + 4 * 32);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int row_tile = blockIdx.x, tok0 = blockIdx.y * TN;
-    const int KB = p.K / GM_KB;
+    // this CTA's K blocks [kb0, kb0 + KB) (split-K part blockIdx.z of a.ksplit)
+    const int KB_all = p.K / GM_KB, ks = blockIdx.z;
+    const int kb0 = (int)(((int64_t)ks * KB_all) / a.ksplit);
+    const int KB = (int)(((int64_t)(ks + 1) * KB_all) / a.ksplit) - kb0;
     auto A_hi = [&](int s) { return ops + (size_t)s * op_bytes; };
     auto A_lo = [&](int s) { return ops + (size_t)s * op_bytes + a_bytes; };
     auto B_hi = [&](int s) { return ops + (size_t)s * op_bytes + NA * a_bytes; };
@@ -187,7 +199,7 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
                 const uint32_t bar = smem_u32(raw_full + rs);
                 mbar_arrive_expect_tx(bar, (uint32_t)a.raw_bytes);
                 const uint32_t dst = smem_u32(raw + (size_t)rs * a.raw_bytes);
-                const int x = kb * a.kb_bytes;
+                const int x = (kb0 + kb) * a.kb_bytes;
                 if (p.map == MAP_GATEUP) {
                     const int g0 = (int)p.row_off + row_tile * 64;
                     tma_load_2d(dst, &tm_w, bar, x, g0, pol);
@@ -213,8 +225,8 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
                 if (!mbar_wait(smem_u32(op_empty + s), ((kb / S) & 1) ^ 1, abort_f, a.err, GM_SPIN_LIMIT)) break;
                 const uint32_t bar = smem_u32(b_full + s);
                 mbar_arrive_expect_tx(bar, (uint32_t)(2 * b_bytes));
-                tma_load_2d(smem_u32(B_hi(s)), &tm_xh, bar, kb * GM_KB, tok0, pol);
-                tma_load_2d(smem_u32(B_lo(s)), &tm_xl, bar, kb * GM_KB, tok0, pol);
+                tma_load_2d(smem_u32(B_hi(s)), &tm_xh, bar, (kb0 + kb) * GM_KB, tok0, pol);
+                tma_load_2d(smem_u32(B_lo(s)), &tm_xl, bar, (kb0 + kb) * GM_KB, tok0, pol);
                 issued = kb + 1;
             }
             if (*abort_f) {
@@ -262,7 +274,7 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
             // INT4 group scales of this row's 64 columns (one group, or two of 32)
             __half2 d0 = __half2half2(__float2half(0.0f)), d1 = d0;
             if (QT == Q_I4 && row_ok) {
-                const int g = (kb * GM_KB) / p.group;
+                const int g = ((kb0 + kb) * GM_KB) / p.group;
                 d0 = __half2half2(sc[pr * ng + g]);
                 d1 = p.group == 32 ? __half2half2(sc[pr * ng + g + 1]) : d0;
             }
@@ -314,34 +326,98 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
         pdl_wait();        // residual / KV / positions come from earlier kernels
         const bool acc_ok = mbar_wait(smem_u32(acc_full), 0, abort_f, a.err, GM_SPIN_LIMIT);
         tc_fence_after();
-        if (acc_ok && !*abort_f) {
+        const uint32_t taddr = tmem + ((uint32_t)((warp & 3) * 32) << 16);
+        const int tile = blockIdx.y * gridDim.x + blockIdx.x;
+        bool run = acc_ok && !*abort_f;
+        if (run && a.ksplit > 1) {
+            // leave this part's accumulators; the last part of the tile to arrive finishes it
+            float *mine = a.partials + ((size_t)tile * a.ksplit + ks) * TN * GM_ROWS;
+            for (int c0 = 0; c0 < TN; c0 += 32) {
+                uint32_t r[32];
+                tmem_ld32(taddr + (uint32_t)c0, r);
+                tmem_wait_ld();
+#pragma unroll
+                for (int i = 0; i < 32; i++) __stcg(mine + (size_t)(c0 + i) * GM_ROWS + j, __uint_as_float(r[i]));
+            }
+            __threadfence();
+            asm volatile("bar.sync 1, 128;" ::: "memory");
+            if (j == 0) *last_f = atomicAdd(a.counters + tile, 1u) == (unsigned)(a.ksplit - 1);
+            asm volatile("bar.sync 1, 128;" ::: "memory");
+            run = *last_f != 0;
+            if (run) __threadfence();
+        }
+        if (run) {
             const float rsc = (QT == Q_I8 && row_ok) ? (p.scale_f32 ? reinterpret_cast<const float *>(p.scales)[pr]
                                                                     : __half2float(sc[pr]))
                                                      : 1.0f;
-            const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
             for (int c0 = 0; c0 < TN; c0 += 32) {
                 uint32_t r[32];
-                tmem_ld32(tmem + lane_base + (uint32_t)c0, r);
+                tmem_ld32(taddr + (uint32_t)c0, r);
                 tmem_wait_ld();
-                if (tok0 + c0 >= p.M) continue;       // uniform across the warp
+                if (tok0 + c0 >= p.M) continue;       // uniform across the epilogue warps
+                float v[32];
+                if (a.ksplit > 1) {
+                    // sum of the parts in split order (this part's own values from TMEM)
+#pragma unroll
+                    for (int i = 0; i < 32; i++) v[i] = 0.0f;
+                    for (int k = 0; k < a.ksplit; k++) {
+                        const float *part = a.partials + ((size_t)tile * a.ksplit + k) * TN * GM_ROWS;
+#pragma unroll
+                        for (int i = 0; i < 32; i++)
+                            v[i] += k == ks ? __uint_as_float(r[i]) : __ldcg(part + (size_t)(c0 + i) * GM_ROWS + j);
+                    }
+                } else {
+#pragma unroll
+                    for (int i = 0; i < 32; i++) v[i] = __uint_as_float(r[i]);
+                }
 #pragma unroll
                 for (int i = 0; i < 32; i++) {
                     const int t = tok0 + c0 + i;
                     const bool tok_ok = t < p.M;
-                    float v = __uint_as_float(r[i]) * (tok_ok ? a.xscale[t] : 0.0f) * rsc;
+                    const float val = v[i] * (tok_ok ? a.xscale[t] : 0.0f) * rsc;
                     if (p.epi == EPI_QKV || p.epi == EPI_GATEUP) {
-                        const float o = __shfl_xor_sync(0xffffffffu, v, 1);
+                        const float o = __shfl_xor_sync(0xffffffffu, val, 1);
                         if (tok_ok && row_ok && (lr & 1) == 0) {
-                            if (p.epi == EPI_GATEUP) p.y[(size_t)t * p.ldy + (lr >> 1)] = (v / (1.0f + expf(-v))) * o;
-                            else gv_epi_pair(p, lr, t, v, o);
+                            if (p.epi == EPI_GATEUP) p.y[(size_t)t * p.ldy + (lr >> 1)] = (val / (1.0f + expf(-val))) * o;
+                            else gv_epi_pair(p, lr, t, val, o);
                         }
+                    } else if (p.epi == EPI_LOGITS) {
+                        if (tok_ok && row_ok && p.logits) p.logits[(size_t)t * p.ldl + lr] = val;
+                        // this tile's (max, argmax) for token t, the reference's tie-break
+                        float bv = (tok_ok && row_ok) ? val : -INFINITY;
+                        int bi = row_ok ? p.vocab_off + lr : 0x7fffffff;
+#pragma unroll
+                        for (int o = 16; o > 0; o >>= 1) {
+                            const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+                            const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+                            if (am_better(ov, oi, bv, bi)) { bv = ov; bi = oi; }
+                        }
+                        if (lane == 0) { am_v[(warp & 3) * 32 + i] = bv; am_i[(warp & 3) * 32 + i] = bi; }
                     } else if (tok_ok && row_ok) {
                         float *dst = p.y + (size_t)t * p.ldy + lr;
-                        if (p.epi == EPI_RESID) *dst += v;
-                        else *dst = v;
+                        if (p.epi == EPI_RESID) *dst += val;
+                        else *dst = val;
                     }
                 }
+                if (p.epi == EPI_LOGITS) {
+                    asm volatile("bar.sync 1, 128;" ::: "memory");
+                    const int t = tok0 + c0 + j;
+                    if (j < 32 && t < p.M) {
+                        float bv = am_v[j];
+                        int bi = am_i[j];
+#pragma unroll
+                        for (int w = 1; w < 4; w++)
+                            if (am_better(am_v[w * 32 + j], am_i[w * 32 + j], bv, bi)) {
+                                bv = am_v[w * 32 + j];
+                                bi = am_i[w * 32 + j];
+                            }
+                        p.am_val[(size_t)t * gridDim.x + row_tile] = bv;
+                        p.am_idx[(size_t)t * gridDim.x + row_tile] = bi;
+                    }
+                    asm volatile("bar.sync 1, 128;" ::: "memory");
+                }
             }
+            if (a.ksplit > 1 && j == 0) a.counters[tile] = 0u;     // every part has arrived: ready for the next launch
         }
     }
 
@@ -413,7 +489,8 @@ static GemmPlan gm_plan(int qt, int M)
     if (env_rs > 0 && env_rs < g.raw_stages) g.raw_stages = env_rs;  // tuning knob: fewer raw-weight stages
     const int na = qt == Q_I4 ? 2 : 1;
     const size_t op = (size_t)na * GM_ROWS * 128 + 2 * (size_t)g.tn * 128;
-    const size_t fixed = 1024 + (size_t)g.raw_stages * g.raw_bytes + 256;    // alignment slack, raw ring, barriers
+    // alignment slack, raw ring, barriers + TMEM slot + flags + argmax scratch
+    const size_t fixed = 1024 + (size_t)g.raw_stages * g.raw_bytes + 256 + 1040;
     int s = (int)((GM_SMEM_BUDGET - fixed) / op);
     g.op_stages = s > 4 ? 4 : s;
     static const int env_s = [] { const char *e = getenv("DU_GEMM_OP_STAGES"); return e ? atoi(e) : 0; }();
@@ -427,7 +504,8 @@ bool gemm_supported(int qt, const GemvParams &p)
 {
     if (p.M <= 0 || p.N <= 0 || p.K <= 0 || (p.K % GM_KB) != 0) return false;
     if (qt == Q_I4 && (p.group < 32 || (p.group & (p.group - 1)) != 0)) return false;
-    if (p.epi != EPI_STORE && p.epi != EPI_RESID && p.epi != EPI_QKV && p.epi != EPI_GATEUP) return false;
+    if (p.epi != EPI_STORE && p.epi != EPI_RESID && p.epi != EPI_QKV && p.epi != EPI_GATEUP && p.epi != EPI_LOGITS)
+        return false;
     if (p.map == MAP_GATEUP && (p.N != 2 * p.map_I || (p.map_I % 64) != 0)) return false;
     if (p.map == MAP_ROPE_PAIR && ((p.map_hd != 64 && p.map_hd != 128) || (p.N % GM_ROWS) != 0)) return false;
     return true;
@@ -506,7 +584,26 @@ int launch_gemm(int qt, const GemvParams &p, const GemmScratch &scr, cudaStream_
     a.kb_bytes = g.kb_bytes;
     a.tmem_cols = g.tmem_cols;
     a.err = scr.err;
-    const dim3 grid((p.N + GM_ROWS - 1) / GM_ROWS, (p.M + g.tn - 1) / g.tn);
+    // split K when the tiles alone leave SMs idle: aim at two CTAs per SM in flight,
+    // at least 4 K blocks per part, within the partial-sum scratch
+    const int row_tiles = (p.N + GM_ROWS - 1) / GM_ROWS, tok_tiles = (p.M + g.tn - 1) / g.tn;
+    const int tiles = row_tiles * tok_tiles, KB = p.K / GM_KB;
+    int ks = 1;
+    if (p.epi != EPI_LOGITS && tiles < num_sms()) {
+        ks = (2 * num_sms() + tiles - 1) / tiles;
+        if (ks > KB / 4) ks = KB / 4;
+        while (ks > 1 && ((size_t)tiles * ks * g.tn * GM_ROWS > scr.partial_floats || (size_t)tiles > scr.counter_n))
+            ks--;
+        if (ks < 1) ks = 1;
+    }
+    static const int env_ks = [] { const char *e = getenv("DU_GEMM_KSPLIT"); return e ? atoi(e) : 0; }();
+    if (env_ks > 0 && env_ks <= KB && (size_t)tiles * env_ks * g.tn * GM_ROWS <= scr.partial_floats &&
+        (size_t)tiles <= scr.counter_n && p.epi != EPI_LOGITS)
+        ks = env_ks;                                              // tuning knob: force a split count
+    a.ksplit = ks;
+    a.partials = scr.partials;
+    a.counters = scr.counters;
+    const dim3 grid(row_tiles, tok_tiles, ks);
     if (qt == Q_I4) return gm_launch<Q_I4>(tw, th, tl, a, grid, g.smem, st);
     if (qt == Q_I8) return gm_launch<Q_I8>(tw, th, tl, a, grid, g.smem, st);
     return gm_launch<Q_F16>(tw, th, tl, a, grid, g.smem, st);

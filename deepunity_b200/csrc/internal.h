@@ -27,10 +27,21 @@ struct GemmScratch {
     float *xscale = nullptr;               // [rows]
     size_t elems = 0, rows = 0;            // capacity: rows * K elements, rows
     int *err = nullptr;                    // device error word of the bounded waits (may be null)
+    float *partials = nullptr;             // split-K partial tiles (may be null: no split)
+    size_t partial_floats = 0;
+    unsigned *counters = nullptr;          // one per (row tile, token tile), zero-initialised
+    size_t counter_n = 0;
 };
 bool gemm_supported(int qt, const GemvParams &p);
 int gemm_min_tokens();                      // smallest M routed to the GEMM (DU_GEMM_MIN_M, default 16)
+// split-K scratch that serves every launch: two CTAs per SM of 128 x 128 partial tiles
+constexpr size_t GEMM_PARTIAL_FLOATS_PER_SM = 2ull * 128 * 128;
 int launch_gemm(int qt, const GemvParams &p, const GemmScratch &scr, cudaStream_t st);
+// tgemv.cu: decode GEMV (M <= 2, INT4) on the tensor cores (tcgen05 kind::i8); shares the GEMM's
+// split scratch (partials, counters)
+bool tgemv_enabled();                        // DU_DECODE_GEMV=tcgen05 in the environment turns it on
+bool tgemv_supported(int qt, const GemvParams &p);
+int launch_tgemv(int qt, const GemvParams &p, const GemmScratch &scr, cudaStream_t st);
 int launch_dequant_rows(int qt, const void *w, const void *scales, int scale_f32, int group, int64_t row0, int nrows,
                         int K, float *out, cudaStream_t st);
 
@@ -63,6 +74,11 @@ int launch_argmax_final_pairs(const float *am_val, const int *am_idx, int M, int
                               cudaStream_t st);
 int launch_argmax_pick_tp(const float *gpairs, int tp, int maxb, int M, int *out_ids, int *feed_ids,
                           TokHist hist, cudaStream_t st);
+// sampler.cu: temperature / top-k / top-p / min-p sampling (or the greedy pick) per row of logits
+bool sample_supported(float temperature, int top_k, float top_p, int V);
+int launch_sample(const float *logits, int rows, int V, int ldl, float temperature, int top_k, float top_p,
+                  float min_p, const int32_t *seeds, int32_t *out, int *feed, TokHist hist, int *err, cudaStream_t st,
+                  const float *dparams);
 int launch_add_inplace(float *y, const float *x, size_t n, cudaStream_t st);
 int launch_quantize_int8(const float *w, int64_t rows, int64_t cols, int8_t *q, __half *s, cudaStream_t st);
 int launch_quantize_int4(const float *w, int64_t rows, int64_t cols, int group, uint8_t *p, __half *s,

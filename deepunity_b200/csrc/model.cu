@@ -91,7 +91,11 @@ struct du_model {
     unsigned long long *d_stamps = nullptr; // per-stage timestamps of the last persistent step
     int stamp_stages = 0;                   // stages of the step that wrote them
     std::vector<int> h_cache_len;
-    std::map<int, du::Graph> graphs;
+    std::map<int, du::Graph> graphs;        // greedy decode step per batch size
+    std::map<int, du::Graph> sgraphs;       // sampling decode step per batch size
+    int32_t *d_seeds = nullptr;             // [maxb] sampler seeds of the next step
+    float *d_sparams = nullptr;             // (temperature, top_k, top_p, min_p) of the next sampling step
+    int32_t *h_pin_seeds = nullptr;         // pinned staging: [maxb] seeds then 4 floats of settings
     int last_batch = 0, last_rows = 0;      // rows of logits written by the last call
     std::atomic<int> busy{0};
     // TP
@@ -234,9 +238,11 @@ static int model_alloc(du_model *m)
     m->logits = (float *)dalloc(m, sizeof(float) * m->maxb * m->V_l, &rc);
     if (m->tp > 1) m->logits_all = (float *)dalloc(m, sizeof(float) * m->tp * m->maxb * m->V_l, &rc);
     m->am_parts = 2 * num_sms();
-    // per-row greedy state is sized for the largest forward chunk (all-position logits)
-    m->am_val = (float *)dalloc(m, sizeof(float) * T * m->am_parts, &rc);
-    m->am_idx = (int *)dalloc(m, sizeof(int) * T * m->am_parts, &rc);
+    // per-row greedy state is sized for the largest forward chunk (all-position logits), and
+    // for the tensor-core head (one partial per 128-row vocab tile)
+    const int am_cap = m->am_parts > (m->V_l + 127) / 128 ? m->am_parts : (m->V_l + 127) / 128;
+    m->am_val = (float *)dalloc(m, sizeof(float) * T * am_cap, &rc);
+    m->am_idx = (int *)dalloc(m, sizeof(int) * T * am_cap, &rc);
     m->best_val = (float *)dalloc(m, sizeof(float) * T * 2, &rc);
     m->gbest_val = (float *)dalloc(m, sizeof(float) * T * 2 * m->tp, &rc);
     const int G = m->hq_l / m->hkv_l;
@@ -251,6 +257,8 @@ static int model_alloc(du_model *m)
     m->fd_counters = (unsigned *)dalloc(m, sizeof(unsigned) * (size_t)T * m->hkv_l, &rc);
     m->d_barrier = (unsigned *)dalloc(m, sizeof(unsigned), &rc);
     m->d_err = (int *)dalloc(m, sizeof(int), &rc);
+    m->d_seeds = (int32_t *)dalloc(m, sizeof(int32_t) * (m->maxb + 4), &rc);
+    m->d_sparams = reinterpret_cast<float *>(m->d_seeds + m->maxb);
     {   // GEMM activation stage: every K a chunk's GEMM can see (H, I_l, hq_l * hd)
         int64_t kmax = H > m->I_l ? H : m->I_l;
         if ((int64_t)m->hq_l * hd > kmax) kmax = (int64_t)m->hq_l * hd;
@@ -260,12 +268,17 @@ static int model_alloc(du_model *m)
         m->gm.xl = (__half *)dalloc(m, 2 * m->gm.elems, &rc);
         m->gm.xscale = (float *)dalloc(m, sizeof(float) * T, &rc);
         m->gm.err = m->d_err;
+        m->gm.partial_floats = GEMM_PARTIAL_FLOATS_PER_SM * (size_t)num_sms();
+        m->gm.partials = (float *)dalloc(m, sizeof(float) * m->gm.partial_floats, &rc);
+        m->gm.counter_n = 1 << 16;
+        m->gm.counters = (unsigned *)dalloc(m, sizeof(unsigned) * m->gm.counter_n, &rc);
     }
     m->d_stamps = (unsigned long long *)dalloc(m, sizeof(unsigned long long) * (5 * (size_t)m->L + 8), &rc);
     if (rc) return rc;
     DU_CUDA_TRY(cudaMallocHost(&m->h_pin_err, sizeof(int)));
     DU_CUDA_TRY(cudaMallocHost(&m->h_pin_ids, sizeof(int) * T));
     DU_CUDA_TRY(cudaMallocHost(&m->h_pin_next, sizeof(int) * m->maxb));
+    DU_CUDA_TRY(cudaMallocHost(&m->h_pin_seeds, sizeof(int32_t) * (m->maxb + 4)));
     m->h_cache_len.assign(m->maxb, 0);
 
     // RoPE tables on the host with the reference formula (MiniCPM5Model.cs:163-191)
@@ -288,11 +301,15 @@ static void model_free(du_model *m)
 {
     cudaSetDevice(m->device);
     if (m->stream) cudaStreamSynchronize(m->stream);
-    for (auto &kv : m->graphs) {
-        if (kv.second.exec) cudaGraphExecDestroy(kv.second.exec);
-        if (kv.second.g) cudaGraphDestroy(kv.second.g);
-        if (kv.second.d_stages) cudaFree(kv.second.d_stages);
-    }
+    for (auto *gm : {&m->graphs, &m->sgraphs})
+        for (auto &kv : *gm) {
+            if (kv.second.exec) cudaGraphExecDestroy(kv.second.exec);
+            if (kv.second.g) cudaGraphDestroy(kv.second.g);
+            if (kv.second.d_stages) cudaFree(kv.second.d_stages);
+        }
+    m->sgraphs.clear();
+    if (m->h_pin_seeds) cudaFreeHost(m->h_pin_seeds);
+    m->h_pin_seeds = nullptr;
     if (m->h_pin_err) cudaFreeHost(m->h_pin_err);
     m->h_pin_err = nullptr;
     m->graphs.clear();
@@ -487,6 +504,11 @@ static int gemv_max_tokens(int qt, int64_t row_bytes)
 // Token-indexed pointers of `p` are advanced per chunk.
 static int run_gemv(du_model *m, int qt, GemvParams p, int M)
 {
+    if (M <= 2) {     // tensor-core decode GEMV (INT4)
+        GemvParams g = p;
+        g.M = M;
+        if (tgemv_supported(qt, g)) return launch_tgemv(qt, g, m->gm, m->stream);
+    }
     if (M >= gemm_min_tokens()) {     // tensor-core GEMM: every weight streamed once for all M rows
         GemvParams g = p;
         g.M = M;
@@ -556,6 +578,7 @@ struct StepIO {
     int *next_out;         // [logits_rows] greedy ids
     int *feed;             // optional: also write ids here (device loop)
     bool advance;          // cache_len[m] += 1 at the end (decode)
+    bool sample = false;   // pick with the stochastic sampler (settings and seeds in device memory)
 };
 
 enum Stage { ST_QKV = 0, ST_ATTN = 1, ST_O = 2, ST_GATEUP = 3, ST_DOWN = 4 };
@@ -713,20 +736,30 @@ static int enqueue_head(du_model *m, const StepIO &io)
     int rc = DU_OK;
     const int R = io.logits_rows;
     GemvParams p = head_gemv_params(m, io);
-    // one CTA count for every token tile (the argmax reads nparts partials per row); a
-    // single row uses the token-tile-1 layout's count, so that it runs in one wave
-    const int nparts = gemv_grid_for(
-        p.N, 1, R == 1 ? gemv_ctas_per_sm(Q_F16, 1, p.row_bytes) * num_sms() : m->am_parts);
-    p.grid = nparts;
-    const int mt = gemv_max_tokens(Q_F16, p.row_bytes);
-    for (int t0 = 0; t0 < R; t0 += mt) {
-        GemvParams c = p;
-        c.M = R - t0 < mt ? R - t0 : mt;
-        c.x = p.x + (size_t)t0 * p.ldx;
-        c.logits = p.logits + (size_t)t0 * p.ldl;
-        c.am_val = m->am_val + (size_t)t0 * nparts;
-        c.am_idx = m->am_idx + (size_t)t0 * nparts;
-        if ((rc = launch_gemv(Q_F16, c, st))) return rc;
+    int nparts;
+    GemvParams g = p;
+    g.M = R;
+    g.am_val = m->am_val;
+    g.am_idx = m->am_idx;
+    if (R >= gemm_min_tokens() && gemm_supported(Q_F16, g)) {
+        // tensor-core head: one (max, argmax) partial per 128-row vocab tile and row
+        nparts = (p.N + 127) / 128;
+        if ((rc = launch_gemm(Q_F16, g, m->gm, st))) return rc;
+    } else {
+        // one CTA count for every token tile (the argmax reads nparts partials per row); a
+        // single row uses the token-tile-1 layout's count, so that it runs in one wave
+        nparts = gemv_grid_for(p.N, 1, R == 1 ? gemv_ctas_per_sm(Q_F16, 1, p.row_bytes) * num_sms() : m->am_parts);
+        p.grid = nparts;
+        const int mt = gemv_max_tokens(Q_F16, p.row_bytes);
+        for (int t0 = 0; t0 < R; t0 += mt) {
+            GemvParams c = p;
+            c.M = R - t0 < mt ? R - t0 : mt;
+            c.x = p.x + (size_t)t0 * p.ldx;
+            c.logits = p.logits + (size_t)t0 * p.ldl;
+            c.am_val = m->am_val + (size_t)t0 * nparts;
+            c.am_idx = m->am_idx + (size_t)t0 * nparts;
+            if ((rc = launch_gemv(Q_F16, c, st))) return rc;
+        }
     }
     TokHist hist;
     if (io.advance) {   // decode: record the greedy id at each sequence's input position
@@ -734,7 +767,12 @@ static int enqueue_head(du_model *m, const StepIO &io)
         hist.cache_len = m->d_cache_len;
         hist.cap = m->cap;
     }
-    if (m->tp == 1) {
+    if (io.sample) {
+        // temperature / top-k / top-p / min-p over the full logits (single GPU)
+        if ((rc = launch_sample(m->logits, R, m->V, m->V_l, 1.0f, 0, 1.0f, 0.0f, m->d_seeds, io.next_out, io.feed, hist,
+                                m->d_err, st, m->d_sparams)))
+            return rc;
+    } else if (m->tp == 1) {
         if ((rc = launch_argmax_final(m->am_val, m->am_idx, R, nparts, io.next_out, io.feed, hist, st))) return rc;
     } else {
         // local best (val, idx) per row, exchange the pairs between ranks, pick the global best
@@ -904,20 +942,22 @@ static int check_step_error(du_model *m)
                           "the call was aborted");
 }
 
-static int get_graph(du_model *m, int batch, cudaGraphExec_t *out, Graph **gout = nullptr)
+static int get_graph(du_model *m, int batch, cudaGraphExec_t *out, Graph **gout = nullptr, bool sample = false)
 {
-    auto it = m->graphs.find(batch);
-    if (it != m->graphs.end()) {
+    std::map<int, Graph> &gm = sample ? m->sgraphs : m->graphs;
+    auto it = gm.find(batch);
+    if (it != gm.end()) {
         *out = it->second.exec;
         if (gout) *gout = &it->second;
         return DU_OK;
     }
-    const StepIO io = decode_io(m, batch);
+    StepIO io = decode_io(m, batch);
+    io.sample = sample;
     Graph g;
     StepPlan plan;
     int qt = 0, mt = 0;
     size_t smem = 0;
-    const bool persistent = build_step_plan(m, io, &plan, &qt, &mt, &smem, &g.d_stages) == DU_OK;
+    const bool persistent = !sample && build_step_plan(m, io, &plan, &qt, &mt, &smem, &g.d_stages) == DU_OK;
     DU_CUDA_TRY(cudaStreamBeginCapture(m->stream, cudaStreamCaptureModeThreadLocal));
     int rc;
     if (persistent) {
@@ -940,9 +980,9 @@ static int get_graph(du_model *m, int batch, cudaGraphExec_t *out, Graph **gout 
         cudaGraphDestroy(g.g);
         return cuda_fail(e, "cudaGraphInstantiate");
     }
-    m->graphs[batch] = g;
+    gm[batch] = g;
     *out = g.exec;
-    if (gout) *gout = &m->graphs[batch];
+    if (gout) *gout = &gm[batch];
     return DU_OK;
 }
 
@@ -1273,6 +1313,45 @@ DU_API int du_decode_step(du_model *m, const int32_t *ids, int batch, int32_t *n
     DU_CUDA_TRY(cudaStreamSynchronize(st));
     if ((rc = check_step_error(m))) {
         sync_cache_len(m);   // the aborted step may or may not have advanced the device copy
+        cudaStreamSynchronize(st);
+        return rc;
+    }
+    memcpy(next_ids, m->h_pin_next, sizeof(int) * batch);
+    for (int b = 0; b < batch; b++) m->h_cache_len[b] += 1;
+    m->last_batch = batch;
+    return DU_OK;
+}
+
+DU_API int du_decode_step_sample(du_model *m, const int32_t *ids, int batch, float temperature, int top_k,
+                                 float top_p, float min_p, const int32_t *seeds, int32_t *next_ids)
+{
+    DU_GUARD(m);
+    DU_CHECK_ARG(ids && seeds && next_ids && batch > 0 && batch <= m->maxb, "du_decode_step_sample: bad arguments");
+    if (m->tp > 1) return fail(DU_ESTATE, "du_decode_step_sample: stochastic sampling runs on a single GPU");
+    if (!sample_supported(temperature, top_k, top_p, m->V))
+        return fail(DU_EINVAL, "du_decode_step_sample: top_p < 1 needs top_k in 1..64 (the reference's parallel sampler)");
+    int rc = check_ids(m, ids, batch);
+    if (rc) return rc;
+    for (int b = 0; b < batch; b++)
+        if (m->h_cache_len[b] + 1 > m->cap) return fail(DU_EINVAL, "du_decode_step_sample: KV cache capacity exceeded");
+    cudaGraphExec_t exec;
+    if ((rc = get_graph(m, batch, &exec, nullptr, true))) return rc;
+    cudaStream_t st = m->stream;
+    memcpy(m->h_pin_ids, ids, sizeof(int) * batch);
+    memcpy(m->h_pin_seeds, seeds, sizeof(int32_t) * batch);
+    float *hp = reinterpret_cast<float *>(m->h_pin_seeds + m->maxb);
+    hp[0] = temperature;
+    hp[1] = (float)top_k;
+    hp[2] = top_p;
+    hp[3] = min_p;
+    DU_CUDA_TRY(cudaMemcpyAsync(m->d_ids, m->h_pin_ids, sizeof(int) * batch, cudaMemcpyHostToDevice, st));
+    DU_CUDA_TRY(cudaMemcpyAsync(m->d_seeds, m->h_pin_seeds, sizeof(int32_t) * (m->maxb + 4), cudaMemcpyHostToDevice, st));
+    DU_CUDA_TRY(cudaGraphLaunch(exec, st));
+    DU_CUDA_TRY(cudaMemcpyAsync(m->h_pin_next, m->d_next, sizeof(int) * batch, cudaMemcpyDeviceToHost, st));
+    DU_CUDA_TRY(cudaMemcpyAsync(m->h_pin_err, m->d_err, sizeof(int), cudaMemcpyDeviceToHost, st));
+    DU_CUDA_TRY(cudaStreamSynchronize(st));
+    if ((rc = check_step_error(m))) {
+        sync_cache_len(m);
         cudaStreamSynchronize(st);
         return rc;
     }

@@ -171,6 +171,20 @@ class LlamaForCausalLM(LLM):
         _lib.call("du_decode_step", self._h, ids.ctypes.data_as(C.c_void_p), ids.size, out.ctypes.data_as(C.c_void_p))
         return out
 
+    def decode_step_sample(self, ids, temperature: float, top_k: int = 0, top_p: float = 1.0, min_p: float = 0.0,
+                           seeds=None) -> np.ndarray:
+        """One sampled decode step (SampleYielding): temperature / top-k / top-p / min-p with a
+        signed 32-bit seed per sequence (random when not given)."""
+        ids = np.ascontiguousarray(np.asarray(ids, dtype=np.int32).reshape(-1))
+        if seeds is None:
+            seeds = np.random.default_rng().integers(-2 ** 31, 2 ** 31 - 1, ids.size)
+        sd = np.ascontiguousarray(np.asarray(seeds, dtype=np.int64).astype(np.int32).reshape(-1))
+        out = np.empty_like(ids)
+        _lib.call("du_decode_step_sample", self._h, ids.ctypes.data_as(C.c_void_p), ids.size, C.c_float(temperature),
+                  int(top_k), C.c_float(top_p), C.c_float(min_p), sd.ctypes.data_as(C.c_void_p),
+                  out.ctypes.data_as(C.c_void_p))
+        return out
+
     def decode_loop(self, ids, steps: int) -> np.ndarray:
         ids = np.ascontiguousarray(np.asarray(ids, dtype=np.int32).reshape(-1))
         out = np.empty((steps, ids.size), np.int32)
@@ -184,23 +198,37 @@ class LlamaForCausalLM(LLM):
         return out
 
     def Generate(self, input_ids, on_token: Optional[Callable[[int], None]] = None,
-                 max_new_tokens: int = 64, stop_tokens: Sequence[int] = ()) -> Iterator[int]:
-        """LLM.Generate (MiniCPM5.cs:133-172), greedy: prefill the prompt, then one
-        graph-replayed decode step per token.  Yields token ids (the reference yields
+                 max_new_tokens: int = 64, stop_tokens: Sequence[int] = (), temperature: float = 0.0,
+                 top_k: int = 0, top_p: float = 1.0, min_p: float = 0.0, seed: Optional[int] = None) -> Iterator[int]:
+        """LLM.Generate (MiniCPM5.cs:133-172): prefill the prompt, then one graph-replayed
+        decode step per token.  temperature <= 0 is greedy; otherwise every token is drawn by
+        the sampler (temperature / top_k / top_p / min_p, SampleYielding M5M:690-705) with
+        seeds from `seed`.  The prompt's last token runs as the first decode step so that the
+        first new token is sampled on the device too.  Yields token ids (the reference yields
         frames and reports text through a callback)."""
         if self._busy:
             raise RuntimeError("LLM is busy")   # LLM.cs:393-406
         self._busy = True
         try:
-            _, nxt = self.forward(np.asarray(input_ids, np.int32).reshape(1, -1), use_cache=True, want_logits=False)
-            tok = int(nxt[0])
+            ids = np.asarray(input_ids, np.int32).reshape(-1)
+            rng = np.random.default_rng(seed)
+            if temperature > 0.0:
+                if ids.size > 1:
+                    self.forward(ids[None, :-1], use_cache=True, want_logits=False)
+                step = lambda t: int(self.decode_step_sample([t], temperature, top_k, top_p, min_p,
+                                                             [int(rng.integers(-2 ** 31, 2 ** 31 - 1))])[0])
+                tok = step(int(ids[-1]))
+            else:
+                _, nxt = self.forward(ids[None, :], use_cache=True, want_logits=False)
+                tok = int(nxt[0])
+                step = lambda t: int(self.decode_step([t])[0])
             for _ in range(max_new_tokens):
                 if on_token:
                     on_token(tok)
                 yield tok
                 if tok in stop_tokens:
                     break
-                tok = int(self.decode_step([tok])[0])
+                tok = step(tok)
         finally:
             self._busy = False
 

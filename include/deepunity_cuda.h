@@ -163,6 +163,19 @@ DU_API int du_forward(du_model *m, const int32_t *ids, int batch, int seq_len, i
  * CUDA graph replay; the first call per batch size captures it. */
 DU_API int du_decode_step(du_model *m, const int32_t *ids, int batch, int32_t *next_ids);
 
+/* One sampled decode step: SampleYielding with temperature / top_k / top_p /
+ * min_p (M5M:653-705 -> SampleToken / SampleTokenSerial, G3CS:932-1132).
+ * seeds (host) [batch]: the sampler's signed 32-bit seed per sequence (the
+ * reference draws one per step from UnityEngine.Random); the draw is
+ * runif(seed) (G3CS:177-186).  temperature <= 0 is the greedy pick.  top_k in
+ * 1..64 uses the reference's parallel sampler (probabilities over the full
+ * vocabulary, candidates = the top_k logits); top_k <= 0 with top_p >= 1 the
+ * full-vocabulary sampler with an index-order draw; top_p < 1 without a top_k
+ * in 1..64 returns DU_EINVAL.  Single GPU (tp_size 1).  The step is a CUDA graph
+ * (one per batch size) whose settings and seeds live in device memory. */
+DU_API int du_decode_step_sample(du_model *m, const int32_t *ids, int batch, float temperature, int top_k,
+                                 float top_p, float min_p, const int32_t *seeds, int32_t *next_ids);
+
 /* Device-resident greedy loop: n_steps decode steps, each feeding its argmax
  * into the next, without host round trips; tokens_out (host) [n_steps, batch].
  * ids (host) [batch] seeds the first step. */
@@ -264,6 +277,13 @@ DU_API int du_quantize_int8(const float *w, int64_t rows, int64_t cols, int8_t *
                             uint16_t *scales_f16, void *stream);
 DU_API int du_quantize_int4(const float *w, int64_t rows, int64_t cols, int group,
                             uint8_t *packed, uint16_t *scales_f16, void *stream);
+
+/* Sampler over rows of logits already on the device (SampleToken /
+ * SampleTokenSerial, G3CS:932-1132; ArgMax when temperature <= 0): logits
+ * [rows][ldl] fp32, seeds [rows] int32, out [rows] int32 (device).  Same
+ * settings rules as du_decode_step_sample. */
+DU_API int du_sample(int32_t *out, const float *logits, int rows, int vocab, int ldl, float temperature, int top_k,
+                     float top_p, float min_p, const int32_t *seeds, void *stream);
 
 /* RmsNormHidden (G3CS:204-223): y = x * rsqrt(mean(x^2) + eps) * (1 + gamma_m1). */
 DU_API int du_rmsnorm(float *y, const float *x, const uint16_t *gamma_m1, int rows, int H, float eps,

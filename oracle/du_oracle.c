@@ -402,6 +402,135 @@ ORC_EXPORT int orc_argmax(const float *logits, int vocab)
     return idx[0];
 }
 
+/* --------------------------------------------------------------- sampler */
+
+/* runif (G3CS:177-186): the shader's hash on its signed int seed.  `>>` on the
+ * signed seed is an arithmetic shift; the divisor 4294967295.0 is an fp32
+ * literal (2^32 after rounding), so u = float(seed) * 2^-32 + 0.5 in [0, 1). */
+ORC_EXPORT float orc_runif(int32_t *seed)
+{
+    uint32_t s = (uint32_t)*seed;
+    s ^= 2747636419u;
+    s *= 2654435769u;
+    s ^= (uint32_t)((int32_t)s >> 16);
+    s *= 2654435769u;
+    s ^= (uint32_t)((int32_t)s >> 16);
+    s *= 2654435769u;
+    *seed = (int32_t)s;
+    return (float)(int32_t)s / 4294967296.0f + 0.5f;
+}
+
+#define SMP_THREADS 256
+#define SMP_MAXK 64
+
+/* SampleToken (G3CS:1029-1132), the parallel path for 1 <= top_k <= 64: probabilities
+ * normalised over the full vocabulary (256 strided partial sums + a tree, as the
+ * shader reduces), the top_k largest scaled logits as candidates in descending order
+ * (ties: the ArgMax tree order, orc_argmax), min-p and top-p cuts as a prefix walk,
+ * then r = runif() * cum against the candidates' running sum.
+ * SampleTokenSerial (G3CS:932-1019) for top_k outside 1..64, restricted here to
+ * top_p >= 1 and top_k <= 0: min-p filter, full renormalisation, r = runif() and an
+ * index-order walk of the cumulative distribution.  temperature <= 0: ArgMax.
+ * Returns the sampled id, or -1 for an unsupported combination. */
+ORC_EXPORT int orc_sample(const float *logits, int vocab, float temperature, int top_k, float top_p,
+                          float min_p, int32_t seed, float *probs_scratch)
+{
+    if (!(temperature > 0.0f)) return orc_argmax(logits, vocab);
+    const float inv_temp = 1.0f / temperature;
+    if (top_k >= 1 && top_k <= SMP_MAXK) {
+        float *sc = probs_scratch;
+        float red[SMP_THREADS];
+        for (int t = 0; t < SMP_THREADS; t++) {
+            float bv = -3.0e38f;
+            for (int i = t; i < vocab; i += SMP_THREADS) {
+                const float v = logits[i] * inv_temp;
+                sc[i] = v;
+                bv = fmaxf(bv, v);
+            }
+            red[t] = bv;
+        }
+        for (int s1 = SMP_THREADS / 2; s1 > 0; s1 >>= 1)
+            for (int t = 0; t < s1; t++) red[t] = fmaxf(red[t], red[t + s1]);
+        const float gmax = red[0];
+        for (int t = 0; t < SMP_THREADS; t++) {
+            float acc = 0.0f;
+            for (int i = t; i < vocab; i += SMP_THREADS) acc = acc + expf(sc[i] - gmax);
+            red[t] = acc;
+        }
+        for (int s2 = SMP_THREADS / 2; s2 > 0; s2 >>= 1)
+            for (int t = 0; t < s2; t++) red[t] = red[t] + red[t + s2];
+        const float sum_exp = red[0] > 1e-12f ? red[0] : 1e-12f;
+        float cand_p[SMP_MAXK];
+        int cand_i[SMP_MAXK];
+        for (int k = 0; k < top_k; k++) {
+            const int wi = orc_argmax(sc, vocab);
+            cand_i[k] = wi;
+            cand_p[k] = expf(sc[wi] - gmax) / sum_exp;
+            sc[wi] = -3.0e38f;
+        }
+        const float min_thresh = min_p > 0.0f ? cand_p[0] * min_p : 0.0f;
+        float cum = 0.0f;
+        int count = 0;
+        for (int c = 0; c < top_k; c++) {
+            const float pc = cand_p[c];
+            if (min_p > 0.0f && pc < min_thresh) break;
+            if (top_p < 1.0f && cum >= top_p) break;
+            cum = cum + pc;
+            count++;
+        }
+        if (count == 0) count = 1;
+        int32_t sd = seed;
+        const float r = orc_runif(&sd) * cum;
+        float cdf = 0.0f;
+        int sampled = cand_i[count - 1];
+        for (int c = 0; c < count; c++) {
+            cdf = cdf + cand_p[c];
+            if (cdf >= r) { sampled = cand_i[c]; break; }
+        }
+        return sampled;
+    }
+    if (top_k > 0 && top_k < vocab) return -1;
+    if (top_p < 1.0f) return -1;
+    float *pr = probs_scratch;
+    float max_l = logits[0];
+    for (int i = 1; i < vocab; i++) max_l = fmaxf(max_l, logits[i]);
+    float sum_exp = 0.0f;
+    for (int i = 0; i < vocab; i++) {
+        const float e = expf((logits[i] - max_l) * inv_temp);
+        pr[i] = e;
+        sum_exp = sum_exp + e;
+    }
+    const float inv_sum = 1.0f / (sum_exp > 1e-12f ? sum_exp : 1e-12f);
+    for (int i = 0; i < vocab; i++) pr[i] = pr[i] * inv_sum;
+    float max_prob = 0.0f;
+    for (int i = 0; i < vocab; i++) max_prob = fmaxf(max_prob, pr[i]);
+    int cand = 0;
+    if (min_p > 0.0f) {
+        const float th = max_prob * min_p;
+        for (int i = 0; i < vocab; i++) {
+            if (pr[i] >= th) cand++;
+            else pr[i] = 0.0f;
+        }
+    } else {
+        for (int i = 0; i < vocab; i++)
+            if (pr[i] > 0.0f) cand++;
+    }
+    if (cand == 0) return orc_argmax(logits, vocab);
+    float new_sum = 0.0f;
+    for (int i = 0; i < vocab; i++) new_sum = new_sum + pr[i];
+    if (new_sum <= 0.0f) return orc_argmax(logits, vocab);
+    const float inv_new = 1.0f / new_sum;
+    for (int i = 0; i < vocab; i++) pr[i] = pr[i] * inv_new;
+    int32_t sd = seed;
+    const float r = orc_runif(&sd);
+    float cdf = 0.0f;
+    for (int i = 0; i < vocab; i++) {
+        cdf = cdf + pr[i];
+        if (cdf >= r) return i;
+    }
+    return 0;
+}
+
 /* ----------------------------------------------------------- whole model */
 
 /* Host-side view of one model (weights as the reference's loader concatenates

@@ -59,6 +59,10 @@ def lib():
                                                  C.c_float, C.c_float, P, P, P, P, P, P, P, P, P,
                                                  C.c_int, P, C.c_int]
         _lib.orc_max_threads.restype = C.c_int
+        _lib.orc_runif.restype = C.c_float
+        _lib.orc_runif.argtypes = [C.POINTER(C.c_int32)]
+        _lib.orc_sample.restype = C.c_int
+        _lib.orc_sample.argtypes = [P, C.c_int, C.c_float, C.c_int, C.c_float, C.c_float, C.c_int32, P]
     return _lib
 
 
@@ -164,6 +168,20 @@ def dense_linear(x: np.ndarray, W: np.ndarray, bias=None, threads: int = 0) -> n
     lib().orc_dense_linear(_p(x), batch, batched, h_in, h_out, _p(W), _p(b) if b is not None else None,
                            _p(y), threads)
     return y
+
+
+def runif(seed: int):
+    """runif (G3CS:177-186): (u in [0, 1), next seed) from a signed 32-bit seed."""
+    sd = C.c_int32(seed)
+    u = float(lib().orc_runif(C.byref(sd)))
+    return u, int(sd.value)
+
+
+def sample(logits: np.ndarray, temperature: float, top_k: int, top_p: float, min_p: float, seed: int) -> int:
+    """SampleToken / SampleTokenSerial restated (G3CS:932-1132); -1 if the combination is not covered."""
+    lg = np.ascontiguousarray(logits, dtype=np.float32)
+    scratch = np.empty(lg.size, np.float32)
+    return int(lib().orc_sample(_p(lg), lg.size, temperature, top_k, top_p, min_p, seed, _p(scratch)))
 
 
 def max_threads() -> int:

@@ -315,3 +315,80 @@ def test_rmsnorm_matches_oracle():
     _lib.call("du_rmsnorm", ptr(y), ptr(xd), ptr(gd), 5, 4096, C.c_float(1e-5), None)
     torch.cuda.synchronize()
     assert relerr(y.cpu().numpy(), ref) < 1e-6
+
+
+# --------------------------------------------------------------- sampler
+SAMPLER_SETTINGS = [(0.0, 0, 1.0, 0.0),      # greedy (ArgMax)
+                    (1.0, 40, 0.9, 0.0),     # top-k + top-p
+                    (0.7, 64, 0.95, 0.05),   # top-k + top-p + min-p
+                    (1.3, 1, 1.0, 0.0),      # top-1
+                    (1.0, 20, 1.0, 0.2),     # top-k + min-p
+                    (1.0, 0, 1.0, 0.0),      # full vocabulary, index-order draw
+                    (0.8, 0, 1.0, 0.1)]      # full vocabulary + min-p
+
+
+@pytest.mark.parametrize("V", [1000, 32000, 128256])
+def test_sampler_matches_oracle(V):
+    """SampleToken / SampleTokenSerial (G3CS:932-1132) with runif (G3CS:177-186):
+    identical ids for the same logits and seeds, every supported setting."""
+    rng = np.random.default_rng(V)
+    rows = 8
+    logits = (rng.standard_normal((rows, V)) * 3).astype(np.float32)
+    logits[1, 100:140] = logits[1].max() + 1.0           # a tie group at the top (tree order decides)
+    lg = dev(logits)
+    out = torch.empty(rows, dtype=torch.int32, device="cuda")
+    for (T, k, p, mp) in SAMPLER_SETTINGS:
+        for rep in range(3):
+            seeds = rng.integers(-2 ** 31, 2 ** 31 - 1, rows, dtype=np.int64).astype(np.int32)
+            sd = dev(seeds)
+            _lib.call("du_sample", ptr(out), ptr(lg), rows, V, V, C.c_float(T), k, C.c_float(p), C.c_float(mp),
+                      ptr(sd), None)
+            torch.cuda.synchronize()
+            ref = [orc.sample(logits[r], T, k, p, mp, int(seeds[r])) for r in range(rows)]
+            assert out.cpu().numpy().tolist() == ref, (T, k, p, mp, rep)
+
+
+def test_sampler_rejects_unbounded_nucleus():
+    lg = torch.zeros((1, 64), device="cuda")
+    sd = torch.zeros(1, dtype=torch.int32, device="cuda")
+    out = torch.empty(1, dtype=torch.int32, device="cuda")
+    rc = _lib.lib().du_sample(ptr(out), ptr(lg), 1, 64, 64, C.c_float(1.0), 0, C.c_float(0.9), C.c_float(0.0), ptr(sd),
+                              None)
+    assert rc == _lib.DU_EINVAL
+
+
+_TC_GEMV_CHILD = r"""
+import ctypes as C, os, sys, numpy as np, torch
+sys.path.insert(0, sys.argv[1])
+from deepunity_b200 import _lib
+from oracle import oracle as orc
+_lib.call("du_init", 0)
+worst = 0.0
+for (N, K, G, M) in [(1000, 4096, 128, 1), (4096, 14336, 128, 2), (300, 2048, 32, 1), (2048, 4096, 64, 2)]:
+    rng = np.random.default_rng(N + K + G + M)
+    w = rng.standard_normal((N, K), dtype=np.float32) * 0.02
+    x = rng.standard_normal((M, K)).astype(np.float32)
+    wq, sc = orc.quantize_int4(w, G)
+    y = torch.empty((M, N), device="cuda")
+    xd, wd, sd = torch.from_numpy(x).cuda(), torch.from_numpy(wq).cuda(), torch.from_numpy(sc).cuda()
+    P = lambda t: C.c_void_p(t.data_ptr())
+    _lib.call("du_gemv_q4", P(y), P(xd), 0, P(wd), P(sd), G, M, N, K, None)
+    torch.cuda.synchronize()
+    ref = orc.gemv(x, wq, sc, "int4", N, G)
+    worst = max(worst, float(np.abs(y.cpu().numpy() - ref).max() / np.abs(ref).max()))
+print(worst)
+"""
+
+
+def test_tcgen05_decode_gemv_opt_in():
+    """The opt-in tensor-core decode GEMV (tcgen05.mma kind::i8 on nibble x byte-plane operands,
+    DU_DECODE_GEMV=tcgen05, read once per process) against the oracle, M = 1 and 2, groups 32-128."""
+    import os
+    import subprocess
+    import sys
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    env = dict(os.environ, DU_DECODE_GEMV="tcgen05")
+    r = subprocess.run([sys.executable, "-c", _TC_GEMV_CHILD, root], env=env, capture_output=True, text=True,
+                       timeout=600)
+    assert r.returncode == 0, r.stderr[-2000:]
+    assert float(r.stdout.strip().splitlines()[-1]) < GEMV_TOL

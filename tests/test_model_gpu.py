@@ -69,10 +69,12 @@ def test_prefill_then_greedy_64_matches_oracle(cfg, path):
 
 
 def test_predict_all_positions_and_device_loop():
+    """Stateless Predict over 20 positions (the lm_head of all positions runs as the
+    tensor-core GEMM with its logits + argmax epilogue), then the device-resident loop."""
     cfg = MID
     w, m = build(cfg, cap=96)
     om = orc.OracleModel(w, capacity=96)
-    prompt = np.random.default_rng(8).integers(0, cfg.vocab, 12).astype(np.int32)
+    prompt = np.random.default_rng(8).integers(0, cfg.vocab, 20).astype(np.int32)
     lg = m.Predict(prompt)
     ref = om.forward(prompt, last_pos_only=False)
     assert lg.shape == ref.shape
@@ -228,4 +230,27 @@ def test_greedy_ties_follow_the_reference_argmax_tree(path):
     m.ResetCache()
     m.forward(prompt[None, :-1])
     assert int(m.decode_step([prompt[-1]])[0]) == expect   # decode graph's head + pick
+    m.Release()
+
+
+@pytest.mark.parametrize("setting", [(0.8, 40, 0.9, 0.0), (1.0, 0, 1.0, 0.05), (0.0, 0, 1.0, 0.0)])
+def test_sampled_decode_matches_oracle(setting):
+    """du_decode_step_sample (SampleYielding, M5M:653-705): 16 sampled steps with a seed per
+    step; each step's id must be what the oracle sampler draws from the oracle's logits."""
+    T, k, p, mp = setting
+    cfg = MID
+    w, m = build(cfg, cap=96)
+    om = orc.OracleModel(w, capacity=96)
+    prompt = np.random.default_rng(12).integers(0, cfg.vocab, 10).astype(np.int32)
+    logits, _ = m.forward(prompt[None, :])
+    ref = om.forward(prompt)
+    rng = np.random.default_rng(99)
+    seed = int(rng.integers(-2 ** 31, 2 ** 31 - 1))
+    tok = orc.sample(ref, T, k, p, mp, seed)
+    toks, rtoks = [tok], [tok]
+    for _ in range(16):
+        seed = int(rng.integers(-2 ** 31, 2 ** 31 - 1))
+        toks.append(int(m.decode_step_sample([toks[-1]], T, k, p, mp, [seed])[0]))
+        rtoks.append(orc.sample(om.forward([rtoks[-1]]), T, k, p, mp, seed))
+    assert toks == rtoks
     m.Release()
