@@ -471,20 +471,26 @@ struct GemmPlan {
     size_t smem;
 };
 
-static int gm_tn_for(int M)
+// Token tile (MMA N).  One thread issues a tcgen05.mma about every 110 cycles; an
+// M = 128, N = 256, K = 16 MMA carries about as much tensor work (128 cycles), an
+// N = 128 one half of it.  So large M takes N = 256 when the tiles still fill the GPU.
+static int gm_tn_for(int M, int N)
 {
+    const int row_tiles = (N + GM_ROWS - 1) / GM_ROWS;
+    if (M > 128 && (int64_t)row_tiles * ((M + 255) / 256) >= num_sms()) return 256;
     if (M > 64) return 128;
     if (M > 32) return 64;
     return 32;
 }
 
-static GemmPlan gm_plan(int qt, int M)
+static GemmPlan gm_plan(int qt, int M, int N)
 {
     GemmPlan g = {};
-    g.tn = gm_tn_for(M);
+    g.tn = gm_tn_for(M, N);
     g.kb_bytes = qt == Q_I4 ? 32 : qt == Q_I8 ? 64 : 128;
     g.raw_bytes = GM_ROWS * g.kb_bytes;
     g.raw_stages = qt == Q_I4 ? 8 : qt == Q_I8 ? 6 : 4;
+    if (g.tn == 256) g.raw_stages = qt == Q_I4 ? 4 : qt == Q_I8 ? 3 : 2;   // two operand stages must fit
     static const int env_rs = [] { const char *e = getenv("DU_GEMM_RAW_STAGES"); return e ? atoi(e) : 0; }();
     if (env_rs > 0 && env_rs < g.raw_stages) g.raw_stages = env_rs;  // tuning knob: fewer raw-weight stages
     const int na = qt == Q_I4 ? 2 : 1;
@@ -563,7 +569,7 @@ int launch_gemm(int qt, const GemvParams &p, const GemmScratch &scr, cudaStream_
                                        scr.xscale));
     }
     // 2. tensor maps
-    const GemmPlan g = gm_plan(qt, p.M);
+    const GemmPlan g = gm_plan(qt, p.M, p.N);
     const int64_t w_rows = p.row_off + (p.map == MAP_GATEUP ? 2 * (int64_t)p.map_I : (int64_t)p.N);
     CUtensorMap tw, th, tl;
     int rc = make_tmap(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, p.w, (uint64_t)p.row_bytes, (uint64_t)w_rows,

@@ -16,10 +16,14 @@ __global__ void __launch_bounds__(NW * 32) qgemv_kernel(const GemvParams p)
     extern __shared__ __align__(16) unsigned char gv_smem[];
     __shared__ GemvShared<MT, NW> sh;
     GemvStream<QT, MT, RW, D, NW, TPR> gs;
+    GV_STAMP(0);
     gs.prefetch(p, gv_smem, blockIdx.x, gridDim.x);
+    GV_STAMP(1);
     // activations of the previous kernel are complete from here on
     pdl_wait();
+    GV_STAMP(2);
     gs.run(p, gv_smem + gemv_ring_bytes<QT, RW, D, NW>(), sh, blockIdx.x, gridDim.x, [] { pdl_trigger(); });
+    GV_STAMP(5);
 }
 
 // ------------------------------------------------------------------ launch

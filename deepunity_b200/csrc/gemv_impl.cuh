@@ -13,6 +13,13 @@
 #include "gemv.cuh"
 #include "tp_fuse.cuh"
 
+// Timing hook: GV_STAMP(event) marks the phases of a GEMV launch (entry,
+// ring issued, dependency met, activations staged, stream done, exit) for a
+// timing build; it compiles to nothing in the library.
+#ifndef GV_STAMP
+#define GV_STAMP(event)
+#endif
+
 namespace du {
 
 // FP16 path: physical float4 slot of logical float4 f of a token row
@@ -434,6 +441,7 @@ struct GemvStream {
     {
         uint4 *xq = reinterpret_cast<uint4 *>(x_smem);
         gv_stage_x<QT, MT, NW>(p, xq, sh, nchunk);
+        GV_STAMP(3);
         after_stage();
         if constexpr (TPR) tp_s = tp_next_seq(*p.tp);
 
@@ -580,6 +588,7 @@ struct GemvStream {
             }
         }
         cp_async_wait_group<0>();
+        GV_STAMP(4);
 
         // groups split between warps: the holder of a group's last unit (which started the
         // group past segment 0) adds the parts of every contributing warp in warp order

@@ -1,9 +1,9 @@
 """Generate the golden vectors that pin the oracle to the reference.
 
-Run in a container where the DeepUnity reference is mounted (default path
-below, or DU_REFERENCE=<project root>):
+Run in a container where the DeepUnity reference is checked out, naming its
+project root in DU_REFERENCE (required; there is no default path):
 
-    python tests/golden/make_golden.py
+    DU_REFERENCE=<project root> python tests/golden/make_golden.py
 
 It writes, next to this script:
   quant_golden.npz   seeded fp32 matrices and what the reference's own
@@ -29,9 +29,15 @@ import sys
 import numpy as np
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-REF = os.environ.get("DU_REFERENCE", "/root/reference")
+REF = os.environ.get("DU_REFERENCE", "")
 IMP_PATH = os.path.join(REF, "Assets/DeepUnity/InferenceEngine/import_params.py")
 EXPORT = os.path.join(REF, "Assets/Resources/Weights/weights_qwen3.5_0.8B_roleplay_1308_int8/layer_3")
+
+
+def require_reference():
+    if not REF or not os.path.isfile(IMP_PATH):
+        sys.exit("make_golden.py: set DU_REFERENCE to the DeepUnity project root "
+                 "(the directory holding Assets/DeepUnity/InferenceEngine/import_params.py)")
 
 
 def load_imp():
@@ -56,6 +62,7 @@ def edge_rows(cols):
 
 
 def main():
+    require_reference()
     imp = load_imp()
     rng = np.random.default_rng(0)
     out = {}
