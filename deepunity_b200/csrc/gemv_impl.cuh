@@ -48,7 +48,8 @@ struct __align__(16) GemvShared {
 
 // Stages the activations of the MT tokens in shared memory.
 //  INT4: one pass; per 32-column chunk 6 plane words x 4 word groups, then
-//        (8 * sum x_int, 2^-s) in the pad words 24, 25; xscale = 1 / rms (or 1)
+//        (128 * sum x_int, 2^-(s + 4)) in the pad words 24, 25 (the factor 16 of
+//        the odd-nibble sums, gv_unit_math); xscale = 1 / rms (or 1)
 //  INT8: per-token power-of-two scale over the normalised x; xscale = 2^-s
 //  FP16: x * (1 + gamma') in fp32, swizzled; xscale = 1 / rms (or 1)
 template <int QT, int MT, int NW>
@@ -176,9 +177,9 @@ __device__ __forceinline__ void gv_stage_x(const GemvParams &p, uint4 *xq, GemvS
                 for (int j = 0; j < 8; j++) mx = fmaxf(mx, fabsf(v[j]));
                 mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
                 mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
-                // chunk scale 2^s with max |v| * 2^s < 2^22 (s capped so 2^s and 2^-s stay normal)
+                // chunk scale 2^s with max |v| * 2^s < 2^22 (s capped so 2^s and 2^-(s + 4) stay normal)
                 int s = mx > 0.0f ? 21 - ilogbf(mx) : 0;
-                if (s > 126) s = 126;
+                if (s > 122) s = 122;
                 const float sc = __int_as_float((127 + s) << 23);
                 int n[8], part = 0;
 #pragma unroll
@@ -204,8 +205,8 @@ __device__ __forceinline__ void gv_stage_x(const GemvParams &p, uint4 *xq, GemvS
                     o[5] = o2;
                     if (wd == 0) {
                         uint32_t *pad = xw + (size_t)c * GvTraits<QT>::XU4 * 4 + 24;
-                        pad[0] = __float_as_uint(8.0f * (float)part);
-                        pad[1] = __float_as_uint(__int_as_float((127 - s) << 23));
+                        pad[0] = __float_as_uint(128.0f * (float)part);
+                        pad[1] = __float_as_uint(__int_as_float((127 - s - 4) << 23));
                     }
                 }
             }
@@ -333,6 +334,124 @@ __device__ __forceinline__ void gv_epilogue(const GemvParams &p, int lr0, const 
     }
 }
 
+
+// One unit: this lane's 16-byte chunk c (of nchunk per row) of the RW rows held
+// in ring slot `stage`, accumulated into acc (INT4 / FP16, fp32) or s8 (INT8,
+// exact int32 sums per activation plane).
+template <int QT, int MT, int RW>
+__device__ __forceinline__ void gv_unit_math(const uint4 *ring, const uint32_t *sring, int stage, int c, int nchunk,
+                                             int gshift, const uint4 *xq, float (&acc)[RW][MT], int (&s8)[RW][MT][3])
+{
+    using T = GvTraits<QT>;
+    uint4 wv[RW];
+#pragma unroll
+    for (int j = 0; j < RW; j++) wv[j] = ring[(stage * RW + j) * 32];
+    if (c < nchunk) {
+        if (QT == Q_I4) {
+            float d[RW];
+            const int hsel = (((c * 32) >> gshift) & 1) * 16;
+#pragma unroll
+            for (int j = 0; j < RW; j++)
+                d[j] = __half2float(__ushort_as_half((unsigned short)(sring[(stage * RW + j) * 32] >> hsel)));
+#pragma unroll
+            for (int m = 0; m < MT; m++) {
+                const uint4 *xp = xq + ((size_t)m * nchunk + c) * T::XU4;
+                uint32_t xw[24];
+#pragma unroll
+                for (int q = 0; q < 6; q++) {
+                    const uint4 t = xp[q];
+                    xw[4 * q] = t.x; xw[4 * q + 1] = t.y; xw[4 * q + 2] = t.z; xw[4 * q + 3] = t.w;
+                }
+                const uint2 pad = *reinterpret_cast<const uint2 *>(xp + 6);
+                const float xs8 = __uint_as_float(pad.x), xcs = __uint_as_float(pad.y);
+#pragma unroll
+                for (int j = 0; j < RW; j++) {
+                    // even / odd nibble streams accumulate separately (shorter dependency chains);
+                    // the odd nibbles stay in the high half of their bytes (16 n, one AND
+                    // instead of a shift and an AND), so the b sums are 16 x their values
+                    int a0 = 0, a1 = 0, a2 = 0, b0 = 0, b1 = 0, b2 = 0;
+#pragma unroll
+                    for (int wd = 0; wd < 4; wd++) {
+                        const uint32_t w = wd == 0 ? wv[j].x : wd == 1 ? wv[j].y : wd == 2 ? wv[j].z : wv[j].w;
+                        const uint32_t lo = w & 0x0F0F0F0Fu, hi = w & 0xF0F0F0F0u;
+                        a0 = dp4a_uu(lo, xw[wd * 6 + 0], a0);
+                        b0 = dp4a_uu(hi, xw[wd * 6 + 1], b0);
+                        a1 = dp4a_uu(lo, xw[wd * 6 + 2], a1);
+                        b1 = dp4a_uu(hi, xw[wd * 6 + 3], b1);
+                        a2 = dp4a_us(lo, xw[wd * 6 + 4], a2);
+                        b2 = dp4a_us(hi, xw[wd * 6 + 5], b2);
+                    }
+                    // 16 x (sum n * x_int - 8 * sum x_int): planes 0 and 1 join exactly in
+                    // int32 (< 2^29), plane 2 (< 2^20 in magnitude) is exact in fp32; the
+                    // staged xs8 = 128 * sum x_int and xcs = 2^-s / 16 carry the factor 16
+                    const int p01 = (a0 * 16 + b0) + ((a1 * 16 + b1) << 8);
+                    const float f = fmaf((float)(a2 * 16 + b2), 65536.0f, (float)p01) - xs8;
+                    acc[j][m] = fmaf(d[j], f * xcs, acc[j][m]);
+                }
+            }
+        } else if (QT == Q_I8) {
+#pragma unroll
+            for (int m = 0; m < MT; m++) {
+                const uint4 *xp = xq + ((size_t)m * nchunk + c) * T::XU4;
+                const uint4 t0 = xp[0], t1 = xp[1], t2 = xp[2];
+                const uint32_t xw[12] = {t0.x, t0.y, t0.z, t0.w, t1.x, t1.y, t1.z, t1.w, t2.x, t2.y, t2.z, t2.w};
+#pragma unroll
+                for (int j = 0; j < RW; j++)
+#pragma unroll
+                    for (int wd = 0; wd < 4; wd++) {
+                        const uint32_t w = wd == 0 ? wv[j].x : wd == 1 ? wv[j].y : wd == 2 ? wv[j].z : wv[j].w;
+                        s8[j][m][0] = dp4a_su(w, xw[wd * 3 + 0], s8[j][m][0]);
+                        s8[j][m][1] = dp4a_su(w, xw[wd * 3 + 1], s8[j][m][1]);
+                        s8[j][m][2] = dp4a_ss(w, xw[wd * 3 + 2], s8[j][m][2]);
+                    }
+            }
+        } else {
+#pragma unroll
+            for (int m = 0; m < MT; m++) {
+                const float4 *xm = reinterpret_cast<const float4 *>(xq) + (size_t)m * nchunk * 2;
+                const float4 a = xm[gv_swz16(c * 2)];
+                const float4 b = xm[gv_swz16(c * 2 + 1)];
+#pragma unroll
+                for (int j = 0; j < RW; j++) {
+                    float2 part = make_float2(0.f, 0.f);
+                    gv_dot_f16(wv[j].x, a.x, a.y, part);
+                    gv_dot_f16(wv[j].y, a.z, a.w, part);
+                    gv_dot_f16(wv[j].z, b.x, b.y, part);
+                    gv_dot_f16(wv[j].w, b.z, b.w, part);
+                    acc[j][m] += part.x + part.y;
+                }
+            }
+        }
+    }
+}
+
+// Folds the lanes' accumulators of a finished run of units into v (every lane
+// holds every value) and resets them.
+template <int QT, int MT, int RW>
+__device__ __forceinline__ void gv_fold(float (&acc)[RW][MT], int (&s8)[RW][MT][3], const float *xscale,
+                                        float (&v)[RW][MT])
+{
+#pragma unroll
+    for (int j = 0; j < RW; j++)
+#pragma unroll
+        for (int m = 0; m < MT; m++) {
+            if (QT == Q_I8) {
+                long long t0 = s8[j][m][0], t1 = s8[j][m][1], t2 = s8[j][m][2];
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) {
+                    t0 += __shfl_xor_sync(0xffffffffu, t0, o);
+                    t1 += __shfl_xor_sync(0xffffffffu, t1, o);
+                    t2 += __shfl_xor_sync(0xffffffffu, t2, o);
+                }
+                const long long tot = t0 + (t1 << 8) + (t2 << 16);   // exact sum q * x_int
+                v[j][m] = (float)tot * xscale[m];
+                s8[j][m][0] = s8[j][m][1] = s8[j][m][2] = 0;
+            } else {
+                v[j][m] = warp_sum(acc[j][m]) * xscale[m];
+                acc[j][m] = 0.0f;
+            }
+        }
+}
 
 // Work split: a CTA owns a contiguous range of row groups; their (group,
 // 512-byte segment) units, group-major, are cut into NW contiguous, equal
@@ -470,108 +589,12 @@ struct GemvStream {
             cp_async_wait_group<D - 1>();
             const int stage = cs_stage;
             if (++cs_stage == D) cs_stage = 0;
-            uint4 wv[RW];
-#pragma unroll
-            for (int j = 0; j < RW; j++) wv[j] = ring[(stage * RW + j) * 32];
-            const int c = cs_s * 32 + lane;
-            if (c < nchunk) {
-                if (QT == Q_I4) {
-                    float d[RW];
-                    const int hsel = (((c * 32) >> gshift) & 1) * 16;
-#pragma unroll
-                    for (int j = 0; j < RW; j++)
-                        d[j] = __half2float(__ushort_as_half((unsigned short)(sring[(stage * RW + j) * 32] >> hsel)));
-#pragma unroll
-                    for (int m = 0; m < MT; m++) {
-                        const uint4 *xp = xq + ((size_t)m * nchunk + c) * T::XU4;
-                        uint32_t xw[24];
-#pragma unroll
-                        for (int q = 0; q < 6; q++) {
-                            const uint4 t = xp[q];
-                            xw[4 * q] = t.x; xw[4 * q + 1] = t.y; xw[4 * q + 2] = t.z; xw[4 * q + 3] = t.w;
-                        }
-                        const uint2 pad = *reinterpret_cast<const uint2 *>(xp + 6);
-                        const float xs8 = __uint_as_float(pad.x), xcs = __uint_as_float(pad.y);
-#pragma unroll
-                        for (int j = 0; j < RW; j++) {
-                            // even / odd nibble streams accumulate separately (shorter dependency chains)
-                            int a0 = 0, a1 = 0, a2 = 0, b0 = 0, b1 = 0, b2 = 0;
-#pragma unroll
-                            for (int wd = 0; wd < 4; wd++) {
-                                const uint32_t w = wd == 0 ? wv[j].x : wd == 1 ? wv[j].y : wd == 2 ? wv[j].z : wv[j].w;
-                                const uint32_t lo = w & 0x0F0F0F0Fu, hi = (w >> 4) & 0x0F0F0F0Fu;
-                                a0 = dp4a_uu(lo, xw[wd * 6 + 0], a0);
-                                b0 = dp4a_uu(hi, xw[wd * 6 + 1], b0);
-                                a1 = dp4a_uu(lo, xw[wd * 6 + 2], a1);
-                                b1 = dp4a_uu(hi, xw[wd * 6 + 3], b1);
-                                a2 = dp4a_us(lo, xw[wd * 6 + 4], a2);
-                                b2 = dp4a_us(hi, xw[wd * 6 + 5], b2);
-                            }
-                            // sum n * x_int - 8 * sum x_int: planes 0 and 1 join exactly in int32
-                            // (< 2^25), plane 2 (< 2^19 in magnitude) is exact in fp32
-                            const int p01 = (a0 + b0) + ((a1 + b1) << 8);
-                            const float f = fmaf((float)(a2 + b2), 65536.0f, (float)p01) - xs8;
-                            acc[j][m] = fmaf(d[j], f * xcs, acc[j][m]);
-                        }
-                    }
-                } else if (QT == Q_I8) {
-#pragma unroll
-                    for (int m = 0; m < MT; m++) {
-                        const uint4 *xp = xq + ((size_t)m * nchunk + c) * T::XU4;
-                        const uint4 t0 = xp[0], t1 = xp[1], t2 = xp[2];
-                        const uint32_t xw[12] = {t0.x, t0.y, t0.z, t0.w, t1.x, t1.y, t1.z, t1.w, t2.x, t2.y, t2.z, t2.w};
-#pragma unroll
-                        for (int j = 0; j < RW; j++)
-#pragma unroll
-                            for (int wd = 0; wd < 4; wd++) {
-                                const uint32_t w = wd == 0 ? wv[j].x : wd == 1 ? wv[j].y : wd == 2 ? wv[j].z : wv[j].w;
-                                s8[j][m][0] = dp4a_su(w, xw[wd * 3 + 0], s8[j][m][0]);
-                                s8[j][m][1] = dp4a_su(w, xw[wd * 3 + 1], s8[j][m][1]);
-                                s8[j][m][2] = dp4a_ss(w, xw[wd * 3 + 2], s8[j][m][2]);
-                            }
-                    }
-                } else {
-#pragma unroll
-                    for (int m = 0; m < MT; m++) {
-                        const float4 *xm = reinterpret_cast<const float4 *>(xq) + (size_t)m * nchunk * 2;
-                        const float4 a = xm[gv_swz16(c * 2)];
-                        const float4 b = xm[gv_swz16(c * 2 + 1)];
-#pragma unroll
-                        for (int j = 0; j < RW; j++) {
-                            float2 part = make_float2(0.f, 0.f);
-                            gv_dot_f16(wv[j].x, a.x, a.y, part);
-                            gv_dot_f16(wv[j].y, a.z, a.w, part);
-                            gv_dot_f16(wv[j].z, b.x, b.y, part);
-                            gv_dot_f16(wv[j].w, b.z, b.w, part);
-                            acc[j][m] += part.x + part.y;
-                        }
-                    }
-                }
-            }
+            gv_unit_math<QT, MT, RW>(ring, sring, stage, cs_s * 32 + lane, nchunk, gshift, xq, acc, s8);
             const bool end_g = ++cs_s == S;
             if (end_g || i == n - 1) {
                 // ---- this warp's part of row group cs_g is done: fold the lanes, reset
                 float v[RW][MT];
-#pragma unroll
-                for (int j = 0; j < RW; j++)
-#pragma unroll
-                    for (int m = 0; m < MT; m++) {
-                        if (QT == Q_I8) {
-                            long long t0 = s8[j][m][0], t1 = s8[j][m][1], t2 = s8[j][m][2];
-#pragma unroll
-                            for (int o = 16; o > 0; o >>= 1) {
-                                t0 += __shfl_xor_sync(0xffffffffu, t0, o);
-                                t1 += __shfl_xor_sync(0xffffffffu, t1, o);
-                                t2 += __shfl_xor_sync(0xffffffffu, t2, o);
-                            }
-                            const long long tot = t0 + (t1 << 8) + (t2 << 16);   // exact sum q * x_int
-                            v[j][m] = (float)tot * sh.xscale[m];
-                            s8[j][m][0] = s8[j][m][1] = s8[j][m][2] = 0;
-                        } else {
-                            v[j][m] = warp_sum(acc[j][m]) * sh.xscale[m];
-                            acc[j][m] = 0.0f;
-                        }
-                    }
+                gv_fold<QT, MT, RW>(acc, s8, sh.xscale, v);
                 if (end_g && (cs_g != first_g || first_whole)) {
                     epilogue(p, cs_g * RW, v, am_v, am_i);            // the whole group was this warp's
                 } else if (lane == 0) {
