@@ -57,6 +57,8 @@ def parse():
     ap.add_argument("--reps", type=int, default=0, help="--sweep: timed launches per case (0 = auto)")
     ap.add_argument("--model", choices=["llama-8b", "llama-1.1b"], default="llama-8b",
                     help="llama-8b: BASELINE config 5 (INT4 g128); llama-1.1b: config 4 (INT8 per row)")
+    ap.add_argument("--kv", choices=["fp16", "int8"], default="fp16",
+                    help="KV cache format (KVQuant.FP16 / KVQuant.INT8)")
     ap.add_argument("--layers", type=int, default=0,
                     help="profiling only: keep the first N decoder layers (smaller device footprint)")
     return ap.parse_args()
@@ -251,7 +253,7 @@ def run_ours(args):
     from datetime import timedelta
 
     from deepunity_b200 import _lib
-    from deepunity_b200.llm import CONFIGS, LlamaForCausalLM, LLMQuant
+    from deepunity_b200.llm import CONFIGS, KVQuant, LlamaForCausalLM, LLMQuant
     import ctypes as C
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -270,7 +272,8 @@ def run_ours(args):
     B = args.batch
     need = args.prompt + args.warmup + 2 * args.steps + 4
     cap = max(CAPACITY if args.model == "llama-8b" else 0, need)
-    m = LlamaForCausalLM(cfg, quant, max_context_length=cap, max_batch=B, seed=0,
+    m = LlamaForCausalLM(cfg, quant, kv_quant=KVQuant.INT8 if args.kv == "int8" else KVQuant.FP16,
+                         max_context_length=cap, max_batch=B, seed=0,
                          device=local, tp_rank=rank, tp_size=world,
                          flags=_lib.FLAG_PERSISTENT if args.path == "persistent" else 0)
     if world > 1:
@@ -371,7 +374,8 @@ def run_ours(args):
     gu_bytes = wbytes(2 * I_l, H) + B * H * 4 + B * I_l * 4
     # K and V rows read per step at the mean cache length of the timed steps
     kv_mean = args.prompt + args.warmup + args.steps // 2 + 1
-    kv_layer = 2 * B * kv_mean * hkv_l * hd * 2
+    # (INT8 cache: one byte an element plus a 4-byte scale / zero-point word per position and kv head)
+    kv_layer = 2 * B * kv_mean * hkv_l * (hd * 2 if args.kv == "fp16" else hd + 4)
     kv_read = cfg.num_layers * kv_layer
     step_bytes = m.weight_bytes() + kv_read
     step_ms = ms / args.steps
@@ -423,7 +427,7 @@ def run_ours(args):
             "value": round(value, 2), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 4), "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None,
-            "dtype": ("int4" if quant == LLMQuant.INT4 else "int8") + " weights x fp32 activations (fp16 KV)",
+            "dtype": ("int4" if quant == LLMQuant.INT4 else "int8") + f" weights x fp32 activations ({args.kv} KV)",
             "data": "synthetic (seeded random-init weights, random prompt ids)",
             "config": {"workload": f"{args.model} {'INT4-g128' if quant == LLMQuant.INT4 else 'INT8-row'} decode, "
                                    f"batch {B}, prompt {args.prompt}, "
@@ -563,7 +567,7 @@ def run_sweep_gemv(args):
                 print(json.dumps({"sweep": "gemv", "quant": quant + {"int4": "-g128", "int8": "-row"}.get(quant, ""),
                                   "N": N, "K": K, "M": M, "path": path, "us": round(ms * 1e3, 2),
                                   "GB_s": round(gbs, 1), "frac_hbm": round(gbs / peak, 4),
-                                  "TFLOP_s": round(tflops, 2), "frac_tensor_bf16": round(tflops * 1e3 / tpeak, 4),
+                                  "TFLOP_s": round(tflops, 2), "frac_tensor_bf16": round(tflops / tpeak, 4),
                                   "peak_kind": kind, "copies": copies,
                                   "timing": "CUDA graph of the launches, weights rotated over >= 1.1 GB"}), flush=True)
             del W, Sc
@@ -579,28 +583,46 @@ def run_sweep_attn(args):
     peak, kind = peaks()
     g = torch.Generator(device="cuda").manual_seed(0)
     hq, hkv, hd = 32, 8, 128
-    for ctx in (512, 2048, 8192, 32768):
-        for B in (1, 8, 32):
-            kv_bytes = B * ctx * hkv * hd * 2 * 2
-            copies = max(2, int(np.ceil(0.6e9 / kv_bytes)))
-            if copies * kv_bytes > 40e9:
-                copies = 1
-            kc = [torch.randn((B, ctx, hkv, hd), device="cuda", generator=g).half() for _ in range(copies)]
-            vc = [torch.randn((B, ctx, hkv, hd), device="cuda", generator=g).half() for _ in range(copies)]
-            q = torch.randn((B, hq, hd), device="cuda", generator=g)
-            out = torch.empty((B, hq, hd), device="cuda")
-            lens = torch.full((B,), ctx, dtype=torch.int32, device="cuda")
-            f = lambda i, st: _lib.call("du_flash_decode", C.c_void_p(out.data_ptr()), C.c_void_p(q.data_ptr()),
-                                        C.c_void_p(kc[i % copies].data_ptr()), C.c_void_p(vc[i % copies].data_ptr()),
-                                        C.c_void_p(lens.data_ptr()), B, hq, hkv, hd, ctx, C.c_float(hd ** -0.5),
-                                        C.c_void_p(st))
-            ms = _graph_ms(f, max(8, min(64, int(2e9 / kv_bytes))))
-            gbs = kv_bytes / (ms / 1e3) / 1e9
-            print(json.dumps({"sweep": "flash_decode", "ctx": ctx, "batch": B, "us": round(ms * 1e3, 2),
-                              "GB_s": round(gbs, 1), "frac_hbm": round(gbs / peak, 4), "peak_kind": kind,
-                              "copies": copies, "kernel": "flash_decode_cluster_kernel (du_flash_decode)",
-                              "timing": "CUDA graph of the launches, caches rotated over >= 0.6 GB"}), flush=True)
-            del kc, vc
+    for kv in ("fp16", "int8"):
+        for ctx in (512, 2048, 8192, 32768):
+            for B in (1, 8, 32):
+                # algorithmic bytes: K and V rows (2 bytes an element, or 1 + a 4-byte
+                # scale / zero-point word per (position, kv head) for the INT8 cache)
+                kv_bytes = B * ctx * hkv * (hd * 2 * 2 if kv == "fp16" else (hd + 4) * 2)
+                copies = max(2, int(np.ceil(0.6e9 / kv_bytes)))
+                if copies * kv_bytes > 40e9:
+                    copies = 1
+                q = torch.randn((B, hq, hd), device="cuda", generator=g)
+                out = torch.empty((B, hq, hd), device="cuda")
+                lens = torch.full((B,), ctx, dtype=torch.int32, device="cuda")
+                if kv == "fp16":
+                    kc = [torch.randn((B, ctx, hkv, hd), device="cuda", generator=g).half() for _ in range(copies)]
+                    vc = [torch.randn((B, ctx, hkv, hd), device="cuda", generator=g).half() for _ in range(copies)]
+                    f = lambda i, st: _lib.call("du_flash_decode", C.c_void_p(out.data_ptr()), C.c_void_p(q.data_ptr()),
+                                                C.c_void_p(kc[i % copies].data_ptr()),
+                                                C.c_void_p(vc[i % copies].data_ptr()), C.c_void_p(lens.data_ptr()),
+                                                B, hq, hkv, hd, ctx, C.c_float(hd ** -0.5), C.c_void_p(st))
+                    kern = "flash_decode_cluster_kernel (du_flash_decode)"
+                else:
+                    kc = [torch.randint(0, 256, (B, ctx, hkv, hd), dtype=torch.uint8, device="cuda", generator=g)
+                          for _ in range(copies)]
+                    vc = [torch.randint(0, 256, (B, ctx, hkv, hd), dtype=torch.uint8, device="cuda", generator=g)
+                          for _ in range(copies)]
+                    # words: fp16 scale 0.01 (0x211F) | fp16 zero point 128 (0x5800) << 16
+                    ksz = torch.full((B, ctx, hkv), 0x5800211F, dtype=torch.int32, device="cuda")
+                    f = lambda i, st: _lib.call("du_flash_decode_kv8", C.c_void_p(out.data_ptr()),
+                                                C.c_void_p(q.data_ptr()), C.c_void_p(kc[i % copies].data_ptr()),
+                                                C.c_void_p(ksz.data_ptr()), C.c_void_p(vc[i % copies].data_ptr()),
+                                                C.c_void_p(ksz.data_ptr()), C.c_void_p(lens.data_ptr()),
+                                                B, hq, hkv, hd, ctx, C.c_float(hd ** -0.5), C.c_void_p(st))
+                    kern = "flash_decode_cluster_kernel, INT8 cache (du_flash_decode_kv8)"
+                ms = _graph_ms(f, max(8, min(64, int(2e9 / kv_bytes))))
+                gbs = kv_bytes / (ms / 1e3) / 1e9
+                print(json.dumps({"sweep": "flash_decode", "kv": kv, "ctx": ctx, "batch": B, "us": round(ms * 1e3, 2),
+                                  "GB_s": round(gbs, 1), "frac_hbm": round(gbs / peak, 4), "peak_kind": kind,
+                                  "copies": copies, "kernel": kern,
+                                  "timing": "CUDA graph of the launches, caches rotated over >= 0.6 GB"}), flush=True)
+                del kc, vc
 
 
 def main():

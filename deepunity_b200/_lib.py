@@ -33,7 +33,7 @@ class ModelConfig(C.Structure):
                 ("embed_scale", C.c_float), ("quant", C.c_int32), ("group_size", C.c_int32),
                 ("kv_capacity", C.c_int32), ("max_batch", C.c_int32), ("tp_rank", C.c_int32),
                 ("tp_size", C.c_int32), ("tie_embedding", C.c_int32), ("flags", C.c_int32),
-                ("reserved", C.c_int32 * 4)]
+                ("kv_quant", C.c_int32), ("reserved", C.c_int32 * 3)]
 
 
 # name -> (restype, argtypes); every symbol of include/deepunity_cuda.h
@@ -66,6 +66,8 @@ SIGNATURES = {
     "du_gemv_q4": (I, [P, P, I, P, P, I, I, I, I, P]),
     "du_gemv_f16": (I, [P, P, I, P, I, I, I, P]),
     "du_flash_decode": (I, [P, P, P, P, P, I, I, I, I, I, F, P]),
+    "du_kv_write_int8": (I, [P, I, I, I, I, P, P, P]),
+    "du_flash_decode_kv8": (I, [P, P, P, P, P, P, P, I, I, I, I, I, F, P]),
     "du_flash_decode_noalloc": (I, [P, P, P, P, P, I, I, I, I, I, F, P]),
     "du_quantize_int8": (I, [P, I64, I64, P, P, P]),
     "du_quantize_int4": (I, [P, I64, I64, I, P, P, P]),

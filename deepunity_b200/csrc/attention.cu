@@ -85,7 +85,15 @@ __host__ __device__ constexpr size_t fdc_recv_bytes()
     return sizeof(float) * ((size_t)C * (FD_MAXG * HD / C) + (size_t)C * FD_MAXG * 2);
 }
 
-template <int HD, int C>
+// Dynamic shared memory of the cluster kernel before the receive buffers: tiles,
+// tensor-core operands and (INT8 cache) the raw staging buffers.
+template <int HD, bool KV8>
+__host__ __device__ constexpr size_t fdc_work_bytes()
+{
+    return (size_t)4 * FD_TILE * (HD + 8) * sizeof(__half) + fd_mma_extra_bytes<HD>() + (KV8 ? fd_kv8_bytes<HD>() : 0);
+}
+
+template <int HD, int C, bool KV8>
 __global__ void __launch_bounds__(FDC_THREADS) flash_decode_cluster_kernel(const FdParams p, int G, int new_rows)
 {
     constexpr int PER_MAX = FD_MAXG * HD / C;        // outputs merged per CTA, at most
@@ -93,15 +101,15 @@ __global__ void __launch_bounds__(FDC_THREADS) flash_decode_cluster_kernel(const
     __shared__ FdShared<HD> sh;
     cg::cluster_group cluster = cg::this_cluster();
     const int split = blockIdx.x, kvh = blockIdx.y, row = blockIdx.z;     // gridDim.x == C == cluster size
-    float *rcv_o = reinterpret_cast<float *>(fd_smem + 4 * FD_TILE * (HD + 8) * sizeof(__half) + fd_mma_extra_bytes<HD>());
+    float *rcv_o = reinterpret_cast<float *>(fd_smem + fdc_work_bytes<HD, KV8>());
     float *rcv_ml = rcv_o + C * PER_MAX;             // [C][FD_MAXG][2]
     // first phase of the cluster barrier: every CTA of the cluster has started before
     // any CTA stores into a peer's shared memory (waited on just before the push)
     asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
-    if (new_rows >= 0) fd_prefetch<HD, FDC_THREADS, true>(p, row, kvh, split, C, new_rows, fd_smem);
+    if (new_rows >= 0) fd_prefetch<HD, FDC_THREADS, true, KV8>(p, row, kvh, split, C, new_rows, fd_smem);
     pdl_wait();      // q (and this step's K/V rows) come from the previous kernel
     pdl_trigger();
-    fd_unit<HD, FDC_THREADS, true>(p, G, row, kvh, split, C, fd_smem, sh, new_rows);
+    fd_unit<HD, FDC_THREADS, true, KV8>(p, G, row, kvh, split, C, fd_smem, sh, new_rows);
     asm volatile("barrier.cluster.wait.aligned;" ::: "memory");
 
     // push: output o of this split's acc goes to CTA o / per, slot [split][o % per];
@@ -139,11 +147,11 @@ __global__ void __launch_bounds__(FDC_THREADS) flash_decode_cluster_kernel(const
     }
 }
 
-template <int HD, int C>
+template <int HD, int C, bool KV8>
 static int fdc_launch(const FdParams &p, int G, int nq, cudaStream_t st, int new_rows, bool probe, int *fits)
 {
-    auto kern = flash_decode_cluster_kernel<HD, C>;
-    const size_t smem = 4 * FD_TILE * (HD + 8) * sizeof(__half) + fd_mma_extra_bytes<HD>() + fdc_recv_bytes<HD, C>();
+    auto kern = flash_decode_cluster_kernel<HD, C, KV8>;
+    const size_t smem = fdc_work_bytes<HD, KV8>() + fdc_recv_bytes<HD, C>();
     int rc = ensure_func_attrs((const void *)kern, (int)smem, C > 8);
     if (rc) return rc;
     cudaLaunchConfig_t cfg = {};
@@ -170,8 +178,9 @@ static int fdc_launch(const FdParams &p, int G, int nq, cudaStream_t st, int new
     return DU_OK;
 }
 
-// Cluster size per device: 16 splits when such clusters can be resident, else 8.
-template <int HD>
+// Cluster size per device (and cache format): 16 splits when such clusters can be
+// resident, else 8.
+template <int HD, bool KV8>
 static int fdc_cluster_size(const FdParams &p, int G, cudaStream_t st)
 {
     static std::mutex mu;
@@ -181,16 +190,24 @@ static int fdc_cluster_size(const FdParams &p, int G, cudaStream_t st)
     std::lock_guard<std::mutex> lk(mu);
     if (chosen[dev & 63] == 0) {
         int n16 = 0;
-        const int rc = fdc_launch<HD, 16>(p, G, 1, st, -1, true, &n16);
+        const int rc = fdc_launch<HD, 16, KV8>(p, G, 1, st, -1, true, &n16);
         if (rc != DU_OK) cudaGetLastError();    // the probe's own failure: 16-CTA clusters unavailable
         chosen[dev & 63] = (rc == DU_OK && n16 > 0) ? 16 : 8;
     }
     return chosen[dev & 63];
 }
 
+template <int HD, bool KV8>
+static int fdc_dispatch(const FdParams &p, int G, int nq, cudaStream_t st, int new_rows)
+{
+    int dummy = 0;
+    return fdc_cluster_size<HD, KV8>(p, G, st) == 16 ? fdc_launch<HD, 16, KV8>(p, G, nq, st, new_rows, false, &dummy)
+                                                     : fdc_launch<HD, 8, KV8>(p, G, nq, st, new_rows, false, &dummy);
+}
+
 int launch_flash_decode_cluster(const float *q, const __half *kc, const __half *vc, const int *seq_of,
                                 const int *kv_len, int kv_len_add, int nq, int hq, int hkv, int hd, int cap,
-                                float scale, float *out, cudaStream_t st, int new_rows)
+                                float scale, float *out, cudaStream_t st, int new_rows, const Kv8Cache *kv8)
 {
     if (nq <= 0) return DU_OK;
     if (hkv <= 0 || hq % hkv != 0) return fail(DU_EINVAL, "flash_decode: hq must be a multiple of hkv");
@@ -200,16 +217,81 @@ int launch_flash_decode_cluster(const float *q, const __half *kc, const __half *
     p.q = q; p.k_cache = kc; p.v_cache = vc; p.seq_of = seq_of; p.kv_len = kv_len;
     p.kv_len_add = kv_len_add;
     p.hq = hq; p.hkv = hkv; p.cap = cap; p.scale = scale; p.out = out;
-    int dummy = 0;
-    if (hd == 128) {
-        return fdc_cluster_size<128>(p, G, st) == 16 ? fdc_launch<128, 16>(p, G, nq, st, new_rows, false, &dummy)
-                                                     : fdc_launch<128, 8>(p, G, nq, st, new_rows, false, &dummy);
+    if (kv8 != nullptr) {
+        p.k8 = kv8->k8; p.v8 = kv8->v8; p.ksz = kv8->ksz; p.vsz = kv8->vsz;
+        if (hd == 128) return fdc_dispatch<128, true>(p, G, nq, st, new_rows);
+        if (hd == 64) return fdc_dispatch<64, true>(p, G, nq, st, new_rows);
+        return fail(DU_EINVAL, "flash_decode: supported head_dim 64/128");
     }
-    if (hd == 64) {
-        return fdc_cluster_size<64>(p, G, st) == 16 ? fdc_launch<64, 16>(p, G, nq, st, new_rows, false, &dummy)
-                                                    : fdc_launch<64, 8>(p, G, nq, st, new_rows, false, &dummy);
-    }
+    if (hd == 128) return fdc_dispatch<128, false>(p, G, nq, st, new_rows);
+    if (hd == 64) return fdc_dispatch<64, false>(p, G, nq, st, new_rows);
     return fail(DU_EINVAL, "flash_decode: supported head_dim 64/128");
+}
+
+// WriteCacheFull, INT8 variant (Gemma3CS.compute:300-380; layout KVCache.hlsl:46-82):
+// one warp per (token, K|V, kv head) row of hd fp32 values from the QKV epilogue's
+// staging buffer [M][nkv][hkv][hd] (nkv = 2: K and V rows; 1: K rows only).  min / max (exact in any order), scale = (max -
+// min) / 255 floored at 1e-9, zp = round(-min / scale) clamped to [0, 255], q =
+// clamp(round(x * (1 / scale)) + zp, 0, 255), round half to even, IEEE division
+// and reciprocal; the row's word (fp16 scale | fp16 zp << 16).
+__global__ void __launch_bounds__(256) kv_quant_int8_kernel(const float *stage, int M, int nkv, int hkv, int hd,
+                                                            const int *pos, int pos_base, const int *seq_of,
+                                                            int seq_off, int cap, Kv8Cache kv)
+{
+    pdl_wait();
+    const int w = (int)((blockIdx.x * blockDim.x + threadIdx.x) >> 5), lane = threadIdx.x & 31;
+    if (w >= M * nkv * hkv) return;
+    const int h = w % hkv, isv = (w / hkv) % nkv, m = w / (nkv * hkv);
+    const int epl = hd >> 5;                         // values per lane (hd = 32 .. 256)
+    const float *x = stage + (size_t)w * hd + lane * epl;
+    float v[8];
+    float mn = 3.0e38f, mx = -3.0e38f;
+#pragma unroll
+    for (int e = 0; e < 8; e++)
+        if (e < epl) {
+            v[e] = x[e];
+            mn = fminf(mn, v[e]);
+            mx = fmaxf(mx, v[e]);
+        }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        mn = fminf(mn, __shfl_xor_sync(0xffffffffu, mn, o));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    }
+    float scale = (mx - mn) / 255.0f;
+    if (scale < 1e-9f) scale = 1e-9f;
+    const float zp = fminf(fmaxf(rintf(-mn / scale), 0.0f), 255.0f);
+    const float inv = 1.0f / scale;
+    const int seq = seq_of ? seq_of[m] : seq_off + m;
+    const size_t row = ((size_t)seq * cap + (pos ? pos[m] : pos_base + m)) * hkv + h;
+    uint8_t *dst = (isv ? kv.v8 : kv.k8) + row * hd + lane * epl;
+#pragma unroll
+    for (int e = 0; e < 8; e++)
+        if (e < epl) dst[e] = (uint8_t)fminf(fmaxf(rintf(v[e] * inv) + zp, 0.0f), 255.0f);
+    if (lane == 0)
+        (isv ? kv.vsz : kv.ksz)[row] = (uint32_t)__half_as_ushort(__float2half_rn(scale)) |
+                                       ((uint32_t)__half_as_ushort(__float2half_rn(zp)) << 16);
+}
+
+int launch_kv_quant_int8(const float *stage, int M, int nkv, int hkv, int hd, const int *pos, int pos_base,
+                         const int *seq_of, int seq_off, int cap, const Kv8Cache &kv, cudaStream_t st)
+{
+    if (M <= 0) return DU_OK;
+    if (hd % 32 != 0 || hd > 256) return fail(DU_EINVAL, "kv_quant_int8: head_dim must be a multiple of 32, <= 256");
+    if (nkv != 1 && nkv != 2) return fail(DU_EINVAL, "kv_quant_int8: nkv must be 1 or 2");
+    const int warps = M * nkv * hkv;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((warps + 7) / 8);
+    cfg.blockDim = dim3(256);
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl_enabled() ? 1 : 0;
+    DU_CUDA_TRY(cudaLaunchKernelEx(&cfg, kv_quant_int8_kernel, stage, M, nkv, hkv, hd, pos, pos_base, seq_of, seq_off,
+                                   cap, kv));
+    return DU_OK;
 }
 
 int fd_choose_splits(int nq, int hkv, int max_kv)

@@ -26,6 +26,10 @@ struct FdParams {
     float *part_o;               // [nq][hkv][nsplit][G][HD]
     float *part_ml;              // [nq][hkv][nsplit][G][2]
     unsigned *counters;          // [nq][hkv], zero between launches
+    // INT8 cache (the KV8 instantiations): uint8 [nseq][cap][hkv][HD] and per-(position,
+    // kv head) words (fp16 scale | fp16 zero point << 16) [nseq][cap][hkv]
+    const uint8_t *k8, *v8;
+    const uint32_t *ksz, *vsz;
 };
 
 // Shared memory of one unit: K/V tiles (dynamic, 4 * FD_TILE * (HD + 8) halves) + these.
@@ -36,7 +40,24 @@ struct __align__(16) FdShared {     // qs is read as float4
     float m[FD_MAXG], l[FD_MAXG], alpha[FD_MAXG];
     float w[FD_MAXG][FD_MAXSPLIT], inv[FD_MAXG];
     unsigned last;
+    // INT8 cache, per tile: K scales, V scales / the tile's largest V scale, that largest scale
+    float kv8_ks[FD_TILE], kv8_vs[FD_TILE], kv8_vm;
 };
+
+// 8 INT8 cache bytes -> 8 halves (q - zp), exact: 0x64 as the high byte makes
+// the half 1024 + q, and 1024 + zp (an integer <= 1279) is exact too.
+__device__ __forceinline__ uint4 fd_q8_to_h8(uint2 r, __half2 base)
+{
+    uint32_t o[4];
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        const uint32_t w = i < 2 ? r.x : r.y;
+        const uint32_t u = __byte_perm(w, 0x64646464u, (i & 1) ? 0x4342u : 0x4140u);
+        __half2 h = __hsub2(*reinterpret_cast<const __half2 *>(&u), base);
+        o[i] = *reinterpret_cast<uint32_t *>(&h);
+    }
+    return make_uint4(o[0], o[1], o[2], o[3]);
+}
 
 __device__ __forceinline__ void fd_cp_async16(void *smem, const void *gmem, bool valid)
 {
@@ -88,10 +109,26 @@ __host__ __device__ constexpr size_t fd_mma_extra_bytes()
     return (size_t)2 * 16 * (HD + 8) * 2 + (size_t)2 * 16 * (FD_TILE + 8) * 2 + (size_t)FD_MAXG * (FD_TILE + 4) * 4;
 }
 
+// INT8 cache: raw rows and their scale / zero-point words, two tile buffers each,
+// after the tensor-core scratch: K [2][FD_TILE][HD] bytes, V the same, then the
+// K and V words [2][FD_TILE] each.
+template <int HD>
+__host__ __device__ constexpr size_t fd_kv8_off()
+{
+    return (size_t)4 * FD_TILE * (HD + 8) * 2 + fd_mma_extra_bytes<HD>();
+}
+template <int HD>
+__host__ __device__ constexpr size_t fd_kv8_bytes()
+{
+    return (size_t)4 * FD_TILE * HD + (size_t)4 * FD_TILE * 4;
+}
+
 // Positions of unit (row, kv head, split).
 struct FdGeom {
     int kv_len, ns_act, start, end, ntiles;
     const __half *kbase, *vbase;
+    const uint8_t *k8base, *v8base;       // INT8 cache
+    const uint32_t *kzbase, *vzbase;
 };
 
 // EVEN: the kv_len's tiles are dealt evenly over the nsplit splits (cluster
@@ -118,14 +155,27 @@ __device__ __forceinline__ FdGeom fd_geom(const FdParams &p, int row, int kvh, i
         g.end = split < g.ns_act ? min(g.start + chunk, g.kv_len) : g.start;
     }
     g.ntiles = g.end > g.start ? (g.end - g.start + FD_TILE - 1) / FD_TILE : 0;
-    g.kbase = p.k_cache + ((size_t)seq * p.cap * p.hkv + kvh) * HD;
-    g.vbase = p.v_cache + ((size_t)seq * p.cap * p.hkv + kvh) * HD;
+    const size_t row0 = (size_t)seq * p.cap * p.hkv + kvh;
+    g.kbase = p.k_cache + row0 * HD;
+    g.vbase = p.v_cache + row0 * HD;
+    g.k8base = p.k8 + row0 * HD;
+    g.v8base = p.v8 + row0 * HD;
+    g.kzbase = p.ksz + row0;
+    g.vzbase = p.vsz + row0;
     return g;
 }
 
+__device__ __forceinline__ void fd_cp_async4(void *smem, const void *gmem, bool valid)
+{
+    const unsigned s = (unsigned)__cvta_generic_to_shared(smem);
+    const int n = valid ? 4 : 0;
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(s), "l"(gmem), "r"(n) : "memory");
+}
+
 // cp.async of the K/V rows of tile t at positions [lo, hi) into buffer buf
-// (rows past the unit's end are zero-filled); one commit group.
-template <int HD, int NT>
+// (rows past the unit's end are zero-filled); one commit group.  KV8: the raw
+// bytes and the scale / zero-point words into the INT8 staging buffers.
+template <int HD, int NT, bool KV8 = false>
 __device__ __forceinline__ void fd_load_rows(const FdParams &p, const FdGeom &g, int t, int buf, int lo, int hi,
                                              unsigned char *tiles)
 {
@@ -137,6 +187,31 @@ __device__ __forceinline__ void fd_load_rows(const FdParams &p, const FdGeom &g,
     const int p0 = g.start + t * FD_TILE;
     lo = max(lo, p0);
     hi = min(hi, p0 + FD_TILE);
+    if constexpr (KV8) {
+        unsigned char *raw = tiles + fd_kv8_off<HD>();
+        auto Kr = reinterpret_cast<uint8_t (*)[FD_TILE][HD]>(raw);
+        auto Vr = reinterpret_cast<uint8_t (*)[FD_TILE][HD]>(raw + 2 * FD_TILE * HD);
+        auto Kz = reinterpret_cast<uint32_t (*)[FD_TILE]>(raw + 4 * FD_TILE * HD);
+        auto Vz = reinterpret_cast<uint32_t (*)[FD_TILE]>(raw + 4 * FD_TILE * HD + 2 * FD_TILE * 4);
+        constexpr int CB = HD / 16;            // 16-byte chunks per INT8 row
+        for (int i = threadIdx.x; i < (hi - lo) * CB; i += NT) {
+            const int j = lo - p0 + i / CB, c = i % CB;
+            const int pos = p0 + j;
+            const bool ok = pos < g.end;
+            const size_t off = (size_t)(ok ? pos : 0) * pos_stride + c * 16;
+            fd_cp_async16(&Kr[buf][j][c * 16], g.k8base + off, ok);
+            fd_cp_async16(&Vr[buf][j][c * 16], g.v8base + off, ok);
+        }
+        for (int i = threadIdx.x; i < hi - lo; i += NT) {
+            const int j = lo - p0 + i, pos = p0 + j;
+            const bool ok = pos < g.end;
+            const size_t off = (size_t)(ok ? pos : 0) * p.hkv;
+            fd_cp_async4(&Kz[buf][j], g.kzbase + off, ok);
+            fd_cp_async4(&Vz[buf][j], g.vzbase + off, ok);
+        }
+        fd_cp_commit();
+        return;
+    }
     for (int i = threadIdx.x; i < (hi - lo) * CPR; i += NT) {
         const int j = lo - p0 + i / CPR, c = i % CPR;
         const int pos = p0 + j;
@@ -151,13 +226,13 @@ __device__ __forceinline__ void fd_load_rows(const FdParams &p, const FdGeom &g,
 // Loads, ahead of the producer of this step's K/V rows, the rows of tiles 0 and
 // 1 (the two tile buffers) that earlier steps wrote: positions below kv_len -
 // new_rows; two commit groups.  The unit is then run with pre_new = new_rows.
-template <int HD, int NT, bool EVEN = false>
+template <int HD, int NT, bool EVEN = false, bool KV8 = false>
 __device__ __forceinline__ void fd_prefetch(const FdParams &p, int row, int kvh, int split, int nsplit, int new_rows,
                                             unsigned char *tiles)
 {
     const FdGeom g = fd_geom<HD, EVEN>(p, row, kvh, split, nsplit);
-    if (g.ntiles > 0) fd_load_rows<HD, NT>(p, g, 0, 0, g.start, g.kv_len - new_rows, tiles);
-    if (g.ntiles > 1) fd_load_rows<HD, NT>(p, g, 1, 1, g.start, g.kv_len - new_rows, tiles);
+    if (g.ntiles > 0) fd_load_rows<HD, NT, KV8>(p, g, 0, 0, g.start, g.kv_len - new_rows, tiles);
+    if (g.ntiles > 1) fd_load_rows<HD, NT, KV8>(p, g, 1, 1, g.start, g.kv_len - new_rows, tiles);
 }
 
 // Processes unit (row, kvh, split) of a launch with `nsplit` splits per
@@ -176,10 +251,18 @@ __device__ __forceinline__ void fd_prefetch(const FdParams &p, int row, int kvh,
 // into fp16 hi + lo parts (x = hi + lo to ~22 bits) and multiplied against the
 // exact fp16 K / V, one MMA per part; rows g >= G of the 16-row A operands are
 // zero.  Needs fd_mma_extra_bytes<HD>() of shared memory after the tiles.
-template <int HD, int NT, bool TO_SMEM = false>
+//
+// KV8 (INT8 cache; tensor-core path only): each tile's raw bytes become (q - zp)
+// halves in the tile buffers, exact.  Scores are q . (k_q - zp) times the row's
+// K scale.  The probabilities enter P.V times (V scale / largest V scale of the
+// tile); the accumulator is kept in units of that largest scale and rescaled
+// with the softmax factor from tile to tile.
+template <int HD, int NT, bool TO_SMEM = false, bool KV8 = false>
 __device__ __forceinline__ void fd_unit(const FdParams &p, int G, int row, int kvh, int split, int nsplit, unsigned char *tiles,
                         FdShared<HD> &sh, int pre_new = -1)
 {
+    static_assert(!KV8 || (TO_SMEM && NT == 256), "the INT8 cache runs on the tensor-core path");
+    static_assert(FD_TILE == 64, "two positions per lane of one warp");
     constexpr int LDS = HD + 8;               // padded row (halves): conflict-free 16 B reads
     constexpr int NW = NT / 32;
     constexpr size_t TILE_BYTES = 4 * FD_TILE * LDS * 2;
@@ -197,7 +280,8 @@ __device__ __forceinline__ void fd_unit(const FdParams &p, int G, int row, int k
     const int ns_act = geo.ns_act, start = geo.start, end = geo.end, ntiles = geo.ntiles;
 
     if (ntiles > 0)
-        fd_load_rows<HD, NT>(p, geo, 0, 0, pre_new < 0 ? start : geo.kv_len - pre_new, 0x7fffffff, tiles);
+        fd_load_rows<HD, NT, KV8>(p, geo, 0, 0, pre_new < 0 ? start : geo.kv_len - pre_new, 0x7fffffff, tiles);
+    float vm_prev = 1.0f;        // KV8: the accumulator's unit (largest V scale of the previous tile)
     if (MMA) {
         // q rows g < G as hi + lo halves (rows G..15 zero); all loads issued before the stores
         constexpr int QV = (16 * HD / 4 + NT - 1) / NT;     // float4 per thread
@@ -254,13 +338,45 @@ __device__ __forceinline__ void fd_unit(const FdParams &p, int G, int row, int k
         const int buf = t & 1;
         if (t + 1 < ntiles) {
             // tile 1's older rows came with the prefetch
-            fd_load_rows<HD, NT>(p, geo, t + 1, buf ^ 1, (t == 0 && pre_new >= 0) ? geo.kv_len - pre_new : 0, 0x7fffffff,
-                                 tiles);
+            fd_load_rows<HD, NT, KV8>(p, geo, t + 1, buf ^ 1, (t == 0 && pre_new >= 0) ? geo.kv_len - pre_new : 0,
+                                      0x7fffffff, tiles);
             fd_cp_wait<1>();
         } else {
             fd_cp_wait<0>();
         }
         __syncthreads();
+        float vm_ratio = 1.0f;
+        if constexpr (KV8) {
+            unsigned char *raw = tiles + fd_kv8_off<HD>();
+            auto Kr = reinterpret_cast<const uint8_t (*)[FD_TILE][HD]>(raw);
+            auto Vr = reinterpret_cast<const uint8_t (*)[FD_TILE][HD]>(raw + 2 * FD_TILE * HD);
+            auto Kz = reinterpret_cast<const uint32_t (*)[FD_TILE]>(raw + 4 * FD_TILE * HD);
+            auto Vz = reinterpret_cast<const uint32_t (*)[FD_TILE]>(raw + 4 * FD_TILE * HD + 2 * FD_TILE * 4);
+            for (int i = tid; i < FD_TILE * HD / 8; i += NT) {
+                const int j = i / (HD / 8), c = i - j * (HD / 8);
+                const float kz = __half2float(__ushort_as_half((unsigned short)(Kz[buf][j] >> 16)));
+                const float vz = __half2float(__ushort_as_half((unsigned short)(Vz[buf][j] >> 16)));
+                *reinterpret_cast<uint4 *>(&Ks[buf][j][c * 8]) =
+                    fd_q8_to_h8(*reinterpret_cast<const uint2 *>(&Kr[buf][j][c * 8]), __float2half2_rn(1024.0f + kz));
+                *reinterpret_cast<uint4 *>(&Vs[buf][j][c * 8]) =
+                    fd_q8_to_h8(*reinterpret_cast<const uint2 *>(&Vr[buf][j][c * 8]), __float2half2_rn(1024.0f + vz));
+            }
+            if (warp == 0) {
+                const float va = __half2float(__ushort_as_half((unsigned short)(Vz[buf][lane] & 0xFFFFu)));
+                const float vb = __half2float(__ushort_as_half((unsigned short)(Vz[buf][lane + 32] & 0xFFFFu)));
+                float vm = warp_max(fmaxf(va, vb));
+                if (!(vm > 0.0f)) vm = 1.0f;     // no V scale above zero: every V value of the tile is 0
+                sh.kv8_ks[lane] = __half2float(__ushort_as_half((unsigned short)(Kz[buf][lane] & 0xFFFFu)));
+                sh.kv8_ks[lane + 32] = __half2float(__ushort_as_half((unsigned short)(Kz[buf][lane + 32] & 0xFFFFu)));
+                sh.kv8_vs[lane] = va / vm;
+                sh.kv8_vs[lane + 32] = vb / vm;
+                if (lane == 0) sh.kv8_vm = vm;
+            }
+            __syncthreads();
+            const float vm = sh.kv8_vm;
+            vm_ratio = vm_prev / vm;
+            vm_prev = vm;
+        }
 
         // ---- scores: each K chunk is read once and used for every head
         if (MMA) {
@@ -278,6 +394,10 @@ __device__ __forceinline__ void fd_unit(const FdParams &p, int G, int row, int k
                 }
             }
             const int g = lane >> 2, j = n0 + (lane & 3) * 2;
+            if (KV8) {
+                c[0] *= sh.kv8_ks[j];
+                c[1] *= sh.kv8_ks[j + 1];
+            }
             if (g < G) {
                 const int pos = start + t * FD_TILE + j;
                 *reinterpret_cast<float2 *>(&pst[g][j]) = make_float2(pos < end ? c[0] : FD_NEG, pos + 1 < end ? c[1] : FD_NEG);
@@ -337,10 +457,11 @@ __device__ __forceinline__ void fd_unit(const FdParams &p, int G, int row, int k
             const float m_new = fmaxf(m_old, mt);
             const float pa = expf(a - m_new), pb = expf(b - m_new);
             if (MMA) {
-                const __half ha = __float2half_rn(pa), hb = __float2half_rn(pb);
+                const float qa = KV8 ? pa * sh.kv8_vs[2 * lane] : pa, qb = KV8 ? pb * sh.kv8_vs[2 * lane + 1] : pb;
+                const __half ha = __float2half_rn(qa), hb = __float2half_rn(qb);
                 *reinterpret_cast<__half2 *>(&ph[0][g][2 * lane]) = __halves2half2(ha, hb);
                 *reinterpret_cast<__half2 *>(&ph[1][g][2 * lane]) =
-                    __halves2half2(__float2half_rn(pa - __half2float(ha)), __float2half_rn(pb - __half2float(hb)));
+                    __halves2half2(__float2half_rn(qa - __half2float(ha)), __float2half_rn(qb - __half2float(hb)));
             } else {
                 sh.ps[2 * lane][g] = pa;
                 sh.ps[2 * lane + 1][g] = pb;
@@ -358,7 +479,7 @@ __device__ __forceinline__ void fd_unit(const FdParams &p, int G, int row, int k
         // ---- P.V over this thread's positions, every head
         if (MMA) {
             const int g = lane >> 2;
-            const float al = g < G ? sh.alpha[g] : 1.0f;
+            const float al = (g < G ? sh.alpha[g] : 1.0f) * vm_ratio;
 #pragma unroll
             for (int n = 0; n < NTL; n++) { oc[n][0] *= al; oc[n][1] *= al; }
             const int d0 = warp * (HD / 8);
@@ -408,11 +529,12 @@ __device__ __forceinline__ void fd_unit(const FdParams &p, int G, int row, int k
     float *so = reinterpret_cast<float *>(tiles);           // [G][HD]; the tiles are free now
     if (MMA) {
         const int g = lane >> 2, d0 = warp * (HD / 8);
+        const float unit = KV8 ? vm_prev : 1.0f;    // KV8: back from units of the last tile's V scale
         if (g < G)
 #pragma unroll
             for (int n = 0; n < NTL; n++) {
-                so[g * HD + d0 + n * 8 + (lane & 3) * 2] = oc[n][0];
-                so[g * HD + d0 + n * 8 + (lane & 3) * 2 + 1] = oc[n][1];
+                so[g * HD + d0 + n * 8 + (lane & 3) * 2] = oc[n][0] * unit;
+                so[g * HD + d0 + n * 8 + (lane & 3) * 2 + 1] = oc[n][1] * unit;
             }
         __syncthreads();
         return;

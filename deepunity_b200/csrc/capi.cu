@@ -280,6 +280,30 @@ DU_API int du_flash_decode(float *out, const float *q, const uint16_t *k_cache, 
                                        hd, capacity, scale, out, static_cast<cudaStream_t>(stream));
 }
 
+DU_API int du_kv_write_int8(const float *kv_new, int seq_len, int hkv, int hd, int cache_len, uint8_t *cache,
+                            uint32_t *sz, void *stream)
+{
+    DU_CHECK_ARG(kv_new && cache && sz, "du_kv_write_int8: null pointer");
+    DU_CHECK_ARG(seq_len >= 0 && hkv > 0 && hd > 0 && cache_len >= 0, "du_kv_write_int8: bad sizes");
+    Kv8Cache kv = {cache, nullptr, sz, nullptr};
+    // one sequence, K rows only: rows land at positions cache_len + m
+    return launch_kv_quant_int8(kv_new, seq_len, 1, hkv, hd, nullptr, cache_len, nullptr, 0, 0, kv,
+                                static_cast<cudaStream_t>(stream));
+}
+
+DU_API int du_flash_decode_kv8(float *out, const float *q, const uint8_t *k8, const uint32_t *ksz, const uint8_t *v8,
+                               const uint32_t *vsz, const int32_t *kv_len, int batch, int hq, int hkv, int hd,
+                               int capacity, float scale, void *stream)
+{
+    DU_CHECK_ARG(out && q && k8 && ksz && v8 && vsz && kv_len, "du_flash_decode_kv8: null pointer");
+    DU_CHECK_ARG(batch >= 0 && hq > 0 && hkv > 0 && capacity > 0, "du_flash_decode_kv8: bad sizes");
+    DU_CHECK_ARG(hq % hkv == 0, "du_flash_decode_kv8: hq must be a multiple of hkv");
+    Kv8Cache kv = {const_cast<uint8_t *>(k8), const_cast<uint8_t *>(v8), const_cast<uint32_t *>(ksz),
+                   const_cast<uint32_t *>(vsz)};
+    return launch_flash_decode_cluster(q, nullptr, nullptr, nullptr, kv_len, 0, batch, hq, hkv, hd, capacity, scale, out,
+                                       static_cast<cudaStream_t>(stream), -1, &kv);
+}
+
 DU_API int du_dequant(float *out, const void *w, const void *scales, int quant, int scale_dtype, int group,
                       int64_t row0, int nrows, int K, void *stream)
 {

@@ -41,6 +41,13 @@ struct TpFuse {
     unsigned spin_limit;             // polls of one peer word before a wait gives up
 };
 
+// INT8 KV cache of one layer: uint8 rows [seq][cap][hkv][hd] and one word per
+// (seq, position, kv head): fp16 scale | fp16 zero point << 16 (KVCache.hlsl:46-82).
+struct Kv8Cache {
+    uint8_t *k8, *v8;
+    uint32_t *ksz, *vsz;
+};
+
 // 16-byte streaming load: weights are read exactly once per launch, so they
 // bypass L1 (no_allocate) and come through the read-only path.
 __device__ __forceinline__ uint4 ldg_stream(const void *p)

@@ -253,6 +253,12 @@ __device__ __forceinline__ void gv_epi_pair(const GemvParams &p, int lr0, int m,
     } else {
         const bool isk = head < p.hq + p.hkv;
         const int kh = isk ? head - p.hq : head - p.hq - p.hkv;
+        if (p.kv_stage != nullptr) {
+            float *dst = p.kv_stage + (((size_t)m * 2 + (isk ? 0 : 1)) * p.hkv + kh) * hd;
+            dst[i] = x1;
+            dst[i + (hd >> 1)] = x2;
+            return;
+        }
         __half *dst = (isk ? p.k_cache : p.v_cache) + (((size_t)seq * p.cap + pos) * p.hkv + kh) * hd;
         dst[i] = __float2half_rn(x1);
         dst[i + (hd >> 1)] = __float2half_rn(x2);

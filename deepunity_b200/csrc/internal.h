@@ -55,7 +55,12 @@ int launch_flash_decode(const float *q, const __half *kc, const __half *vc, cons
 // The model's path: splits of a (row, kv head) combined inside a thread-block cluster.
 int launch_flash_decode_cluster(const float *q, const __half *kc, const __half *vc, const int *seq_of,
                                 const int *kv_len, int kv_len_add, int nq, int hq, int hkv, int hd, int cap,
-                                float scale, float *out, cudaStream_t st, int new_rows = -1);
+                                float scale, float *out, cudaStream_t st, int new_rows = -1,
+                                const Kv8Cache *kv8 = nullptr);
+// INT8 KV: quantizes fp32 rows [M][nkv][hkv][hd] (nkv 2: K then V; 1: K only) into the
+// cache at sequence seq_of[m] (or seq_off + m), position pos[m] (or pos_base + m).
+int launch_kv_quant_int8(const float *stage, int M, int nkv, int hkv, int hd, const int *pos, int pos_base,
+                         const int *seq_of, int seq_off, int cap, const Kv8Cache &kv, cudaStream_t st);
 
 // elementwise.cu
 int launch_embed(const int *ids, const __half *embed, float scale, int M, int H, float *out, cudaStream_t st);

@@ -63,6 +63,10 @@ struct du_model {
     __half *rope_cos = nullptr, *rope_sin = nullptr;
     __half *k_cache = nullptr, *v_cache = nullptr;      // [L][maxb][cap][hkv_l][hd]
     size_t kv_layer_elems = 0;
+    bool kv8 = false;                                    // INT8 cache instead of the fp16 one:
+    uint8_t *k8 = nullptr, *v8 = nullptr;                // [L][maxb][cap][hkv_l][hd]
+    uint32_t *ksz = nullptr, *vsz = nullptr;             // [L][maxb][cap][hkv_l] scale | zp << 16
+    float *kv_stage = nullptr;                           // QKV epilogue's fp32 K / V rows [T][2][hkv_l][hd]
     // device state
     int *d_cache_len = nullptr;             // [maxb]
     int *d_ids = nullptr;                   // [max_tokens] input ids
@@ -185,6 +189,8 @@ static int check_cfg(const du_model_config &c)
     }
     DU_CHECK_ARG(H % 32 == 0 && I_l % 32 == 0 && K_o % 32 == 0, "config: K dims must be multiples of 32");
     DU_CHECK_ARG(c.tie_embedding == 0 || tp == 1, "config: tied embedding with tp > 1 is not supported");
+    DU_CHECK_ARG(c.kv_quant == 0 || c.kv_quant == DU_KV_FP16 || c.kv_quant == DU_KV_INT8,
+                 "config: kv_quant must be DU_KV_FP16 or DU_KV_INT8");
     return DU_OK;
 }
 
@@ -220,8 +226,15 @@ static int model_alloc(du_model *m)
     m->rope_cos = (__half *)dalloc(m, (size_t)m->cap * (hd / 2) * 2, &rc);
     m->rope_sin = (__half *)dalloc(m, (size_t)m->cap * (hd / 2) * 2, &rc);
     m->kv_layer_elems = (size_t)m->maxb * m->cap * m->hkv_l * hd;
-    m->k_cache = (__half *)dalloc(m, m->kv_layer_elems * m->L * 2, &rc);
-    m->v_cache = (__half *)dalloc(m, m->kv_layer_elems * m->L * 2, &rc);
+    if (m->kv8) {
+        m->k8 = (uint8_t *)dalloc(m, m->kv_layer_elems * m->L, &rc);
+        m->v8 = (uint8_t *)dalloc(m, m->kv_layer_elems * m->L, &rc);
+        m->ksz = (uint32_t *)dalloc(m, m->kv_layer_elems / hd * m->L * 4, &rc);
+        m->vsz = (uint32_t *)dalloc(m, m->kv_layer_elems / hd * m->L * 4, &rc);
+    } else {
+        m->k_cache = (__half *)dalloc(m, m->kv_layer_elems * m->L * 2, &rc);
+        m->v_cache = (__half *)dalloc(m, m->kv_layer_elems * m->L * 2, &rc);
+    }
     const int T = m->max_tokens;
     m->d_cache_len = (int *)dalloc(m, sizeof(int) * m->maxb, &rc);
     m->d_ids = (int *)dalloc(m, sizeof(int) * T, &rc);
@@ -235,6 +248,7 @@ static int model_alloc(du_model *m)
     m->q = (float *)dalloc(m, sizeof(float) * T * m->hq_l * hd, &rc);
     m->att = (float *)dalloc(m, sizeof(float) * T * m->hq_l * hd, &rc);
     m->inter = (float *)dalloc(m, sizeof(float) * T * m->I_l, &rc);
+    if (m->kv8) m->kv_stage = (float *)dalloc(m, sizeof(float) * T * 2 * m->hkv_l * hd, &rc);
     m->logits = (float *)dalloc(m, sizeof(float) * m->maxb * m->V_l, &rc);
     if (m->tp > 1) m->logits_all = (float *)dalloc(m, sizeof(float) * m->tp * m->maxb * m->V_l, &rc);
     m->am_parts = 2 * num_sms();
@@ -521,6 +535,7 @@ static int run_gemv(du_model *m, int qt, GemvParams p, int M)
         c.x = p.x + (size_t)t0 * p.ldx;
         if (p.y) c.y = p.y + (size_t)t0 * p.ldy;
         if (p.q_out) c.q_out = p.q_out + (size_t)t0 * p.hq * p.hd;
+        if (p.kv_stage) c.kv_stage = p.kv_stage + (size_t)t0 * 2 * p.hkv * p.hd;
         if (p.pos) c.pos = p.pos + t0;
         if (p.seq_of) c.seq_of = p.seq_of + t0;
         else c.seq_off = p.seq_off + t0;      // token t0 + m belongs to sequence t0 + m
@@ -602,6 +617,14 @@ static bool tp_fuse_enabled(const du_model *m)
     return force < 0 ? m->tp <= 4 : force == 1;
 }
 
+// Layer l's part of the INT8 cache.
+static Kv8Cache kv8_layer(const du_model *m, int l)
+{
+    const size_t rows = m->kv_layer_elems / m->hd;
+    return Kv8Cache{m->k8 + (size_t)l * m->kv_layer_elems, m->v8 + (size_t)l * m->kv_layer_elems, m->ksz + (size_t)l * rows,
+                    m->vsz + (size_t)l * rows};
+}
+
 // One stage of layer l for the token rows of `io`.  With tensor parallelism
 // the O and down stages end in an allreduce of the partial sums plus the
 // residual add (collective = false leaves both out, for kernel timing).
@@ -619,8 +642,12 @@ static GemvParams stage_gemv_params(du_model *m, const StepIO &io, int l, int st
         p.x = m->x_res; p.ldx = H; p.gamma = ly.ln1; p.eps = m->cfg.rms_eps;
         p.N = m->qkv_rows; p.map = MAP_ROPE_PAIR; p.map_hd = hd;
         p.epi = EPI_QKV; p.q_out = m->q;
-        p.k_cache = m->k_cache + (size_t)l * m->kv_layer_elems;
-        p.v_cache = m->v_cache + (size_t)l * m->kv_layer_elems;
+        if (m->kv8) {
+            p.kv_stage = m->kv_stage;      // quantized into the INT8 cache by the next kernel
+        } else {
+            p.k_cache = m->k_cache + (size_t)l * m->kv_layer_elems;
+            p.v_cache = m->v_cache + (size_t)l * m->kv_layer_elems;
+        }
         p.pos = io.pos; p.seq_of = io.seq_of; p.hq = m->hq_l; p.hkv = m->hkv_l; p.hd = hd; p.cap = m->cap;
         p.rope_cos = m->rope_cos; p.rope_sin = m->rope_sin;
         break;
@@ -681,6 +708,11 @@ static int enqueue_stage(du_model *m, const StepIO &io, int l, int stage, bool c
     cudaStream_t st = m->stream;
     int rc = DU_OK;
     if (stage == ST_ATTN) {
+        if (m->kv8) {
+            const Kv8Cache kv = kv8_layer(m, l);
+            return launch_flash_decode_cluster(m->q, nullptr, nullptr, io.seq_of, io.kv_len, io.kv_len_add, M, m->hq_l,
+                                               m->hkv_l, hd, m->cap, powf((float)hd, -0.5f), m->att, st, io.kv_new, &kv);
+        }
         __half *kc = m->k_cache + (size_t)l * m->kv_layer_elems;
         __half *vc = m->v_cache + (size_t)l * m->kv_layer_elems;
         return launch_flash_decode_cluster(m->q, kc, vc, io.seq_of, io.kv_len, io.kv_len_add, M, m->hq_l, m->hkv_l,
@@ -690,6 +722,8 @@ static int enqueue_stage(du_model *m, const StepIO &io, int l, int stage, bool c
     GemvParams gp = stage_gemv_params(m, io, l, stage);
     if (gp.epi == EPI_TP_RESID && !collective) gp.epi = EPI_STORE;     // partial sums into m->part only
     if ((rc = run_gemv(m, qt, gp, M))) return rc;
+    if (stage == ST_QKV && m->kv8)     // this pass's K / V rows into the INT8 cache
+        return launch_kv_quant_int8(m->kv_stage, M, 2, m->hkv_l, hd, io.pos, 0, io.seq_of, 0, m->cap, kv8_layer(m, l), st);
     if ((stage == ST_O || stage == ST_DOWN) && m->tp > 1 && collective && gp.epi != EPI_TP_RESID) {
         if (tp_peer_ok(m, io)) return launch_tp_allreduce(&m->tpc, m->part, m->x_res, (size_t)M * H, st);
         if ((rc = allreduce_sum(m, m->part, (size_t)M * H))) return rc;
@@ -848,7 +882,8 @@ static int build_step_plan(du_model *m, const StepIO &io, StepPlan *plan, int *q
                            StepStage **d_stages)
 {
     *d_stages = nullptr;
-    if (!(m->cfg.flags & DU_FLAG_PERSISTENT) || (m->cfg.flags & DU_FLAG_NO_PERSISTENT) || m->tp > 1 || io.M > 8)
+    if (!(m->cfg.flags & DU_FLAG_PERSISTENT) || (m->cfg.flags & DU_FLAG_NO_PERSISTENT) || m->tp > 1 || io.M > 8 ||
+        m->kv8)
         return DU_ESTATE;
     const int qt = qt_of(m->quant);
     const int mt = io.M <= 1 ? 1 : io.M <= 2 ? 2 : io.M <= 4 ? 4 : 8;
@@ -1018,6 +1053,7 @@ DU_API int du_model_create(const du_model_config *cfg, du_model **out)
     m->quant = cfg->quant;
     m->group = cfg->quant == DU_QUANT_INT4 ? cfg->group_size : 32;
     m->cap = cfg->kv_capacity;
+    m->kv8 = cfg->kv_quant == DU_KV_INT8;
     m->maxb = cfg->max_batch;
     m->max_tokens = m->maxb > 256 ? m->maxb : 256;
     if (m->cfg.embed_scale == 0.0f) m->cfg.embed_scale = 1.0f;

@@ -82,9 +82,10 @@ class LlamaForCausalLM(LLM):
                  max_context_length: int = 8192, max_batch: int = 1, params_path: Optional[str] = None,
                  seed: Optional[int] = 0, init_std: float = 0.02, device: int = 0,
                  tp_rank: int = 0, tp_size: int = 1, flags: int = 0):
-        if kv_quant != KVQuant.FP16:
-            raise NotImplementedError("only the fp16 KV cache is implemented (KVQuant.FP16)")
+        if kv_quant not in (KVQuant.FP16, KVQuant.INT8):
+            raise NotImplementedError("KV cache formats: KVQuant.FP16 and KVQuant.INT8 (the fp32 cache is not built)")
         self.config = config
+        self.kv_quant = KVQuant(kv_quant)
         self.quant = LLMQuant(quant)
         self.max_batch = max_batch
         self.capacity = max_context_length
@@ -99,6 +100,7 @@ class LlamaForCausalLM(LLM):
         cfg.kv_capacity, cfg.max_batch = max_context_length, max_batch
         cfg.tp_rank, cfg.tp_size, cfg.tie_embedding = tp_rank, tp_size, int(config.tie_embedding)
         cfg.flags = flags     # FLAG_PERSISTENT: decode steps as one persistent kernel (default: per-stage graph)
+        cfg.kv_quant = int(self.kv_quant)   # 1 fp16, 2 INT8 (asymmetric uint8 rows + fp16 scale / zero point)
         h = C.c_void_p()
         _lib.call("du_model_create", C.byref(cfg), C.byref(h))
         self._h = h

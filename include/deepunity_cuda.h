@@ -67,8 +67,16 @@ typedef struct du_model_config {
     int32_t tp_size;
     int32_t tie_embedding;   /* 1: lm_head = embedding */
     int32_t flags;           /* DU_FLAG_* */
-    int32_t reserved[4];
+    int32_t kv_quant;        /* DU_KV_FP16 (0 or 1) or DU_KV_INT8 (KVQuant, LLM/Base/LLM.cs:15-87) */
+    int32_t reserved[3];
 } du_model_config;
+
+/* du_model_config.kv_quant */
+enum {
+    DU_KV_FP16 = 1,   /* fp16 cache (0 selects it too) */
+    DU_KV_INT8 = 2    /* asymmetric uint8 rows + per-(position, kv head) fp16 scale / zero point
+                         (WriteCacheFull KV_INT8, G3CS:300-380); the per-stage decode graph */
+};
 
 /* du_model_config.flags */
 enum {
@@ -250,6 +258,22 @@ DU_API int du_dequant(float *out, const void *w, const void *scales, int quant, 
 DU_API int du_flash_decode(float *out, const float *q, const uint16_t *k_cache,
                            const uint16_t *v_cache, const int32_t *kv_len, int batch, int hq,
                            int hkv, int hd, int capacity, float scale, void *stream);
+
+/* INT8 KV cache (KVQuant.INT8; WriteCacheFull's KV_INT8 variant, G3CS:300-380,
+ * layout KVCache.hlsl:46-82): quantizes kv_new fp32 [seq_len, hkv, hd] (device)
+ * into rows cache_len .. cache_len + seq_len - 1 of one sequence's cache: uint8
+ * [capacity, hkv, hd] plus one word per (position, kv head), fp16 scale | fp16
+ * zero point << 16, in sz [capacity, hkv].  Per row: scale = (max - min) / 255
+ * (at least 1e-9), zp = round(-min / scale) clamped to [0, 255], q = clamp(round(
+ * x / scale) + zp, 0, 255), round half to even.  hd a multiple of 32, <= 256. */
+DU_API int du_kv_write_int8(const float *kv_new, int seq_len, int hkv, int hd, int cache_len, uint8_t *cache,
+                            uint32_t *sz, void *stream);
+/* du_flash_decode over INT8 caches: k8 / v8 uint8 [batch, capacity, hkv, hd],
+ * ksz / vsz words [batch, capacity, hkv]; a cached value is (q - zp) * scale
+ * (kv_unpack8, KVCache.hlsl:55-62).  hd 64 or 128. */
+DU_API int du_flash_decode_kv8(float *out, const float *q, const uint8_t *k8, const uint32_t *ksz, const uint8_t *v8,
+                               const uint32_t *vsz, const int32_t *kv_len, int batch, int hq, int hkv, int hd,
+                               int capacity, float scale, void *stream);
 
 /* Same computation as du_flash_decode, but it allocates nothing: for callers
  * that must not call cudaMalloc / cudaFree, such as a game engine plugin

@@ -321,14 +321,73 @@ ORC_EXPORT void orc_kv_write(const float *kv_new, int seq_len, int hkv, int head
     for (int64_t i = 0; i < n; i++) cache[off + i] = orc_f32_to_f16(kv_new[i]);
 }
 
+/* WriteCacheFull, INT8 variant (G3CS:300-380, KVH:46-82): one (token, kv head)
+ * row of head_dim values at a time.  min / max over the row, scale = (max -
+ * min) / 255 (floored at 1e-9), zp = round(-min / scale) clamped to [0, 255],
+ * q = clamp(round(x * (1 / scale)) + zp, 0, 255); round() is round-half-even
+ * (HLSL round); the row's fp16 (scale | zp << 16) word goes to sz[pos * hkv + h].
+ * Divisions and the reciprocal are IEEE fp32. */
+ORC_EXPORT void orc_kv_write_int8(const float *kv_new, int seq_len, int hkv, int head_dim,
+                                  int cache_len, uint8_t *cache, uint32_t *sz)
+{
+    for (int l = 0; l < seq_len; l++)
+        for (int h = 0; h < hkv; h++) {
+            const float *x = kv_new + ((int64_t)l * hkv + h) * head_dim;
+            float mn = 3.0e38f, mx = -3.0e38f;
+            for (int d = 0; d < head_dim; d++) {
+                mn = fminf(mn, x[d]);
+                mx = fmaxf(mx, x[d]);
+            }
+            float scale = (mx - mn) / 255.0f;
+            if (scale < 1e-9f) scale = 1e-9f;
+            float zp = rintf(-mn / scale);
+            zp = zp < 0.0f ? 0.0f : (zp > 255.0f ? 255.0f : zp);
+            const float inv = 1.0f / scale;
+            const int64_t row = ((int64_t)(cache_len + l) * hkv + h);
+            for (int d = 0; d < head_dim; d++) {
+                float v = rintf(x[d] * inv) + zp;
+                v = v < 0.0f ? 0.0f : (v > 255.0f ? 255.0f : v);
+                cache[row * head_dim + d] = (uint8_t)v;
+            }
+            sz[row] = (uint32_t)orc_f32_to_f16(scale) | ((uint32_t)orc_f32_to_f16(zp) << 16);
+        }
+}
+
+/* kv_unpack8 (KVH:55-62): element d of cache row `row`. */
+static inline float read_kv8(const uint8_t *cache, const uint32_t *sz, int64_t row, int hd, int d)
+{
+    const uint32_t w = sz[row];
+    const float scale = orc_f16_to_f32((uint16_t)(w & 0xffffu)), zp = orc_f16_to_f32((uint16_t)(w >> 16));
+    return ((float)cache[row * hd + d] - zp) * scale;
+}
+
 /* FlashAttention (G3CS:643-753): one (query position, q head) at a time, KV
  * tiles of 256, tree max / tree sum per tile, online rescale, causal
  * j_hi = abs_q, out = acc / max(l, 1e-12).  K/V are fp16 caches laid out
  * [pos, Hkv, hd]; Q and out are fp32 [seq_q, Hq, hd]. */
 #define FA_T 256
+static void flash_attention_any(const float *Q, const uint16_t *Kc, const uint16_t *Vc, const uint8_t *K8,
+                                const uint32_t *Ksz, const uint8_t *V8, const uint32_t *Vsz,
+                                int seq_q, int kv_len, int hq, int hkv, int hd, float scale, float *out);
+
 ORC_EXPORT void orc_flash_attention(const float *Q, const uint16_t *Kc, const uint16_t *Vc,
                                     int seq_q, int kv_len, int hq, int hkv, int hd,
                                     float scale, float *out)
+{
+    flash_attention_any(Q, Kc, Vc, NULL, NULL, NULL, NULL, seq_q, kv_len, hq, hkv, hd, scale, out);
+}
+
+/* The same over an INT8 cache (KV_READ_K / KV_READ_V of the KV_INT8 variant). */
+ORC_EXPORT void orc_flash_attention_kv8(const float *Q, const uint8_t *K8, const uint32_t *Ksz,
+                                        const uint8_t *V8, const uint32_t *Vsz, int seq_q, int kv_len,
+                                        int hq, int hkv, int hd, float scale, float *out)
+{
+    flash_attention_any(Q, NULL, NULL, K8, Ksz, V8, Vsz, seq_q, kv_len, hq, hkv, hd, scale, out);
+}
+
+static void flash_attention_any(const float *Q, const uint16_t *Kc, const uint16_t *Vc, const uint8_t *K8,
+                                const uint32_t *Ksz, const uint8_t *V8, const uint32_t *Vsz,
+                                int seq_q, int kv_len, int hq, int hkv, int hd, float scale, float *out)
 {
     int grp = hq / (hkv > 0 ? hkv : 1);
     if (grp < 1) grp = 1;
@@ -348,9 +407,14 @@ ORC_EXPORT void orc_flash_attention(const float *Q, const uint16_t *Kc, const ui
                     int j = tile + t;
                     s[t] = -3.0e38f;
                     if (j <= j_hi) {
-                        const uint16_t *kr = Kc + ((int64_t)j * hkv + kvh) * hd;
                         float dot = 0.0f;
-                        for (int d = 0; d < hd; d++) dot = dot + fq[d] * read_h(kr, d);
+                        if (K8) {
+                            for (int d = 0; d < hd; d++)
+                                dot = dot + fq[d] * read_kv8(K8, Ksz, (int64_t)j * hkv + kvh, hd, d);
+                        } else {
+                            const uint16_t *kr = Kc + ((int64_t)j * hkv + kvh) * hd;
+                            for (int d = 0; d < hd; d++) dot = dot + fq[d] * read_h(kr, d);
+                        }
                         s[t] = dot;
                     }
                     red[t] = s[t];
@@ -372,7 +436,8 @@ ORC_EXPORT void orc_flash_attention(const float *Q, const uint16_t *Kc, const ui
                 for (int d = 0; d < hd; d++) {
                     float a = acc[d] * alpha;
                     for (int jj = 0; jj < n_valid; jj++)
-                        a = a + p[jj] * read_h(Vc, ((int64_t)(tile + jj) * hkv + kvh) * hd + d);
+                        a = a + p[jj] * (V8 ? read_kv8(V8, Vsz, (int64_t)(tile + jj) * hkv + kvh, hd, d)
+                                            : read_h(Vc, ((int64_t)(tile + jj) * hkv + kvh) * hd + d));
                     acc[d] = a;
                 }
                 m = m_new;
@@ -548,8 +613,10 @@ typedef struct {
     const uint16_t *embed;
     const uint16_t *lm_head;
     const uint16_t *rope_cos; const uint16_t *rope_sin;
-    uint16_t **k_cache; uint16_t **v_cache;     /* per layer [capacity, hkv, hd] */
+    uint16_t **k_cache; uint16_t **v_cache;     /* per layer [capacity, hkv, hd]; uint8 for kv_quant 2 */
     int32_t cache_len;
+    int32_t kv_quant;                            /* 2: INT8 cache (k_sz / v_sz per layer [capacity, hkv]) */
+    uint32_t **k_sz; uint32_t **v_sz;
 } orc_model;
 
 /* MiniCPM5Model.Forward(ids, useCache = true, lastPosOnly) (M5M:531-549) with
@@ -587,9 +654,17 @@ ORC_EXPORT int orc_forward(orc_model *md, const int32_t *ids, int seq_len, int l
         }
         orc_rope_apply(q, S, hq, hd, cache_len, md->rope_cos, md->rope_sin);
         orc_rope_apply(k, S, hkv, hd, cache_len, md->rope_cos, md->rope_sin);
-        orc_kv_write(k, S, hkv, hd, cache_len, md->k_cache[li]);
-        orc_kv_write(v, S, hkv, hd, cache_len, md->v_cache[li]);
-        orc_flash_attention(q, md->k_cache[li], md->v_cache[li], S, kv_len, hq, hkv, hd, scale, att);
+        if (md->kv_quant == 2) {
+            orc_kv_write_int8(k, S, hkv, hd, cache_len, (uint8_t *)md->k_cache[li], md->k_sz[li]);
+            orc_kv_write_int8(v, S, hkv, hd, cache_len, (uint8_t *)md->v_cache[li], md->v_sz[li]);
+            orc_flash_attention_kv8(q, (const uint8_t *)md->k_cache[li], md->k_sz[li],
+                                    (const uint8_t *)md->v_cache[li], md->v_sz[li], S, kv_len, hq, hkv, hd,
+                                    scale, att);
+        } else {
+            orc_kv_write(k, S, hkv, hd, cache_len, md->k_cache[li]);
+            orc_kv_write(v, S, hkv, hd, cache_len, md->v_cache[li]);
+            orc_flash_attention(q, md->k_cache[li], md->v_cache[li], S, kv_len, hq, hkv, hd, scale, att);
+        }
         orc_gemv(att, S, inner, md->w_o[li], md->s_o[li], md->quant, md->group, 0, H, ao);
         for (int64_t i = 0; i < (int64_t)S * H; i++) ao[i] = ao[i] + skip[i];     /* AddResidual */
         memcpy(skip, ao, sizeof(float) * S * H);

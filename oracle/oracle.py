@@ -50,6 +50,9 @@ def lib():
         _lib.orc_kv_write.argtypes = [P, C.c_int, C.c_int, C.c_int, C.c_int, P]
         _lib.orc_flash_attention.argtypes = [P, P, P, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int,
                                              C.c_float, P]
+        _lib.orc_kv_write_int8.argtypes = [P, C.c_int, C.c_int, C.c_int, C.c_int, P, P]
+        _lib.orc_flash_attention_kv8.argtypes = [P, P, P, P, P, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int,
+                                                 C.c_float, P]
         _lib.orc_argmax.restype = C.c_int
         _lib.orc_argmax.argtypes = [P, C.c_int]
         _lib.orc_forward.restype = C.c_int
@@ -151,6 +154,36 @@ def flash_attention(q: np.ndarray, k_cache: np.ndarray, v_cache: np.ndarray, kv_
     return out
 
 
+def kv_write_int8(kv_new: np.ndarray, hkv: int, hd: int):
+    """WriteCacheFull, INT8 variant, of fp32 rows [seq, hkv, hd] into a fresh cache:
+    returns (uint8 [seq, hkv, hd], uint32 (fp16 scale | fp16 zp << 16) [seq, hkv])."""
+    x = np.ascontiguousarray(kv_new, dtype=np.float32)
+    seq = x.size // (hkv * hd)
+    q = np.zeros((seq, hkv, hd), np.uint8)
+    sz = np.zeros((seq, hkv), np.uint32)
+    lib().orc_kv_write_int8(_p(x), seq, hkv, hd, 0, _p(q), _p(sz))
+    return q, sz
+
+
+def kv8_dequant(q: np.ndarray, sz: np.ndarray) -> np.ndarray:
+    """kv_unpack8: (q - zp) * scale, fp16 scale and zp, fp32 result."""
+    scale = (sz & 0xFFFF).astype(np.uint16).view(np.float16).astype(np.float32)
+    zp = (sz >> 16).astype(np.uint16).view(np.float16).astype(np.float32)
+    return (q.astype(np.float32) - zp[..., None]) * scale[..., None]
+
+
+def flash_attention_kv8(q: np.ndarray, k8, ksz, v8, vsz, kv_len: int, hq: int, hkv: int, hd: int,
+                        scale: float) -> np.ndarray:
+    """FA-1 restatement over an INT8 cache (uint8 [pos, hkv, hd] + scale/zp words [pos, hkv])."""
+    q = np.ascontiguousarray(q, dtype=np.float32)
+    seq_q = q.size // (hq * hd)
+    out = np.empty((seq_q, hq, hd), np.float32)
+    lib().orc_flash_attention_kv8(_p(q), _p(np.ascontiguousarray(k8, np.uint8)), _p(np.ascontiguousarray(ksz, np.uint32)),
+                                  _p(np.ascontiguousarray(v8, np.uint8)), _p(np.ascontiguousarray(vsz, np.uint32)),
+                                  seq_q, kv_len, hq, hkv, hd, scale, _p(out))
+    return out
+
+
 def argmax(logits: np.ndarray) -> int:
     lg = np.ascontiguousarray(logits, dtype=np.float32)
     return int(lib().orc_argmax(_p(lg), lg.size))
@@ -200,19 +233,23 @@ class _OrcModel(C.Structure):
                 ("final_norm", C.c_void_p), ("embed", C.c_void_p), ("lm_head", C.c_void_p),
                 ("rope_cos", C.c_void_p), ("rope_sin", C.c_void_p),
                 ("k_cache", C.POINTER(C.c_void_p)), ("v_cache", C.POINTER(C.c_void_p)),
-                ("cache_len", C.c_int32)]
+                ("cache_len", C.c_int32), ("kv_quant", C.c_int32),
+                ("k_sz", C.POINTER(C.c_void_p)), ("v_sz", C.POINTER(C.c_void_p))]
 
 
 class OracleModel:
     """One sequence of the reference llama executor (MiniCPM5Model.Forward with
     use_cache = true) over host weights from :class:`tests.modelgen.ModelWeights`."""
 
-    def __init__(self, weights, capacity: int):
+    def __init__(self, weights, capacity: int, kv_int8: bool = False):
         cfg = weights.cfg
         self.cfg, self.w = cfg, weights
         L = cfg.layers
-        self.k_cache = [np.zeros((capacity, cfg.hkv, cfg.hd), np.uint16) for _ in range(L)]
-        self.v_cache = [np.zeros((capacity, cfg.hkv, cfg.hd), np.uint16) for _ in range(L)]
+        kvt = np.uint8 if kv_int8 else np.uint16
+        self.k_cache = [np.zeros((capacity, cfg.hkv, cfg.hd), kvt) for _ in range(L)]
+        self.v_cache = [np.zeros((capacity, cfg.hkv, cfg.hd), kvt) for _ in range(L)]
+        self.k_sz = [np.zeros((capacity, cfg.hkv), np.uint32) for _ in range(L)]
+        self.v_sz = [np.zeros((capacity, cfg.hkv), np.uint32) for _ in range(L)]
         self.rope_cos, self.rope_sin = rope_table(capacity, cfg.hd, cfg.theta)
 
         def arr(lst):
@@ -237,9 +274,13 @@ class OracleModel:
         m.rope_cos = _p(self.rope_cos).value
         m.rope_sin = _p(self.rope_sin).value
         kc, vc = arr(self.k_cache), arr(self.v_cache)
-        self._keep += [kc, vc]
+        ks, vs = arr(self.k_sz), arr(self.v_sz)
+        self._keep += [kc, vc, ks, vs]
         m.k_cache = C.cast(kc, C.POINTER(C.c_void_p))
         m.v_cache = C.cast(vc, C.POINTER(C.c_void_p))
+        m.k_sz = C.cast(ks, C.POINTER(C.c_void_p))
+        m.v_sz = C.cast(vs, C.POINTER(C.c_void_p))
+        m.kv_quant = 2 if kv_int8 else 1
         m.cache_len = 0
         self.m = m
 

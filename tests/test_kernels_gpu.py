@@ -317,6 +317,93 @@ def test_rmsnorm_matches_oracle():
     assert relerr(y.cpu().numpy(), ref) < 1e-6
 
 
+# ------------------------------------------------------------- INT8 KV cache
+def _kv_rows(rng, n, hkv, hd):
+    """Rows with the reference's edge cases: constant (scale floor), all positive (zp 0),
+    all negative (zp clamped to 255, values clipped), half-step ties, a wide range."""
+    x = (rng.standard_normal((n, hkv, hd)) * 2).astype(np.float32)
+    x[0, 0, :] = 0.25
+    x[1 % n, hkv - 1, :] = np.abs(x[1 % n, hkv - 1, :]) + 1.0
+    x[2 % n, 0, :] = -np.abs(x[2 % n, 0, :]) - 1.0
+    x[3 % n, 0, :] = (np.arange(hd) - hd / 2).astype(np.float32) * (1.0 / 255.0)
+    x[4 % n, hkv - 1, ::3] *= 100.0
+    return x
+
+
+@pytest.mark.parametrize("hd", [64, 128])
+def test_kv_write_int8_bit_exact(hd):
+    """WriteCacheFull's INT8 variant (G3CS:300-380): the cache bytes and the
+    (fp16 scale | fp16 zp << 16) words equal the oracle's, bit for bit."""
+    rng = np.random.default_rng(hd)
+    hkv, n, cap, c0 = 8, 300, 512, 17
+    x = _kv_rows(rng, n, hkv, hd)
+    q_ref, sz_ref = orc.kv_write_int8(x, hkv, hd)
+    cache = torch.zeros((cap, hkv, hd), dtype=torch.uint8, device="cuda")
+    sz = torch.zeros((cap, hkv), dtype=torch.int32, device="cuda")
+    xd = dev(x)
+    _lib.call("du_kv_write_int8", ptr(xd), n, hkv, hd, c0, ptr(cache), ptr(sz), None)
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(cache.cpu().numpy()[c0:c0 + n], q_ref)
+    np.testing.assert_array_equal(sz.cpu().numpy().view(np.uint32)[c0:c0 + n], sz_ref)
+    assert not cache.cpu().numpy()[:c0].any() and not cache.cpu().numpy()[c0 + n:].any()
+
+
+def _kv8_cache(rng, B, cap, hkv, hd):
+    x = (rng.standard_normal((B, cap, hkv, hd))).astype(np.float32)
+    q8 = np.empty((B, cap, hkv, hd), np.uint8)
+    sz = np.empty((B, cap, hkv), np.uint32)
+    for b in range(B):
+        q8[b], sz[b] = orc.kv_write_int8(x[b], hkv, hd)
+    return q8, sz
+
+
+@pytest.mark.parametrize("hq,hkv,hd", [(32, 8, 128), (32, 4, 64), (8, 8, 64)])
+def test_flash_decode_kv8_matches_oracle(hq, hkv, hd):
+    """Flash-decode over the INT8 cache (KV_READ_K / KV_READ_V of KV_INT8) against the
+    oracle's FlashAttention on the same bytes, ragged lengths."""
+    rng = np.random.default_rng(hq + hd)
+    B, cap = 3, 700
+    lens = np.array([1, 129, 700], np.int32)
+    q = rng.standard_normal((B, hq, hd)).astype(np.float32)
+    k8, ksz = _kv8_cache(rng, B, cap, hkv, hd)
+    v8, vsz = _kv8_cache(rng, B, cap, hkv, hd)
+    scale = 1.0 / np.sqrt(hd)
+    out = torch.empty((B, hq, hd), dtype=torch.float32, device="cuda")
+    args = [dev(a) for a in (q, k8, ksz.view(np.int32), v8, vsz.view(np.int32), lens)]   # kept alive until the sync
+    _lib.call("du_flash_decode_kv8", ptr(out), *[ptr(a) for a in args], B, hq, hkv, hd, cap, C.c_float(scale), None)
+    torch.cuda.synchronize()
+    got = out.cpu().numpy()
+    for b in range(B):
+        ref = orc.flash_attention_kv8(q[b:b + 1], k8[b], ksz[b], v8[b], vsz[b], int(lens[b]), hq, hkv, hd, scale)[0]
+        assert relerr(got[b], ref) < ATTN_TOL, b
+
+
+@pytest.mark.parametrize("ctx,B", [(2048, 1), (8192, 8), (32768, 1)])
+def test_flash_decode_kv8_config3(ctx, B):
+    """BASELINE config 3 shapes over the INT8 cache; the oracle checks the first and last
+    sequence."""
+    hq, hkv, hd = 32, 8, 128
+    rng = np.random.default_rng(ctx + B)
+    q = rng.standard_normal((B, hq, hd)).astype(np.float32)
+    k8 = rng.integers(0, 256, (B, ctx, hkv, hd), dtype=np.uint8)
+    v8 = rng.integers(0, 256, (B, ctx, hkv, hd), dtype=np.uint8)
+    def words(n):
+        sc = (rng.uniform(0.002, 0.02, n)).astype(np.float16).view(np.uint16).astype(np.uint32)
+        zp = rng.integers(0, 256, n).astype(np.float16).view(np.uint16).astype(np.uint32)
+        return (sc | (zp << 16)).reshape(B, ctx, hkv)
+    ksz, vsz = words(B * ctx * hkv), words(B * ctx * hkv)
+    lens = np.full(B, ctx, np.int32)
+    out = torch.empty((B, hq, hd), dtype=torch.float32, device="cuda")
+    args = [dev(a) for a in (q, k8, ksz.view(np.int32), v8, vsz.view(np.int32), lens)]   # kept alive until the sync
+    _lib.call("du_flash_decode_kv8", ptr(out), *[ptr(a) for a in args], B, hq, hkv, hd, ctx,
+              C.c_float(1.0 / np.sqrt(hd)), None)
+    torch.cuda.synchronize()
+    got = out.cpu().numpy()
+    for b in sorted({0, B - 1}):
+        ref = orc.flash_attention_kv8(q[b:b + 1], k8[b], ksz[b], v8[b], vsz[b], ctx, hq, hkv, hd, 1.0 / np.sqrt(hd))[0]
+        assert relerr(got[b], ref) < ATTN_TOL, b
+
+
 # --------------------------------------------------------------- sampler
 SAMPLER_SETTINGS = [(0.0, 0, 1.0, 0.0),      # greedy (ArgMax)
                     (1.0, 40, 0.9, 0.0),     # top-k + top-p

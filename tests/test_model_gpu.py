@@ -9,7 +9,7 @@ import numpy as np
 import pytest
 import torch
 
-from deepunity_b200 import DUError, LlamaForCausalLM, LLMQuant, _lib
+from deepunity_b200 import DUError, KVQuant, LlamaForCausalLM, LLMQuant, _lib
 from oracle import oracle as orc
 from tests.modelgen import C4, C5_SLICE, MID, SMALL, ModelWeights, TestConfig
 
@@ -28,10 +28,11 @@ def relerr(a, b):
     return float(np.max(np.abs(a - b)) / max(np.max(np.abs(b)), 1e-30))
 
 
-def build(cfg: TestConfig, seed=0, cap=128, max_batch=1, flags=0):
+def build(cfg: TestConfig, seed=0, cap=128, max_batch=1, flags=0, kv_quant=KVQuant.FP16):
     w = ModelWeights(cfg, seed=seed)
     q = {"int8": LLMQuant.INT8, "int4": LLMQuant.INT4, "fp16": LLMQuant.FP16}[cfg.quant]
-    m = LlamaForCausalLM(cfg.du_kwargs(), q, max_context_length=cap, max_batch=max_batch, seed=None, flags=flags)
+    m = LlamaForCausalLM(cfg.du_kwargs(), q, kv_quant=kv_quant, max_context_length=cap, max_batch=max_batch, seed=None,
+                         flags=flags)
     w.load_into(m)
     return w, m
 
@@ -253,4 +254,64 @@ def test_sampled_decode_matches_oracle(setting):
         toks.append(int(m.decode_step_sample([toks[-1]], T, k, p, mp, [seed])[0]))
         rtoks.append(orc.sample(om.forward([rtoks[-1]]), T, k, p, mp, seed))
     assert toks == rtoks
+    m.Release()
+
+
+KV8_LOGIT_TOL = 5e-3
+
+
+def _near_tie(logits, tol=2e-3):
+    """The two largest logits lie within tol * max|logit| of each other."""
+    top = np.sort(logits)[-2:]
+    return float(top[1] - top[0]) <= tol * float(np.max(np.abs(logits)))
+
+
+@pytest.mark.parametrize("cfg", [SMALL, TestConfig(256, 512, 2, 4, 2, 128, 1024, quant="int4", group=128)],
+                         ids=lambda c: f"{c.quant}-hd{c.hd}")
+def test_int8_kv_cache_teacher_forced_64_matches_oracle(cfg):
+    """KVQuant.INT8 (WriteCacheFull KV_INT8 + KV_READ_K / KV_READ_V): a 24-token prefill then
+    64 teacher-forced decode steps (both sides are fed the oracle's greedy ids).  Every
+    step's logits within 5e-3 and the greedy id equal unless the oracle's top two logits
+    are a near-tie.  The 8-bit quantizer rounds each K / V value to its row's step
+    (range / 255); fp32 values that differ by an ulp can round to neighbouring bytes, so
+    the two caches may differ by one step in a few elements: that widens the logit gate
+    from 1e-3 and makes free-running greedy comparisons flip at near-ties."""
+    w, m = build(cfg, cap=128, kv_quant=KVQuant.INT8)
+    om = orc.OracleModel(w, capacity=128, kv_int8=True)
+    prompt = np.random.default_rng(11).integers(0, cfg.vocab, 24).astype(np.int32)
+    logits, nxt = m.forward(prompt[None, :])
+    ref = om.forward(prompt)
+    assert relerr(logits[0], ref) < KV8_LOGIT_TOL
+    tok = orc.argmax(ref)
+    assert int(nxt[0]) == tok or _near_tie(ref)
+    for step in range(64):
+        got_id = int(m.decode_step([tok])[0])
+        r = om.forward([tok])
+        assert relerr(m.read_logits(1)[0], r) < KV8_LOGIT_TOL, step
+        tok = orc.argmax(r)
+        assert got_id == tok or _near_tie(r), step
+    assert m.cache_len() == 24 + 64
+    m.Release()
+
+
+def test_int8_kv_cache_batched():
+    """Three sequences decoding together over the INT8 cache, teacher-forced, each against
+    its own oracle."""
+    cfg = SMALL
+    w, m = build(cfg, cap=96, max_batch=3, kv_quant=KVQuant.INT8)
+    prompts = np.random.default_rng(12).integers(0, cfg.vocab, (3, 10)).astype(np.int32)
+    logits, nxt = m.forward(prompts)
+    oms = [orc.OracleModel(w, capacity=96, kv_int8=True) for _ in range(3)]
+    refs = [oms[i].forward(prompts[i]) for i in range(3)]
+    for i in range(3):
+        assert relerr(logits[i], refs[i]) < KV8_LOGIT_TOL
+    cur = [orc.argmax(r) for r in refs]
+    for step in range(24):
+        got = m.decode_step(cur)
+        lg = m.read_logits(3)
+        refs = [oms[i].forward([cur[i]]) for i in range(3)]
+        for i in range(3):
+            assert relerr(lg[i], refs[i]) < KV8_LOGIT_TOL, (step, i)
+            assert int(got[i]) == orc.argmax(refs[i]) or _near_tie(refs[i]), (step, i)
+        cur = [orc.argmax(r) for r in refs]
     m.Release()

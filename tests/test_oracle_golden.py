@@ -120,3 +120,36 @@ def test_gemv_matches_float64(oracle, qg):
         y = oracle.gemv(x, wq, s, quant, w.shape[0], group or 32)
         ref = x.astype(np.float64) @ deq.astype(np.float64).T
         np.testing.assert_allclose(y, ref, rtol=1e-5, atol=1e-5)
+
+
+def _kv_int8_numpy(x):
+    """Independent numpy restatement of WriteCacheFull's INT8 variant (G3CS:300-380) in
+    IEEE fp32: the oracle's C version must agree with it bit for bit."""
+    x = x.astype(np.float32)
+    mn, mx = x.min(axis=-1), x.max(axis=-1)
+    scale = ((mx - mn) / np.float32(255.0)).astype(np.float32)
+    scale = np.where(scale < np.float32(1e-9), np.float32(1e-9), scale).astype(np.float32)
+    zp = np.clip(np.rint((-mn / scale).astype(np.float32)), 0, 255).astype(np.float32)
+    inv = (np.float32(1.0) / scale).astype(np.float32)
+    q = np.clip(np.rint((x * inv[..., None]).astype(np.float32)) + zp[..., None], 0, 255).astype(np.uint8)
+    sz = (scale.astype(np.float16).view(np.uint16).astype(np.uint32)
+          | (zp.astype(np.float16).view(np.uint16).astype(np.uint32) << 16))
+    return q, sz
+
+
+def test_kv_write_int8_oracle_matches_numpy_restatement(oracle):
+    rng = np.random.default_rng(5)
+    x = (rng.standard_normal((40, 4, 64)) * 3).astype(np.float32)
+    x[0, 0] = 0.5                                        # constant row: scale floor, fp16 scale 0
+    x[1, 1] = np.abs(x[1, 1]) + 2                        # all positive: zp 0
+    x[2, 2] = -np.abs(x[2, 2]) - 2                       # all negative: zp clamps to 255
+    x[3, 3] = (np.arange(64) - 32).astype(np.float32) / 255.0
+    q, sz = oracle.kv_write_int8(x, 4, 64)
+    qn, szn = _kv_int8_numpy(x)
+    np.testing.assert_array_equal(q, qn)
+    np.testing.assert_array_equal(sz, szn)
+    # kv_unpack8 round trip: within half a step for rows whose range holds 0
+    d = oracle.kv8_dequant(q, sz)
+    ok = (x.min(-1) <= 0) & (x.max(-1) >= 0) & (np.ptp(x, axis=-1) > 1e-3)
+    step = (sz & 0xFFFF).astype(np.uint16).view(np.float16).astype(np.float32)
+    assert np.all(np.abs(d - x)[ok] <= (step[ok][:, None] * 0.5 + np.abs(x[ok]) * 2e-3 + 1e-6))
