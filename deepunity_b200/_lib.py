@@ -12,7 +12,7 @@ import os
 HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "libdeepunity_cuda.so")
 
-DU_OK, DU_EINVAL, DU_ECUDA, DU_ENOMEM, DU_EBUSY, DU_ENCCL, DU_ENOTFOUND, DU_ESTATE = range(8)
+DU_OK, DU_EINVAL, DU_ECUDA, DU_ENOMEM, DU_EBUSY, DU_ENCCL, DU_ENOTFOUND, DU_ESTATE, DU_EIO = range(9)
 QUANT_FP16, QUANT_INT8, QUANT_INT4 = 0, 1, 2
 DTYPE_F32, DTYPE_F16, DTYPE_BF16 = 0, 1, 2
 FLAG_NO_PERSISTENT = 1
@@ -67,6 +67,13 @@ SIGNATURES = {
     "du_gemv_f16": (I, [P, P, I, P, I, I, I, P]),
     "du_flash_decode": (I, [P, P, P, P, P, I, I, I, I, I, F, P]),
     "du_kv_write_int8": (I, [P, I, I, I, I, P, P, P]),
+    "du_model_load_folder": (I, [P, C.c_char_p, C.POINTER(I)]),
+    "du_model_save_cache": (I, [P, I, C.c_char_p]),
+    "du_model_load_cache": (I, [P, I, C.c_char_p, C.POINTER(I)]),
+    "du_model_save_kv": (I, [P, I, C.c_char_p, U64, P, I]),
+    "du_model_load_kv": (I, [P, I, C.c_char_p, U64, C.POINTER(I)]),
+    "du_kv_file_peek": (I, [C.c_char_p, C.POINTER(I), C.POINTER(U64), C.POINTER(I), C.POINTER(I), C.POINTER(I), P, I,
+                            C.POINTER(I)]),
     "du_flash_decode_kv8": (I, [P, P, P, P, P, P, P, I, I, I, I, I, F, P]),
     "du_flash_decode_noalloc": (I, [P, P, P, P, P, I, I, I, I, I, F, P]),
     "du_quantize_int8": (I, [P, I64, I64, P, P, P]),

@@ -16,7 +16,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(HERE, "csrc")
 LIB = os.path.join(HERE, "libdeepunity_cuda.so")
 SOURCES = ["capi.cu", "gemv.cu", "gemm.cu", "tgemv.cu", "attention.cu", "elementwise.cu", "model.cu", "noalloc.cu",
-           "decode_step.cu", "tp_comm.cu", "sampler.cu"]
+           "decode_step.cu", "tp_comm.cu", "sampler.cu", "snapshot.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

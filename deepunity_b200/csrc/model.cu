@@ -29,86 +29,7 @@
 #include "nccl_shim.h"
 #include "step_plan.h"
 #include "tp_comm.h"
-
-namespace du {
-
-struct Layer {
-    uint8_t *w_qkv = nullptr; __half *s_qkv = nullptr;    // [(hq+2hkv)*hd local rows, H]
-    uint8_t *w_o = nullptr;   __half *s_o = nullptr;      // [H, hq_l*hd]
-    uint8_t *w_gu = nullptr;  __half *s_gu = nullptr;     // gate|up [2*I_l, H]
-    uint8_t *w_d = nullptr;   __half *s_d = nullptr;      // [H, I_l]
-    __half *ln1 = nullptr, *ln2 = nullptr;                // gamma - 1, [H]
-};
-
-struct Graph {
-    cudaGraph_t g = nullptr;
-    cudaGraphExec_t exec = nullptr;
-    StepStage *d_stages = nullptr;   // stage list of the persistent decode-step kernel (device)
-    bool persistent = false;
-};
-
-}  // namespace du
-
-struct du_model {
-    du_model_config cfg;
-    int device = 0;
-    cudaStream_t stream = nullptr;
-    int H, I, L, hq, hkv, hd, V, tp, rank;
-    int hq_l, hkv_l, I_l, V_l, qkv_rows;
-    int quant, group, cap, maxb;
-    int max_tokens;                         // tokens per forward chunk (prefill)
-    std::vector<du::Layer> layers;
-    std::vector<void *> allocs;
-    __half *final_norm = nullptr, *embed = nullptr, *lm_head = nullptr;
-    __half *rope_cos = nullptr, *rope_sin = nullptr;
-    __half *k_cache = nullptr, *v_cache = nullptr;      // [L][maxb][cap][hkv_l][hd]
-    size_t kv_layer_elems = 0;
-    bool kv8 = false;                                    // INT8 cache instead of the fp16 one:
-    uint8_t *k8 = nullptr, *v8 = nullptr;                // [L][maxb][cap][hkv_l][hd]
-    uint32_t *ksz = nullptr, *vsz = nullptr;             // [L][maxb][cap][hkv_l] scale | zp << 16
-    float *kv_stage = nullptr;                           // QKV epilogue's fp32 K / V rows [T][2][hkv_l][hd]
-    // device state
-    int *d_cache_len = nullptr;             // [maxb]
-    int *d_ids = nullptr;                   // [max_tokens] input ids
-    int *d_next = nullptr;                  // [max_tokens] greedy ids
-    int *d_hist = nullptr;                  // [maxb][cap] greedy id chosen at each input position
-    int *d_pos = nullptr, *d_seq = nullptr, *d_kvlen = nullptr;   // per-token (prefill)
-    float *x_res = nullptr;                 // [max_tokens][H]
-    float *part = nullptr;                  // [max_tokens][H] TP partial sums
-    float *q = nullptr;                     // [max_tokens][hq_l*hd]
-    float *att = nullptr;                   // [max_tokens][hq_l*hd]
-    float *inter = nullptr;                 // [max_tokens][I_l]
-    float *logits = nullptr;                // [maxb][V_l] local shard
-    float *logits_all = nullptr;            // [tp][maxb][V_l] (TP gather)
-    float *am_val = nullptr; int *am_idx = nullptr;   // [maxb][am_parts]
-    float *best_val = nullptr; int *best_idx = nullptr;  // TP: [maxb] local, [tp][maxb] gathered
-    float *gbest_val = nullptr; int *gbest_idx = nullptr;
-    int am_parts = 0;
-    du::GemmScratch gm;                     // staged activations of the tensor-core GEMM (M >= 16 rows)
-    float *fd_scratch = nullptr; unsigned *fd_counters = nullptr;
-    int fd_nsplit_decode = 1;
-    size_t fd_scratch_fl = 0;
-    int *h_pin_ids = nullptr, *h_pin_next = nullptr;
-    unsigned *d_barrier = nullptr;          // grid-barrier counter of the persistent step kernel
-    int *d_err = nullptr;                   // its error word (barrier timeout)
-    int *h_pin_err = nullptr;
-    unsigned long long *d_stamps = nullptr; // per-stage timestamps of the last persistent step
-    int stamp_stages = 0;                   // stages of the step that wrote them
-    std::vector<int> h_cache_len;
-    std::map<int, du::Graph> graphs;        // greedy decode step per batch size
-    std::map<int, du::Graph> sgraphs;       // sampling decode step per batch size
-    int32_t *d_seeds = nullptr;             // [maxb] sampler seeds of the next step
-    float *d_sparams = nullptr;             // (temperature, top_k, top_p, min_p) of the next sampling step
-    int32_t *h_pin_seeds = nullptr;         // pinned staging: [maxb] seeds then 4 floats of settings
-    int last_batch = 0, last_rows = 0;      // rows of logits written by the last call
-    std::atomic<int> busy{0};
-    // TP
-    ncclComm_t comm = nullptr;
-    bool tp_ready = false;
-    du::TpComm tpc;                         // peer-memory allreduce of decode-sized reductions
-    int nccl_timeout_ms = 60000;
-    uint64_t weight_bytes = 0;
-};
+#include "model_state.h"
 
 namespace du {
 
@@ -400,7 +321,7 @@ static int tensor_kind_of(const char *stem)
 }
 
 // Places one IMP tensor (weights, or its scales) into the sharded device layout.
-static int place_tensor(du_model *m, const char *name, const void *src, size_t bytes, cudaMemcpyKind kind)
+int place_tensor(du_model *m, const char *name, const void *src, size_t bytes, cudaMemcpyKind kind)
 {
     cudaStream_t st = m->stream;
     const int H = m->H, hd = m->hd, r = m->rank;
@@ -825,28 +746,7 @@ static int enqueue_head(du_model *m, const StepIO &io)
 }
 
 // One forward per call at a time per handle (LLM Busy guard, LLM.cs:393-406).
-struct CallGuard {
-    du_model *m;
-    bool ok;
-    explicit CallGuard(du_model *mm) : m(mm), ok(false)
-    {
-        if (m && m->busy.exchange(1) == 0) {
-            ok = true;
-            cudaSetDevice(m->device);
-        }
-    }
-    ~CallGuard()
-    {
-        if (ok) m->busy.store(0);
-    }
-};
-
-#define DU_GUARD(m)                                                                   \
-    if (!(m)) return fail(DU_EINVAL, "null model handle");                            \
-    CallGuard _guard(m);                                                              \
-    if (!_guard.ok) return fail(DU_EBUSY, "model is busy with another call")
-
-static int sync_cache_len(du_model *m)
+int sync_cache_len(du_model *m)
 {
     DU_CUDA_TRY(cudaMemcpyAsync(m->d_cache_len, m->h_cache_len.data(), sizeof(int) * m->maxb, cudaMemcpyHostToDevice,
                                 m->stream));

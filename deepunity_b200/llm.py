@@ -115,14 +115,68 @@ class LlamaForCausalLM(LLM):
         a = np.ascontiguousarray(data)
         _lib.call("du_model_load_tensor", self._h, name.encode(), a.ctypes.data_as(C.c_void_p), a.nbytes)
 
-    def load_params(self, folder: str):
-        """Streams an import_params.py export folder (MiniCPM5Weights' role)."""
-        for root, _, files in os.walk(folder):
-            for f in sorted(files):
-                if not f.endswith(".bin"):
-                    continue
-                rel = os.path.relpath(os.path.join(root, f), folder).replace(os.sep, "/")
-                self.load_tensor(rel, np.fromfile(os.path.join(root, f), dtype=np.uint8))
+    def load_params(self, folder: str) -> int:
+        """Loads an import_params.py export folder (MiniCPM5Weights' role) with the native
+        loader: every *.bin under `folder`, memory-mapped, placed by its relative name.
+        Returns the number of tensors loaded."""
+        n = C.c_int(0)
+        _lib.call("du_model_load_folder", self._h, os.fsencode(folder), C.byref(n))
+        return n.value
+
+    # ---------------------------------------------------------------- KV snapshots
+    def SaveCache(self, folder: str, seq: int = 0):
+        """MiniCPM5Cache.SaveAsync (M5/MiniCPM5Cache.cs:78-150): the cached prefix of
+        sequence `seq` as an "M5KV" v1 folder (fp16 cache only)."""
+        _lib.call("du_model_save_cache", self._h, seq, os.fsencode(folder))
+
+    def TryLoadCache(self, folder: str, seq: int = 0) -> bool:
+        """MiniCPM5Cache.TryLoadAsync (M5/MiniCPM5Cache.cs:153-200): True when the folder
+        matched this model and its rows are now the cached prefix of sequence `seq`."""
+        ok = C.c_int(0)
+        _lib.call("du_model_load_cache", self._h, seq, os.fsencode(folder), C.byref(ok))
+        return bool(ok.value)
+
+    def SaveConversationKV(self, path: str, context_hash: int, extra: bytes = b"", seq: int = 0):
+        """LLM.SaveConversationKV (LLMB/LLM.cs:599-607) in the version-2 one-file layout
+        (fp16 or INT8 cache), tagged with the caller's context hash and opaque state."""
+        buf = C.create_string_buffer(bytes(extra), max(len(extra), 1))
+        _lib.call("du_model_save_kv", self._h, seq, os.fsencode(path), C.c_uint64(context_hash & (2 ** 64 - 1)),
+                  buf, len(extra))
+
+    @staticmethod
+    def PeekConversationKV(path: str):
+        """(context_hash, kv_format, tokens, layers, extra) of a saved conversation, or None."""
+        valid, h, fmt, tok, nl, xl = C.c_int(0), C.c_uint64(0), C.c_int(0), C.c_int(0), C.c_int(0), C.c_int(0)
+        _lib.call("du_kv_file_peek", os.fsencode(path), C.byref(valid), C.byref(h), C.byref(fmt), C.byref(tok),
+                  C.byref(nl), None, 0, C.byref(xl))
+        if not valid.value:
+            return None
+        extra = C.create_string_buffer(max(xl.value, 1))
+        _lib.call("du_kv_file_peek", os.fsencode(path), C.byref(valid), None, None, None, None, extra, xl.value,
+                  C.byref(xl))
+        return int(h.value), int(fmt.value), int(tok.value), int(nl.value), extra.raw[:xl.value]
+
+    def TryRestoreConversationKV(self, path: str, context_hash: int, seq: int = 0,
+                                 accept_extra: Optional[Callable[[bytes], bool]] = None) -> bool:
+        """LLM.TryRestoreConversationKV (LLMB/LLM.cs:622-642): False on any mismatch (hash,
+        cache format, layout, sizes) or when `accept_extra` vetoes the saved caller state;
+        nothing reaches the device in those cases."""
+        head = self.PeekConversationKV(path)
+        if head is None or head[0] != (context_hash & (2 ** 64 - 1)):
+            return False
+        if accept_extra is not None and not accept_extra(head[4]):
+            return False
+        ok = C.c_int(0)
+        _lib.call("du_model_load_kv", self._h, seq, os.fsencode(path), C.c_uint64(context_hash & (2 ** 64 - 1)),
+                  C.byref(ok))
+        return bool(ok.value)
+
+    @staticmethod
+    def DeleteConversationKV(path: str):
+        """LLM.DeleteConversationKV (LLMB/LLM.cs:611-616)."""
+        for p in (path, path + ".tmp"):
+            if os.path.exists(p):
+                os.remove(p)
 
     # ---------------------------------------------------------------- inference
     @property

@@ -38,7 +38,8 @@ enum {
     DU_EBUSY = 4,      /* handle already inside a call (reference Busy guard) */
     DU_ENCCL = 5,      /* NCCL error or collective timeout */
     DU_ENOTFOUND = 6,  /* unknown tensor name */
-    DU_ESTATE = 7      /* call not valid in the current state */
+    DU_ESTATE = 7,     /* call not valid in the current state */
+    DU_EIO = 8         /* file or directory error */
 };
 
 /* Weight formats of IMP (LLMQuant, LLMB/LLM.cs:15-59). */
@@ -119,6 +120,12 @@ DU_API int du_model_load_tensor(du_model *m, const char *name, const void *host,
  * ~N(0, std) quantized with the IMP formulas, embedding / lm_head fp16
  * ~N(0, std), norm gammas 1 (stored as gamma - 1 = 0, IMP:314-315).  No
  * reference counterpart: stands in for a checkpoint when none exists. */
+/* Loads every "*.bin" tensor of an import_params.py export folder (IMP's file
+ * layout, see du_model_load_tensor), memory-mapped and placed by its path
+ * relative to `folder`; replaces MiniCPM5Weights' upload pump (M5W:315-380).
+ * n_files (optional) receives the number of tensors loaded. */
+DU_API int du_model_load_folder(du_model *m, const char *folder, int *n_files);
+
 DU_API int du_model_init_random(du_model *m, uint64_t seed, float std);
 
 /* Writes a 128-byte NCCL unique id (call on rank 0, share with the others). */
@@ -195,6 +202,31 @@ DU_API int du_read_logits(du_model *m, float *host_out, int batch);
 
 /* MiniCPM5Model.ResetCache (M5M:714) / CachedTokenCount (M5C:16-22). */
 DU_API int du_reset_cache(du_model *m);
+
+/* KV snapshots of sequence `seq` (system-prompt / conversation reuse).
+ * du_model_save_cache / du_model_load_cache: MiniCPM5Cache's "M5KV" version-1
+ * folder (M5C:31-32, 78-200): meta.bin (int32 magic 0x4D354B56, version 1,
+ * layers, kv heads, head_dim, tokens) and k_cache_layer_<i>.bin /
+ * v_cache_layer_<i>.bin (tokens x kv heads x head_dim fp16, position-major).
+ * Loading converts as the reference reader does (fp16 subnormals -> 0) and sets
+ * the sequence's cache length; *loaded = 0 (not an error) on any mismatch, a
+ * missing or short file, or with the INT8 cache (not kept in this format; its
+ * save returns DU_ESTATE).  Nothing cached: the save writes nothing. */
+DU_API int du_model_save_cache(du_model *m, int seq, const char *folder);
+DU_API int du_model_load_cache(du_model *m, int seq, const char *folder, int *loaded);
+/* One-file snapshot with the reference's version-2 prompt-cache layout
+ * (Qwen3_5Cache.cs:149-170) for all-full-attention layers: magic 'LMKV',
+ * version 2, uint64 context hash, uint8 kv format (DU_KV_*), tokens, layers,
+ * caller bytes (`extra`), then per layer the K and V rows (+ the INT8 scale /
+ * zero-point words).  Written to <path>.tmp and renamed.  The load checks hash,
+ * format, layer count and every blob size before uploading; *loaded = 0 on any
+ * mismatch.  du_kv_file_peek reads the header (and the caller bytes when
+ * extra_cap suffices) without a model, so a caller can veto a restore first. */
+DU_API int du_model_save_kv(du_model *m, int seq, const char *path, uint64_t context_hash, const void *extra,
+                            int extra_len);
+DU_API int du_model_load_kv(du_model *m, int seq, const char *path, uint64_t expected_hash, int *loaded);
+DU_API int du_kv_file_peek(const char *path, int *valid, uint64_t *context_hash, int *kv_format, int *tokens,
+                           int *layers, void *extra_out, int extra_cap, int *extra_len);
 DU_API int du_cache_len(du_model *m, int seq, int *out);
 /* Model stream (cudaStream_t) for callers that chain their own work. */
 DU_API int du_model_stream(du_model *m, void **stream_out);
