@@ -17,6 +17,7 @@ QUANT_FP16, QUANT_INT8, QUANT_INT4 = 0, 1, 2
 DTYPE_F32, DTYPE_F16, DTYPE_BF16 = 0, 1, 2
 FLAG_NO_PERSISTENT = 1
 FLAG_PERSISTENT = 2
+ARCH_QK_NORM, ARCH_SANDWICH, ARCH_GELU = 1, 2, 4
 
 
 class DUError(RuntimeError):
@@ -33,7 +34,9 @@ class ModelConfig(C.Structure):
                 ("embed_scale", C.c_float), ("quant", C.c_int32), ("group_size", C.c_int32),
                 ("kv_capacity", C.c_int32), ("max_batch", C.c_int32), ("tp_rank", C.c_int32),
                 ("tp_size", C.c_int32), ("tie_embedding", C.c_int32), ("flags", C.c_int32),
-                ("kv_quant", C.c_int32), ("reserved", C.c_int32 * 3)]
+                ("kv_quant", C.c_int32), ("arch_flags", C.c_int32), ("sliding_window", C.c_int32),
+                ("sliding_pattern", C.c_int32), ("rope_theta_local", C.c_float), ("attn_scale", C.c_float),
+                ("reserved", C.c_int32 * 2)]
 
 
 # name -> (restype, argtypes); every symbol of include/deepunity_cuda.h
@@ -67,6 +70,7 @@ SIGNATURES = {
     "du_gemv_f16": (I, [P, P, I, P, I, I, I, P]),
     "du_flash_decode": (I, [P, P, P, P, P, I, I, I, I, I, F, P]),
     "du_kv_write_int8": (I, [P, I, I, I, I, P, P, P]),
+    "du_flash_decode_window": (I, [P, P, P, P, P, I, I, I, I, I, F, I, P]),
     "du_model_load_folder": (I, [P, C.c_char_p, C.POINTER(I)]),
     "du_model_save_cache": (I, [P, I, C.c_char_p]),
     "du_model_load_cache": (I, [P, I, C.c_char_p, C.POINTER(I)]),

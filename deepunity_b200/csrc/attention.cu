@@ -207,7 +207,8 @@ static int fdc_dispatch(const FdParams &p, int G, int nq, cudaStream_t st, int n
 
 int launch_flash_decode_cluster(const float *q, const __half *kc, const __half *vc, const int *seq_of,
                                 const int *kv_len, int kv_len_add, int nq, int hq, int hkv, int hd, int cap,
-                                float scale, float *out, cudaStream_t st, int new_rows, const Kv8Cache *kv8)
+                                float scale, float *out, cudaStream_t st, int new_rows, const Kv8Cache *kv8,
+                                int window)
 {
     if (nq <= 0) return DU_OK;
     if (hkv <= 0 || hq % hkv != 0) return fail(DU_EINVAL, "flash_decode: hq must be a multiple of hkv");
@@ -217,15 +218,17 @@ int launch_flash_decode_cluster(const float *q, const __half *kc, const __half *
     p.q = q; p.k_cache = kc; p.v_cache = vc; p.seq_of = seq_of; p.kv_len = kv_len;
     p.kv_len_add = kv_len_add;
     p.hq = hq; p.hkv = hkv; p.cap = cap; p.scale = scale; p.out = out;
+    p.window = window;
     if (kv8 != nullptr) {
         p.k8 = kv8->k8; p.v8 = kv8->v8; p.ksz = kv8->ksz; p.vsz = kv8->vsz;
         if (hd == 128) return fdc_dispatch<128, true>(p, G, nq, st, new_rows);
         if (hd == 64) return fdc_dispatch<64, true>(p, G, nq, st, new_rows);
-        return fail(DU_EINVAL, "flash_decode: supported head_dim 64/128");
+        return fail(DU_EINVAL, "flash_decode: the INT8 cache supports head_dim 64/128");
     }
     if (hd == 128) return fdc_dispatch<128, false>(p, G, nq, st, new_rows);
     if (hd == 64) return fdc_dispatch<64, false>(p, G, nq, st, new_rows);
-    return fail(DU_EINVAL, "flash_decode: supported head_dim 64/128");
+    if (hd == 256) return fdc_dispatch<256, false>(p, G, nq, st, new_rows);
+    return fail(DU_EINVAL, "flash_decode: supported head_dim 64/128/256");
 }
 
 // WriteCacheFull, INT8 variant (Gemma3CS.compute:300-380; layout KVCache.hlsl:46-82):
@@ -245,32 +248,11 @@ __global__ void __launch_bounds__(256) kv_quant_int8_kernel(const float *stage, 
     const int epl = hd >> 5;                         // values per lane (hd = 32 .. 256)
     const float *x = stage + (size_t)w * hd + lane * epl;
     float v[8];
-    float mn = 3.0e38f, mx = -3.0e38f;
 #pragma unroll
-    for (int e = 0; e < 8; e++)
-        if (e < epl) {
-            v[e] = x[e];
-            mn = fminf(mn, v[e]);
-            mx = fmaxf(mx, v[e]);
-        }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-        mn = fminf(mn, __shfl_xor_sync(0xffffffffu, mn, o));
-        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-    }
-    float scale = (mx - mn) / 255.0f;
-    if (scale < 1e-9f) scale = 1e-9f;
-    const float zp = fminf(fmaxf(rintf(-mn / scale), 0.0f), 255.0f);
-    const float inv = 1.0f / scale;
+    for (int e = 0; e < 8; e++) v[e] = e < epl ? x[e] : 0.0f;
     const int seq = seq_of ? seq_of[m] : seq_off + m;
     const size_t row = ((size_t)seq * cap + (pos ? pos[m] : pos_base + m)) * hkv + h;
-    uint8_t *dst = (isv ? kv.v8 : kv.k8) + row * hd + lane * epl;
-#pragma unroll
-    for (int e = 0; e < 8; e++)
-        if (e < epl) dst[e] = (uint8_t)fminf(fmaxf(rintf(v[e] * inv) + zp, 0.0f), 255.0f);
-    if (lane == 0)
-        (isv ? kv.vsz : kv.ksz)[row] = (uint32_t)__half_as_ushort(__float2half_rn(scale)) |
-                                       ((uint32_t)__half_as_ushort(__float2half_rn(zp)) << 16);
+    kv8_store_row(v, epl, lane, (isv ? kv.v8 : kv.k8) + row * hd, (isv ? kv.vsz : kv.ksz) + row);
 }
 
 int launch_kv_quant_int8(const float *stage, int M, int nkv, int hkv, int hd, const int *pos, int pos_base,
@@ -318,7 +300,7 @@ int launch_flash_decode(const float *q, const __half *kc, const __half *vc, cons
     if (nq <= 0) return DU_OK;
     if (hkv <= 0 || hq % hkv != 0) return fail(DU_EINVAL, "flash_decode: hq must be a multiple of hkv");
     const int G = hq / hkv;
-    FdParams p;
+    FdParams p = {};
     p.q = q; p.k_cache = kc; p.v_cache = vc; p.seq_of = seq_of; p.kv_len = kv_len;
     p.kv_len_add = kv_len_add;
     p.hq = hq; p.hkv = hkv; p.cap = cap; p.scale = scale; p.out = out;

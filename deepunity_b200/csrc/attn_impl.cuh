@@ -30,6 +30,7 @@ struct FdParams {
     // kv head) words (fp16 scale | fp16 zero point << 16) [nseq][cap][hkv]
     const uint8_t *k8, *v8;
     const uint32_t *ksz, *vsz;
+    int window;                  // > 0: a query at position kv_len - 1 sees positions >= kv_len - 1 - window
 };
 
 // Shared memory of one unit: K/V tiles (dynamic, 4 * FD_TILE * (HD + 8) halves) + these.
@@ -140,18 +141,20 @@ __device__ __forceinline__ FdGeom fd_geom(const FdParams &p, int row, int kvh, i
     FdGeom g;
     const int seq = p.seq_of ? p.seq_of[row] : row;
     g.kv_len = p.kv_len[row] + p.kv_len_add;
-    const int T = (g.kv_len + FD_TILE - 1) / FD_TILE;
+    // sliding window (G3CS:673-686): the query (position kv_len - 1) sees lo .. kv_len - 1
+    const int lo = (p.window > 0 && g.kv_len - 1 > p.window) ? g.kv_len - 1 - p.window : 0;
+    const int T = (g.kv_len - lo + FD_TILE - 1) / FD_TILE;
     if (EVEN) {
         g.ns_act = nsplit;
-        g.start = (int)(((int64_t)split * T) / nsplit) * FD_TILE;
-        g.end = min((int)(((int64_t)(split + 1) * T) / nsplit) * FD_TILE, g.kv_len);
+        g.start = lo + (int)(((int64_t)split * T) / nsplit) * FD_TILE;
+        g.end = min(lo + (int)(((int64_t)(split + 1) * T) / nsplit) * FD_TILE, g.kv_len);
         if (g.end < g.start) g.end = g.start;
     } else {
         // splits actually used for this length: at least one tile each
         g.ns_act = max(1, min(nsplit, T));
-        int chunk = (g.kv_len + g.ns_act - 1) / g.ns_act;
+        int chunk = (g.kv_len - lo + g.ns_act - 1) / g.ns_act;
         chunk = (chunk + FD_TILE - 1) & ~(FD_TILE - 1);
-        g.start = split * chunk;
+        g.start = lo + split * chunk;
         g.end = split < g.ns_act ? min(g.start + chunk, g.kv_len) : g.start;
     }
     g.ntiles = g.end > g.start ? (g.end - g.start + FD_TILE - 1) / FD_TILE : 0;
@@ -486,9 +489,17 @@ __device__ __forceinline__ void fd_unit(const FdParams &p, int G, int row, int k
 #pragma unroll
             for (int ks = 0; ks < FD_TILE / 16; ks++) {
                 const int pos = ks * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
-                uint32_t b[4];
-                if (NTL == 2) fd_ldsm_x4_t(b, &Vs[buf][pos][d0 + (lane >> 4) * 8]);
-                else fd_ldsm_x2_t(b[0], b[1], &Vs[buf][pos][d0]);
+                uint32_t b[2 * NTL > 4 ? 2 * NTL : 4];
+                if (NTL == 1) {
+                    fd_ldsm_x2_t(b[0], b[1], &Vs[buf][pos][d0]);
+                } else {
+#pragma unroll
+                    for (int n2 = 0; n2 < NTL / 2; n2++) {     // two 8-dim n-tiles per transposed x4 load
+                        uint32_t r[4];
+                        fd_ldsm_x4_t(r, &Vs[buf][pos][d0 + n2 * 16 + (lane >> 4) * 8]);
+                        b[4 * n2] = r[0]; b[4 * n2 + 1] = r[1]; b[4 * n2 + 2] = r[2]; b[4 * n2 + 3] = r[3];
+                    }
+                }
 #pragma unroll
                 for (int hl = 0; hl < 2; hl++) {
                     uint32_t a[4];

@@ -280,6 +280,19 @@ DU_API int du_flash_decode(float *out, const float *q, const uint16_t *k_cache, 
                                        hd, capacity, scale, out, static_cast<cudaStream_t>(stream));
 }
 
+DU_API int du_flash_decode_window(float *out, const float *q, const uint16_t *k_cache, const uint16_t *v_cache,
+                                  const int32_t *kv_len, int batch, int hq, int hkv, int hd, int capacity, float scale,
+                                  int window, void *stream)
+{
+    DU_CHECK_ARG(out && q && k_cache && v_cache && kv_len, "du_flash_decode_window: null pointer");
+    DU_CHECK_ARG(batch >= 0 && hq > 0 && hkv > 0 && capacity > 0, "du_flash_decode_window: bad sizes");
+    DU_CHECK_ARG(hq % hkv == 0, "du_flash_decode_window: hq must be a multiple of hkv");
+    return launch_flash_decode_cluster(q, reinterpret_cast<const __half *>(k_cache),
+                                       reinterpret_cast<const __half *>(v_cache), nullptr, kv_len, 0, batch, hq, hkv,
+                                       hd, capacity, scale, out, static_cast<cudaStream_t>(stream), -1, nullptr,
+                                       window > 0 ? window : 0);
+}
+
 DU_API int du_kv_write_int8(const float *kv_new, int seq_len, int hkv, int hd, int cache_len, uint8_t *cache,
                             uint32_t *sz, void *stream)
 {

@@ -48,6 +48,37 @@ struct Kv8Cache {
     uint32_t *ksz, *vsz;
 };
 
+// WriteCacheFull's INT8 quantization (Gemma3CS.compute:300-380) of one (position,
+// kv head) row held by a warp, lane values v[0 .. epl) = elements lane * epl + e:
+// min / max (exact in any order), scale = (max - min) / 255 floored at 1e-9, zp =
+// round(-min / scale) clamped to [0, 255], q = clamp(round(x * (1 / scale)) + zp,
+// 0, 255), round half to even, IEEE division and reciprocal; the row's word is
+// fp16 scale | fp16 zp << 16.  All 32 lanes call it.
+__device__ __forceinline__ void kv8_store_row(const float (&v)[8], int epl, int lane, uint8_t *row, uint32_t *word)
+{
+    float mn = 3.0e38f, mx = -3.0e38f;
+#pragma unroll
+    for (int e = 0; e < 8; e++)
+        if (e < epl) {
+            mn = fminf(mn, v[e]);
+            mx = fmaxf(mx, v[e]);
+        }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        mn = fminf(mn, __shfl_xor_sync(0xffffffffu, mn, o));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    }
+    float scale = (mx - mn) / 255.0f;
+    if (scale < 1e-9f) scale = 1e-9f;
+    const float zp = fminf(fmaxf(rintf(-mn / scale), 0.0f), 255.0f);
+    const float inv = 1.0f / scale;
+#pragma unroll
+    for (int e = 0; e < 8; e++)
+        if (e < epl) row[lane * epl + e] = (uint8_t)fminf(fmaxf(rintf(v[e] * inv) + zp, 0.0f), 255.0f);
+    if (lane == 0)
+        *word = (uint32_t)__half_as_ushort(__float2half_rn(scale)) | ((uint32_t)__half_as_ushort(__float2half_rn(zp)) << 16);
+}
+
 // 16-byte streaming load: weights are read exactly once per launch, so they
 // bypass L1 (no_allocate) and come through the read-only path.
 __device__ __forceinline__ uint4 ldg_stream(const void *p)
@@ -79,6 +110,16 @@ __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;"
 __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;"); }
 
 __device__ __forceinline__ float silu(float x) { return x / (1.0f + __expf(-x)); }
+
+// gelu of the reference (Gemma3CS.compute:162-172): tanh form, tanh through
+// exp(-2|t|) with sign(0) = 0.
+__device__ __forceinline__ float gelu_tanh(float x)
+{
+    const float t = 0.7978845608f * (x + 0.044715f * x * x * x);
+    const float e = expf(-2.0f * fabsf(t));
+    const float sg = t > 0.0f ? 1.0f : (t < 0.0f ? -1.0f : 0.0f);
+    return 0.5f * x * (1.0f + sg * ((1.0f - e) / (1.0f + e)));
+}
 
 // Greedy tie-break of the reference's ArgMax (Gemma3CS.compute:911-928): 256
 // threads stride the vocabulary keeping their first strict maximum (lowest

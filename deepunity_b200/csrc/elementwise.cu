@@ -48,6 +48,124 @@ int launch_rmsnorm(const float *x, const __half *g, int rows, int H, float eps, 
     return DU_OK;
 }
 
+// RmsNormHidden + AddResidual (Gemma3Model.cs:515-528, 575-585): the sandwich
+// norm of a block output y, then the residual: x_res += y * rms(y) * (1 + gamma').
+__global__ void norm_add_kernel(const float *y, const __half *g, int H, float eps, float *x_res)
+{
+    __shared__ float part[32];
+    pdl_wait();
+    const float *yr = y + (size_t)blockIdx.x * H;
+    float *xr = x_res + (size_t)blockIdx.x * H;
+    float ss = 0.0f;
+    for (int i = threadIdx.x; i < H; i += blockDim.x) ss += yr[i] * yr[i];
+    ss = warp_sum(ss);
+    if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    float tot = 0.0f;
+    for (int i = 0; i < (int)(blockDim.x >> 5); i++) tot += part[i];
+    const float inv = 1.0f / sqrtf(tot / (float)H + eps);
+    for (int i = threadIdx.x; i < H; i += blockDim.x) xr[i] = yr[i] * inv * (1.0f + __half2float(g[i])) + xr[i];
+}
+
+int launch_norm_add(const float *y, const __half *g, int rows, int H, float eps, float *x_res, cudaStream_t st)
+{
+    if (rows <= 0) return DU_OK;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(rows);
+    cfg.blockDim = dim3(256);
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl_enabled() ? 1 : 0;
+    DU_CUDA_TRY(cudaLaunchKernelEx(&cfg, norm_add_kernel, y, g, H, eps, x_res));
+    return DU_OK;
+}
+
+// After an EPI_STORE QKV GEMV of a qk-norm model: one warp per (token, head) of
+// the fp32 rows [M][hq + 2 hkv][hd] (q heads, k heads, v heads).  q and k:
+// RmsNormHead (Gemma3CS.compute:227-245) with their gammas, then split-half RoPE
+// (ApplyRopeSplitHalf, :271-297) at the token's position; q goes to q_out, k and
+// v to the fp16 cache, or through the INT8 quantization into the INT8 cache.
+// A lane holds elements lane * epl .. lane * epl + epl - 1, so a RoPE pair
+// (i, i + hd / 2) sits on lanes l and l + 16.
+__global__ void __launch_bounds__(256) qkv_post_kernel(QkvPost a)
+{
+    pdl_wait();
+    const int w = (int)((blockIdx.x * blockDim.x + threadIdx.x) >> 5), lane = threadIdx.x & 31;
+    const int nh = a.hq + 2 * a.hkv;
+    if (w >= a.M * nh) return;
+    const int m = w / nh, h = w - m * nh;
+    const int epl = a.hd >> 5;
+    const float *x = a.qkv + ((size_t)m * nh + h) * a.hd + lane * epl;
+    float v[8];
+#pragma unroll
+    for (int e = 0; e < 8; e++) v[e] = e < epl ? x[e] : 0.0f;
+    const bool isq = h < a.hq, isk = !isq && h < a.hq + a.hkv;
+    const __half *gam = isq ? a.q_norm : (isk ? a.k_norm : nullptr);
+    if (gam != nullptr) {
+        float ss = 0.0f;
+#pragma unroll
+        for (int e = 0; e < 8; e++) ss += v[e] * v[e];
+        ss = warp_sum(ss);
+        const float rms = 1.0f / sqrtf(ss / (float)a.hd + a.eps);
+#pragma unroll
+        for (int e = 0; e < 8; e++)
+            if (e < epl) v[e] = v[e] * rms * (1.0f + __half2float(gam[lane * epl + e]));
+    }
+    const int pos = a.pos[m];
+    if (isq || isk) {
+        const int hd2 = a.hd >> 1;
+#pragma unroll
+        for (int e = 0; e < 8; e++) {
+            const float o = __shfl_xor_sync(0xffffffffu, v[e], 16);
+            if (e < epl) {
+                const int i = (lane & 15) * epl + e;
+                const float c = __half2float(a.rope_cos[(size_t)pos * hd2 + i]);
+                const float s = __half2float(a.rope_sin[(size_t)pos * hd2 + i]);
+                v[e] = lane < 16 ? v[e] * c - o * s : v[e] * c + o * s;
+            }
+        }
+    }
+    if (isq) {
+        float *dst = a.q_out + ((size_t)m * a.hq + h) * a.hd + lane * epl;
+#pragma unroll
+        for (int e = 0; e < 8; e++)
+            if (e < epl) dst[e] = v[e];
+        return;
+    }
+    const int kh = isk ? h - a.hq : h - a.hq - a.hkv;
+    const int seq = a.seq_of ? a.seq_of[m] : a.seq_off + m;
+    const size_t row = ((size_t)seq * a.cap + pos) * a.hkv + kh;
+    if (a.kv8.k8 != nullptr) {
+        kv8_store_row(v, epl, lane, (isk ? a.kv8.k8 : a.kv8.v8) + row * a.hd, (isk ? a.kv8.ksz : a.kv8.vsz) + row);
+        return;
+    }
+    __half *dst = (isk ? a.k_cache : a.v_cache) + row * a.hd + lane * epl;
+#pragma unroll
+    for (int e = 0; e < 8; e++)
+        if (e < epl) dst[e] = __float2half_rn(v[e]);
+}
+
+int launch_qkv_post(const QkvPost &a, cudaStream_t st)
+{
+    if (a.M <= 0) return DU_OK;
+    if (a.hd % 64 != 0 || a.hd > 256) return fail(DU_EINVAL, "qkv_post: head_dim must be 64, 128, 192 or 256");
+    const int warps = a.M * (a.hq + 2 * a.hkv);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((warps + 7) / 8);
+    cfg.blockDim = dim3(256);
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl_enabled() ? 1 : 0;
+    DU_CUDA_TRY(cudaLaunchKernelEx(&cfg, qkv_post_kernel, a));
+    return DU_OK;
+}
+
 // Final greedy pick from the per-CTA (max, argmax) partials of the lm_head
 // GEMV: the largest value wins, ties follow the reference's ArgMax tree
 // (am_better, common.cuh).  Writes the id (and optionally the next step's input

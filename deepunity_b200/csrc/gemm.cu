@@ -378,7 +378,8 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
                     if (p.epi == EPI_QKV || p.epi == EPI_GATEUP) {
                         const float o = __shfl_xor_sync(0xffffffffu, val, 1);
                         if (tok_ok && row_ok && (lr & 1) == 0) {
-                            if (p.epi == EPI_GATEUP) p.y[(size_t)t * p.ldy + (lr >> 1)] = (val / (1.0f + expf(-val))) * o;
+                            if (p.epi == EPI_GATEUP)
+                                p.y[(size_t)t * p.ldy + (lr >> 1)] = (p.act == 1 ? gelu_tanh(val) : val / (1.0f + expf(-val))) * o;
                             else gv_epi_pair(p, lr, t, val, o);
                         }
                     } else if (p.epi == EPI_LOGITS) {

@@ -79,6 +79,7 @@ struct GemvParams {
     const __half *rope_cos, *rope_sin;  // [cap][hd/2]
     float *kv_stage;        // optional (INT8 KV): K / V rows as fp32 [M][2][hkv][hd] instead of the
                             // fp16 cache; the next kernel quantizes them into the cache
+    int act;                // EPI_GATEUP: 0 SiLU(g) * u, 1 gelu(g) * u (tanh form)
     // EPI_LOGITS: logits[m][row] of this rank's vocab shard (optional) + per-CTA
     // (max, argmax) with the global vocab index vocab_off + row
     float *logits;

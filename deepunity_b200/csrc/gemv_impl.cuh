@@ -231,7 +231,7 @@ __device__ __forceinline__ void gv_stage_x(const GemvParams &p, uint4 *xq, GemvS
 __device__ __forceinline__ void gv_epi_pair(const GemvParams &p, int lr0, int m, float x1, float x2)
 {
     if (p.epi == EPI_GATEUP) {
-        p.y[(size_t)m * p.ldy + (lr0 >> 1)] = (x1 / (1.0f + expf(-x1))) * x2;
+        p.y[(size_t)m * p.ldy + (lr0 >> 1)] = (p.act == 1 ? gelu_tanh(x1) : x1 / (1.0f + expf(-x1))) * x2;
         return;
     }
     // EPI_QKV: rows (lr0, lr0 + 1) are the RoPE pair (i, i + hd/2) of one head

@@ -56,13 +56,29 @@ int launch_flash_decode(const float *q, const __half *kc, const __half *vc, cons
 int launch_flash_decode_cluster(const float *q, const __half *kc, const __half *vc, const int *seq_of,
                                 const int *kv_len, int kv_len_add, int nq, int hq, int hkv, int hd, int cap,
                                 float scale, float *out, cudaStream_t st, int new_rows = -1,
-                                const Kv8Cache *kv8 = nullptr);
+                                const Kv8Cache *kv8 = nullptr, int window = 0);
 // INT8 KV: quantizes fp32 rows [M][nkv][hkv][hd] (nkv 2: K then V; 1: K only) into the
 // cache at sequence seq_of[m] (or seq_off + m), position pos[m] (or pos_base + m).
 int launch_kv_quant_int8(const float *stage, int M, int nkv, int hkv, int hd, const int *pos, int pos_base,
                          const int *seq_of, int seq_off, int cap, const Kv8Cache &kv, cudaStream_t st);
 
 // elementwise.cu
+// Gemma-style attention input: qk-norm + RoPE + cache write after an EPI_STORE QKV GEMV.
+struct QkvPost {
+    const float *qkv;                    // [M][hq + 2 hkv][hd], q heads then k heads then v heads
+    int M, hq, hkv, hd;
+    const __half *q_norm, *k_norm;       // gamma' [hd] (nullptr: no qk-norm)
+    float eps;
+    const int *pos, *seq_of;             // per token: cache slot / RoPE position, sequence (nullptr: seq_off + m)
+    int seq_off, cap;
+    const __half *rope_cos, *rope_sin;   // [cap][hd / 2]
+    float *q_out;                        // [M][hq][hd]
+    __half *k_cache, *v_cache;           // fp16 cache [seq][cap][hkv][hd], or
+    Kv8Cache kv8;                        // the INT8 cache (kv8.k8 != nullptr)
+};
+int launch_qkv_post(const QkvPost &a, cudaStream_t st);
+// x_res += y * rms(y) * (1 + gamma') per row (sandwich norm + residual)
+int launch_norm_add(const float *y, const __half *gamma_m1, int rows, int H, float eps, float *x_res, cudaStream_t st);
 int launch_embed(const int *ids, const __half *embed, float scale, int M, int H, float *out, cudaStream_t st);
 int launch_rmsnorm(const float *x, const __half *gamma_m1, int rows, int H, float eps, float *y,
                    cudaStream_t st);

@@ -90,7 +90,10 @@ static int check_cfg(const du_model_config &c)
     DU_CHECK_ARG(c.hidden_size > 0 && c.intermediate_size > 0 && c.num_layers > 0, "config: non-positive dims");
     DU_CHECK_ARG(c.num_heads_q > 0 && c.num_heads_kv > 0 && c.num_heads_q % c.num_heads_kv == 0,
                  "config: num_heads_q must be a multiple of num_heads_kv");
-    DU_CHECK_ARG(c.head_dim == 64 || c.head_dim == 128, "config: head_dim must be 64 or 128");
+    DU_CHECK_ARG(c.head_dim == 64 || c.head_dim == 128 || c.head_dim == 256, "config: head_dim must be 64, 128 or 256");
+    DU_CHECK_ARG(c.kv_quant != DU_KV_INT8 || c.head_dim <= 128, "config: the INT8 KV cache supports head_dim 64/128");
+    DU_CHECK_ARG((c.arch_flags & ~(DU_ARCH_QK_NORM | DU_ARCH_SANDWICH | DU_ARCH_GELU)) == 0, "config: unknown arch_flags");
+    DU_CHECK_ARG(c.sliding_window >= 0 && c.attn_scale >= 0.0f, "config: negative sliding_window / attn_scale");
     const int G = c.num_heads_q / c.num_heads_kv;
     DU_CHECK_ARG(G == 1 || G == 2 || G == 4 || G == 8, "config: GQA group must be 1, 2, 4 or 8");
     DU_CHECK_ARG(c.vocab_size > 0 && c.kv_capacity > 0 && c.max_batch > 0, "config: vocab/capacity/batch");
@@ -135,6 +138,16 @@ static int model_alloc(du_model *m)
         ly.s_d = (__half *)dalloc(m, sbytes(m->quant, m->group, H, m->I_l), &rc);
         ly.ln1 = (__half *)dalloc(m, (size_t)H * 2, &rc);
         ly.ln2 = (__half *)dalloc(m, (size_t)H * 2, &rc);
+        if (m->arch & DU_ARCH_QK_NORM) {
+            ly.q_norm = (__half *)dalloc(m, (size_t)hd * 2, &rc);
+            ly.k_norm = (__half *)dalloc(m, (size_t)hd * 2, &rc);
+            m->weight_bytes += 4LL * hd;
+        }
+        if (m->arch & DU_ARCH_SANDWICH) {
+            ly.post_attn = (__half *)dalloc(m, (size_t)H * 2, &rc);
+            ly.post_ffn = (__half *)dalloc(m, (size_t)H * 2, &rc);
+            m->weight_bytes += 4LL * H;
+        }
         m->weight_bytes += qbytes(m->quant, m->qkv_rows, H) + sbytes(m->quant, m->group, m->qkv_rows, H) +
                            qbytes(m->quant, H, Ko) + sbytes(m->quant, m->group, H, Ko) +
                            qbytes(m->quant, 2LL * m->I_l, H) + sbytes(m->quant, m->group, 2LL * m->I_l, H) +
@@ -146,6 +159,10 @@ static int model_alloc(du_model *m)
     m->weight_bytes += 2ull * H + 2ull * m->V_l * H;
     m->rope_cos = (__half *)dalloc(m, (size_t)m->cap * (hd / 2) * 2, &rc);
     m->rope_sin = (__half *)dalloc(m, (size_t)m->cap * (hd / 2) * 2, &rc);
+    if (m->window > 0) {
+        m->rope_cos_local = (__half *)dalloc(m, (size_t)m->cap * (hd / 2) * 2, &rc);
+        m->rope_sin_local = (__half *)dalloc(m, (size_t)m->cap * (hd / 2) * 2, &rc);
+    }
     m->kv_layer_elems = (size_t)m->maxb * m->cap * m->hkv_l * hd;
     if (m->kv8) {
         m->k8 = (uint8_t *)dalloc(m, m->kv_layer_elems * m->L, &rc);
@@ -170,6 +187,7 @@ static int model_alloc(du_model *m)
     m->att = (float *)dalloc(m, sizeof(float) * T * m->hq_l * hd, &rc);
     m->inter = (float *)dalloc(m, sizeof(float) * T * m->I_l, &rc);
     if (m->kv8) m->kv_stage = (float *)dalloc(m, sizeof(float) * T * 2 * m->hkv_l * hd, &rc);
+    if (m->arch & DU_ARCH_QK_NORM) m->qkv_buf = (float *)dalloc(m, sizeof(float) * T * m->qkv_rows, &rc);
     m->logits = (float *)dalloc(m, sizeof(float) * m->maxb * m->V_l, &rc);
     if (m->tp > 1) m->logits_all = (float *)dalloc(m, sizeof(float) * m->tp * m->maxb * m->V_l, &rc);
     m->am_parts = 2 * num_sms();
@@ -216,18 +234,22 @@ static int model_alloc(du_model *m)
     DU_CUDA_TRY(cudaMallocHost(&m->h_pin_seeds, sizeof(int32_t) * (m->maxb + 4)));
     m->h_cache_len.assign(m->maxb, 0);
 
-    // RoPE tables on the host with the reference formula (MiniCPM5Model.cs:163-191)
+    // RoPE tables on the host with the reference formula (MiniCPM5Model.cs:163-191); the
+    // sliding-window layers' tables use the local base (Gemma3Model: ropeCosLocal)
     const int hd2 = hd / 2;
     std::vector<uint16_t> c((size_t)m->cap * hd2), s((size_t)m->cap * hd2);
-    for (int pos = 0; pos < m->cap; pos++)
-        for (int i = 0; i < hd2; i++) {
-            const float f = 1.0f / powf(m->cfg.rope_theta, 2.0f * (float)i / (float)hd);
-            const float ang = (float)pos * f;
-            c[(size_t)pos * hd2 + i] = f32_to_f16(cosf(ang));
-            s[(size_t)pos * hd2 + i] = f32_to_f16(sinf(ang));
-        }
-    DU_CUDA_TRY(cudaMemcpy(m->rope_cos, c.data(), c.size() * 2, cudaMemcpyHostToDevice));
-    DU_CUDA_TRY(cudaMemcpy(m->rope_sin, s.data(), s.size() * 2, cudaMemcpyHostToDevice));
+    for (int table = 0; table < (m->window > 0 ? 2 : 1); table++) {
+        const float theta = table == 0 || m->cfg.rope_theta_local <= 0.0f ? m->cfg.rope_theta : m->cfg.rope_theta_local;
+        for (int pos = 0; pos < m->cap; pos++)
+            for (int i = 0; i < hd2; i++) {
+                const float f = 1.0f / powf(theta, 2.0f * (float)i / (float)hd);
+                const float ang = (float)pos * f;
+                c[(size_t)pos * hd2 + i] = f32_to_f16(cosf(ang));
+                s[(size_t)pos * hd2 + i] = f32_to_f16(sinf(ang));
+            }
+        DU_CUDA_TRY(cudaMemcpy(table ? m->rope_cos_local : m->rope_cos, c.data(), c.size() * 2, cudaMemcpyHostToDevice));
+        DU_CUDA_TRY(cudaMemcpy(table ? m->rope_sin_local : m->rope_sin, s.data(), s.size() * 2, cudaMemcpyHostToDevice));
+    }
     DU_CUDA_TRY(cudaDeviceSynchronize());
     return DU_OK;
 }
@@ -358,9 +380,24 @@ int place_tensor(du_model *m, const char *name, const void *src, size_t bytes, c
         return fail(DU_ENOTFOUND, std::string("unknown tensor: ") + name);
     Layer &ly = m->layers[li];
     std::string t(rest);
-    if (t == "input_layernorm.bin" || t == "post_attention_layernorm.bin") {
+    if (t == "input_layernorm.bin" || t == "post_attention_layernorm.bin" || t == "pre_feedforward_layernorm.bin" ||
+        t == "post_feedforward_layernorm.bin") {
         DU_CHECK_ARG(bytes == (size_t)H * 2, "layernorm: size mismatch");
-        DU_CUDA_TRY(cudaMemcpyAsync(t[0] == 'i' ? ly.ln1 : ly.ln2, src, bytes, kind, st));
+        // llama: post_attention_layernorm is the pre-MLP norm; with sandwich norms (Gemma3) it
+        // is the norm of the attention output, and pre_feedforward_layernorm the pre-MLP one
+        const bool sw = m->arch & DU_ARCH_SANDWICH;
+        __half *dst = t == "input_layernorm.bin" ? ly.ln1
+                      : t == "post_attention_layernorm.bin" ? (sw ? ly.post_attn : ly.ln2)
+                      : t == "pre_feedforward_layernorm.bin" ? (sw ? ly.ln2 : nullptr)
+                                                             : ly.post_ffn;
+        if (dst == nullptr) return fail(DU_ENOTFOUND, std::string("tensor of a sandwich-norm model: ") + name);
+        DU_CUDA_TRY(cudaMemcpyAsync(dst, src, bytes, kind, st));
+        return DU_OK;
+    }
+    if (t == "self_attn_q_norm.bin" || t == "self_attn_k_norm.bin") {
+        if (!(m->arch & DU_ARCH_QK_NORM)) return fail(DU_ENOTFOUND, std::string("tensor of a qk-norm model: ") + name);
+        DU_CHECK_ARG(bytes == (size_t)hd * 2, "qk-norm: size mismatch");
+        DU_CUDA_TRY(cudaMemcpyAsync(t[10] == 'q' ? ly.q_norm : ly.k_norm, src, bytes, kind, st));
         return DU_OK;
     }
     static const struct { const char *stem; TensorKind k; } stems[] = {
@@ -551,17 +588,33 @@ static Kv8Cache kv8_layer(const du_model *m, int l)
 // residual add (collective = false leaves both out, for kernel timing).
 // GEMV parameters of stage `stage` of layer l for the token rows of `io`
 // (shared by the per-kernel path and the persistent decode-step plan).
+// Layer l is a sliding-window layer (Gemma3Config.layer_types: every
+// sliding_pattern-th layer, 1-based, is full attention).
+static bool layer_sliding(const du_model *m, int l)
+{
+    return m->window > 0 && (m->pattern <= 0 || (l + 1) % m->pattern != 0);
+}
+
 static GemvParams stage_gemv_params(du_model *m, const StepIO &io, int l, int stage)
 {
     const int H = m->H, hd = m->hd;
     const int64_t Ko = (int64_t)m->hq_l * hd;
     const Layer &ly = m->layers[l];
+    const bool sw = layer_sliding(m, l);
     GemvParams p;
     switch (stage) {
     case ST_QKV:   // RMSNorm(ln1) -> QKV GEMV -> RoPE -> q, fp16 K/V into the cache
         p = gp_base(m, ly.w_qkv, ly.s_qkv, H);
         p.x = m->x_res; p.ldx = H; p.gamma = ly.ln1; p.eps = m->cfg.rms_eps;
-        p.N = m->qkv_rows; p.map = MAP_ROPE_PAIR; p.map_hd = hd;
+        p.N = m->qkv_rows;
+        if (m->arch & DU_ARCH_QK_NORM) {
+            // qk-norm needs whole heads: the rows go out as they are; the qkv-post kernel
+            // normalises, rotates and writes the cache
+            p.map = MAP_IDENT;
+            p.epi = EPI_STORE; p.y = m->qkv_buf; p.ldy = m->qkv_rows;
+            break;
+        }
+        p.map = MAP_ROPE_PAIR; p.map_hd = hd;
         p.epi = EPI_QKV; p.q_out = m->q;
         if (m->kv8) {
             p.kv_stage = m->kv_stage;      // quantized into the INT8 cache by the next kernel
@@ -570,7 +623,8 @@ static GemvParams stage_gemv_params(du_model *m, const StepIO &io, int l, int st
             p.v_cache = m->v_cache + (size_t)l * m->kv_layer_elems;
         }
         p.pos = io.pos; p.seq_of = io.seq_of; p.hq = m->hq_l; p.hkv = m->hkv_l; p.hd = hd; p.cap = m->cap;
-        p.rope_cos = m->rope_cos; p.rope_sin = m->rope_sin;
+        p.rope_cos = sw ? m->rope_cos_local : m->rope_cos;
+        p.rope_sin = sw ? m->rope_sin_local : m->rope_sin;
         break;
     case ST_O:
     case ST_DOWN:  // O / down GEMV -> residual add (TP1) or partial sum for the allreduce
@@ -582,7 +636,8 @@ static GemvParams stage_gemv_params(du_model *m, const StepIO &io, int l, int st
             p.x = m->inter; p.ldx = m->I_l;
         }
         p.N = H; p.map = MAP_IDENT;
-        if (m->tp == 1) { p.epi = EPI_RESID; p.y = m->x_res; p.ldy = H; }
+        if (m->arch & DU_ARCH_SANDWICH) { p.epi = EPI_STORE; p.y = m->part; p.ldy = H; }   // norm, then residual
+        else if (m->tp == 1) { p.epi = EPI_RESID; p.y = m->x_res; p.ldy = H; }
         else if (tp_peer_ok(m, io) && tp_fuse_enabled(m)) {
             // decode: the allreduce over peer memory runs in the GEMV's epilogue
             p.epi = EPI_TP_RESID; p.y = m->part; p.ldy = H; p.tp = m->tpc.dev; p.resid = m->x_res;
@@ -593,6 +648,7 @@ static GemvParams stage_gemv_params(du_model *m, const StepIO &io, int l, int st
         p.x = m->x_res; p.ldx = H; p.gamma = ly.ln2; p.eps = m->cfg.rms_eps;
         p.N = 2 * m->I_l; p.map = MAP_GATEUP; p.map_I = m->I_l;
         p.epi = EPI_GATEUP; p.y = m->inter; p.ldy = m->I_l;
+        p.act = (m->arch & DU_ARCH_GELU) ? 1 : 0;
         break;
     }
     p.M = io.M;
@@ -602,7 +658,7 @@ static GemvParams stage_gemv_params(du_model *m, const StepIO &io, int l, int st
 // Attention parameters of layer l (scratch split for `nsplit` splits of io.M rows).
 static FdParams stage_attn_params(du_model *m, const StepIO &io, int l, int nsplit, int *G)
 {
-    FdParams a;
+    FdParams a = {};
     const int g = m->hq_l / m->hkv_l;
     a.q = m->q;
     a.k_cache = m->k_cache + (size_t)l * m->kv_layer_elems;
@@ -611,7 +667,8 @@ static FdParams stage_attn_params(du_model *m, const StepIO &io, int l, int nspl
     a.kv_len = io.kv_len;
     a.kv_len_add = io.kv_len_add;
     a.hq = m->hq_l; a.hkv = m->hkv_l; a.cap = m->cap;
-    a.scale = powf((float)m->hd, -0.5f);
+    a.scale = m->attn_scale;
+    a.window = layer_sliding(m, l) ? m->window : 0;
     a.out = m->att;
     a.part_o = m->fd_scratch;
     a.part_ml = m->fd_scratch + (size_t)io.M * m->hkv_l * nsplit * g * m->hd;
@@ -628,23 +685,49 @@ static int enqueue_stage(du_model *m, const StepIO &io, int l, int stage, bool c
     const int H = m->H, hd = m->hd, M = io.M, qt = qt_of(m->quant);
     cudaStream_t st = m->stream;
     int rc = DU_OK;
+    const bool sw = layer_sliding(m, l);
     if (stage == ST_ATTN) {
+        const int window = sw ? m->window : 0;
         if (m->kv8) {
             const Kv8Cache kv = kv8_layer(m, l);
             return launch_flash_decode_cluster(m->q, nullptr, nullptr, io.seq_of, io.kv_len, io.kv_len_add, M, m->hq_l,
-                                               m->hkv_l, hd, m->cap, powf((float)hd, -0.5f), m->att, st, io.kv_new, &kv);
+                                               m->hkv_l, hd, m->cap, m->attn_scale, m->att, st, io.kv_new, &kv, window);
         }
         __half *kc = m->k_cache + (size_t)l * m->kv_layer_elems;
         __half *vc = m->v_cache + (size_t)l * m->kv_layer_elems;
         return launch_flash_decode_cluster(m->q, kc, vc, io.seq_of, io.kv_len, io.kv_len_add, M, m->hq_l, m->hkv_l,
-                                           hd, m->cap, powf((float)hd, -0.5f), m->att, st, io.kv_new);
+                                           hd, m->cap, m->attn_scale, m->att, st, io.kv_new, nullptr, window);
     }
     if (stage < ST_QKV || stage > ST_DOWN) return fail(DU_EINVAL, "unknown stage");
     GemvParams gp = stage_gemv_params(m, io, l, stage);
     if (gp.epi == EPI_TP_RESID && !collective) gp.epi = EPI_STORE;     // partial sums into m->part only
     if ((rc = run_gemv(m, qt, gp, M))) return rc;
+    if (stage == ST_QKV && (m->arch & DU_ARCH_QK_NORM)) {
+        // qk-norm (Gemma3): normalise and rotate q / k per head, then the cache write
+        const Layer &ly = m->layers[l];
+        QkvPost a = {};
+        a.qkv = m->qkv_buf; a.M = M; a.hq = m->hq_l; a.hkv = m->hkv_l; a.hd = hd;
+        a.q_norm = ly.q_norm; a.k_norm = ly.k_norm; a.eps = m->cfg.rms_eps;
+        a.pos = io.pos; a.seq_of = io.seq_of; a.seq_off = 0; a.cap = m->cap;
+        a.rope_cos = sw ? m->rope_cos_local : m->rope_cos;
+        a.rope_sin = sw ? m->rope_sin_local : m->rope_sin;
+        a.q_out = m->q;
+        if (m->kv8) a.kv8 = kv8_layer(m, l);
+        else {
+            a.k_cache = m->k_cache + (size_t)l * m->kv_layer_elems;
+            a.v_cache = m->v_cache + (size_t)l * m->kv_layer_elems;
+        }
+        return launch_qkv_post(a, st);
+    }
     if (stage == ST_QKV && m->kv8)     // this pass's K / V rows into the INT8 cache
         return launch_kv_quant_int8(m->kv_stage, M, 2, m->hkv_l, hd, io.pos, 0, io.seq_of, 0, m->cap, kv8_layer(m, l), st);
+    if ((stage == ST_O || stage == ST_DOWN) && (m->arch & DU_ARCH_SANDWICH)) {
+        // sandwich norms (Gemma3): the block output (summed over the ranks) is normalised,
+        // then added to the residual
+        if (m->tp > 1 && collective && (rc = allreduce_sum(m, m->part, (size_t)M * H))) return rc;
+        const Layer &ly = m->layers[l];
+        return launch_norm_add(m->part, stage == ST_O ? ly.post_attn : ly.post_ffn, M, H, m->cfg.rms_eps, m->x_res, st);
+    }
     if ((stage == ST_O || stage == ST_DOWN) && m->tp > 1 && collective && gp.epi != EPI_TP_RESID) {
         if (tp_peer_ok(m, io)) return launch_tp_allreduce(&m->tpc, m->part, m->x_res, (size_t)M * H, st);
         if ((rc = allreduce_sum(m, m->part, (size_t)M * H))) return rc;
@@ -783,7 +866,7 @@ static int build_step_plan(du_model *m, const StepIO &io, StepPlan *plan, int *q
 {
     *d_stages = nullptr;
     if (!(m->cfg.flags & DU_FLAG_PERSISTENT) || (m->cfg.flags & DU_FLAG_NO_PERSISTENT) || m->tp > 1 || io.M > 8 ||
-        m->kv8)
+        m->kv8 || m->arch != 0 || m->window > 0 || m->hd > 128)
         return DU_ESTATE;
     const int qt = qt_of(m->quant);
     const int mt = io.M <= 1 ? 1 : io.M <= 2 ? 2 : io.M <= 4 ? 4 : 8;
@@ -954,6 +1037,10 @@ DU_API int du_model_create(const du_model_config *cfg, du_model **out)
     m->group = cfg->quant == DU_QUANT_INT4 ? cfg->group_size : 32;
     m->cap = cfg->kv_capacity;
     m->kv8 = cfg->kv_quant == DU_KV_INT8;
+    m->arch = cfg->arch_flags;
+    m->window = cfg->sliding_window;
+    m->pattern = cfg->sliding_pattern;
+    m->attn_scale = cfg->attn_scale > 0.0f ? cfg->attn_scale : powf((float)cfg->head_dim, -0.5f);
     m->maxb = cfg->max_batch;
     m->max_tokens = m->maxb > 256 ? m->maxb : 256;
     if (m->cfg.embed_scale == 0.0f) m->cfg.embed_scale = 1.0f;

@@ -20,7 +20,10 @@ struct Layer {
     uint8_t *w_o = nullptr;   __half *s_o = nullptr;      // [H, hq_l*hd]
     uint8_t *w_gu = nullptr;  __half *s_gu = nullptr;     // gate|up [2*I_l, H]
     uint8_t *w_d = nullptr;   __half *s_d = nullptr;      // [H, I_l]
-    __half *ln1 = nullptr, *ln2 = nullptr;                // gamma - 1, [H]
+    __half *ln1 = nullptr, *ln2 = nullptr;                // gamma - 1, [H] (ln2: the pre-MLP norm)
+    // Gemma3 variants: qk-norm gammas [hd]; sandwich norms after attention / the MLP [H]
+    __half *q_norm = nullptr, *k_norm = nullptr;
+    __half *post_attn = nullptr, *post_ffn = nullptr;
 };
 
 struct Graph {
@@ -50,6 +53,11 @@ struct du_model {
     uint8_t *k8 = nullptr, *v8 = nullptr;                // [L][maxb][cap][hkv_l][hd]
     uint32_t *ksz = nullptr, *vsz = nullptr;             // [L][maxb][cap][hkv_l] scale | zp << 16
     float *kv_stage = nullptr;                           // QKV epilogue's fp32 K / V rows [T][2][hkv_l][hd]
+    // Gemma3 variants (du_model_config.arch_flags / sliding_window)
+    int arch = 0, window = 0, pattern = 0;
+    float attn_scale = 0.0f;                             // softmax scale
+    __half *rope_cos_local = nullptr, *rope_sin_local = nullptr;   // RoPE of the sliding-window layers
+    float *qkv_buf = nullptr;                            // qk-norm models: QKV GEMV output [T][qkv_rows]
     // device state
     int *d_cache_len = nullptr;             // [maxb]
     int *d_ids = nullptr;                   // [max_tokens] input ids

@@ -136,7 +136,8 @@ __device__ __forceinline__ void tg_epilogue(const GemvParams &p, int lr, bool ro
         if (p.epi == EPI_QKV || p.epi == EPI_GATEUP) {
             const float o = __shfl_xor_sync(0xffffffffu, v, 1);
             if (m < p.M && row_ok && (lr & 1) == 0) {
-                if (p.epi == EPI_GATEUP) p.y[(size_t)m * p.ldy + (lr >> 1)] = (v / (1.0f + expf(-v))) * o;
+                if (p.epi == EPI_GATEUP)
+                    p.y[(size_t)m * p.ldy + (lr >> 1)] = (p.act == 1 ? gelu_tanh(v) : v / (1.0f + expf(-v))) * o;
                 else gv_epi_pair(p, lr, m, v, o);
             }
         } else if (m < p.M && row_ok) {

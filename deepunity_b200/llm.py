@@ -49,6 +49,13 @@ class LlamaConfig:
     tie_embedding: bool = False
     group_size: int = 128
     name: str = "llama"
+    # Gemma3 variants on the same kernels (Gemma3Model.cs:315-590); defaults = llama
+    arch_flags: int = 0              # _lib.ARCH_QK_NORM | ARCH_SANDWICH | ARCH_GELU
+    sliding_window: int = 0          # > 0: sliding-window layers (G3CS:673-686)
+    sliding_pattern: int = 0         # every n-th layer (1-based) is full attention
+    rope_theta_local: float = 0.0    # RoPE base of the sliding-window layers
+    attn_scale: float = 0.0          # softmax scale (0: head_dim^-0.5)
+    embed_scale: float = 1.0         # embedding multiplier (Gemma3: sqrt(hidden))
 
 
 # Configurations named by the benchmark (BASELINE configs 4 and 5) and the
@@ -58,6 +65,12 @@ CONFIGS = {
     "llama-8b": LlamaConfig(4096, 14336, 32, 32, 8, 128, 128256, 1e-5, 10000.0, name="llama-8b"),
     "MiniCPM5-1B": LlamaConfig(1536, 4608, 24, 16, 2, 128, 130560, 1e-6, 5_000_000.0, group_size=32,
                                name="MiniCPM5-1B"),
+    # Gemma3-270M (LLM/Gemma3/Gemma3Config.cs): 5 sliding-window layers to 1 full, qk-norm,
+    # sandwich norms, GELU GLU, sqrt(hidden) embedding scale, tied embedding
+    "gemma3-270m": LlamaConfig(640, 2048, 18, 4, 1, 256, 262144, 1e-6, 1_000_000.0, tie_embedding=True,
+                               name="gemma3-270m", arch_flags=_lib.ARCH_QK_NORM | _lib.ARCH_SANDWICH | _lib.ARCH_GELU,
+                               sliding_window=512, sliding_pattern=6, rope_theta_local=10_000.0,
+                               attn_scale=256 ** -0.5, embed_scale=640 ** 0.5),
 }
 
 
@@ -95,7 +108,10 @@ class LlamaForCausalLM(LLM):
         cfg.hidden_size, cfg.intermediate_size = config.hidden_size, config.intermediate_size
         cfg.num_layers, cfg.num_heads_q, cfg.num_heads_kv = config.num_layers, config.num_heads_q, config.num_heads_kv
         cfg.head_dim, cfg.vocab_size = config.head_dim, config.vocab_size
-        cfg.rms_eps, cfg.rope_theta, cfg.embed_scale = config.rms_eps, config.rope_theta, 1.0
+        cfg.rms_eps, cfg.rope_theta, cfg.embed_scale = config.rms_eps, config.rope_theta, config.embed_scale
+        cfg.arch_flags, cfg.sliding_window, cfg.sliding_pattern = (config.arch_flags, config.sliding_window,
+                                                                   config.sliding_pattern)
+        cfg.rope_theta_local, cfg.attn_scale = config.rope_theta_local, config.attn_scale
         cfg.quant, cfg.group_size = int(self.quant), config.group_size
         cfg.kv_capacity, cfg.max_batch = max_context_length, max_batch
         cfg.tp_rank, cfg.tp_size, cfg.tie_embedding = tp_rank, tp_size, int(config.tie_embedding)

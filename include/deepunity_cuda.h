@@ -69,8 +69,25 @@ typedef struct du_model_config {
     int32_t tie_embedding;   /* 1: lm_head = embedding */
     int32_t flags;           /* DU_FLAG_* */
     int32_t kv_quant;        /* DU_KV_FP16 (0 or 1) or DU_KV_INT8 (KVQuant, LLM/Base/LLM.cs:15-87) */
-    int32_t reserved[3];
+    /* Gemma3 variants on the same kernels (Gemma3Model.cs:315-590); all 0 for llama */
+    int32_t arch_flags;      /* DU_ARCH_* */
+    int32_t sliding_window;  /* > 0: sliding-window layers see positions abs_q - window .. abs_q (G3CS:673-686) */
+    int32_t sliding_pattern; /* every sliding_pattern-th layer (1-based) is full attention; <= 0: none */
+    float rope_theta_local;  /* RoPE base of the sliding-window layers (0: rope_theta) */
+    float attn_scale;        /* softmax scale (0: head_dim^-0.5; Gemma3: query_pre_attn_scalar^-0.5) */
+    int32_t reserved[2];
 } du_model_config;
+
+/* du_model_config.arch_flags */
+enum {
+    DU_ARCH_QK_NORM = 1,     /* RmsNormHead on q and k before RoPE (G3CS:227-245); tensors
+                                layer_<i>/self_attn_q_norm.bin, self_attn_k_norm.bin [head_dim] */
+    DU_ARCH_SANDWICH = 2,    /* post-attention and post-FFN RMSNorm before each residual add;
+                                layer_<i>/post_attention_layernorm.bin is then the post-attention
+                                norm, pre_feedforward_layernorm.bin the pre-MLP one and
+                                post_feedforward_layernorm.bin the post-FFN one */
+    DU_ARCH_GELU = 4         /* GLU activation gelu (tanh form, G3CS:162-172) instead of SiLU */
+};
 
 /* du_model_config.kv_quant */
 enum {
@@ -306,6 +323,13 @@ DU_API int du_kv_write_int8(const float *kv_new, int seq_len, int hkv, int hd, i
 DU_API int du_flash_decode_kv8(float *out, const float *q, const uint8_t *k8, const uint32_t *ksz, const uint8_t *v8,
                                const uint32_t *vsz, const int32_t *kv_len, int batch, int hq, int hkv, int hd,
                                int capacity, float scale, void *stream);
+
+/* du_flash_decode with a sliding window (Gemma3 sliding-window layers, G3CS:673-686):
+ * the query of a sequence with kv_len positions sees positions kv_len - 1 - window
+ * .. kv_len - 1 (all of them when window <= 0).  hd 64, 128 or 256. */
+DU_API int du_flash_decode_window(float *out, const float *q, const uint16_t *k_cache, const uint16_t *v_cache,
+                                  const int32_t *kv_len, int batch, int hq, int hkv, int hd, int capacity, float scale,
+                                  int window, void *stream);
 
 /* Same computation as du_flash_decode, but it allocates nothing: for callers
  * that must not call cudaMalloc / cudaFree, such as a game engine plugin

@@ -261,6 +261,28 @@ ORC_EXPORT void orc_gemv(const float *x, int M, int K, const void *w, const uint
 
 static float silu_ref(float x) { return x / (1.0f + expf(-x)); }   /* G3CS:173-176 */
 
+/* gelu / safe_tanh (G3CS:162-172): tanh through exp(-2|x|), sign(0) = 0. */
+static float gelu_ref(float x)
+{
+    const float t = 0.7978845608f * (x + 0.044715f * x * x * x);
+    const float a = fabsf(t), e = expf(-2.0f * a);
+    const float sg = t > 0.0f ? 1.0f : (t < 0.0f ? -1.0f : 0.0f);
+    return 0.5f * x * (1.0f + sg * ((1.0f - e) / (1.0f + e)));
+}
+
+/* RmsNormHead (G3CS:227-245): every hd-vector of buf [n, hd] in place,
+ * x * rms * (1 + gamma[i]). */
+static void rmsnorm_heads(float *buf, int n, int hd, const uint16_t *gamma, float eps)
+{
+    for (int v = 0; v < n; v++) {
+        float *x = buf + (int64_t)v * hd;
+        float sum_sq = 0.0f;
+        for (int i = 0; i < hd; i++) sum_sq = sum_sq + x[i] * x[i];
+        const float rms = 1.0f / sqrtf(sum_sq / (float)hd + eps);
+        for (int i = 0; i < hd; i++) x[i] = x[i] * rms * (1.0f + read_h(gamma, i));
+    }
+}
+
 /* RmsNormHidden (G3CS:204-223): one row at a time, sequential sum of squares,
  * y = x * rsqrt(mean + eps) * (1 + gamma') with gamma' = gamma - 1 stored fp16
  * (IMP:314-315).  rsqrt is restated as 1/sqrt. */
@@ -368,13 +390,14 @@ static inline float read_kv8(const uint8_t *cache, const uint32_t *sz, int64_t r
 #define FA_T 256
 static void flash_attention_any(const float *Q, const uint16_t *Kc, const uint16_t *Vc, const uint8_t *K8,
                                 const uint32_t *Ksz, const uint8_t *V8, const uint32_t *Vsz,
-                                int seq_q, int kv_len, int hq, int hkv, int hd, float scale, float *out);
+                                int seq_q, int kv_len, int hq, int hkv, int hd, float scale, int window,
+                                float *out);
 
 ORC_EXPORT void orc_flash_attention(const float *Q, const uint16_t *Kc, const uint16_t *Vc,
                                     int seq_q, int kv_len, int hq, int hkv, int hd,
                                     float scale, float *out)
 {
-    flash_attention_any(Q, Kc, Vc, NULL, NULL, NULL, NULL, seq_q, kv_len, hq, hkv, hd, scale, out);
+    flash_attention_any(Q, Kc, Vc, NULL, NULL, NULL, NULL, seq_q, kv_len, hq, hkv, hd, scale, 0, out);
 }
 
 /* The same over an INT8 cache (KV_READ_K / KV_READ_V of the KV_INT8 variant). */
@@ -382,12 +405,23 @@ ORC_EXPORT void orc_flash_attention_kv8(const float *Q, const uint8_t *K8, const
                                         const uint8_t *V8, const uint32_t *Vsz, int seq_q, int kv_len,
                                         int hq, int hkv, int hd, float scale, float *out)
 {
-    flash_attention_any(Q, NULL, NULL, K8, Ksz, V8, Vsz, seq_q, kv_len, hq, hkv, hd, scale, out);
+    flash_attention_any(Q, NULL, NULL, K8, Ksz, V8, Vsz, seq_q, kv_len, hq, hkv, hd, scale, 0, out);
+}
+
+/* Sliding-window FlashAttention (G3CS:673-686): query abs_q sees positions
+ * j_lo .. abs_q, j_lo = abs_q - window when abs_q > window (else 0); the tile
+ * walk starts at j_lo. */
+ORC_EXPORT void orc_flash_attention_window(const float *Q, const uint16_t *Kc, const uint16_t *Vc,
+                                           int seq_q, int kv_len, int hq, int hkv, int hd, float scale,
+                                           int window, float *out)
+{
+    flash_attention_any(Q, Kc, Vc, NULL, NULL, NULL, NULL, seq_q, kv_len, hq, hkv, hd, scale, window, out);
 }
 
 static void flash_attention_any(const float *Q, const uint16_t *Kc, const uint16_t *Vc, const uint8_t *K8,
                                 const uint32_t *Ksz, const uint8_t *V8, const uint32_t *Vsz,
-                                int seq_q, int kv_len, int hq, int hkv, int hd, float scale, float *out)
+                                int seq_q, int kv_len, int hq, int hkv, int hd, float scale, int window,
+                                float *out)
 {
     int grp = hq / (hkv > 0 ? hkv : 1);
     if (grp < 1) grp = 1;
@@ -398,11 +432,12 @@ static void flash_attention_any(const float *Q, const uint16_t *Kc, const uint16
             int kl = kv_len > 1 ? kv_len : 1;
             int abs_q = (kl - seq_q) + qp;
             int j_hi = abs_q < kl - 1 ? abs_q : kl - 1;
+            int j_lo = (window > 0 && abs_q > window) ? abs_q - window : 0;
             float fq[512], acc[512], s[FA_T], p[FA_T], red[FA_T];
             const float *q = Q + ((int64_t)qp * hq + h) * hd;
             for (int d = 0; d < hd; d++) { fq[d] = q[d] * scale; acc[d] = 0.0f; }
             float m = -3.0e38f, l = 0.0f;
-            for (int tile = 0; tile <= j_hi; tile += FA_T) {
+            for (int tile = j_lo; tile <= j_hi; tile += FA_T) {
                 for (int t = 0; t < FA_T; t++) {
                     int j = tile + t;
                     s[t] = -3.0e38f;
@@ -617,7 +652,21 @@ typedef struct {
     int32_t cache_len;
     int32_t kv_quant;                            /* 2: INT8 cache (k_sz / v_sz per layer [capacity, hkv]) */
     uint32_t **k_sz; uint32_t **v_sz;
+    /* Gemma3 variants (Gemma3Model.cs:315-590): arch bits 1 qk-norm (q_norm / k_norm [hd]),
+     * 2 sandwich norms (post_attn_ln / post_ffn_ln [H]; ln2 is then the pre-MLP norm),
+     * 4 GELU GLU; sliding-window layers (window > 0: every layer except each pattern-th)
+     * use the local RoPE tables; attn_scale 0 = hd^-0.5. */
+    int32_t arch, window, pattern;
+    float attn_scale;
+    const uint16_t *rope_cos_local; const uint16_t *rope_sin_local;
+    const uint16_t **q_norm; const uint16_t **k_norm;
+    const uint16_t **post_attn_ln; const uint16_t **post_ffn_ln;
 } orc_model;
+
+static int layer_is_sliding(const orc_model *md, int li)
+{
+    return md->window > 0 && (md->pattern <= 0 || (li + 1) % md->pattern != 0);
+}
 
 /* MiniCPM5Model.Forward(ids, useCache = true, lastPosOnly) (M5M:531-549) with
  * DispatchLayer (M5M:294-518) and DispatchFinalLast / DispatchFinalAll
@@ -630,7 +679,7 @@ ORC_EXPORT int orc_forward(orc_model *md, const int32_t *ids, int seq_len, int l
     const int inner = hq * hd, qkvd = inner + 2 * hkv * hd, S = seq_len;
     if (md->cache_len + S > md->capacity) return -1;
     const int cache_len = md->cache_len, kv_len = cache_len + S;
-    const float scale = powf((float)hd, -0.5f);
+    const float scale = md->attn_scale > 0.0f ? md->attn_scale : powf((float)hd, -0.5f);
 
     float *hidden = malloc(sizeof(float) * S * H), *skip = malloc(sizeof(float) * S * H);
     float *norm = malloc(sizeof(float) * S * H), *qkv = malloc(sizeof(float) * S * qkvd);
@@ -652,27 +701,41 @@ ORC_EXPORT int orc_forward(orc_model *md, const int32_t *ids, int seq_len, int l
             memcpy(k + (int64_t)l * hkv * hd, qkv + (int64_t)l * qkvd + inner, sizeof(float) * hkv * hd);
             memcpy(v + (int64_t)l * hkv * hd, qkv + (int64_t)l * qkvd + inner + hkv * hd, sizeof(float) * hkv * hd);
         }
-        orc_rope_apply(q, S, hq, hd, cache_len, md->rope_cos, md->rope_sin);
-        orc_rope_apply(k, S, hkv, hd, cache_len, md->rope_cos, md->rope_sin);
+        if (md->arch & 1) {                                        /* RmsNormHead on q and k */
+            rmsnorm_heads(q, S * hq, hd, md->q_norm[li], md->eps);
+            rmsnorm_heads(k, S * hkv, hd, md->k_norm[li], md->eps);
+        }
+        const int sw = layer_is_sliding(md, li);
+        const uint16_t *rc = sw && md->rope_cos_local ? md->rope_cos_local : md->rope_cos;
+        const uint16_t *rs = sw && md->rope_sin_local ? md->rope_sin_local : md->rope_sin;
+        const int win = sw ? md->window : 0;
+        orc_rope_apply(q, S, hq, hd, cache_len, rc, rs);
+        orc_rope_apply(k, S, hkv, hd, cache_len, rc, rs);
         if (md->kv_quant == 2) {
             orc_kv_write_int8(k, S, hkv, hd, cache_len, (uint8_t *)md->k_cache[li], md->k_sz[li]);
             orc_kv_write_int8(v, S, hkv, hd, cache_len, (uint8_t *)md->v_cache[li], md->v_sz[li]);
-            orc_flash_attention_kv8(q, (const uint8_t *)md->k_cache[li], md->k_sz[li],
-                                    (const uint8_t *)md->v_cache[li], md->v_sz[li], S, kv_len, hq, hkv, hd,
-                                    scale, att);
+            flash_attention_any(q, NULL, NULL, (const uint8_t *)md->k_cache[li], md->k_sz[li],
+                                (const uint8_t *)md->v_cache[li], md->v_sz[li], S, kv_len, hq, hkv, hd, scale, win,
+                                att);
         } else {
             orc_kv_write(k, S, hkv, hd, cache_len, md->k_cache[li]);
             orc_kv_write(v, S, hkv, hd, cache_len, md->v_cache[li]);
-            orc_flash_attention(q, md->k_cache[li], md->v_cache[li], S, kv_len, hq, hkv, hd, scale, att);
+            flash_attention_any(q, md->k_cache[li], md->v_cache[li], NULL, NULL, NULL, NULL, S, kv_len, hq, hkv, hd,
+                                scale, win, att);
         }
         orc_gemv(att, S, inner, md->w_o[li], md->s_o[li], md->quant, md->group, 0, H, ao);
+        if (md->arch & 2) {                                        /* post-attention norm, then the residual */
+            orc_rmsnorm(ao, S, H, md->post_attn_ln[li], md->eps, norm);
+            memcpy(ao, norm, sizeof(float) * S * H);
+        }
         for (int64_t i = 0; i < (int64_t)S * H; i++) ao[i] = ao[i] + skip[i];     /* AddResidual */
         memcpy(skip, ao, sizeof(float) * S * H);
         orc_rmsnorm(ao, S, H, md->ln2[li], md->eps, hidden);
         /* GateUp1VecCoal (G3CS:1244-1267): gate rows [0,I), up rows [I,2I) */
         orc_gemv(hidden, S, H, md->w_mlp[li], md->s_mlp[li], md->quant, md->group, 0, I, g);
         orc_gemv(hidden, S, H, md->w_mlp[li], md->s_mlp[li], md->quant, md->group, I, I, u);
-        for (int64_t i = 0; i < (int64_t)S * I; i++) mid[i] = silu_ref(g[i]) * u[i];
+        for (int64_t i = 0; i < (int64_t)S * I; i++)
+            mid[i] = ((md->arch & 4) ? gelu_ref(g[i]) : silu_ref(g[i])) * u[i];
         /* Down1VecCoal (G3CS:1269-1282): rows [2I, 2I+H) of the concat, K = I */
         {
             orc_w W = { md->w_mlp[li], md->s_mlp[li], md->quant, md->group };
@@ -683,6 +746,10 @@ ORC_EXPORT int orc_forward(orc_model *md, const int32_t *ids, int seq_len, int l
                     hidden[(int64_t)l * H + n] = coal_dot(mid + (int64_t)l * I, I, &W, base) *
                                                  w_scale(&W, 2ull * I + n);
                 }
+        }
+        if (md->arch & 2) {                                        /* post-FFN norm, then the residual */
+            orc_rmsnorm(hidden, S, H, md->post_ffn_ln[li], md->eps, norm);
+            memcpy(hidden, norm, sizeof(float) * S * H);
         }
         for (int64_t i = 0; i < (int64_t)S * H; i++) hidden[i] = hidden[i] + skip[i];
     }

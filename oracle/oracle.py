@@ -51,6 +51,8 @@ def lib():
         _lib.orc_flash_attention.argtypes = [P, P, P, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int,
                                              C.c_float, P]
         _lib.orc_kv_write_int8.argtypes = [P, C.c_int, C.c_int, C.c_int, C.c_int, P, P]
+        _lib.orc_flash_attention_window.argtypes = [P, P, P, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int,
+                                                    C.c_float, C.c_int, P]
         _lib.orc_flash_attention_kv8.argtypes = [P, P, P, P, P, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int,
                                                  C.c_float, P]
         _lib.orc_argmax.restype = C.c_int
@@ -154,6 +156,18 @@ def flash_attention(q: np.ndarray, k_cache: np.ndarray, v_cache: np.ndarray, kv_
     return out
 
 
+def flash_attention_window(q: np.ndarray, k_cache: np.ndarray, v_cache: np.ndarray, kv_len: int,
+                           hq: int, hkv: int, hd: int, scale: float, window: int) -> np.ndarray:
+    """Sliding-window FA-1 restatement (window <= 0: full attention)."""
+    q = np.ascontiguousarray(q, dtype=np.float32)
+    seq_q = q.size // (hq * hd)
+    out = np.empty((seq_q, hq, hd), np.float32)
+    lib().orc_flash_attention_window(_p(q), _p(np.ascontiguousarray(k_cache, np.uint16)),
+                                     _p(np.ascontiguousarray(v_cache, np.uint16)), seq_q, kv_len, hq, hkv, hd,
+                                     scale, window, _p(out))
+    return out
+
+
 def kv_write_int8(kv_new: np.ndarray, hkv: int, hd: int):
     """WriteCacheFull, INT8 variant, of fp32 rows [seq, hkv, hd] into a fresh cache:
     returns (uint8 [seq, hkv, hd], uint32 (fp16 scale | fp16 zp << 16) [seq, hkv])."""
@@ -234,7 +248,11 @@ class _OrcModel(C.Structure):
                 ("rope_cos", C.c_void_p), ("rope_sin", C.c_void_p),
                 ("k_cache", C.POINTER(C.c_void_p)), ("v_cache", C.POINTER(C.c_void_p)),
                 ("cache_len", C.c_int32), ("kv_quant", C.c_int32),
-                ("k_sz", C.POINTER(C.c_void_p)), ("v_sz", C.POINTER(C.c_void_p))]
+                ("k_sz", C.POINTER(C.c_void_p)), ("v_sz", C.POINTER(C.c_void_p)),
+                ("arch", C.c_int32), ("window", C.c_int32), ("pattern", C.c_int32), ("attn_scale", C.c_float),
+                ("rope_cos_local", C.c_void_p), ("rope_sin_local", C.c_void_p),
+                ("q_norm", C.POINTER(C.c_void_p)), ("k_norm", C.POINTER(C.c_void_p)),
+                ("post_attn_ln", C.POINTER(C.c_void_p)), ("post_ffn_ln", C.POINTER(C.c_void_p))]
 
 
 class OracleModel:
@@ -263,7 +281,7 @@ class OracleModel:
         m.hidden, m.inter, m.layers = cfg.hidden, cfg.inter, L
         m.hq, m.hkv, m.hd, m.vocab = cfg.hq, cfg.hkv, cfg.hd, cfg.vocab
         m.quant, m.group, m.capacity = _QUANT_IDS[cfg.quant], cfg.group, capacity
-        m.eps, m.theta, m.embed_scale = cfg.eps, cfg.theta, 1.0
+        m.eps, m.theta, m.embed_scale = cfg.eps, cfg.theta, getattr(cfg, "embed_scale", 1.0)
         for name in ("w_qkv", "s_qkv", "w_o", "s_o", "w_mlp", "s_mlp", "ln1", "ln2"):
             a = arr(getattr(weights, name))
             self._keep.append(a)
@@ -281,6 +299,20 @@ class OracleModel:
         m.k_sz = C.cast(ks, C.POINTER(C.c_void_p))
         m.v_sz = C.cast(vs, C.POINTER(C.c_void_p))
         m.kv_quant = 2 if kv_int8 else 1
+        # Gemma3 variants
+        m.arch, m.window, m.pattern = getattr(cfg, "arch", 0), getattr(cfg, "window", 0), getattr(cfg, "pattern", 0)
+        m.attn_scale = getattr(cfg, "attn_scale", 0.0)
+        if m.window > 0:
+            tl = getattr(cfg, "theta_local", 0.0) or cfg.theta
+            self.rope_cos_local, self.rope_sin_local = rope_table(capacity, cfg.hd, tl)
+            m.rope_cos_local, m.rope_sin_local = _p(self.rope_cos_local).value, _p(self.rope_sin_local).value
+        for name in ("q_norm", "k_norm", "post_attn", "post_ffn"):
+            lst = getattr(weights, name, [])
+            if lst:
+                a = arr(lst)
+                self._keep.append(a)
+                setattr(m, {"post_attn": "post_attn_ln", "post_ffn": "post_ffn_ln"}.get(name, name),
+                        C.cast(a, C.POINTER(C.c_void_p)))
         m.cache_len = 0
         self.m = m
 

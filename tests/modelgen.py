@@ -24,11 +24,22 @@ class TestConfig:
     group: int = 128
     eps: float = 1e-5
     theta: float = 10000.0
+    # Gemma3 variants: arch bits (1 qk-norm, 2 sandwich norms, 4 GELU), sliding window / pattern,
+    # local RoPE base, softmax scale, embedding scale
+    arch: int = 0
+    window: int = 0
+    pattern: int = 0
+    theta_local: float = 0.0
+    attn_scale: float = 0.0
+    embed_scale: float = 1.0
 
     def du_kwargs(self):
         from deepunity_b200.llm import LlamaConfig
         return LlamaConfig(self.hidden, self.inter, self.layers, self.hq, self.hkv, self.hd, self.vocab,
-                           self.eps, self.theta, group_size=self.group if self.quant == "int4" else 128)
+                           self.eps, self.theta, group_size=self.group if self.quant == "int4" else 128,
+                           arch_flags=self.arch, sliding_window=self.window, sliding_pattern=self.pattern,
+                           rope_theta_local=self.theta_local, attn_scale=self.attn_scale,
+                           embed_scale=self.embed_scale)
 
 
 SMALL = TestConfig(hidden=256, inter=512, layers=2, hq=4, hkv=2, hd=64, vocab=1024)
@@ -46,6 +57,7 @@ class ModelWeights:
         self.files = {}
         self.w_qkv, self.s_qkv, self.w_o, self.s_o, self.w_mlp, self.s_mlp = [], [], [], [], [], []
         self.ln1, self.ln2 = [], []
+        self.q_norm, self.k_norm, self.post_attn, self.post_ffn = [], [], [], []
         ext = {"int8": ".int8.bin", "int4": ".int4.bin", "fp16": ".bin"}[cfg.quant]
 
         def quant(w):
@@ -82,7 +94,23 @@ class ModelWeights:
             self.ln1.append(g1)
             self.ln2.append(g2)
             self.files[f"layer_{li}/input_layernorm.bin"] = g1
-            self.files[f"layer_{li}/post_attention_layernorm.bin"] = g2
+            if cfg.arch & 2:      # sandwich norms: ln2 is the pre-MLP norm under Gemma3's name
+                pa = (rng.standard_normal(H).astype(np.float32) * gamma_std).astype(np.float16).view(np.uint16)
+                pf = (rng.standard_normal(H).astype(np.float32) * gamma_std).astype(np.float16).view(np.uint16)
+                self.post_attn.append(pa)
+                self.post_ffn.append(pf)
+                self.files[f"layer_{li}/post_attention_layernorm.bin"] = pa
+                self.files[f"layer_{li}/pre_feedforward_layernorm.bin"] = g2
+                self.files[f"layer_{li}/post_feedforward_layernorm.bin"] = pf
+            else:
+                self.files[f"layer_{li}/post_attention_layernorm.bin"] = g2
+            if cfg.arch & 1:
+                qn = (rng.standard_normal(hd).astype(np.float32) * gamma_std).astype(np.float16).view(np.uint16)
+                kn = (rng.standard_normal(hd).astype(np.float32) * gamma_std).astype(np.float16).view(np.uint16)
+                self.q_norm.append(qn)
+                self.k_norm.append(kn)
+                self.files[f"layer_{li}/self_attn_q_norm.bin"] = qn
+                self.files[f"layer_{li}/self_attn_k_norm.bin"] = kn
         self.final_norm = (rng.standard_normal(H).astype(np.float32) * gamma_std).astype(np.float16).view(np.uint16)
         self.files["norm.bin"] = self.final_norm
         self.embed = (rng.standard_normal((cfg.vocab, H), dtype=np.float32) * std).astype(np.float16).view(np.uint16)

@@ -317,6 +317,30 @@ def test_rmsnorm_matches_oracle():
     assert relerr(y.cpu().numpy(), ref) < 1e-6
 
 
+# ----------------------------------------------- Gemma3 attention variants
+@pytest.mark.parametrize("hq,hkv,hd,window", [(4, 1, 256, 0), (4, 1, 256, 100), (32, 8, 128, 512), (8, 2, 64, 63)])
+def test_flash_decode_window_and_hd256(hq, hkv, hd, window):
+    """Sliding-window flash-decode (G3CS:673-686) and head_dim 256 (Gemma3-270M) on the
+    cluster kernel, against the oracle's FlashAttention with the same window."""
+    rng = np.random.default_rng(hd + window)
+    B, cap = 3, 1100
+    lens = np.array([40, 700, 1100], np.int32)
+    q = rng.standard_normal((B, hq, hd)).astype(np.float32)
+    kc = rng.standard_normal((B, cap, hkv, hd)).astype(np.float16)
+    vc = rng.standard_normal((B, cap, hkv, hd)).astype(np.float16)
+    scale = 1.0 / np.sqrt(hd)
+    out = torch.empty((B, hq, hd), dtype=torch.float32, device="cuda")
+    args = [dev(a) for a in (q, kc, vc, lens)]
+    _lib.call("du_flash_decode_window", ptr(out), *[ptr(a) for a in args], B, hq, hkv, hd, cap, C.c_float(scale),
+              window, None)
+    torch.cuda.synchronize()
+    got = out.cpu().numpy()
+    for b in range(B):
+        ref = orc.flash_attention_window(q[b:b + 1], kc[b].view(np.uint16), vc[b].view(np.uint16), int(lens[b]),
+                                         hq, hkv, hd, scale, window)[0]
+        assert relerr(got[b], ref) < ATTN_TOL, b
+
+
 # ------------------------------------------------------------- INT8 KV cache
 def _kv_rows(rng, n, hkv, hd):
     """Rows with the reference's edge cases: constant (scale floor), all positive (zp 0),

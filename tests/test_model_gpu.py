@@ -315,3 +315,53 @@ def test_int8_kv_cache_batched():
             assert int(got[i]) == orc.argmax(refs[i]) or _near_tie(refs[i]), (step, i)
         cur = [orc.argmax(r) for r in refs]
     m.Release()
+
+
+# Gemma3 variants on the same kernels (Gemma3Model.cs:315-590): qk-norm, sandwich norms,
+# GELU GLU, sqrt(H) embedding scale, sliding-window layers (every 3rd layer full) with
+# their own RoPE base, a softmax scale of their own
+GEMMA_VARIANTS = [
+    TestConfig(256, 512, 3, 4, 1, 128, 1024, quant="int8", theta=1_000_000.0, arch=7, window=16, pattern=3,
+               theta_local=10000.0, attn_scale=0.1, embed_scale=16.0, eps=1e-6),
+    TestConfig(512, 1024, 3, 2, 1, 256, 1024, quant="int4", group=128, theta=1_000_000.0, arch=7, window=20,
+               pattern=3, theta_local=10000.0, attn_scale=256 ** -0.5, embed_scale=512 ** 0.5, eps=1e-6),
+]
+
+
+@pytest.mark.parametrize("cfg", GEMMA_VARIANTS, ids=lambda c: f"{c.quant}-hd{c.hd}")
+def test_gemma3_variant_greedy_64_matches_oracle(cfg):
+    """A 24-token prompt then 64 greedy steps: positions run well past the sliding window,
+    so the sliding-window layers attend to a moving band and the full layers to all."""
+    w, m = build(cfg, cap=128)
+    om = orc.OracleModel(w, capacity=128)
+    prompt = np.random.default_rng(13).integers(0, cfg.vocab, 24).astype(np.int32)
+    logits, nxt = m.forward(prompt[None, :])
+    ref = om.forward(prompt)
+    assert relerr(logits[0], ref) < LOGIT_TOL
+    toks, rtoks = [int(nxt[0])], [orc.argmax(ref)]
+    for _ in range(63):
+        toks.append(int(m.decode_step([toks[-1]])[0]))
+        r = om.forward([rtoks[-1]])
+        rtoks.append(orc.argmax(r))
+    assert toks == rtoks
+    assert relerr(m.read_logits(1)[0], r) < LOGIT_TOL
+    m.Release()
+
+
+def test_gemma3_variant_int8_kv_teacher_forced():
+    """The Gemma3 variant over the INT8 cache (the qkv-post kernel quantizes k / v rows)."""
+    cfg = GEMMA_VARIANTS[0]
+    w, m = build(cfg, cap=128, kv_quant=KVQuant.INT8)
+    om = orc.OracleModel(w, capacity=128, kv_int8=True)
+    prompt = np.random.default_rng(14).integers(0, cfg.vocab, 24).astype(np.int32)
+    logits, nxt = m.forward(prompt[None, :])
+    ref = om.forward(prompt)
+    assert relerr(logits[0], ref) < KV8_LOGIT_TOL
+    tok = orc.argmax(ref)
+    for step in range(48):
+        got_id = int(m.decode_step([tok])[0])
+        r = om.forward([tok])
+        assert relerr(m.read_logits(1)[0], r) < KV8_LOGIT_TOL, step
+        tok = orc.argmax(r)
+        assert got_id == tok or _near_tie(r), step
+    m.Release()
