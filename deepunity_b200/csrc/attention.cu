@@ -29,9 +29,11 @@
 // partials, atomics or remote-read round trips.
 #include <cooperative_groups.h>
 
+#include <cstring>
 #include <mutex>
 
 #include "attn_impl.cuh"
+#include "gemm_impl.cuh"
 #include "internal.h"
 
 namespace du {
@@ -93,16 +95,75 @@ __host__ __device__ constexpr size_t fdc_work_bytes()
     return (size_t)4 * FD_TILE * (HD + 8) * sizeof(__half) + fd_mma_extra_bytes<HD>() + (KV8 ? fd_kv8_bytes<HD>() : 0);
 }
 
-template <int HD, int C, bool KV8>
-__global__ void __launch_bounds__(FDC_THREADS) flash_decode_cluster_kernel(const FdParams p, int G, int new_rows)
+// Fused O projection (OF): after the combine, the C CTAs of a (row, kv head)
+// cluster hold that kv head's G * HD attention outputs; each CTA multiplies them
+// with its slice of W_o rows (rows [split * R, split * R + R), R = ceil(H / C),
+// this kv head's G * HD columns), copied into shared memory by the bulk-copy unit
+// at kernel start, while attention runs.  The hkv clusters' partial sums meet in
+// global scratch; the cluster that arrives last for a row slice adds them in kv
+// head order to the residual (no cluster waits for another).
+constexpr int FDC_OF_MAX_BYTES = 96 * 1024;         // W_o slice per CTA
+constexpr int FDC_OF_MAX_SCALES = 4096;             // its scales (halves)
+template <int HD>
+__host__ __device__ constexpr size_t fdc_of_bytes()
+{
+    // attention outputs, W_o slice (128-byte aligned: 128 bytes of slack), its scales, mbarrier
+    return (size_t)FD_MAXG * HD * 4 + 128 + FDC_OF_MAX_BYTES + FDC_OF_MAX_SCALES * 2 + 16;
+}
+
+template <int HD, int C, bool KV8, bool OF>
+__global__ void __launch_bounds__(FDC_THREADS)
+    flash_decode_cluster_kernel(const FdParams p, int G, int new_rows, const __grid_constant__ CUtensorMap tm_wo)
 {
     constexpr int PER_MAX = FD_MAXG * HD / C;        // outputs merged per CTA, at most
     extern __shared__ __align__(16) unsigned char fd_smem[];
     __shared__ FdShared<HD> sh;
+    __shared__ int of_abort;
     cg::cluster_group cluster = cg::this_cluster();
     const int split = blockIdx.x, kvh = blockIdx.y, row = blockIdx.z;     // gridDim.x == C == cluster size
     float *rcv_o = reinterpret_cast<float *>(fd_smem + fdc_work_bytes<HD, KV8>());
     float *rcv_ml = rcv_o + C * PER_MAX;             // [C][FD_MAXG][2]
+    unsigned char *of_base = fd_smem + fdc_work_bytes<HD, KV8>() + fdc_recv_bytes<HD, C>();
+    float *att_s = reinterpret_cast<float *>(of_base);                         // [G * HD]
+    // W_o slice: TMA boxes of 256 columns x R rows, [box][row][256 bytes]
+    uint8_t *wo_s = reinterpret_cast<uint8_t *>(
+        (reinterpret_cast<uintptr_t>(of_base + (size_t)FD_MAXG * HD * 4) + 127) & ~(uintptr_t)127);
+    __half *sc_s = reinterpret_cast<__half *>(wo_s + FDC_OF_MAX_BYTES);         // the slice's scales
+    uint64_t *of_bar = reinterpret_cast<uint64_t *>(wo_s + FDC_OF_MAX_BYTES + FDC_OF_MAX_SCALES * 2);
+    const int ghd = G * HD;
+    const int of_rows = (p.H + C - 1) / C, of_n0 = split * of_rows;
+    const int of_nr = OF ? max(0, min(of_rows, p.H - of_n0)) : 0;
+    const int of_rb = p.wo_quant == Q_I4 ? ghd / 2 : ghd;                       // bytes of a slice row
+    const int of_spr = p.wo_quant == Q_I4 ? ghd / p.wo_group : 1;              // scales per slice row
+    if constexpr (OF) {
+        // W_o rows of this CTA (weights, so issued before the dependency wait): one TMA
+        // box per 256 columns; rows past H arrive zero-filled and are not used
+        const uint32_t bar = smem_u32(of_bar);
+        if (threadIdx.x == 0) {
+            of_abort = 0;
+            mbar_init(bar, 1);
+            mbar_fence_init();
+            const int nb = of_rb / 256;
+            mbar_arrive_expect_tx(bar, (uint32_t)(nb * of_rows * 256));
+            const uint64_t pol = l2_policy_evict_first();
+            for (int b = 0; b < nb; b++)
+                tma_load_2d(smem_u32(wo_s + (size_t)b * of_rows * 256), &tm_wo, bar, kvh * of_rb + b * 256, of_n0, pol);
+        }
+        // the slice's scales with plain loads, all of a thread's loads issued before its stores
+        const size_t spr_all = p.wo_quant == Q_I4 ? (size_t)p.hq * HD / p.wo_group : 1;
+        constexpr int SPT = FDC_OF_MAX_SCALES / FDC_THREADS;
+        __half sv[SPT];
+#pragma unroll
+        for (int k = 0; k < SPT; k++) {
+            const int i = threadIdx.x + k * FDC_THREADS, r = i / of_spr, g = i - r * of_spr;
+            sv[k] = i < of_nr * of_spr
+                        ? p.wo_scales[(size_t)(of_n0 + r) * spr_all + (p.wo_quant == Q_I4 ? (size_t)kvh * of_spr + g : 0)]
+                        : __float2half(0.0f);
+        }
+#pragma unroll
+        for (int k = 0; k < SPT; k++)
+            if (threadIdx.x + k * FDC_THREADS < of_nr * of_spr) sc_s[threadIdx.x + k * FDC_THREADS] = sv[k];
+    }
     // first phase of the cluster barrier: every CTA of the cluster has started before
     // any CTA stores into a peer's shared memory (waited on just before the push)
     asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
@@ -143,15 +204,84 @@ __global__ void __launch_bounds__(FDC_THREADS) flash_decode_cluster_kernel(const
             L = fmaf(rcv_ml[(r * FD_MAXG + g) * 2 + 1], w, L);
             O = fmaf(rcv_o[r * PER_MAX + i], w, O);
         }
-        p.out[((size_t)row * p.hq + kvh * G) * HD + o] = O * (1.0f / fmaxf(L, 1e-12f));
+        const float v = O * (1.0f / fmaxf(L, 1e-12f));
+        p.out[((size_t)row * p.hq + kvh * G) * HD + o] = v;
+        if (OF)     // every CTA of the cluster gets this kv head's outputs for its W_o rows
+#pragma unroll 4
+            for (int j = 0; j < C; j++) cluster.map_shared_rank(att_s, j)[o] = v;
+    }
+    if constexpr (OF) {
+        cluster.sync();      // att_s complete in every CTA; no peer stores after this point
+        const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+        const int cpl = ghd >> 5;                     // columns per lane: 8 or 16
+        float xa[16];
+#pragma unroll
+        for (int j = 0; j < 16; j++) xa[j] = j < cpl ? att_s[lane * cpl + j] : 0.0f;
+        const bool ok = mbar_wait(smem_u32(of_bar), 0, &of_abort, p.err, 2000000000ull);
+        if (ok) {
+            for (int r = warp; r < of_nr; r += FDC_THREADS / 32) {
+                const int n = of_n0 + r;
+                // byte c of slice row r: box c / 256, [r][c % 256]
+                auto wr = [&](int c) { return wo_s + ((size_t)(c >> 8) * of_rows + r) * 256 + (c & 255); };
+                float a = 0.0f, d;
+                if (p.wo_quant == Q_I4) {
+                    // low nibble = even column; nibble j of word w is column lane * cpl + 8 w + j
+                    const uint2 w2 = cpl == 16 ? *reinterpret_cast<const uint2 *>(wr(lane * 8))
+                                               : make_uint2(*reinterpret_cast<const uint32_t *>(wr(lane * 4)), 0u);
+#pragma unroll
+                    for (int j = 0; j < 16; j++)
+                        if (j < cpl) {
+                            const uint32_t w = j < 8 ? w2.x : w2.y;
+                            a = fmaf((float)((int)((w >> (4 * (j & 7))) & 15u) - 8), xa[j], a);
+                        }
+                    d = __half2float(sc_s[r * of_spr + (lane * cpl) / p.wo_group]);
+                } else {
+                    const uint4 w4 = cpl == 16 ? *reinterpret_cast<const uint4 *>(wr(lane * 16))
+                                               : make_uint4(*reinterpret_cast<const uint32_t *>(wr(lane * 8)),
+                                                            *reinterpret_cast<const uint32_t *>(wr(lane * 8 + 4)), 0u, 0u);
+                    const uint32_t ww[4] = {w4.x, w4.y, w4.z, w4.w};
+#pragma unroll
+                    for (int j = 0; j < 16; j++)
+                        if (j < cpl) a = fmaf((float)(int8_t)((ww[j >> 2] >> (8 * (j & 3))) & 0xFFu), xa[j], a);
+                    d = __half2float(sc_s[r]);
+                }
+                const float v = warp_sum(a * d);
+                if (lane == 0) p.opart[(size_t)kvh * p.H + n] = v;
+            }
+        }
+        __syncthreads();
+        // this kv head's part of rows [of_n0, of_n0 + of_nr) is out; the last kv head to
+        // arrive adds all parts in kv head order to the residual
+        if (threadIdx.x == 0) {
+            __threadfence();
+            sh.last = atomicAdd(&p.ocnt[split], 1u) == (unsigned)(p.hkv - 1) ? 1u : 0u;
+        }
+        __syncthreads();
+        if (sh.last) {
+            __threadfence();
+            for (int r = threadIdx.x; r < of_nr; r += FDC_THREADS) {
+                const int n = of_n0 + r;
+                float part[FD_MAXG * 2];                // every kv head's part, loads issued together
+#pragma unroll
+                for (int k = 0; k < FD_MAXG * 2; k++)
+                    part[k] = k < p.hkv ? __ldcg(p.opart + (size_t)k * p.H + n) : 0.0f;
+                float sum = 0.0f;
+#pragma unroll
+                for (int k = 0; k < FD_MAXG * 2; k++)
+                    if (k < p.hkv) sum += part[k];
+                p.resid[n] += sum;
+            }
+            if (threadIdx.x == 0) p.ocnt[split] = 0u;     // ready for the next launch
+        }
     }
 }
 
-template <int HD, int C, bool KV8>
-static int fdc_launch(const FdParams &p, int G, int nq, cudaStream_t st, int new_rows, bool probe, int *fits)
+template <int HD, int C, bool KV8, bool OF = false>
+static int fdc_launch(const FdParams &p, int G, int nq, cudaStream_t st, int new_rows, bool probe, int *fits,
+                      const CUtensorMap *tm = nullptr)
 {
-    auto kern = flash_decode_cluster_kernel<HD, C, KV8>;
-    const size_t smem = fdc_work_bytes<HD, KV8>() + fdc_recv_bytes<HD, C>();
+    auto kern = flash_decode_cluster_kernel<HD, C, KV8, OF>;
+    const size_t smem = fdc_work_bytes<HD, KV8>() + fdc_recv_bytes<HD, C>() + (OF ? fdc_of_bytes<HD>() : 0);
     int rc = ensure_func_attrs((const void *)kern, (int)smem, C > 8);
     if (rc) return rc;
     cudaLaunchConfig_t cfg = {};
@@ -174,7 +304,9 @@ static int fdc_launch(const FdParams &p, int G, int nq, cudaStream_t st, int new
         *fits = n;
         return DU_OK;
     }
-    DU_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, p, G, new_rows));
+    CUtensorMap none;
+    memset(&none, 0, sizeof none);
+    DU_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, p, G, new_rows, tm ? *tm : none));
     return DU_OK;
 }
 
@@ -193,16 +325,77 @@ static int fdc_cluster_size(const FdParams &p, int G, cudaStream_t st)
         const int rc = fdc_launch<HD, 16, KV8>(p, G, 1, st, -1, true, &n16);
         if (rc != DU_OK) cudaGetLastError();    // the probe's own failure: 16-CTA clusters unavailable
         chosen[dev & 63] = (rc == DU_OK && n16 > 0) ? 16 : 8;
+        const char *e = getenv("DU_FD_CLUSTER");   // tuning knob: 8 forces 8-CTA clusters
+        if (e != nullptr && atoi(e) == 8) chosen[dev & 63] = 8;
     }
     return chosen[dev & 63];
 }
 
+// Cluster size per launch.  16 splits only when there are few clusters (query rows x
+// kv heads <= 8) and the cache is fp16: 16-CTA clusters hold a whole SM each and at
+// most 7 are resident on a B200, so with more clusters the 8-CTA form (about twice
+// as many resident) wins despite twice the positions per CTA.  Measured on the
+// 8B shapes (32 / 8 heads of 128, CUDA-graph timed): batch 8, ctx 512 24.9 -> 13.2 us,
+// batch 32, ctx 2048 134.8 -> 96.1 us, INT8 cache batch 1, ctx 512 9.1 -> 4.9 us;
+// batch 1, ctx 8192 stays on 16 (19.2 vs 26.0 us).
 template <int HD, bool KV8>
 static int fdc_dispatch(const FdParams &p, int G, int nq, cudaStream_t st, int new_rows)
 {
     int dummy = 0;
-    return fdc_cluster_size<HD, KV8>(p, G, st) == 16 ? fdc_launch<HD, 16, KV8>(p, G, nq, st, new_rows, false, &dummy)
-                                                     : fdc_launch<HD, 8, KV8>(p, G, nq, st, new_rows, false, &dummy);
+    const bool few = !KV8 && (int64_t)nq * p.hkv <= 8;
+    return few && fdc_cluster_size<HD, KV8>(p, G, st) == 16
+               ? fdc_launch<HD, 16, KV8>(p, G, nq, st, new_rows, false, &dummy)
+               : fdc_launch<HD, 8, KV8>(p, G, nq, st, new_rows, false, &dummy);
+}
+
+// Whether flash-decode with the fused O projection can run: one query row, 16-CTA
+// clusters, fp16 cache, G * HD of 256 or 512, INT4 / INT8 W_o, a slice that fits.
+bool flash_decode_fuse_o_supported(int nq, int hq, int hkv, int hd, int H, int quant, int group)
+{
+    if (nq != 1 || hkv <= 0 || hq % hkv != 0 || (hd != 64 && hd != 128)) return false;
+    const int ghd = hq / hkv * hd;
+    if (ghd != 256 && ghd != 512) return false;
+    if (quant != Q_I4 && quant != Q_I8) return false;
+    if (quant == Q_I4 && (group < 16 || (ghd / 32) % 8 != 0 || group % (ghd / 32) != 0)) return false;
+    const int rb = quant == Q_I4 ? ghd / 2 : ghd;
+    if ((size_t)((H + 15) / 16) * rb > (size_t)FDC_OF_MAX_BYTES || rb % 256 != 0 || (H + 15) / 16 > 256) return false;
+    if ((size_t)((H + 15) / 16) * (quant == Q_I4 ? ghd / group : 1) > (size_t)FDC_OF_MAX_SCALES) return false;
+    if (hkv > FD_MAXG * 2) return false;
+    FdParams p = {};
+    p.hq = hq; p.hkv = hkv;
+    if (hd == 128 ? fdc_cluster_size<128, false>(p, hq / hkv, 0) != 16 : fdc_cluster_size<64, false>(p, hq / hkv, 0) != 16)
+        return false;
+    // every kv head's cluster must be resident at once: a second wave of 16-CTA clusters
+    // costs more than the separate O GEMV saves (8B shapes: 8 clusters, 7 resident,
+    // 41 vs 8 + 10.5 us serialised)
+    int fits = 0;
+    const int rc = hd == 128 ? fdc_launch<128, 16, false, true>(p, hq / hkv, 1, 0, -1, true, &fits)
+                             : fdc_launch<64, 16, false, true>(p, hq / hkv, 1, 0, -1, true, &fits);
+    if (rc != DU_OK) cudaGetLastError();      // the probe's own failure
+    return rc == DU_OK && fits >= hkv;
+}
+
+int launch_flash_decode_fuse_o(const float *q, const __half *kc, const __half *vc, const int *seq_of, const int *kv_len,
+                               int kv_len_add, int hq, int hkv, int hd, int cap, float scale, float *att, cudaStream_t st,
+                               int new_rows, const FuseO &o)
+{
+    FdParams p = {};
+    p.q = q; p.k_cache = kc; p.v_cache = vc; p.seq_of = seq_of; p.kv_len = kv_len; p.kv_len_add = kv_len_add;
+    p.hq = hq; p.hkv = hkv; p.cap = cap; p.scale = scale; p.out = att;
+    p.wo = o.w; p.wo_scales = o.scales; p.wo_quant = o.quant; p.wo_group = o.group; p.H = o.H;
+    p.resid = o.resid; p.opart = o.part; p.ocnt = o.cnt; p.err = o.err;
+    int dummy = 0;
+    const int G = hq / hkv, rb = o.quant == Q_I4 ? G * hd / 2 : G * hd;
+    // W_o as bytes [H][row bytes]; box 256 bytes x ceil(H / 16) rows
+    CUtensorMap tm;
+    const uint64_t row_bytes = o.quant == Q_I4 ? (uint64_t)hq * hd / 2 : (uint64_t)hq * hd;
+    int rc = make_tmap(&tm, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, o.w, row_bytes, (uint64_t)o.H, 256u,
+                       (uint32_t)((o.H + 15) / 16), CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (rc) return rc;
+    if (rb % 256 != 0) return fail(DU_EINVAL, "flash_decode_fuse_o: W_o slice rows must be multiples of 256 bytes");
+    if (hd == 128) return fdc_launch<128, 16, false, true>(p, G, 1, st, new_rows, false, &dummy, &tm);
+    if (hd == 64) return fdc_launch<64, 16, false, true>(p, G, 1, st, new_rows, false, &dummy, &tm);
+    return fail(DU_EINVAL, "flash_decode_fuse_o: head_dim 64/128");
 }
 
 int launch_flash_decode_cluster(const float *q, const __half *kc, const __half *vc, const int *seq_of,

@@ -31,6 +31,15 @@ struct FdParams {
     const uint8_t *k8, *v8;
     const uint32_t *ksz, *vsz;
     int window;                  // > 0: a query at position kv_len - 1 sees positions >= kv_len - 1 - window
+    // O projection fused after the cluster combine (the OF instantiations; one query row):
+    // resid[n] += sum over kv heads of W_o[n][kvh's G*HD columns] . att(kvh)
+    const uint8_t *wo;           // INT4 nibbles or INT8 bytes, row-major [H][hq * HD]
+    const __half *wo_scales;     // INT4 [H][hq * HD / group], INT8 [H]
+    int wo_quant, wo_group, H;
+    float *resid;                // [H]
+    float *opart;                // [hkv][H] per-kv-head partial sums
+    unsigned *ocnt;              // [C] arrivals per row slice, zero between launches
+    int *err;                    // a bounded wait that gave up
 };
 
 // Shared memory of one unit: K/V tiles (dynamic, 4 * FD_TILE * (HD + 8) halves) + these.

@@ -450,8 +450,8 @@ static EncodeTiledFn encode_fn()
 }
 
 // 2-D tensor map over a row-major [rows, inner] array (inner elements contiguous).
-static int make_tmap(CUtensorMap *tm, CUtensorMapDataType dt, int esize, const void *ptr, uint64_t inner,
-                     uint64_t rows, uint32_t box_inner, uint32_t box_rows, CUtensorMapSwizzle sw)
+int make_tmap(CUtensorMap *tm, CUtensorMapDataType dt, int esize, const void *ptr, uint64_t inner, uint64_t rows,
+              uint32_t box_inner, uint32_t box_rows, CUtensorMapSwizzle sw)
 {
     EncodeTiledFn enc = encode_fn();
     if (!enc) return fail(DU_ECUDA, "gemm: cuTensorMapEncodeTiled is unavailable");

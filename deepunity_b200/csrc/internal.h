@@ -1,6 +1,8 @@
 // internal.h -- declarations shared by the library's translation units.
 #pragma once
 
+#include <cuda.h>
+
 #include "../../include/deepunity_cuda.h"
 #include "common.cuh"
 
@@ -57,6 +59,25 @@ int launch_flash_decode_cluster(const float *q, const __half *kc, const __half *
                                 const int *kv_len, int kv_len_add, int nq, int hq, int hkv, int hd, int cap,
                                 float scale, float *out, cudaStream_t st, int new_rows = -1,
                                 const Kv8Cache *kv8 = nullptr, int window = 0);
+// Flash-decode of one query row with the O projection fused after the cluster
+// combine: resid += W_o . att (attention.cu).
+struct FuseO {
+    const uint8_t *w;            // W_o [H][hq * hd], INT4 or INT8
+    const __half *scales;
+    int quant, group, H;
+    float *resid;                // [H]
+    float *part;                 // [hkv][H] scratch
+    unsigned *cnt;               // [16] arrivals, zero between launches
+    int *err;
+};
+// 2-D tiled tensor map (row-major [rows][inner] elements of esize bytes; box
+// [box_rows][box_inner]) through the driver's encoder (gemm.cu).
+int make_tmap(CUtensorMap *tm, CUtensorMapDataType dt, int esize, const void *ptr, uint64_t inner, uint64_t rows,
+              uint32_t box_inner, uint32_t box_rows, CUtensorMapSwizzle sw);
+bool flash_decode_fuse_o_supported(int nq, int hq, int hkv, int hd, int H, int quant, int group);
+int launch_flash_decode_fuse_o(const float *q, const __half *kc, const __half *vc, const int *seq_of, const int *kv_len,
+                               int kv_len_add, int hq, int hkv, int hd, int cap, float scale, float *att, cudaStream_t st,
+                               int new_rows, const FuseO &o);
 // INT8 KV: quantizes fp32 rows [M][nkv][hkv][hd] (nkv 2: K then V; 1: K only) into the
 // cache at sequence seq_of[m] (or seq_off + m), position pos[m] (or pos_base + m).
 int launch_kv_quant_int8(const float *stage, int M, int nkv, int hkv, int hd, const int *pos, int pos_base,

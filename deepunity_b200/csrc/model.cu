@@ -120,6 +120,8 @@ static int check_cfg(const du_model_config &c)
 
 // -------------------------------------------------------------- creation
 
+static int qt_of(int quant);
+
 static int model_alloc(du_model *m)
 {
     int rc = DU_OK;
@@ -188,6 +190,18 @@ static int model_alloc(du_model *m)
     m->inter = (float *)dalloc(m, sizeof(float) * T * m->I_l, &rc);
     if (m->kv8) m->kv_stage = (float *)dalloc(m, sizeof(float) * T * 2 * m->hkv_l * hd, &rc);
     if (m->arch & DU_ARCH_QK_NORM) m->qkv_buf = (float *)dalloc(m, sizeof(float) * T * m->qkv_rows, &rc);
+    // one-row decode steps fold the O projection into flash-decode when the shapes allow
+    // (DU_FUSE_ATTN_O=0 in the environment keeps them separate)
+    {
+        const char *e = getenv("DU_FUSE_ATTN_O");
+        const bool want = e == nullptr || atoi(e) != 0;
+        m->fuse_o = want && m->tp == 1 && !m->kv8 && !(m->arch & DU_ARCH_SANDWICH) &&
+                    flash_decode_fuse_o_supported(1, m->hq_l, m->hkv_l, hd, H, qt_of(m->quant), m->group);
+        if (m->fuse_o) {
+            m->o_part = (float *)dalloc(m, sizeof(float) * (size_t)m->hkv_l * H, &rc);
+            m->o_cnt = (unsigned *)dalloc(m, sizeof(unsigned) * 16, &rc);
+        }
+    }
     m->logits = (float *)dalloc(m, sizeof(float) * m->maxb * m->V_l, &rc);
     if (m->tp > 1) m->logits_all = (float *)dalloc(m, sizeof(float) * m->tp * m->maxb * m->V_l, &rc);
     m->am_parts = 2 * num_sms();
@@ -686,6 +700,18 @@ static int enqueue_stage(du_model *m, const StepIO &io, int l, int stage, bool c
     cudaStream_t st = m->stream;
     int rc = DU_OK;
     const bool sw = layer_sliding(m, l);
+    const bool fused_o = m->fuse_o && M == 1 && collective && !sw;
+    if (stage == ST_O && fused_o) return DU_OK;      // ran inside flash-decode
+    if (stage == ST_ATTN && fused_o) {
+        const Layer &ly = m->layers[l];
+        FuseO o = {};
+        o.w = ly.w_o; o.scales = ly.s_o; o.quant = qt; o.group = m->group; o.H = H;
+        o.resid = m->x_res; o.part = m->o_part; o.cnt = m->o_cnt; o.err = m->d_err;
+        return launch_flash_decode_fuse_o(m->q, m->k_cache + (size_t)l * m->kv_layer_elems,
+                                          m->v_cache + (size_t)l * m->kv_layer_elems, io.seq_of, io.kv_len,
+                                          io.kv_len_add, m->hq_l, m->hkv_l, hd, m->cap, m->attn_scale, m->att, st,
+                                          io.kv_new, o);
+    }
     if (stage == ST_ATTN) {
         const int window = sw ? m->window : 0;
         if (m->kv8) {

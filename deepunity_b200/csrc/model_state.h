@@ -58,6 +58,8 @@ struct du_model {
     float attn_scale = 0.0f;                             // softmax scale
     __half *rope_cos_local = nullptr, *rope_sin_local = nullptr;   // RoPE of the sliding-window layers
     float *qkv_buf = nullptr;                            // qk-norm models: QKV GEMV output [T][qkv_rows]
+    bool fuse_o = false;                                 // one-row decode: O projection inside flash-decode
+    float *o_part = nullptr; unsigned *o_cnt = nullptr;  // its per-kv-head partial sums and arrival counters
     // device state
     int *d_cache_len = nullptr;             // [maxb]
     int *d_ids = nullptr;                   // [max_tokens] input ids
