@@ -53,6 +53,9 @@ def parse():
     ap.add_argument("--nccl-only", action="store_true", help="TP: decode reductions with ncclAllReduce only")
     ap.add_argument("--sweep", choices=["gemv", "attn"], default=None,
                     help="kernel sweeps (one JSON line per case): config-2 GEMV, config-3 flash-decode")
+    ap.add_argument("--gemv-phases", action="store_true",
+                    help="timing build (python -m deepunity_b200.build --stamps): per-CTA phase stamps of the "
+                         "decode GEMVs over two decode steps, medians per stage boundary")
     ap.add_argument("--case", default=None, help="--sweep gemv: one cell quant:N:K:M, quant int4 / int8 / f16 (e.g. int4:14336:4096:1)")
     ap.add_argument("--reps", type=int, default=0, help="--sweep: timed launches per case (0 = auto)")
     ap.add_argument("--model", choices=["llama-8b", "llama-1.1b"], default="llama-8b",
@@ -625,8 +628,95 @@ def run_sweep_attn(args):
                 del kc, vc
 
 
+def run_gemv_phases(args):
+    """Where the time of a decode GEMV goes, from the timing build's per-CTA
+    %globaltimer stamps (gemv_stamps.cuh): for each stage boundary (previous GEMV
+    -> this GEMV; attention sits between QKV and O), medians over the layers of the
+    second of two decode steps of: this launch's first / median / last CTA entry,
+    the moment its dependency wait returned (one instant for every CTA), activation
+    staging, the weight stream of the last warp and the last exit, all in ns after
+    the previous GEMV's last stamp; and per SM the gap between the previous
+    kernel's last stamp on that SM and this kernel's first CTA entry there."""
+    import ctypes as C
+    import torch
+    from deepunity_b200 import _lib
+    from deepunity_b200.build import STAMPS_LIB
+    if not os.path.exists(STAMPS_LIB):
+        raise SystemExit(f"{STAMPS_LIB} is missing: python -m deepunity_b200.build --stamps")
+    _lib.LIB_PATH = STAMPS_LIB          # before the library is first loaded
+    from deepunity_b200.llm import CONFIGS, KVQuant, LlamaForCausalLM, LLMQuant
+    torch.cuda.set_device(0)
+    cfg = CONFIGS[args.model]
+    quant = LLMQuant.INT4 if args.model == "llama-8b" else LLMQuant.INT8
+    m = LlamaForCausalLM(cfg, quant, kv_quant=KVQuant.INT8 if args.kv == "int8" else KVQuant.FP16,
+                         max_context_length=args.prompt + 64, max_batch=1, seed=0, device=0)
+    prompt = np.random.default_rng(0).integers(0, cfg.vocab_size, (1, args.prompt)).astype(np.int32)
+    _, nxt = m.forward(prompt, want_logits=False)
+    toks = m.decode_loop(nxt.copy(), max(args.warmup, 3))
+    L = C.CDLL(STAMPS_LIB)
+    torch.cuda.synchronize()
+    if L.du_gemv_stamps_reset() != 0:
+        raise SystemExit("du_gemv_stamps_reset failed")
+    m.decode_loop(toks[-1].copy(), 2)
+    torch.cuda.synchronize()
+    slots, ctas = C.c_int(), C.c_int()
+    L.du_gemv_stamps_read(None, None, C.byref(slots), C.byref(ctas))
+    buf = np.zeros(slots.value * ctas.value * 8, np.uint64)
+    cnt = np.zeros(ctas.value, np.uint32)
+    if L.du_gemv_stamps_read(buf.ctypes.data_as(C.c_void_p), cnt.ctypes.data_as(C.c_void_p),
+                             C.byref(slots), C.byref(ctas)) != 0:
+        raise SystemExit("du_gemv_stamps_read failed")
+    buf = buf.reshape(slots.value, ctas.value, 8).astype(np.int64)
+    n0 = int(cnt[0])
+    if n0 < 4 or n0 > slots.value or n0 % 2:
+        raise SystemExit(f"unexpected launch count {n0}")
+    tag = lambda s_, c: (int(buf[s_, c, 7] >> 40), int((buf[s_, c, 7] >> 16) & 0xFFFFFF))
+    # each CTA index's records are its launches in order; CTA 0 takes part in all of them
+    seqs = [[tag(s_, c) for s_ in range(int(cnt[c]))] for c in range(ctas.value)]
+    seq0 = seqs[0]
+    part = []                                   # per launch: {cta: slot}
+    for k in range(n0):
+        part.append({})
+    for c in range(ctas.value):
+        j = 0
+        for k in range(n0):
+            if j < len(seqs[c]) and seqs[c][j] == seq0[k]:
+                part[k][c] = j
+                j += 1
+    H, I = cfg.hidden_size, cfg.intermediate_size
+    hd = cfg.head_dim
+    names = {((cfg.num_heads_q + 2 * cfg.num_heads_kv) * hd, H): "qkv", (H, cfg.num_heads_q * hd): "o_proj",
+             (2 * I, H): "gate_up", (H, I): "down"}
+    def rec(k):
+        cs = sorted(part[k])
+        return np.array([buf[part[k][c], c, :] for c in cs])
+    out = {}
+    for k in range(n0 // 2 + 1, n0):
+        a, b = rec(k - 1), rec(k)
+        na, nb = names.get(seq0[k - 1], "lm_head"), names.get(seq0[k], "lm_head")
+        if "lm_head" in (na, nb):
+            continue
+        a_last = np.maximum(a[:, 4], a[:, 5])
+        t0 = a_last.max()
+        a_sm, b_sm = a[:, 7] & 0xFFFF, b[:, 7] & 0xFFFF
+        hand = [b[b_sm == s_, 0].min() - a_last[a_sm == s_].max() for s_ in np.unique(b_sm) if (a_sm == s_).any()]
+        row = [b[:, 0].min() - t0, np.median(b[:, 0]) - t0, b[:, 0].max() - t0, b[:, 2].min() - t0,
+               np.median(b[:, 3] - b[:, 2]), np.median(b[:, 4] - b[:, 3]), (b[:, 4] - b[:, 3]).max(),
+               np.maximum(b[:, 4], b[:, 5]).max() - t0, np.median(hand) if hand else float("nan")]
+        out.setdefault(f"{na} -> {nb}", []).append(row)
+    keys = ["entry_first", "entry_median", "entry_last", "dependency_met", "staging_median", "stream_median",
+            "stream_max", "last_exit", "sm_handoff_median"]
+    for key, rows in out.items():
+        med = np.median(np.array(rows, dtype=np.float64), axis=0)
+        print(json.dumps({"gemv_phases": key, "layers": len(rows), "unit": "ns after the previous GEMV's last stamp",
+                          **{k_: round(float(v), 0) for k_, v in zip(keys, med)},
+                          "model": args.model, "kv": args.kv, "prompt": args.prompt}), flush=True)
+
+
 def main():
     args = parse()
+    if args.gemv_phases:
+        return run_gemv_phases(args)
     if args.sweep == "gemv":
         return run_sweep_gemv(args)
     if args.sweep == "attn":

@@ -70,6 +70,29 @@ def build(force: bool = False, verbose: bool = False) -> str:
     return LIB
 
 
+STAMPS_LIB = os.path.join(HERE, "libdeepunity_cuda_stamps.so")
+
+
+def build_stamps() -> str:
+    """The timing build: the library with gemv.cu compiled under DU_GEMV_STAMPS
+    (per-CTA phase stamps of every decode GEMV launch, gemv_stamps.cuh), for
+    ``bench.py --gemv-phases``.  The other objects are those of the library."""
+    build()
+    objdir = os.path.join(HERE, "_build")
+    flags = ARCH + ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC,-fvisibility=hidden",
+                    "--expt-relaxed-constexpr", "-ccbin", "g++", "-DDU_GEMV_STAMPS"]
+    obj = os.path.join(objdir, "gemv_stamps.o")
+    subprocess.run([nvcc(), "-c", os.path.join(CSRC, "gemv.cu"), "-o", obj] + flags, check=True)
+    objs = [obj] + [os.path.join(objdir, s.replace(".cu", ".o")) for s in SOURCES if s != "gemv.cu"]
+    tmp = STAMPS_LIB + ".tmp"
+    subprocess.run([nvcc(), "-shared", "-o", tmp] + objs + ARCH + ["-ccbin", "g++", "-ldl", "-lcudart"], check=True)
+    os.replace(tmp, STAMPS_LIB)
+    return STAMPS_LIB
+
+
 if __name__ == "__main__":
-    build(force="--force" in sys.argv, verbose="-v" in sys.argv)
-    print(LIB)
+    if "--stamps" in sys.argv:
+        print(build_stamps())
+    else:
+        build(force="--force" in sys.argv, verbose="-v" in sys.argv)
+        print(LIB)

@@ -1,6 +1,9 @@
 // gemv.cu -- standalone decode GEMV kernel (device code in gemv_impl.cuh) and its launcher.
 #include <cstdlib>
 
+#ifdef DU_GEMV_STAMPS
+#include "gemv_stamps.cuh"     // timing build: per-CTA phase stamps (libdeepunity_cuda_stamps.so)
+#endif
 #include "gemv_impl.cuh"
 #include "internal.h"
 

@@ -35,9 +35,14 @@ __device__ __forceinline__ float gv_xval(const GemvParams &p, const float *xr, f
     return v;
 }
 
+// Residual rows a CTA of an EPI_RESID launch keeps in shared memory (more rows:
+// the epilogue reads the residual from global memory instead).
+constexpr int GV_YRES_ROWS = 32;
+
 // Shared-memory scratch a GEMV run needs besides the ring and activation stage.
 template <int MT, int NW = GV_WARPS>
 struct __align__(16) GemvShared {
+    float yres[GV_YRES_ROWS * MT];   // EPI_RESID: this CTA's residual rows, [row - first row][token]
     float red[2 * NW];
     float ssq[NW][MT];   // per-warp sums of squares (RMSNorm)
     float xscale[MT];          // per-token factor of the folded dot product
@@ -286,9 +291,12 @@ __host__ __device__ constexpr size_t gemv_ring_bytes()
 // holds every value); lane j * MT + m owns output (row j, token m).
 // TPR: the EPI_TP_RESID kernels (a separate instantiation, so that the other
 // epilogues compile exactly as without it): each output goes to every rank.
+// yres (EPI_RESID, may be null): the residual of rows yr0.. staged in shared memory
+// before the stream, so that the epilogue only stores.
 template <int QT, int MT, int RW, bool TPR = false>
 __device__ __forceinline__ void gv_epilogue(const GemvParams &p, int lr0, const float (&v)[RW][MT], float *am_v,
-                                        int *am_i, int lane, unsigned tp_s = 0u)
+                                        int *am_i, int lane, unsigned tp_s = 0u, const float *yres = nullptr,
+                                        int yr0 = 0)
 {
     if constexpr (TPR) {
 #pragma unroll
@@ -333,6 +341,7 @@ __device__ __forceinline__ void gv_epilogue(const GemvParams &p, int lr0, const 
                         float f = v[j][m];
                         if (QT == Q_I8) f *= gv_row_scale<QT>(p, lr);
                         if (p.epi == EPI_STORE) p.y[(size_t)m * p.ldy + lr] = f;
+                        else if (yres != nullptr) p.y[(size_t)m * p.ldy + lr] = yres[(lr - yr0) * MT + m] + f;
                         else p.y[(size_t)m * p.ldy + lr] += f;      // EPI_RESID
                     }
                 }
@@ -482,6 +491,8 @@ struct GemvStream {
     int ipr[RW];
     uint64_t pol;         // L2 evict-first policy of the weight stream
     unsigned tp_s;        // TPR: sequence number of this launch's reduction
+    const float *yres;    // EPI_RESID: residual rows in shared memory (null: read y in the epilogue)
+    int yr0;              // first row of yres
 
     __device__ __forceinline__ int unit_lo(int w) const { return (int)(((int64_t)w * U) / NW); }
 
@@ -555,7 +566,7 @@ struct GemvStream {
     __device__ __forceinline__ void epilogue(const GemvParams &p, int lr0, const float (&v)[RW][MT], float *am_v,
                                              int *am_i) const
     {
-        gv_epilogue<QT, MT, RW, TPR>(p, lr0, v, am_v, am_i, lane, tp_s);
+        gv_epilogue<QT, MT, RW, TPR>(p, lr0, v, am_v, am_i, lane, tp_s, yres, yr0);
     }
 
     // Phase 2: activations -> smem, stream, epilogue.  All threads of the CTA call it.
@@ -565,7 +576,24 @@ struct GemvStream {
                                         int ncta, AfterStage after_stage)
     {
         uint4 *xq = reinterpret_cast<uint4 *>(x_smem);
+        // EPI_RESID: the residual of this CTA's rows, loaded now (the previous kernels are
+        // complete) so that the loads overlap the activation staging and the epilogues
+        // do not wait on a read of y
+        yres = nullptr;
+        yr0 = g_begin * RW;
+        const int yrows = min((g_begin + U / S) * RW, p.N) - yr0;
+        const bool ystage = !TPR && p.epi == EPI_RESID && yrows > 0 && yrows <= GV_YRES_ROWS;
+        float yv = 0.0f;
+        if (ystage && (int)threadIdx.x < yrows * MT) {
+            const int r = threadIdx.x / MT, m = threadIdx.x - r * MT;
+            if (m < p.M) yv = p.y[(size_t)m * p.ldy + yr0 + r];
+        }
         gv_stage_x<QT, MT, NW>(p, xq, sh, nchunk);
+        if (ystage) {
+            if ((int)threadIdx.x < yrows * MT) sh.yres[threadIdx.x] = yv;
+            __syncthreads();
+            yres = sh.yres;
+        }
         GV_STAMP(3);
         after_stage();
         if constexpr (TPR) tp_s = tp_next_seq(*p.tp);
