@@ -233,7 +233,32 @@ __device__ __forceinline__ void gv_stage_x(const GemvParams &p, uint4 *xq, GemvS
     __syncthreads();
 }
 
-__device__ __forceinline__ void gv_epi_pair(const GemvParams &p, int lr0, int m, float x1, float x2)
+// Inputs of a lane's epilogue that live in global memory, read when the warp
+// starts the row group (gv_epi_fetch) so that the loads complete under the
+// group's weight stream instead of stalling the epilogue (at the end of the
+// launch, a stalled epilogue delays the exit of the CTA and the next kernel).
+struct GvEpiPre {
+    float sa, sb;       // INT8 row scales of the lane's row(s)
+    float c, s;         // EPI_QKV: RoPE cos / sin of the lane's pair
+};
+
+// Per-token inputs of EPI_QKV: cache slot / RoPE position and sequence of token m.
+struct GvTok {
+    int pos, seq;
+};
+
+__device__ __forceinline__ GvTok gv_tok(const GemvParams &p, int m)
+{
+    GvTok t = {0, 0};
+    if (p.epi == EPI_QKV && m < p.M) {
+        t.pos = p.pos[m];
+        t.seq = p.seq_of ? p.seq_of[m] : p.seq_off + m;
+    }
+    return t;
+}
+
+__device__ __forceinline__ void gv_epi_pair(const GemvParams &p, int lr0, int m, float x1, float x2, const GvEpiPre &e,
+                                            const GvTok &tk)
 {
     if (p.epi == EPI_GATEUP) {
         p.y[(size_t)m * p.ldy + (lr0 >> 1)] = (p.act == 1 ? gelu_tanh(x1) : x1 / (1.0f + expf(-x1))) * x2;
@@ -241,11 +266,11 @@ __device__ __forceinline__ void gv_epi_pair(const GemvParams &p, int lr0, int m,
     }
     // EPI_QKV: rows (lr0, lr0 + 1) are the RoPE pair (i, i + hd/2) of one head
     const int hd = p.hd, head = lr0 / hd, i = (lr0 - head * hd) >> 1;
-    const int pos = p.pos[m];
-    const int seq = p.seq_of ? p.seq_of[m] : p.seq_off + m;
+    const int pos = tk.pos;
+    const int seq = tk.seq;
     if (head < p.hq + p.hkv) {
-        const float c = __half2float(p.rope_cos[(size_t)pos * (hd >> 1) + i]);
-        const float s = __half2float(p.rope_sin[(size_t)pos * (hd >> 1) + i]);
+        const float c = e.c;
+        const float s = e.s;
         const float r1 = x1 * c - x2 * s;
         const float r2 = x2 * c + x1 * s;
         x1 = r1;
@@ -270,6 +295,22 @@ __device__ __forceinline__ void gv_epi_pair(const GemvParams &p, int lr0, int m,
     }
 }
 
+// The same, reading its inputs here (callers without a prefetch: the tensor-core
+// GEMM and GEMV epilogues).
+__device__ __forceinline__ void gv_epi_pair(const GemvParams &p, int lr0, int m, float x1, float x2)
+{
+    GvEpiPre e = {1.0f, 1.0f, 1.0f, 0.0f};
+    const GvTok tk = gv_tok(p, m);
+    if (p.epi == EPI_QKV) {
+        const int hd = p.hd, head = lr0 / hd, i = (lr0 - head * hd) >> 1;
+        if (head < p.hq + p.hkv) {
+            e.c = __half2float(p.rope_cos[(size_t)tk.pos * (hd >> 1) + i]);
+            e.s = __half2float(p.rope_sin[(size_t)tk.pos * (hd >> 1) + i]);
+        }
+    }
+    gv_epi_pair(p, lr0, m, x1, x2, e, tk);
+}
+
 template <int QT>
 __device__ __forceinline__ float gv_row_scale(const GemvParams &p, int lr)
 {
@@ -291,12 +332,41 @@ __host__ __device__ constexpr size_t gemv_ring_bytes()
 // holds every value); lane j * MT + m owns output (row j, token m).
 // TPR: the EPI_TP_RESID kernels (a separate instantiation, so that the other
 // epilogues compile exactly as without it): each output goes to every rank.
+// The global inputs of lane `lane`'s share of the epilogue of the row group at
+// logical row lr0 (the lane's rows as gv_epilogue assigns them).
+template <int QT, int MT, int RW, bool TPR = false>
+__device__ __forceinline__ GvEpiPre gv_epi_fetch(const GemvParams &p, int lr0, int lane, const GvTok &tk)
+{
+    GvEpiPre e = {1.0f, 1.0f, 1.0f, 0.0f};
+    if (!TPR && (p.epi == EPI_QKV || p.epi == EPI_GATEUP)) {
+        const int pair = lane / MT, jp = 2 * pair;
+        if (pair < RW / 2 && lr0 + jp + 1 < p.N) {
+            if (QT == Q_I8) {
+                e.sa = gv_row_scale<QT>(p, lr0 + jp);
+                e.sb = gv_row_scale<QT>(p, lr0 + jp + 1);
+            }
+            if (p.epi == EPI_QKV && lane - pair * MT < p.M) {
+                const int hd = p.hd, head = (lr0 + jp) / hd, i = (lr0 + jp - head * hd) >> 1;
+                if (head < p.hq + p.hkv) {
+                    e.c = __half2float(p.rope_cos[(size_t)tk.pos * (hd >> 1) + i]);
+                    e.s = __half2float(p.rope_sin[(size_t)tk.pos * (hd >> 1) + i]);
+                }
+            }
+        }
+    } else if (QT == Q_I8 && p.epi != EPI_LOGITS) {
+        const int j = lane / MT;
+        if (j < RW && lr0 + j < p.N) e.sa = gv_row_scale<QT>(p, lr0 + j);
+    }
+    return e;
+}
+
 // yres (EPI_RESID, may be null): the residual of rows yr0.. staged in shared memory
-// before the stream, so that the epilogue only stores.
+// before the stream, so that the epilogue only stores.  e / tk: the lane's
+// prefetched inputs (gv_epi_fetch, gv_tok).
 template <int QT, int MT, int RW, bool TPR = false>
 __device__ __forceinline__ void gv_epilogue(const GemvParams &p, int lr0, const float (&v)[RW][MT], float *am_v,
-                                        int *am_i, int lane, unsigned tp_s = 0u, const float *yres = nullptr,
-                                        int yr0 = 0)
+                                        int *am_i, int lane, unsigned tp_s, const float *yres, int yr0,
+                                        const GvEpiPre &e, const GvTok &tk)
 {
     if constexpr (TPR) {
 #pragma unroll
@@ -306,7 +376,7 @@ __device__ __forceinline__ void gv_epilogue(const GemvParams &p, int lr0, const 
                 const int lr = lr0 + j;
                 if (lane == j * MT + m && m < p.M && lr < p.N) {
                     float f = v[j][m];
-                    if (QT == Q_I8) f *= gv_row_scale<QT>(p, lr);
+                    if (QT == Q_I8) f *= e.sa;
                     tp_push(*p.tp, tp_s, (size_t)m * p.N + lr, f);
                 }
             }
@@ -320,10 +390,10 @@ __device__ __forceinline__ void gv_epilogue(const GemvParams &p, int lr0, const 
                 if (lane == (jp / 2) * MT + m && m < p.M && lr0 + jp + 1 < p.N) {
                     float x1 = v[jp][m], x2 = v[jp + 1][m];
                     if (QT == Q_I8) {
-                        x1 *= gv_row_scale<QT>(p, lr0 + jp);
-                        x2 *= gv_row_scale<QT>(p, lr0 + jp + 1);
+                        x1 *= e.sa;
+                        x2 *= e.sb;
                     }
-                    gv_epi_pair(p, lr0 + jp, m, x1, x2);
+                    gv_epi_pair(p, lr0 + jp, m, x1, x2, e, tk);
                 }
     } else {
 #pragma unroll
@@ -339,7 +409,7 @@ __device__ __forceinline__ void gv_epilogue(const GemvParams &p, int lr0, const 
                         if (lane == j * MT + m && p.logits) p.logits[(size_t)m * p.ldl + lr] = f;
                     } else if (lane == j * MT + m) {
                         float f = v[j][m];
-                        if (QT == Q_I8) f *= gv_row_scale<QT>(p, lr);
+                        if (QT == Q_I8) f *= e.sa;
                         if (p.epi == EPI_STORE) p.y[(size_t)m * p.ldy + lr] = f;
                         else if (yres != nullptr) p.y[(size_t)m * p.ldy + lr] = yres[(lr - yr0) * MT + m] + f;
                         else p.y[(size_t)m * p.ldy + lr] += f;      // EPI_RESID
@@ -564,9 +634,9 @@ struct GemvStream {
     }
 
     __device__ __forceinline__ void epilogue(const GemvParams &p, int lr0, const float (&v)[RW][MT], float *am_v,
-                                             int *am_i) const
+                                             int *am_i, const GvEpiPre &e, const GvTok &tk) const
     {
-        gv_epilogue<QT, MT, RW, TPR>(p, lr0, v, am_v, am_i, lane, tp_s, yres, yr0);
+        gv_epilogue<QT, MT, RW, TPR>(p, lr0, v, am_v, am_i, lane, tp_s, yres, yr0, e, tk);
     }
 
     // Phase 2: activations -> smem, stream, epilogue.  All threads of the CTA call it.
@@ -588,6 +658,7 @@ struct GemvStream {
             const int r = threadIdx.x / MT, m = threadIdx.x - r * MT;
             if (m < p.M) yv = p.y[(size_t)m * p.ldy + yr0 + r];
         }
+        const GvTok tk = gv_tok(p, lane % MT);       // the lane's token in gv_epilogue
         gv_stage_x<QT, MT, NW>(p, xq, sh, nchunk);
         if (ystage) {
             if ((int)threadIdx.x < yrows * MT) sh.yres[threadIdx.x] = yv;
@@ -618,6 +689,10 @@ struct GemvStream {
         const int first_g = cs_g;
         const bool first_whole = cs_s == 0;       // this warp starts its first group at segment 0
         const int n = u1 - u0;
+        // epilogue inputs of the current group, and of the first group (whose epilogue,
+        // if the group is split between warps, runs after the stream)
+        const GvEpiPre e_first = n > 0 ? gv_epi_fetch<QT, MT, RW, TPR>(p, first_g * RW, lane, tk) : GvEpiPre{};
+        GvEpiPre e_cur = e_first;
         for (int i = 0; i < n; i++) {
             issue(p);
             cp_async_wait_group<D - 1>();
@@ -630,7 +705,7 @@ struct GemvStream {
                 float v[RW][MT];
                 gv_fold<QT, MT, RW>(acc, s8, sh.xscale, v);
                 if (end_g && (cs_g != first_g || first_whole)) {
-                    epilogue(p, cs_g * RW, v, am_v, am_i);            // the whole group was this warp's
+                    epilogue(p, cs_g * RW, v, am_v, am_i, e_cur, tk);   // the whole group was this warp's
                 } else if (lane == 0) {
                     float *pb = sh.pbuf[warp][cs_g == first_g ? 0 : 1];
 #pragma unroll
@@ -641,6 +716,7 @@ struct GemvStream {
                 if (end_g) {
                     cs_s = 0;
                     cs_g++;
+                    if (i + 1 < n) e_cur = gv_epi_fetch<QT, MT, RW, TPR>(p, cs_g * RW, lane, tk);
                 }
             }
         }
@@ -666,7 +742,7 @@ struct GemvStream {
 #pragma unroll
                     for (int m = 0; m < MT; m++) v[j][m] += pb[j * MT + m];
             }
-            epilogue(p, (g_begin + gl) * RW, v, am_v, am_i);
+            epilogue(p, (g_begin + gl) * RW, v, am_v, am_i, e_first, tk);
         }
 
         if constexpr (TPR) {
