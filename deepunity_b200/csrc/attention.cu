@@ -289,15 +289,21 @@ static int fdc_launch(const FdParams &p, int G, int nq, cudaStream_t st, int new
     cfg.blockDim = dim3(FDC_THREADS);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = st;
-    cudaLaunchAttribute attr[2];
+    // Load-balanced cluster scheduling lets the hardware place CTAs of one cluster on
+    // an SM that already holds another (two fit per SM with the fp16 cache): batched
+    // fp16 attention 15-22 % faster at batch 8 (8B shapes, ctx 512..32768), 2-6 % at
+    // batch 32; unchanged at batch 1 and with the INT8 cache.
+    cudaLaunchAttribute attr[3];
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.x = C;
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = 1;
-    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    attr[1].id = cudaLaunchAttributeClusterSchedulingPolicyPreference;
+    attr[1].val.clusterSchedulingPolicyPreference = cudaClusterSchedulingPolicyLoadBalancing;
+    attr[2].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[2].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = pdl_enabled() ? 2 : 1;
+    cfg.numAttrs = pdl_enabled() ? 3 : 2;
     if (probe) {
         int n = 0;
         DU_CUDA_TRY(cudaOccupancyMaxActiveClusters(&n, kern, &cfg));
