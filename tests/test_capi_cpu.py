@@ -70,3 +70,28 @@ def test_init_without_gpu_reports_an_error():
     rc = _lib.lib().du_init(0)
     assert rc != _lib.DU_OK
     assert _lib.last_error()
+
+
+def test_timing_build_compiles_and_stays_out_of_the_library():
+    """The GEMV timing build (gemv.cu with DU_GEMV_STAMPS: per-CTA phase stamps
+    for bench.py --gemv-phases) still compiles for sm_100a, and the library proper
+    exports none of its symbols (the hook compiles to nothing there)."""
+    import shutil
+    import subprocess
+    import tempfile
+    from deepunity_b200 import build as B
+    try:
+        nvcc = B.nvcc()
+    except RuntimeError:
+        pytest.skip("nvcc not available")
+    assert not hasattr(_lib.lib(), "du_gemv_stamps_read")
+    with tempfile.TemporaryDirectory() as d:
+        obj = os.path.join(d, "gemv_stamps.o")
+        r = subprocess.run([nvcc, "-c", os.path.join(B.CSRC, "gemv.cu"), "-o", obj] + B.ARCH +
+                           ["-O1", "-std=c++17", "-Xcompiler", "-fPIC", "--expt-relaxed-constexpr", "-DDU_GEMV_STAMPS"],
+                           capture_output=True, text=True)
+        assert r.returncode == 0, r.stdout + r.stderr
+        nm = shutil.which("nm")
+        if nm:
+            syms = subprocess.run([nm, obj], capture_output=True, text=True).stdout
+            assert "du_gemv_stamps_read" in syms and "du_gemv_stamps_reset" in syms
