@@ -87,6 +87,9 @@ SIGNATURES = {
     "du_dequant": (I, [P, P, P, I, I, I, I64, I, I, P]),
     "du_sample": (I, [P, P, I, I, I, F, I, F, F, P, P]),
     "du_decode_step_sample": (I, [P, P, I, F, I, F, F, P, P]),
+    "du_decode_step_sample_ex": (I, [P, P, I, F, I, F, F, F, F, P, P]),
+    "du_apply_penalties": (I, [P, I, I, I, P, I, F, F, P]),
+    "du_mark_seen": (I, [P, I, I, I, P, P]),
 }
 
 _lib = None

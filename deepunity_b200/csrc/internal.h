@@ -121,6 +121,10 @@ bool sample_supported(float temperature, int top_k, float top_p, int V);
 int launch_sample(const float *logits, int rows, int V, int ldl, float temperature, int top_k, float top_p,
                   float min_p, const int32_t *seeds, int32_t *out, int *feed, TokHist hist, int *err, cudaStream_t st,
                   const float *dparams);
+// sampler.cu: repetition / presence penalty in place over rows of logits (in_ids: the step's
+// input id per row counts as seen and is added to seen; dp: device (presence, repetition))
+int launch_penalties(float *logits, int rows, int V, int ldl, unsigned *seen, int ld_seen, const int *in_ids,
+                     const float *dp, float presence, float repetition, cudaStream_t st);
 int launch_add_inplace(float *y, const float *x, size_t n, cudaStream_t st);
 int launch_quantize_int8(const float *w, int64_t rows, int64_t cols, int8_t *q, __half *s, cudaStream_t st);
 int launch_quantize_int4(const float *w, int64_t rows, int64_t cols, int group, uint8_t *p, __half *s,

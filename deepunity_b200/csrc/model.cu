@@ -224,8 +224,9 @@ static int model_alloc(du_model *m)
     m->fd_counters = (unsigned *)dalloc(m, sizeof(unsigned) * (size_t)T * m->hkv_l, &rc);
     m->d_barrier = (unsigned *)dalloc(m, sizeof(unsigned), &rc);
     m->d_err = (int *)dalloc(m, sizeof(int), &rc);
-    m->d_seeds = (int32_t *)dalloc(m, sizeof(int32_t) * (m->maxb + 4), &rc);
+    m->d_seeds = (int32_t *)dalloc(m, sizeof(int32_t) * (m->maxb + SAMPLE_PARAMS), &rc);
     m->d_sparams = reinterpret_cast<float *>(m->d_seeds + m->maxb);
+    if (m->tp == 1) m->d_seen = (unsigned *)dalloc(m, sizeof(unsigned) * (size_t)m->maxb * m->V, &rc);
     {   // GEMM activation stage: every K a chunk's GEMM can see (H, I_l, hq_l * hd)
         int64_t kmax = H > m->I_l ? H : m->I_l;
         if ((int64_t)m->hq_l * hd > kmax) kmax = (int64_t)m->hq_l * hd;
@@ -245,7 +246,7 @@ static int model_alloc(du_model *m)
     DU_CUDA_TRY(cudaMallocHost(&m->h_pin_err, sizeof(int)));
     DU_CUDA_TRY(cudaMallocHost(&m->h_pin_ids, sizeof(int) * T));
     DU_CUDA_TRY(cudaMallocHost(&m->h_pin_next, sizeof(int) * m->maxb));
-    DU_CUDA_TRY(cudaMallocHost(&m->h_pin_seeds, sizeof(int32_t) * (m->maxb + 4)));
+    DU_CUDA_TRY(cudaMallocHost(&m->h_pin_seeds, sizeof(int32_t) * (m->maxb + SAMPLE_PARAMS)));
     m->h_cache_len.assign(m->maxb, 0);
 
     // RoPE tables on the host with the reference formula (MiniCPM5Model.cs:163-191); the
@@ -272,13 +273,14 @@ static void model_free(du_model *m)
 {
     cudaSetDevice(m->device);
     if (m->stream) cudaStreamSynchronize(m->stream);
-    for (auto *gm : {&m->graphs, &m->sgraphs})
+    for (auto *gm : {&m->graphs, &m->sgraphs, &m->pgraphs})
         for (auto &kv : *gm) {
             if (kv.second.exec) cudaGraphExecDestroy(kv.second.exec);
             if (kv.second.g) cudaGraphDestroy(kv.second.g);
             if (kv.second.d_stages) cudaFree(kv.second.d_stages);
         }
     m->sgraphs.clear();
+    m->pgraphs.clear();
     if (m->h_pin_seeds) cudaFreeHost(m->h_pin_seeds);
     m->h_pin_seeds = nullptr;
     if (m->h_pin_err) cudaFreeHost(m->h_pin_err);
@@ -566,6 +568,7 @@ struct StepIO {
     int *feed;             // optional: also write ids here (device loop)
     bool advance;          // cache_len[m] += 1 at the end (decode)
     bool sample = false;   // pick with the stochastic sampler (settings and seeds in device memory)
+    bool penalize = false; // sample: repetition / presence penalty over the sequence's seen ids first
 };
 
 enum Stage { ST_QKV = 0, ST_ATTN = 1, ST_O = 2, ST_GATEUP = 3, ST_DOWN = 4 };
@@ -832,7 +835,12 @@ static int enqueue_head(du_model *m, const StepIO &io)
         hist.cap = m->cap;
     }
     if (io.sample) {
-        // temperature / top-k / top-p / min-p over the full logits (single GPU)
+        // repetition / presence penalty (settings in device memory), counting this step's
+        // input ids as seen; then temperature / top-k / top-p / min-p over the full logits
+        // (single GPU)
+        if (io.penalize && (rc = launch_penalties(m->logits, R, m->V, m->V_l, m->d_seen, m->V, io.ids,
+                                                  m->d_sparams + 4, 0.0f, 1.0f, st)))
+            return rc;
         if ((rc = launch_sample(m->logits, R, m->V, m->V_l, 1.0f, 0, 1.0f, 0.0f, m->d_seeds, io.next_out, io.feed, hist,
                                 m->d_err, st, m->d_sparams)))
             return rc;
@@ -986,9 +994,10 @@ static int check_step_error(du_model *m)
                           "the call was aborted");
 }
 
-static int get_graph(du_model *m, int batch, cudaGraphExec_t *out, Graph **gout = nullptr, bool sample = false)
+static int get_graph(du_model *m, int batch, cudaGraphExec_t *out, Graph **gout = nullptr, bool sample = false,
+                     bool penalize = false)
 {
-    std::map<int, Graph> &gm = sample ? m->sgraphs : m->graphs;
+    std::map<int, Graph> &gm = penalize ? m->pgraphs : sample ? m->sgraphs : m->graphs;
     auto it = gm.find(batch);
     if (it != gm.end()) {
         *out = it->second.exec;
@@ -996,12 +1005,13 @@ static int get_graph(du_model *m, int batch, cudaGraphExec_t *out, Graph **gout 
         return DU_OK;
     }
     StepIO io = decode_io(m, batch);
-    io.sample = sample;
+    io.sample = sample || penalize;
+    io.penalize = penalize;
     Graph g;
     StepPlan plan;
     int qt = 0, mt = 0;
     size_t smem = 0;
-    const bool persistent = !sample && build_step_plan(m, io, &plan, &qt, &mt, &smem, &g.d_stages) == DU_OK;
+    const bool persistent = !io.sample && build_step_plan(m, io, &plan, &qt, &mt, &smem, &g.d_stages) == DU_OK;
     DU_CUDA_TRY(cudaStreamBeginCapture(m->stream, cudaStreamCaptureModeThreadLocal));
     int rc;
     if (persistent) {
@@ -1371,20 +1381,27 @@ DU_API int du_decode_step(du_model *m, const int32_t *ids, int batch, int32_t *n
     return DU_OK;
 }
 
-DU_API int du_decode_step_sample(du_model *m, const int32_t *ids, int batch, float temperature, int top_k,
-                                 float top_p, float min_p, const int32_t *seeds, int32_t *next_ids)
+}  // extern "C"
+
+namespace du {
+
+// One sampled decode step (du_decode_step_sample / _ex): settings and seeds go to
+// device memory, then the captured graph of this batch size runs.
+static int decode_step_sample_impl(du_model *m, const int32_t *ids, int batch, float temperature, int top_k,
+                                   float top_p, float min_p, bool penalize, float presence, float repetition,
+                                   const int32_t *seeds, int32_t *next_ids, const char *name)
 {
-    DU_GUARD(m);
-    DU_CHECK_ARG(ids && seeds && next_ids && batch > 0 && batch <= m->maxb, "du_decode_step_sample: bad arguments");
-    if (m->tp > 1) return fail(DU_ESTATE, "du_decode_step_sample: stochastic sampling runs on a single GPU");
+    DU_CHECK_ARG(ids && seeds && next_ids && batch > 0 && batch <= m->maxb, std::string(name) + ": bad arguments");
+    if (m->tp > 1) return fail(DU_ESTATE, std::string(name) + ": stochastic sampling runs on a single GPU");
     if (!sample_supported(temperature, top_k, top_p, m->V))
-        return fail(DU_EINVAL, "du_decode_step_sample: top_p < 1 needs top_k in 1..64 (the reference's parallel sampler)");
+        return fail(DU_EINVAL, std::string(name) + ": top_p < 1 needs top_k in 1..64 (the reference's parallel sampler)");
+    if (penalize && !(repetition > 0.0f)) return fail(DU_EINVAL, std::string(name) + ": repetition_penalty must be > 0");
     int rc = check_ids(m, ids, batch);
     if (rc) return rc;
     for (int b = 0; b < batch; b++)
-        if (m->h_cache_len[b] + 1 > m->cap) return fail(DU_EINVAL, "du_decode_step_sample: KV cache capacity exceeded");
+        if (m->h_cache_len[b] + 1 > m->cap) return fail(DU_EINVAL, std::string(name) + ": KV cache capacity exceeded");
     cudaGraphExec_t exec;
-    if ((rc = get_graph(m, batch, &exec, nullptr, true))) return rc;
+    if ((rc = get_graph(m, batch, &exec, nullptr, true, penalize))) return rc;
     cudaStream_t st = m->stream;
     memcpy(m->h_pin_ids, ids, sizeof(int) * batch);
     memcpy(m->h_pin_seeds, seeds, sizeof(int32_t) * batch);
@@ -1393,8 +1410,11 @@ DU_API int du_decode_step_sample(du_model *m, const int32_t *ids, int batch, flo
     hp[1] = (float)top_k;
     hp[2] = top_p;
     hp[3] = min_p;
+    hp[4] = penalize ? presence : 0.0f;
+    hp[5] = penalize ? repetition : 1.0f;
     DU_CUDA_TRY(cudaMemcpyAsync(m->d_ids, m->h_pin_ids, sizeof(int) * batch, cudaMemcpyHostToDevice, st));
-    DU_CUDA_TRY(cudaMemcpyAsync(m->d_seeds, m->h_pin_seeds, sizeof(int32_t) * (m->maxb + 4), cudaMemcpyHostToDevice, st));
+    DU_CUDA_TRY(cudaMemcpyAsync(m->d_seeds, m->h_pin_seeds, sizeof(int32_t) * (m->maxb + SAMPLE_PARAMS),
+                                cudaMemcpyHostToDevice, st));
     DU_CUDA_TRY(cudaGraphLaunch(exec, st));
     DU_CUDA_TRY(cudaMemcpyAsync(m->h_pin_next, m->d_next, sizeof(int) * batch, cudaMemcpyDeviceToHost, st));
     DU_CUDA_TRY(cudaMemcpyAsync(m->h_pin_err, m->d_err, sizeof(int), cudaMemcpyDeviceToHost, st));
@@ -1408,6 +1428,27 @@ DU_API int du_decode_step_sample(du_model *m, const int32_t *ids, int batch, flo
     for (int b = 0; b < batch; b++) m->h_cache_len[b] += 1;
     m->last_batch = batch;
     return DU_OK;
+}
+
+}  // namespace du
+
+extern "C" {
+
+DU_API int du_decode_step_sample(du_model *m, const int32_t *ids, int batch, float temperature, int top_k,
+                                 float top_p, float min_p, const int32_t *seeds, int32_t *next_ids)
+{
+    DU_GUARD(m);
+    return decode_step_sample_impl(m, ids, batch, temperature, top_k, top_p, min_p, false, 0.0f, 1.0f, seeds, next_ids,
+                                   "du_decode_step_sample");
+}
+
+DU_API int du_decode_step_sample_ex(du_model *m, const int32_t *ids, int batch, float temperature, int top_k,
+                                    float top_p, float min_p, float presence_penalty, float repetition_penalty,
+                                    const int32_t *seeds, int32_t *next_ids)
+{
+    DU_GUARD(m);
+    return decode_step_sample_impl(m, ids, batch, temperature, top_k, top_p, min_p, true, presence_penalty,
+                                   repetition_penalty, seeds, next_ids, "du_decode_step_sample_ex");
 }
 
 DU_API int du_decode_loop(du_model *m, const int32_t *ids, int batch, int n_steps, int32_t *tokens_out)
@@ -1452,6 +1493,9 @@ DU_API int du_reset_cache(du_model *m)
     for (int b = 0; b < m->maxb; b++) m->h_cache_len[b] = 0;
     int rc = sync_cache_len(m);
     if (rc) return rc;
+    // ZeroTokenSeen (Qwen3_5CS.compute:1443-1451, on ResetCache): penalties start fresh
+    if (m->d_seen)
+        DU_CUDA_TRY(cudaMemsetAsync(m->d_seen, 0, sizeof(unsigned) * (size_t)m->maxb * m->V, m->stream));
     DU_CUDA_TRY(cudaStreamSynchronize(m->stream));
     return DU_OK;
 }

@@ -26,6 +26,10 @@ struct Layer {
     __half *post_attn = nullptr, *post_ffn = nullptr;
 };
 
+// Floats of sampler settings after the seeds: temperature, top_k, top_p, min_p,
+// presence penalty, repetition penalty, two spare.
+constexpr int SAMPLE_PARAMS = 8;
+
 struct Graph {
     cudaGraph_t g = nullptr;
     cudaGraphExec_t exec = nullptr;
@@ -90,9 +94,13 @@ struct du_model {
     std::vector<int> h_cache_len;
     std::map<int, du::Graph> graphs;        // greedy decode step per batch size
     std::map<int, du::Graph> sgraphs;       // sampling decode step per batch size
+    std::map<int, du::Graph> pgraphs;       // sampling decode step with repetition / presence penalty
     int32_t *d_seeds = nullptr;             // [maxb] sampler seeds of the next step
-    float *d_sparams = nullptr;             // (temperature, top_k, top_p, min_p) of the next sampling step
-    int32_t *h_pin_seeds = nullptr;         // pinned staging: [maxb] seeds then 4 floats of settings
+    float *d_sparams = nullptr;             // (temperature, top_k, top_p, min_p, presence, repetition) of the next
+                                            // sampling step
+    int32_t *h_pin_seeds = nullptr;         // pinned staging: [maxb] seeds then SAMPLE_PARAMS floats of settings
+    unsigned *d_seen = nullptr;             // [maxb][V] ids seen per sequence since the last cache reset
+                                            // (single GPU; the penalties' token_seen)
     int last_batch = 0, last_rows = 0;      // rows of logits written by the last call
     std::atomic<int> busy{0};
     // TP

@@ -332,9 +332,87 @@ int launch_sample(const float *logits, int rows, int V, int ldl, float temperatu
     return DU_OK;
 }
 
+// Repetition + presence penalty (ApplyRepetitionPresencePenalty, Qwen3_5CS.compute:1421-1433),
+// in place on rows of logits, for the ids already seen in the row's sequence:
+// l = l > 0 ? l / repetition : l * repetition, then l -= presence (once per id,
+// whatever its count).  seen [rows][ld_seen] occurrence counts.  in_ids (optional,
+// decode steps): the step's input id per row, which was the previous pick; it counts
+// as seen here and one thread adds it to seen (MarkSampledTokenSeen,
+// Qwen3_5CS.compute:1436-1441, moved from after the pick to the next step's start).
+// The penalty depends only on whether a count is non-zero, so the increment racing
+// with the reads of the same word cannot change a result.  dp (optional): device
+// (presence, repetition) overriding the scalars (one captured graph for all settings).
+constexpr int PEN_THREADS = 256;
+constexpr int PEN_PER_THREAD = 4;
+
+__global__ void __launch_bounds__(PEN_THREADS) penalty_kernel(float *logits, int V, int ldl, unsigned *seen, int ld_seen,
+                                                              const int *in_ids, const float *dp, float presence,
+                                                              float repetition)
+{
+    if (dp != nullptr) {
+        presence = dp[0];
+        repetition = dp[1];
+    }
+    const int row = blockIdx.y;
+    float *lg = logits + (size_t)row * ldl;
+    const unsigned *sn = seen + (size_t)row * ld_seen;
+    const int in = in_ids != nullptr ? in_ids[row] : -1;
+    const int base = blockIdx.x * PEN_THREADS * PEN_PER_THREAD + threadIdx.x;
+#pragma unroll
+    for (int k = 0; k < PEN_PER_THREAD; k++) {
+        const int i = base + k * PEN_THREADS;
+        if (i < V && (sn[i] != 0u || i == in)) {
+            float l = lg[i];
+            l = l > 0.0f ? l / repetition : l * repetition;
+            lg[i] = l - presence;
+        }
+    }
+    if (in_ids != nullptr && blockIdx.x == 0 && threadIdx.x == 0 && in >= 0 && in < V)
+        seen[(size_t)row * ld_seen + in] += 1u;
+}
+
+int launch_penalties(float *logits, int rows, int V, int ldl, unsigned *seen, int ld_seen, const int *in_ids,
+                     const float *dp, float presence, float repetition, cudaStream_t st)
+{
+    if (rows <= 0) return DU_OK;
+    const dim3 grid((V + PEN_THREADS * PEN_PER_THREAD - 1) / (PEN_THREADS * PEN_PER_THREAD), rows);
+    penalty_kernel<<<grid, PEN_THREADS, 0, st>>>(logits, V, ldl, seen, ld_seen, in_ids, dp, presence, repetition);
+    DU_CUDA_TRY(cudaGetLastError());
+    return DU_OK;
+}
+
+// MarkSampledTokenSeen (Qwen3_5CS.compute:1436-1441) for several rows: seen[r][ids[r]] += 1.
+__global__ void mark_seen_kernel(unsigned *seen, int rows, int ld_seen, int V, const int32_t *ids)
+{
+    const int r = blockIdx.x * blockDim.x + threadIdx.x;
+    if (r < rows) {
+        const int id = ids[r];
+        if (id >= 0 && id < V) atomicAdd(&seen[(size_t)r * ld_seen + id], 1u);
+    }
+}
+
 }  // namespace du
 
 using namespace du;
+
+extern "C" DU_API int du_apply_penalties(float *logits, int rows, int vocab, int ldl, const uint32_t *seen, int ld_seen,
+                                         float presence_penalty, float repetition_penalty, void *stream)
+{
+    DU_CHECK_ARG(logits && seen && rows >= 0 && vocab > 0 && ldl >= vocab && ld_seen >= vocab,
+                 "du_apply_penalties: bad arguments");
+    DU_CHECK_ARG(repetition_penalty > 0.0f, "du_apply_penalties: repetition_penalty must be > 0");
+    return launch_penalties(logits, rows, vocab, ldl, const_cast<unsigned *>(seen), ld_seen, nullptr, nullptr,
+                            presence_penalty, repetition_penalty, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" DU_API int du_mark_seen(uint32_t *seen, int rows, int ld_seen, int vocab, const int32_t *ids, void *stream)
+{
+    DU_CHECK_ARG(seen && ids && rows >= 0 && vocab > 0 && ld_seen >= vocab, "du_mark_seen: bad arguments");
+    if (rows == 0) return DU_OK;
+    mark_seen_kernel<<<(rows + 127) / 128, 128, 0, static_cast<cudaStream_t>(stream)>>>(seen, rows, ld_seen, vocab, ids);
+    DU_CUDA_TRY(cudaGetLastError());
+    return DU_OK;
+}
 
 extern "C" DU_API int du_sample(int32_t *out, const float *logits, int rows, int vocab, int ldl, float temperature,
                                 int top_k, float top_p, float min_p, const int32_t *seeds, void *stream)

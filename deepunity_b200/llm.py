@@ -257,6 +257,22 @@ class LlamaForCausalLM(LLM):
                   out.ctypes.data_as(C.c_void_p))
         return out
 
+    def decode_step_sample_ex(self, ids, temperature: float, top_k: int = 0, top_p: float = 1.0, min_p: float = 0.0,
+                              presence_penalty: float = 0.0, repetition_penalty: float = 1.0,
+                              seeds=None) -> np.ndarray:
+        """decode_step_sample with the repetition / presence penalties over the ids this
+        entry point has been fed since the last ResetCache (DispatchSampleKernels,
+        Qwen3_5Model.cs:1010-1058)."""
+        ids = np.ascontiguousarray(np.asarray(ids, dtype=np.int32).reshape(-1))
+        if seeds is None:
+            seeds = np.random.default_rng().integers(-2 ** 31, 2 ** 31 - 1, ids.size)
+        sd = np.ascontiguousarray(np.asarray(seeds, dtype=np.int64).astype(np.int32).reshape(-1))
+        out = np.empty_like(ids)
+        _lib.call("du_decode_step_sample_ex", self._h, ids.ctypes.data_as(C.c_void_p), ids.size,
+                  C.c_float(temperature), int(top_k), C.c_float(top_p), C.c_float(min_p), C.c_float(presence_penalty),
+                  C.c_float(repetition_penalty), sd.ctypes.data_as(C.c_void_p), out.ctypes.data_as(C.c_void_p))
+        return out
+
     def decode_loop(self, ids, steps: int) -> np.ndarray:
         ids = np.ascontiguousarray(np.asarray(ids, dtype=np.int32).reshape(-1))
         out = np.empty((steps, ids.size), np.int32)
@@ -271,19 +287,23 @@ class LlamaForCausalLM(LLM):
 
     def Generate(self, input_ids, on_token: Optional[Callable[[int], None]] = None,
                  max_new_tokens: int = 64, stop_tokens: Sequence[int] = (), temperature: float = 0.0,
-                 top_k: int = 0, top_p: float = 1.0, min_p: float = 0.0, seed: Optional[int] = None) -> Iterator[int]:
+                 top_k: int = 0, top_p: float = 1.0, min_p: float = 0.0, seed: Optional[int] = None,
+                 presence_penalty: float = 0.0, repetition_penalty: float = 1.0) -> Iterator[int]:
         """LLM.Generate (MiniCPM5.cs:133-172): prefill the prompt, then one graph-replayed
         decode step per token.  temperature <= 0 is greedy; otherwise every token is drawn by
         the sampler (temperature / top_k / top_p / min_p, SampleYielding M5M:690-705) with
         seeds from `seed`.  The prompt's last token runs as the first decode step so that the
-        first new token is sampled on the device too.  Yields token ids (the reference yields
-        frames and reports text through a callback)."""
+        first new token is sampled on the device too.  presence_penalty / repetition_penalty
+        (LLM.cs:438-440; Qwen3_5Model.cs:1010-1058) penalise the ids generated so far from the
+        second new token on (the first has nothing to penalise).  Yields token ids (the
+        reference yields frames and reports text through a callback)."""
         if self._busy:
             raise RuntimeError("LLM is busy")   # LLM.cs:393-406
         self._busy = True
         try:
             ids = np.asarray(input_ids, np.int32).reshape(-1)
             rng = np.random.default_rng(seed)
+            penalized = presence_penalty != 0.0 or repetition_penalty != 1.0
             if temperature > 0.0:
                 if ids.size > 1:
                     self.forward(ids[None, :-1], use_cache=True, want_logits=False)
@@ -294,6 +314,10 @@ class LlamaForCausalLM(LLM):
                 _, nxt = self.forward(ids[None, :], use_cache=True, want_logits=False)
                 tok = int(nxt[0])
                 step = lambda t: int(self.decode_step([t])[0])
+            if penalized:     # each later step's input (the previous pick) is counted as seen
+                step = lambda t: int(self.decode_step_sample_ex(
+                    [t], temperature, top_k, top_p, min_p, presence_penalty, repetition_penalty,
+                    [int(rng.integers(-2 ** 31, 2 ** 31 - 1))])[0])
             for _ in range(max_new_tokens):
                 if on_token:
                     on_token(tok)

@@ -208,6 +208,21 @@ DU_API int du_decode_step(du_model *m, const int32_t *ids, int batch, int32_t *n
 DU_API int du_decode_step_sample(du_model *m, const int32_t *ids, int batch, float temperature, int top_k,
                                  float top_p, float min_p, const int32_t *seeds, int32_t *next_ids);
 
+/* du_decode_step_sample with the repetition and presence penalties of
+ * DispatchSampleKernels (Qwen3_5/Qwen3_5Model.cs:1010-1058 ->
+ * ApplyRepetitionPresencePenalty, MarkSampledTokenSeen, Qwen3_5CS.compute:1417-1441):
+ * before the pick (greedy when temperature <= 0), every id already seen in the
+ * sequence has its logit l replaced by (l > 0 ? l / repetition_penalty :
+ * l * repetition_penalty) - presence_penalty, once per id whatever its count.
+ * The ids seen are those fed to this entry point's steps since the last
+ * du_reset_cache (ZeroTokenSeen), this step's ids included: each is the previous
+ * step's pick, which the reference marks right after picking it.  (1, 0) are
+ * no-ops.  repetition_penalty must be > 0.  Single GPU; its own captured graph
+ * per batch size. */
+DU_API int du_decode_step_sample_ex(du_model *m, const int32_t *ids, int batch, float temperature, int top_k,
+                                    float top_p, float min_p, float presence_penalty, float repetition_penalty,
+                                    const int32_t *seeds, int32_t *next_ids);
+
 /* Device-resident greedy loop: n_steps decode steps, each feeding its argmax
  * into the next, without host round trips; tokens_out (host) [n_steps, batch].
  * ids (host) [batch] seeds the first step. */
@@ -364,6 +379,18 @@ DU_API int du_quantize_int4(const float *w, int64_t rows, int64_t cols, int grou
  * settings rules as du_decode_step_sample. */
 DU_API int du_sample(int32_t *out, const float *logits, int rows, int vocab, int ldl, float temperature, int top_k,
                      float top_p, float min_p, const int32_t *seeds, void *stream);
+
+/* ApplyRepetitionPresencePenalty (Qwen3_5CS.compute:1421-1433) in place over rows
+ * of device logits [rows][ldl]: for each id with seen[r][id] != 0 (counts,
+ * [rows][ld_seen] uint32, device), l = (l > 0 ? l / repetition_penalty :
+ * l * repetition_penalty) - presence_penalty.  repetition_penalty must be > 0. */
+DU_API int du_apply_penalties(float *logits, int rows, int vocab, int ldl, const uint32_t *seen, int ld_seen,
+                              float presence_penalty, float repetition_penalty, void *stream);
+
+/* MarkSampledTokenSeen (Qwen3_5CS.compute:1436-1441) for several rows:
+ * seen[r][ids[r]] += 1 (device arrays; ids outside [0, vocab) are skipped).
+ * ZeroTokenSeen (:1443-1451) is a memset of seen. */
+DU_API int du_mark_seen(uint32_t *seen, int rows, int ld_seen, int vocab, const int32_t *ids, void *stream);
 
 /* RmsNormHidden (G3CS:204-223): y = x * rsqrt(mean(x^2) + eps) * (1 + gamma_m1). */
 DU_API int du_rmsnorm(float *y, const float *x, const uint16_t *gamma_m1, int rows, int H, float eps,

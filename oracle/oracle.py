@@ -231,6 +231,26 @@ def sample(logits: np.ndarray, temperature: float, top_k: int, top_p: float, min
     return int(lib().orc_sample(_p(lg), lg.size, temperature, top_k, top_p, min_p, seed, _p(scratch)))
 
 
+def apply_penalties(logits: np.ndarray, seen: np.ndarray, presence: float, repetition: float) -> np.ndarray:
+    """ApplyRepetitionPresencePenalty restated (Qwen3_5CS.compute:1421-1433), fp32: for
+    every id with a non-zero count, l = l / repetition if l > 0 else l * repetition, then
+    l -= presence (once per id).  logits [..., V], seen [..., V] counts; returns a copy."""
+    lg = np.array(logits, dtype=np.float32, copy=True)
+    m = np.asarray(seen) != 0
+    rep, pres = np.float32(repetition), np.float32(presence)
+    v = lg[m]
+    v = np.where(v > np.float32(0), v / rep, v * rep).astype(np.float32)
+    lg[m] = (v - pres).astype(np.float32)
+    return lg
+
+
+def mark_seen(seen: np.ndarray, ids) -> None:
+    """MarkSampledTokenSeen restated (Qwen3_5CS.compute:1436-1441) per row: seen[r, ids[r]] += 1."""
+    for r, i in enumerate(np.asarray(ids).reshape(-1)):
+        if 0 <= int(i) < seen.shape[-1]:
+            seen[r, int(i)] += 1
+
+
 def max_threads() -> int:
     return int(lib().orc_max_threads())
 

@@ -487,6 +487,47 @@ def test_sampler_matches_oracle(V):
                 assert got == ref, (T, k, p, mp, rep)
 
 
+@pytest.mark.parametrize("V", [1000, 128256])
+def test_penalties_and_mark_seen_match_oracle(V):
+    """du_apply_penalties (ApplyRepetitionPresencePenalty, Qwen3_5CS.compute:1421-1433)
+    bit-exact against the oracle over rows of logits with zero, negative and positive
+    values and seen counts of 0..3; du_mark_seen (MarkSampledTokenSeen, :1436-1441)
+    adds one per row and skips ids outside the vocabulary."""
+    rng = np.random.default_rng(V + 1)
+    rows, ld = 4, V + 16
+    logits = (rng.standard_normal((rows, V)) * 5).astype(np.float32)
+    logits[:, :3] = [0.0, -2.5, 7.0]
+    seen = ((rng.random((rows, V)) < 0.05) * rng.integers(1, 4, (rows, V))).astype(np.uint32)
+    seen[:, :3] = 1
+    seen_pad = np.zeros((rows, ld), np.uint32)
+    seen_pad[:, :V] = seen
+    lg_pad = np.zeros((rows, ld), np.float32)
+    lg_pad[:, :V] = logits
+    for presence, repetition in [(0.5, 1.3), (0.0, 1.0), (1.5, 0.8)]:
+        lg = dev(lg_pad)
+        sn = dev(seen_pad)
+        _lib.call("du_apply_penalties", ptr(lg), rows, V, ld, ptr(sn), ld, C.c_float(presence),
+                  C.c_float(repetition), None)
+        torch.cuda.synchronize()
+        got = lg.cpu().numpy()[:, :V]
+        ref = orc.apply_penalties(logits, seen, presence, repetition)
+        assert np.array_equal(got.view(np.uint32), ref.view(np.uint32)), (presence, repetition)
+        assert np.array_equal(lg.cpu().numpy()[:, V:], lg_pad[:, V:])          # padding untouched
+    sn = dev(seen_pad)
+    ids = np.array([5, 5, -1, V], np.int32)
+    idd = dev(ids)
+    for _ in range(2):
+        _lib.call("du_mark_seen", ptr(sn), rows, ld, V, ptr(idd), None)
+    torch.cuda.synchronize()
+    want = seen_pad.copy()
+    want[0, 5] += 2
+    want[1, 5] += 2
+    assert np.array_equal(sn.cpu().numpy(), want)
+    rc = _lib.lib().du_apply_penalties(ptr(dev(lg_pad)), rows, V, ld, ptr(sn), ld, C.c_float(0.0), C.c_float(0.0),
+                                       None)
+    assert rc == _lib.DU_EINVAL                     # repetition_penalty must be > 0
+
+
 def test_sampler_rejects_unbounded_nucleus():
     lg = torch.zeros((1, 64), device="cuda")
     sd = torch.zeros(1, dtype=torch.int32, device="cuda")

@@ -257,6 +257,47 @@ def test_sampled_decode_matches_oracle(setting):
     m.Release()
 
 
+@pytest.mark.parametrize("setting", [(0.0, 0, 1.0, 0.0, 0.4, 1.3), (0.8, 40, 0.9, 0.0, 0.5, 1.2)])
+def test_penalized_sampled_decode_matches_oracle(setting):
+    """du_decode_step_sample_ex (DispatchSampleKernels, Qwen3_5Model.cs:1010-1058): the
+    first id is picked from the prefill logits with nothing seen, then 16 steps whose
+    input ids (the previous picks) count as seen; each step's id must be what the oracle
+    picks after applying the same penalties to its logits.  ResetCache clears the counts:
+    the first step after it sees only its own input."""
+    T, k, p, mp, pres, rep = setting
+    cfg = MID
+    w, m = build(cfg, cap=96)
+    om = orc.OracleModel(w, capacity=96)
+    prompt = np.random.default_rng(13).integers(0, cfg.vocab, 10).astype(np.int32)
+    m.forward(prompt[None, :])
+    ref = om.forward(prompt)
+    rng = np.random.default_rng(7)
+    seed = int(rng.integers(-2 ** 31, 2 ** 31 - 1))
+    tok = orc.sample(ref, T, k, p, mp, seed)
+    toks, rtoks = [tok], [tok]
+    seen = np.zeros((1, cfg.vocab), np.uint32)
+    for _ in range(16):
+        seed = int(rng.integers(-2 ** 31, 2 ** 31 - 1))
+        toks.append(int(m.decode_step_sample_ex([toks[-1]], T, k, p, mp, pres, rep, [seed])[0]))
+        orc.mark_seen(seen, [rtoks[-1]])
+        r = orc.apply_penalties(om.forward([rtoks[-1]]), seen[0], pres, rep)
+        rtoks.append(orc.sample(r, T, k, p, mp, seed))
+    assert toks == rtoks
+    assert len(set(toks)) > 1
+    # after a cache reset only the new step's input is seen
+    m.ResetCache()
+    om.reset()
+    m.forward(prompt[None, :])
+    om.forward(prompt)
+    seed = int(rng.integers(-2 ** 31, 2 ** 31 - 1))
+    got = int(m.decode_step_sample_ex([toks[3]], T, k, p, mp, pres, rep, [seed])[0])
+    fresh = np.zeros(cfg.vocab, np.uint32)
+    fresh[toks[3]] = 1
+    want = orc.sample(orc.apply_penalties(om.forward([toks[3]]), fresh, pres, rep), T, k, p, mp, seed)
+    assert got == want
+    m.Release()
+
+
 KV8_LOGIT_TOL = 5e-3
 
 
