@@ -17,7 +17,7 @@ QUANT_FP16, QUANT_INT8, QUANT_INT4 = 0, 1, 2
 DTYPE_F32, DTYPE_F16, DTYPE_BF16 = 0, 1, 2
 FLAG_NO_PERSISTENT = 1
 FLAG_PERSISTENT = 2
-ARCH_QK_NORM, ARCH_SANDWICH, ARCH_GELU = 1, 2, 4
+ARCH_QK_NORM, ARCH_SANDWICH, ARCH_GELU, ARCH_ATTN_GATE = 1, 2, 4, 8
 
 
 class DUError(RuntimeError):
@@ -36,7 +36,7 @@ class ModelConfig(C.Structure):
                 ("tp_size", C.c_int32), ("tie_embedding", C.c_int32), ("flags", C.c_int32),
                 ("kv_quant", C.c_int32), ("arch_flags", C.c_int32), ("sliding_window", C.c_int32),
                 ("sliding_pattern", C.c_int32), ("rope_theta_local", C.c_float), ("attn_scale", C.c_float),
-                ("reserved", C.c_int32 * 2)]
+                ("rope_rot_dim", C.c_int32), ("reserved", C.c_int32 * 1)]
 
 
 # name -> (restype, argtypes); every symbol of include/deepunity_cuda.h

@@ -98,11 +98,20 @@ __global__ void __launch_bounds__(256) qkv_post_kernel(QkvPost a)
     if (w >= a.M * nh) return;
     const int m = w / nh, h = w - m * nh;
     const int epl = a.hd >> 5;
-    const float *x = a.qkv + ((size_t)m * nh + h) * a.hd + lane * epl;
+    // token row: q heads (each hd q rows, then hd gate rows when gated), k heads, v heads
+    const int qw = a.gated ? 2 : 1;
+    const float *row_m = a.qkv + (size_t)m * (a.hq * qw + 2 * a.hkv) * a.hd;
+    const float *x = row_m + (h < a.hq ? (size_t)h * qw * a.hd : (size_t)(a.hq * (qw - 1) + h) * a.hd) + lane * epl;
     float v[8];
 #pragma unroll
     for (int e = 0; e < 8; e++) v[e] = e < epl ? x[e] : 0.0f;
     const bool isq = h < a.hq, isk = !isq && h < a.hq + a.hkv;
+    if (isq && a.gated) {            // the head's gate rows, as computed (QProjGated's split)
+        float *g = a.gate_out + ((size_t)m * a.hq + h) * a.hd + lane * epl;
+#pragma unroll
+        for (int e = 0; e < 8; e++)
+            if (e < epl) g[e] = x[a.hd + e];
+    }
     const __half *gam = isq ? a.q_norm : (isk ? a.k_norm : nullptr);
     if (gam != nullptr) {
         float ss = 0.0f;
@@ -116,15 +125,20 @@ __global__ void __launch_bounds__(256) qkv_post_kernel(QkvPost a)
     }
     const int pos = a.pos[m];
     if (isq || isk) {
-        const int hd2 = a.hd >> 1;
+        // split-half RoPE over the first rot dims (all of them: ApplyRopeSplitHalf; fewer:
+        // ApplyRopePartial, Qwen3_5CS.compute:367-393): dim d < rot/2 pairs with d + rot/2,
+        // which lives rot/2 / epl lanes away; dims >= rot are left as they are
+        const int hd2 = a.hd >> 1, rot = a.rot > 0 ? a.rot : a.hd, r2 = rot >> 1, d0 = lane * epl;
+        const int xs = r2 / epl;                         // a power of two <= 16 (checked on the host)
 #pragma unroll
         for (int e = 0; e < 8; e++) {
-            const float o = __shfl_xor_sync(0xffffffffu, v[e], 16);
-            if (e < epl) {
-                const int i = (lane & 15) * epl + e;
+            const float o = __shfl_xor_sync(0xffffffffu, v[e], xs);
+            if (e < epl && d0 < rot) {
+                const bool first = d0 < r2;
+                const int i = (first ? d0 : d0 - r2) + e;
                 const float c = __half2float(a.rope_cos[(size_t)pos * hd2 + i]);
                 const float s = __half2float(a.rope_sin[(size_t)pos * hd2 + i]);
-                v[e] = lane < 16 ? v[e] * c - o * s : v[e] * c + o * s;
+                v[e] = first ? v[e] * c - o * s : v[e] * c + o * s;
             }
         }
     }
@@ -146,6 +160,31 @@ __global__ void __launch_bounds__(256) qkv_post_kernel(QkvPost a)
 #pragma unroll
     for (int e = 0; e < 8; e++)
         if (e < epl) dst[e] = __float2half_rn(v[e]);
+}
+
+// ApplyAttnGate (Qwen3_5CS.compute:706-714): att[i] *= 1 / (1 + exp(-gate[i])).
+__global__ void __launch_bounds__(256) attn_gate_kernel(float *att, const float *gate, size_t n)
+{
+    pdl_wait();
+    pdl_trigger();
+    const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) att[i] = att[i] * (1.0f / (1.0f + expf(-gate[i])));
+}
+
+int launch_attn_gate(float *att, const float *gate, size_t n, cudaStream_t st)
+{
+    if (n == 0) return DU_OK;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)((n + 255) / 256));
+    cfg.blockDim = dim3(256);
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl_enabled() ? 1 : 0;
+    DU_CUDA_TRY(cudaLaunchKernelEx(&cfg, attn_gate_kernel, att, gate, n));
+    return DU_OK;
 }
 
 int launch_qkv_post(const QkvPost &a, cudaStream_t st)

@@ -96,8 +96,13 @@ struct QkvPost {
     float *q_out;                        // [M][hq][hd]
     __half *k_cache, *v_cache;           // fp16 cache [seq][cap][hkv][hd], or
     Kv8Cache kv8;                        // the INT8 cache (kv8.k8 != nullptr)
+    int gated;                           // q heads carry hd gate rows after their hd q rows
+    float *gate_out;                     // gated: [M][hq][hd] gate values
+    int rot;                             // rotated dims per head (0: hd)
 };
 int launch_qkv_post(const QkvPost &a, cudaStream_t st);
+// att[i] *= sigmoid(gate[i]) (Qwen3.5 attention output gate)
+int launch_attn_gate(float *att, const float *gate, size_t n, cudaStream_t st);
 // x_res += y * rms(y) * (1 + gamma') per row (sandwich norm + residual)
 int launch_norm_add(const float *y, const __half *gamma_m1, int rows, int H, float eps, float *x_res, cudaStream_t st);
 int launch_embed(const int *ids, const __half *embed, float scale, int M, int H, float *out, cudaStream_t st);

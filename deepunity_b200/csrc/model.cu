@@ -92,7 +92,20 @@ static int check_cfg(const du_model_config &c)
                  "config: num_heads_q must be a multiple of num_heads_kv");
     DU_CHECK_ARG(c.head_dim == 64 || c.head_dim == 128 || c.head_dim == 256, "config: head_dim must be 64, 128 or 256");
     DU_CHECK_ARG(c.kv_quant != DU_KV_INT8 || c.head_dim <= 128, "config: the INT8 KV cache supports head_dim 64/128");
-    DU_CHECK_ARG((c.arch_flags & ~(DU_ARCH_QK_NORM | DU_ARCH_SANDWICH | DU_ARCH_GELU)) == 0, "config: unknown arch_flags");
+    DU_CHECK_ARG((c.arch_flags & ~(DU_ARCH_QK_NORM | DU_ARCH_SANDWICH | DU_ARCH_GELU | DU_ARCH_ATTN_GATE)) == 0,
+                 "config: unknown arch_flags");
+    if (c.arch_flags & DU_ARCH_ATTN_GATE)
+        DU_CHECK_ARG((c.arch_flags & DU_ARCH_QK_NORM) && (c.tp_size <= 1),
+                     "config: DU_ARCH_ATTN_GATE needs DU_ARCH_QK_NORM and a single GPU");
+    if (c.rope_rot_dim != 0 && c.rope_rot_dim != c.head_dim) {
+        // partial RoPE runs in the qk-norm kernel: rot/2 must be whole lanes of a warp's head
+        // (head_dim / 32 values per lane) and a power-of-two number of them
+        const int epl = c.head_dim / 32, r2 = c.rope_rot_dim / 2;
+        DU_CHECK_ARG(c.rope_rot_dim > 0 && c.rope_rot_dim < c.head_dim && c.rope_rot_dim % 2 == 0 &&
+                         (c.arch_flags & DU_ARCH_QK_NORM) && r2 % epl == 0 && ((r2 / epl) & (r2 / epl - 1)) == 0,
+                     "config: rope_rot_dim must be head_dim, or an even number below it whose half is a power-of-two "
+                     "multiple of head_dim / 32, with DU_ARCH_QK_NORM");
+    }
     DU_CHECK_ARG(c.sliding_window >= 0 && c.attn_scale >= 0.0f, "config: negative sliding_window / attn_scale");
     const int G = c.num_heads_q / c.num_heads_kv;
     DU_CHECK_ARG(G == 1 || G == 2 || G == 4 || G == 8, "config: GQA group must be 1, 2, 4 or 8");
@@ -190,6 +203,7 @@ static int model_alloc(du_model *m)
     m->inter = (float *)dalloc(m, sizeof(float) * T * m->I_l, &rc);
     if (m->kv8) m->kv_stage = (float *)dalloc(m, sizeof(float) * T * 2 * m->hkv_l * hd, &rc);
     if (m->arch & DU_ARCH_QK_NORM) m->qkv_buf = (float *)dalloc(m, sizeof(float) * T * m->qkv_rows, &rc);
+    if (m->arch & DU_ARCH_ATTN_GATE) m->gate_buf = (float *)dalloc(m, sizeof(float) * T * m->hq_l * hd, &rc);
     // one-row decode steps fold the O projection into flash-decode when the shapes allow
     // (DU_FUSE_ATTN_O=0 in the environment keeps them separate)
     {
@@ -252,12 +266,15 @@ static int model_alloc(du_model *m)
     // RoPE tables on the host with the reference formula (MiniCPM5Model.cs:163-191); the
     // sliding-window layers' tables use the local base (Gemma3Model: ropeCosLocal)
     const int hd2 = hd / 2;
+    const int rot = m->cfg.rope_rot_dim > 0 ? m->cfg.rope_rot_dim : hd;
     std::vector<uint16_t> c((size_t)m->cap * hd2), s((size_t)m->cap * hd2);
     for (int table = 0; table < (m->window > 0 ? 2 : 1); table++) {
         const float theta = table == 0 || m->cfg.rope_theta_local <= 0.0f ? m->cfg.rope_theta : m->cfg.rope_theta_local;
         for (int pos = 0; pos < m->cap; pos++)
             for (int i = 0; i < hd2; i++) {
-                const float f = 1.0f / powf(theta, 2.0f * (float)i / (float)hd);
+                // over the rotated dims (Qwen3.5 partial RoPE: Qwen3_5Model.cs:228-260); entries
+                // i >= rot / 2 are not read then
+                const float f = 1.0f / powf(theta, 2.0f * (float)i / (float)rot);
                 const float ang = (float)pos * f;
                 c[(size_t)pos * hd2 + i] = f32_to_f16(cosf(ang));
                 s[(size_t)pos * hd2 + i] = f32_to_f16(sinf(ang));
@@ -331,11 +348,14 @@ static int shard_window(const du_model_config &c, int tk, ShardWindow *w)
     const int tp = c.tp_size <= 0 ? 1 : c.tp_size, r = c.tp_rank;
     const int64_t H = c.hidden_size, hd = c.head_dim, I = c.intermediate_size;
     const int64_t hq_l = c.num_heads_q / tp, hkv_l = c.num_heads_kv / tp, I_l = I / tp, V_l = c.vocab_size / tp;
+    const int64_t qw = (c.arch_flags & DU_ARCH_ATTN_GATE) ? 2 : 1;     // q rows then gate rows per head
     ShardWindow s = {};
     switch (tk) {
-    case T_Q: s = {c.num_heads_q * hd, H, r * hq_l * hd, (r + 1) * hq_l * hd, 0, H, 0, H}; break;
-    case T_K: s = {c.num_heads_kv * hd, H, r * hkv_l * hd, (r + 1) * hkv_l * hd, 0, H, hq_l * hd, H}; break;
-    case T_V: s = {c.num_heads_kv * hd, H, r * hkv_l * hd, (r + 1) * hkv_l * hd, 0, H, (hq_l + hkv_l) * hd, H}; break;
+    case T_Q: s = {c.num_heads_q * qw * hd, H, r * hq_l * qw * hd, (r + 1) * hq_l * qw * hd, 0, H, 0, H}; break;
+    case T_K: s = {c.num_heads_kv * hd, H, r * hkv_l * hd, (r + 1) * hkv_l * hd, 0, H, hq_l * qw * hd, H}; break;
+    case T_V:
+        s = {c.num_heads_kv * hd, H, r * hkv_l * hd, (r + 1) * hkv_l * hd, 0, H, (hq_l * qw + hkv_l) * hd, H};
+        break;
     case T_O: s = {H, c.num_heads_q * hd, 0, H, r * hq_l * hd, (r + 1) * hq_l * hd, 0, hq_l * hd}; break;
     case T_GATE: s = {I, H, r * I_l, (r + 1) * I_l, 0, H, 0, H}; break;
     case T_UP: s = {I, H, r * I_l, (r + 1) * I_l, 0, H, I_l, H}; break;
@@ -703,7 +723,7 @@ static int enqueue_stage(du_model *m, const StepIO &io, int l, int stage, bool c
     cudaStream_t st = m->stream;
     int rc = DU_OK;
     const bool sw = layer_sliding(m, l);
-    const bool fused_o = m->fuse_o && M == 1 && collective && !sw;
+    const bool fused_o = m->fuse_o && M == 1 && collective && !sw && !(m->arch & DU_ARCH_ATTN_GATE);
     if (stage == ST_O && fused_o) return DU_OK;      // ran inside flash-decode
     if (stage == ST_ATTN && fused_o) {
         const Layer &ly = m->layers[l];
@@ -719,13 +739,18 @@ static int enqueue_stage(du_model *m, const StepIO &io, int l, int stage, bool c
         const int window = sw ? m->window : 0;
         if (m->kv8) {
             const Kv8Cache kv = kv8_layer(m, l);
-            return launch_flash_decode_cluster(m->q, nullptr, nullptr, io.seq_of, io.kv_len, io.kv_len_add, M, m->hq_l,
-                                               m->hkv_l, hd, m->cap, m->attn_scale, m->att, st, io.kv_new, &kv, window);
+            rc = launch_flash_decode_cluster(m->q, nullptr, nullptr, io.seq_of, io.kv_len, io.kv_len_add, M, m->hq_l,
+                                             m->hkv_l, hd, m->cap, m->attn_scale, m->att, st, io.kv_new, &kv, window);
+        } else {
+            __half *kc = m->k_cache + (size_t)l * m->kv_layer_elems;
+            __half *vc = m->v_cache + (size_t)l * m->kv_layer_elems;
+            rc = launch_flash_decode_cluster(m->q, kc, vc, io.seq_of, io.kv_len, io.kv_len_add, M, m->hq_l, m->hkv_l,
+                                             hd, m->cap, m->attn_scale, m->att, st, io.kv_new, nullptr, window);
         }
-        __half *kc = m->k_cache + (size_t)l * m->kv_layer_elems;
-        __half *vc = m->v_cache + (size_t)l * m->kv_layer_elems;
-        return launch_flash_decode_cluster(m->q, kc, vc, io.seq_of, io.kv_len, io.kv_len_add, M, m->hq_l, m->hkv_l,
-                                           hd, m->cap, m->attn_scale, m->att, st, io.kv_new, nullptr, window);
+        // Qwen3.5: attention output * sigmoid(gate) before o_proj (ApplyAttnGate)
+        if (rc == DU_OK && (m->arch & DU_ARCH_ATTN_GATE))
+            rc = launch_attn_gate(m->att, m->gate_buf, (size_t)M * m->hq_l * hd, st);
+        return rc;
     }
     if (stage < ST_QKV || stage > ST_DOWN) return fail(DU_EINVAL, "unknown stage");
     GemvParams gp = stage_gemv_params(m, io, l, stage);
@@ -741,6 +766,9 @@ static int enqueue_stage(du_model *m, const StepIO &io, int l, int stage, bool c
         a.rope_cos = sw ? m->rope_cos_local : m->rope_cos;
         a.rope_sin = sw ? m->rope_sin_local : m->rope_sin;
         a.q_out = m->q;
+        a.gated = (m->arch & DU_ARCH_ATTN_GATE) ? 1 : 0;
+        a.gate_out = m->gate_buf;
+        a.rot = m->cfg.rope_rot_dim;
         if (m->kv8) a.kv8 = kv8_layer(m, l);
         else {
             a.k_cache = m->k_cache + (size_t)l * m->kv_layer_elems;
@@ -1068,7 +1096,7 @@ DU_API int du_model_create(const du_model_config *cfg, du_model **out)
     m->H = cfg->hidden_size; m->I = cfg->intermediate_size; m->L = cfg->num_layers;
     m->hq = cfg->num_heads_q; m->hkv = cfg->num_heads_kv; m->hd = cfg->head_dim; m->V = cfg->vocab_size;
     m->hq_l = m->hq / m->tp; m->hkv_l = m->hkv / m->tp; m->I_l = m->I / m->tp; m->V_l = m->V / m->tp;
-    m->qkv_rows = (m->hq_l + 2 * m->hkv_l) * m->hd;
+    m->qkv_rows = (m->hq_l * ((cfg->arch_flags & DU_ARCH_ATTN_GATE) ? 2 : 1) + 2 * m->hkv_l) * m->hd;
     m->quant = cfg->quant;
     m->group = cfg->quant == DU_QUANT_INT4 ? cfg->group_size : 32;
     m->cap = cfg->kv_capacity;

@@ -62,6 +62,7 @@ struct du_model {
     float attn_scale = 0.0f;                             // softmax scale
     __half *rope_cos_local = nullptr, *rope_sin_local = nullptr;   // RoPE of the sliding-window layers
     float *qkv_buf = nullptr;                            // qk-norm models: QKV GEMV output [T][qkv_rows]
+    float *gate_buf = nullptr;                           // DU_ARCH_ATTN_GATE: attention output gates [T][hq_l][hd]
     bool fuse_o = false;                                 // one-row decode: O projection inside flash-decode
     float *o_part = nullptr; unsigned *o_cnt = nullptr;  // its per-kv-head partial sums and arrival counters
     // device state

@@ -55,6 +55,7 @@ class LlamaConfig:
     sliding_pattern: int = 0         # every n-th layer (1-based) is full attention
     rope_theta_local: float = 0.0    # RoPE base of the sliding-window layers
     attn_scale: float = 0.0          # softmax scale (0: head_dim^-0.5)
+    rope_rot_dim: int = 0            # rotated dims per head (0: head_dim; Qwen3.5 partial RoPE)
     embed_scale: float = 1.0         # embedding multiplier (Gemma3: sqrt(hidden))
 
 
@@ -112,6 +113,7 @@ class LlamaForCausalLM(LLM):
         cfg.arch_flags, cfg.sliding_window, cfg.sliding_pattern = (config.arch_flags, config.sliding_window,
                                                                    config.sliding_pattern)
         cfg.rope_theta_local, cfg.attn_scale = config.rope_theta_local, config.attn_scale
+        cfg.rope_rot_dim = config.rope_rot_dim
         cfg.quant, cfg.group_size = int(self.quant), config.group_size
         cfg.kv_capacity, cfg.max_batch = max_context_length, max_batch
         cfg.tp_rank, cfg.tp_size, cfg.tie_embedding = tp_rank, tp_size, int(config.tie_embedding)

@@ -75,7 +75,9 @@ typedef struct du_model_config {
     int32_t sliding_pattern; /* every sliding_pattern-th layer (1-based) is full attention; <= 0: none */
     float rope_theta_local;  /* RoPE base of the sliding-window layers (0: rope_theta) */
     float attn_scale;        /* softmax scale (0: head_dim^-0.5; Gemma3: query_pre_attn_scalar^-0.5) */
-    int32_t reserved[2];
+    int32_t rope_rot_dim;    /* rotated dims per head (0: head_dim); < head_dim needs DU_ARCH_QK_NORM
+                                (Qwen3.5 partial RoPE, Qwen3_5CS.compute:367-393) */
+    int32_t reserved[1];
 } du_model_config;
 
 /* du_model_config.arch_flags */
@@ -86,7 +88,12 @@ enum {
                                 layer_<i>/post_attention_layernorm.bin is then the post-attention
                                 norm, pre_feedforward_layernorm.bin the pre-MLP one and
                                 post_feedforward_layernorm.bin the post-FFN one */
-    DU_ARCH_GELU = 4         /* GLU activation gelu (tanh form, G3CS:162-172) instead of SiLU */
+    DU_ARCH_GELU = 4,        /* GLU activation gelu (tanh form, G3CS:162-172) instead of SiLU */
+    DU_ARCH_ATTN_GATE = 8    /* Qwen3.5 full-attention layers (Qwen3_5Model.cs:397-574): the q
+                                projection holds, per head, head_dim q rows then head_dim gate rows
+                                (QProjGated, Qwen3_5CS.compute:306-330), and the attention output
+                                is multiplied by sigmoid(gate) before o_proj (ApplyAttnGate,
+                                :706-714).  Needs DU_ARCH_QK_NORM and tp_size 1 */
 };
 
 /* du_model_config.kv_quant */

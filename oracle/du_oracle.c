@@ -314,6 +314,26 @@ ORC_EXPORT void orc_rope_table(int max_seq, int head_dim, float theta,
         }
 }
 
+/* ApplyRopePartial (Qwen3_5CS.compute:367-393): pair (i, i + rot/2) for i < rot/2 of
+ * every head, dims [rot, hd) untouched; tables [pos, rot/2] (Qwen3_5Model.cs:228-260:
+ * inv_freq_i = 1 / theta^(2i/rot)). */
+static void rope_apply_partial(float *buf, int seq_len, int num_heads, int head_dim, int rot, int position_offset,
+                               const uint16_t *cos_tab, const uint16_t *sin_tab)
+{
+    int r2 = rot / 2;
+    for (int l = 0; l < seq_len; l++)
+        for (int h = 0; h < num_heads; h++) {
+            float *b = buf + ((int64_t)l * num_heads + h) * head_dim;
+            int64_t p = (int64_t)(position_offset + l) * r2;
+            for (int i = 0; i < r2; i++) {
+                float x1 = b[i], x2 = b[i + r2];
+                float c = read_h(cos_tab, p + i), s = read_h(sin_tab, p + i);
+                b[i] = x1 * c - x2 * s;
+                b[i + r2] = x2 * c + x1 * s;
+            }
+        }
+}
+
 /* ApplyRopeSplitHalf (G3CS:271-297): pair (i, i + hd/2) of every head. */
 ORC_EXPORT void orc_rope_apply(float *buf, int seq_len, int num_heads, int head_dim,
                                int position_offset, const uint16_t *cos_tab,
@@ -661,6 +681,12 @@ typedef struct {
     const uint16_t *rope_cos_local; const uint16_t *rope_sin_local;
     const uint16_t **q_norm; const uint16_t **k_norm;
     const uint16_t **post_attn_ln; const uint16_t **post_ffn_ln;
+    /* Qwen3.5 full-attention layers (Qwen3_5Model.cs:397-574): arch bit 8 = gated q
+     * (QProjGated, Qwen3_5CS.compute:306-330: head h's rows are hd q rows then hd gate rows;
+     * ApplyAttnGate :706-714: attended *= sigmoid(gate)); rot_dim < hd = partial RoPE with
+     * the rope_*_partial tables [pos, rot_dim/2]. */
+    int32_t rot_dim;
+    const uint16_t *rope_cos_partial; const uint16_t *rope_sin_partial;
 } orc_model;
 
 static int layer_is_sliding(const orc_model *md, int li)
@@ -676,7 +702,9 @@ ORC_EXPORT int orc_forward(orc_model *md, const int32_t *ids, int seq_len, int l
                            float *logits)
 {
     const int H = md->hidden, I = md->inter, hq = md->hq, hkv = md->hkv, hd = md->hd;
-    const int inner = hq * hd, qkvd = inner + 2 * hkv * hd, S = seq_len;
+    const int gated = (md->arch & 8) != 0;
+    const int inner = hq * hd, qkvd = (gated ? 2 : 1) * inner + 2 * hkv * hd, S = seq_len;
+    const int rot = md->rot_dim > 0 && md->rot_dim < hd ? md->rot_dim : hd;
     if (md->cache_len + S > md->capacity) return -1;
     const int cache_len = md->cache_len, kv_len = cache_len + S;
     const float scale = md->attn_scale > 0.0f ? md->attn_scale : powf((float)hd, -0.5f);
@@ -687,6 +715,7 @@ ORC_EXPORT int orc_forward(orc_model *md, const int32_t *ids, int seq_len, int l
     float *v = malloc(sizeof(float) * S * hkv * hd), *att = malloc(sizeof(float) * S * inner);
     float *ao = malloc(sizeof(float) * S * H), *mid = malloc(sizeof(float) * S * I);
     float *g = malloc(sizeof(float) * S * I), *u = malloc(sizeof(float) * S * I);
+    float *gate = malloc(sizeof(float) * S * inner);
 
     for (int l = 0; l < S; l++)                                   /* EmbeddingLookup G3CS:189-201 */
         for (int h = 0; h < H; h++)
@@ -696,10 +725,18 @@ ORC_EXPORT int orc_forward(orc_model *md, const int32_t *ids, int seq_len, int l
         memcpy(skip, hidden, sizeof(float) * S * H);
         orc_rmsnorm(hidden, S, H, md->ln1[li], md->eps, norm);
         orc_gemv(norm, S, H, md->w_qkv[li], md->s_qkv[li], md->quant, md->group, 0, qkvd, qkv);
+        const int kv0 = (gated ? 2 : 1) * inner;                    /* first k row */
         for (int l = 0; l < S; l++) {                              /* SplitQKV G3CS:249-269 */
-            memcpy(q + (int64_t)l * inner, qkv + (int64_t)l * qkvd, sizeof(float) * inner);
-            memcpy(k + (int64_t)l * hkv * hd, qkv + (int64_t)l * qkvd + inner, sizeof(float) * hkv * hd);
-            memcpy(v + (int64_t)l * hkv * hd, qkv + (int64_t)l * qkvd + inner + hkv * hd, sizeof(float) * hkv * hd);
+            if (gated)                                             /* QProjGated's split */
+                for (int h = 0; h < hq; h++) {
+                    memcpy(q + (int64_t)l * inner + h * hd, qkv + (int64_t)l * qkvd + h * 2 * hd, sizeof(float) * hd);
+                    memcpy(gate + (int64_t)l * inner + h * hd, qkv + (int64_t)l * qkvd + h * 2 * hd + hd,
+                           sizeof(float) * hd);
+                }
+            else
+                memcpy(q + (int64_t)l * inner, qkv + (int64_t)l * qkvd, sizeof(float) * inner);
+            memcpy(k + (int64_t)l * hkv * hd, qkv + (int64_t)l * qkvd + kv0, sizeof(float) * hkv * hd);
+            memcpy(v + (int64_t)l * hkv * hd, qkv + (int64_t)l * qkvd + kv0 + hkv * hd, sizeof(float) * hkv * hd);
         }
         if (md->arch & 1) {                                        /* RmsNormHead on q and k */
             rmsnorm_heads(q, S * hq, hd, md->q_norm[li], md->eps);
@@ -709,8 +746,13 @@ ORC_EXPORT int orc_forward(orc_model *md, const int32_t *ids, int seq_len, int l
         const uint16_t *rc = sw && md->rope_cos_local ? md->rope_cos_local : md->rope_cos;
         const uint16_t *rs = sw && md->rope_sin_local ? md->rope_sin_local : md->rope_sin;
         const int win = sw ? md->window : 0;
-        orc_rope_apply(q, S, hq, hd, cache_len, rc, rs);
-        orc_rope_apply(k, S, hkv, hd, cache_len, rc, rs);
+        if (rot < hd) {
+            rope_apply_partial(q, S, hq, hd, rot, cache_len, md->rope_cos_partial, md->rope_sin_partial);
+            rope_apply_partial(k, S, hkv, hd, rot, cache_len, md->rope_cos_partial, md->rope_sin_partial);
+        } else {
+            orc_rope_apply(q, S, hq, hd, cache_len, rc, rs);
+            orc_rope_apply(k, S, hkv, hd, cache_len, rc, rs);
+        }
         if (md->kv_quant == 2) {
             orc_kv_write_int8(k, S, hkv, hd, cache_len, (uint8_t *)md->k_cache[li], md->k_sz[li]);
             orc_kv_write_int8(v, S, hkv, hd, cache_len, (uint8_t *)md->v_cache[li], md->v_sz[li]);
@@ -723,6 +765,8 @@ ORC_EXPORT int orc_forward(orc_model *md, const int32_t *ids, int seq_len, int l
             flash_attention_any(q, md->k_cache[li], md->v_cache[li], NULL, NULL, NULL, NULL, S, kv_len, hq, hkv, hd,
                                 scale, win, att);
         }
+        if (gated)                                                 /* ApplyAttnGate */
+            for (int64_t i = 0; i < (int64_t)S * inner; i++) att[i] = att[i] * (1.0f / (1.0f + expf(-gate[i])));
         orc_gemv(att, S, inner, md->w_o[li], md->s_o[li], md->quant, md->group, 0, H, ao);
         if (md->arch & 2) {                                        /* post-attention norm, then the residual */
             orc_rmsnorm(ao, S, H, md->post_attn_ln[li], md->eps, norm);
@@ -761,7 +805,7 @@ ORC_EXPORT int orc_forward(orc_model *md, const int32_t *ids, int seq_len, int l
     orc_gemv(norm, rows, H, md->lm_head, NULL, ORC_FP16, 0, 0, md->vocab, logits);
 
     free(hidden); free(skip); free(norm); free(qkv); free(q); free(k); free(v);
-    free(att); free(ao); free(mid); free(g); free(u);
+    free(att); free(ao); free(mid); free(g); free(u); free(gate);
     return 0;
 }
 

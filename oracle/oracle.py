@@ -272,7 +272,8 @@ class _OrcModel(C.Structure):
                 ("arch", C.c_int32), ("window", C.c_int32), ("pattern", C.c_int32), ("attn_scale", C.c_float),
                 ("rope_cos_local", C.c_void_p), ("rope_sin_local", C.c_void_p),
                 ("q_norm", C.POINTER(C.c_void_p)), ("k_norm", C.POINTER(C.c_void_p)),
-                ("post_attn_ln", C.POINTER(C.c_void_p)), ("post_ffn_ln", C.POINTER(C.c_void_p))]
+                ("post_attn_ln", C.POINTER(C.c_void_p)), ("post_ffn_ln", C.POINTER(C.c_void_p)),
+                ("rot_dim", C.c_int32), ("rope_cos_partial", C.c_void_p), ("rope_sin_partial", C.c_void_p)]
 
 
 class OracleModel:
@@ -326,6 +327,13 @@ class OracleModel:
             tl = getattr(cfg, "theta_local", 0.0) or cfg.theta
             self.rope_cos_local, self.rope_sin_local = rope_table(capacity, cfg.hd, tl)
             m.rope_cos_local, m.rope_sin_local = _p(self.rope_cos_local).value, _p(self.rope_sin_local).value
+        # Qwen3.5 full-attention layers: partial RoPE tables [pos, rot/2] over the rotated dims
+        rot = getattr(cfg, "rot", 0)
+        m.rot_dim = rot
+        if 0 < rot < cfg.hd:
+            self.rope_cos_partial, self.rope_sin_partial = rope_table(capacity, rot, cfg.theta)
+            m.rope_cos_partial = _p(self.rope_cos_partial).value
+            m.rope_sin_partial = _p(self.rope_sin_partial).value
         for name in ("q_norm", "k_norm", "post_attn", "post_ffn"):
             lst = getattr(weights, name, [])
             if lst:

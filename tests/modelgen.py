@@ -32,6 +32,9 @@ class TestConfig:
     theta_local: float = 0.0
     attn_scale: float = 0.0
     embed_scale: float = 1.0
+    # Qwen3.5 full-attention layers: arch bit 8 (q projection with an output gate per head),
+    # rotary dims (0 = head_dim)
+    rot: int = 0
 
     def du_kwargs(self):
         from deepunity_b200.llm import LlamaConfig
@@ -39,7 +42,7 @@ class TestConfig:
                            self.eps, self.theta, group_size=self.group if self.quant == "int4" else 128,
                            arch_flags=self.arch, sliding_window=self.window, sliding_pattern=self.pattern,
                            rope_theta_local=self.theta_local, attn_scale=self.attn_scale,
-                           embed_scale=self.embed_scale)
+                           embed_scale=self.embed_scale, rope_rot_dim=self.rot)
 
 
 SMALL = TestConfig(hidden=256, inter=512, layers=2, hq=4, hkv=2, hd=64, vocab=1024)
@@ -68,7 +71,8 @@ class ModelWeights:
             return w.astype(np.float16).view(np.uint16), None
 
         for li in range(cfg.layers):
-            shapes = {"self_attn_q_proj": (cfg.hq * hd, H), "self_attn_k_proj": (cfg.hkv * hd, H),
+            qrows = cfg.hq * hd * (2 if cfg.arch & 8 else 1)        # QProjGated: q then gate rows per head
+            shapes = {"self_attn_q_proj": (qrows, H), "self_attn_k_proj": (cfg.hkv * hd, H),
                       "self_attn_v_proj": (cfg.hkv * hd, H), "self_attn_o_proj": (H, cfg.hq * hd),
                       "mlp_gate_proj": (I, H), "mlp_up_proj": (I, H), "mlp_down_proj": (H, I)}
             qd = {}

@@ -45,7 +45,13 @@ def _cfg(**kw):
 
 @pytest.mark.parametrize("bad", [dict(num_heads_q=3), dict(head_dim=96), dict(quant=7),
                                  dict(quant=2, group_size=48), dict(tp_size=2, tp_rank=2),
-                                 dict(tp_size=3), dict(max_batch=0), dict(hidden_size=250)])
+                                 dict(tp_size=3), dict(max_batch=0), dict(hidden_size=250),
+                                 # Qwen3.5 attention gate without qk-norm, or over two ranks
+                                 dict(arch_flags=8), dict(arch_flags=9, tp_size=2, tp_rank=0),
+                                 # partial RoPE: half not a power-of-two multiple of hd/32, odd,
+                                 # above head_dim, or without qk-norm
+                                 dict(arch_flags=1, rope_rot_dim=48), dict(arch_flags=1, rope_rot_dim=33),
+                                 dict(arch_flags=1, rope_rot_dim=128), dict(rope_rot_dim=32)])
 def test_model_create_rejects_bad_config(bad):
     h = C.c_void_p()
     rc = _lib.lib().du_model_create(C.byref(_cfg(**bad)), C.byref(h))

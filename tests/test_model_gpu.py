@@ -389,6 +389,35 @@ def test_gemma3_variant_greedy_64_matches_oracle(cfg):
     m.Release()
 
 
+# Qwen3.5 full-attention layers on the same kernels (Qwen3_5Model.cs:397-574): q projection
+# with a per-head output gate, qk-norm, partial RoPE over the first rot dims, attention output
+# times sigmoid(gate) before o_proj
+QWEN35_VARIANTS = [
+    TestConfig(512, 1024, 3, 4, 1, 256, 1024, quant="int4", group=128, theta=10_000_000.0, arch=9, rot=64, eps=1e-6),
+    TestConfig(256, 512, 2, 4, 2, 128, 1024, quant="int8", arch=9, rot=32, eps=1e-6),
+]
+
+
+@pytest.mark.parametrize("cfg", QWEN35_VARIANTS, ids=lambda c: f"{c.quant}-hd{c.hd}-rot{c.rot}")
+def test_qwen35_full_attention_greedy_64_matches_oracle(cfg):
+    """A 24-token prompt then 64 greedy steps: identical ids and final logits within 1e-3 of
+    the oracle's restatement of QProjGated, RmsNormHead, ApplyRopePartial and ApplyAttnGate."""
+    w, m = build(cfg, cap=128)
+    om = orc.OracleModel(w, capacity=128)
+    prompt = np.random.default_rng(17).integers(0, cfg.vocab, 24).astype(np.int32)
+    logits, nxt = m.forward(prompt[None, :])
+    ref = om.forward(prompt)
+    assert relerr(logits[0], ref) < LOGIT_TOL
+    toks, rtoks = [int(nxt[0])], [orc.argmax(ref)]
+    for _ in range(63):
+        toks.append(int(m.decode_step([toks[-1]])[0]))
+        r = om.forward([rtoks[-1]])
+        rtoks.append(orc.argmax(r))
+    assert toks == rtoks
+    assert relerr(m.read_logits(1)[0], r) < LOGIT_TOL
+    m.Release()
+
+
 def test_gemma3_variant_int8_kv_teacher_forced():
     """The Gemma3 variant over the INT8 cache (the qkv-post kernel quantizes k / v rows)."""
     cfg = GEMMA_VARIANTS[0]
