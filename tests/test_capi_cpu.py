@@ -59,6 +59,20 @@ def test_model_create_rejects_bad_config(bad):
     assert h.value is None
 
 
+def test_penalty_entry_points_validate_before_touching_the_device():
+    """du_apply_penalties / du_mark_seen / du_decode_step_sample_ex reject bad arguments
+    with a status (no GPU needed)."""
+    L = _lib.lib()
+    p = C.c_void_p(16)
+    assert L.du_apply_penalties(None, 1, 8, 8, p, 8, C.c_float(0.0), C.c_float(1.0), None) == _lib.DU_EINVAL
+    assert L.du_apply_penalties(p, 1, 8, 4, p, 8, C.c_float(0.0), C.c_float(1.0), None) == _lib.DU_EINVAL  # ldl < vocab
+    assert L.du_apply_penalties(p, 1, 8, 8, p, 8, C.c_float(0.0), C.c_float(-1.0), None) == _lib.DU_EINVAL
+    assert L.du_mark_seen(p, 1, 4, 8, p, None) == _lib.DU_EINVAL                                      # ld < vocab
+    assert L.du_mark_seen(None, 1, 8, 8, p, None) == _lib.DU_EINVAL
+    assert L.du_decode_step_sample_ex(None, None, 1, C.c_float(0.0), 0, C.c_float(1.0), C.c_float(0.0),
+                                      C.c_float(0.0), C.c_float(1.0), None, None) != 0
+
+
 def test_kernel_entry_points_validate_before_touching_the_device():
     L = _lib.lib()
     assert L.du_gemv_q4(None, None, 0, None, None, 128, 1, 1, 128, None) == _lib.DU_EINVAL
