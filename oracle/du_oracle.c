@@ -317,8 +317,8 @@ ORC_EXPORT void orc_rope_table(int max_seq, int head_dim, float theta,
 /* ApplyRopePartial (Qwen3_5CS.compute:367-393): pair (i, i + rot/2) for i < rot/2 of
  * every head, dims [rot, hd) untouched; tables [pos, rot/2] (Qwen3_5Model.cs:228-260:
  * inv_freq_i = 1 / theta^(2i/rot)). */
-static void rope_apply_partial(float *buf, int seq_len, int num_heads, int head_dim, int rot, int position_offset,
-                               const uint16_t *cos_tab, const uint16_t *sin_tab)
+ORC_EXPORT void orc_rope_apply_partial(float *buf, int seq_len, int num_heads, int head_dim, int rot,
+                                       int position_offset, const uint16_t *cos_tab, const uint16_t *sin_tab)
 {
     int r2 = rot / 2;
     for (int l = 0; l < seq_len; l++)
@@ -747,8 +747,8 @@ ORC_EXPORT int orc_forward(orc_model *md, const int32_t *ids, int seq_len, int l
         const uint16_t *rs = sw && md->rope_sin_local ? md->rope_sin_local : md->rope_sin;
         const int win = sw ? md->window : 0;
         if (rot < hd) {
-            rope_apply_partial(q, S, hq, hd, rot, cache_len, md->rope_cos_partial, md->rope_sin_partial);
-            rope_apply_partial(k, S, hkv, hd, rot, cache_len, md->rope_cos_partial, md->rope_sin_partial);
+            orc_rope_apply_partial(q, S, hq, hd, rot, cache_len, md->rope_cos_partial, md->rope_sin_partial);
+            orc_rope_apply_partial(k, S, hkv, hd, rot, cache_len, md->rope_cos_partial, md->rope_sin_partial);
         } else {
             orc_rope_apply(q, S, hq, hd, cache_len, rc, rs);
             orc_rope_apply(k, S, hkv, hd, cache_len, rc, rs);

@@ -47,6 +47,7 @@ def lib():
         _lib.orc_rmsnorm.argtypes = [P, C.c_int, C.c_int, P, C.c_float, P]
         _lib.orc_rope_table.argtypes = [C.c_int, C.c_int, C.c_float, P, P]
         _lib.orc_rope_apply.argtypes = [P, C.c_int, C.c_int, C.c_int, C.c_int, P, P]
+        _lib.orc_rope_apply_partial.argtypes = [P, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, P, P]
         _lib.orc_kv_write.argtypes = [P, C.c_int, C.c_int, C.c_int, C.c_int, P]
         _lib.orc_flash_attention.argtypes = [P, P, P, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int,
                                              C.c_float, P]
@@ -135,6 +136,15 @@ def rope_table(max_seq: int, head_dim: int, theta: float):
     s = np.empty((max_seq, head_dim // 2), np.uint16)
     lib().orc_rope_table(max_seq, head_dim, theta, _p(c), _p(s))
     return c, s
+
+
+def rope_apply_partial(buf: np.ndarray, num_heads: int, head_dim: int, rot: int, pos_offset: int, cos_t, sin_t):
+    """ApplyRopePartial restated (Qwen3_5CS.compute:367-393) on [seq, heads, hd] in place;
+    tables [pos, rot/2] from rope_table(max_seq, rot, theta)."""
+    b = np.ascontiguousarray(buf, dtype=np.float32)
+    seq = b.size // (num_heads * head_dim)
+    lib().orc_rope_apply_partial(_p(b), seq, num_heads, head_dim, rot, pos_offset, _p(cos_t), _p(sin_t))
+    return b
 
 
 def rope_apply(buf: np.ndarray, num_heads: int, head_dim: int, pos_offset: int, cos_t, sin_t):
